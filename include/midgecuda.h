@@ -1,0 +1,208 @@
+/* midgecuda.h -- C ABI of libmidgecuda.so, the sm_100a quantized-MoE hot path.
+ *
+ * The reference engine (drmihirbrahme/midge) calls its kernels directly as
+ * static C functions; this header is the seam a C host binds instead.  Each
+ * entry point names the reference interface it replaces (file:line within the
+ * reference project).  Conventions:
+ *   - every function returns MG_OK (0) or a negative MG_ERR_* code and never
+ *     exits the process; mg_last_error() gives the message of the calling
+ *     thread's last failure;
+ *   - "kernel level" functions take DEVICE pointers and a cudaStream_t passed
+ *     as void* (NULL = legacy default stream); they are asynchronous;
+ *   - "model level" functions take HOST pointers and synchronise before they
+ *     return; one host thread drives one mg_model.
+ * Weight dtypes and byte layouts are exactly the midge container's
+ * (engine/mten.h:24-31): q8r = int8 rows + f32 row scales; q4g32 / mxfp4 =
+ * packed nibbles (low nibble = even column) + one scale per 32 columns.
+ */
+#ifndef MIDGECUDA_H
+#define MIDGECUDA_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* weight dtypes: same codes as engine/mten.h:42 */
+enum { MG_F32 = 0, MG_Q8R = 1, MG_Q4G32 = 2, MG_MXFP4 = 3 };
+/* encoding of the per-32-column scales of q4g32/mxfp4 */
+enum { MG_SCALE_F16 = 0, MG_SCALE_UE8M0 = 1 };
+
+enum {
+    MG_OK = 0,
+    MG_ERR_ARG = -1,     /* bad argument */
+    MG_ERR_CUDA = -2,    /* CUDA runtime error */
+    MG_ERR_OOM = -3,     /* device allocation failed */
+    MG_ERR_STATE = -4,   /* call out of order (e.g. forward before ready) */
+    MG_ERR_RANGE = -5,   /* context full or token out of range: the reference exits 4 (engine/midge.c:554-555) */
+    MG_ERR_SPEC = -6,    /* bad spec / missing tensor: the reference exits 3 (engine/midge.c:136,195-201) */
+    MG_ERR_TIMEOUT = -8, /* a bounded device wait gave up */
+    MG_ERR_COMM = -9     /* expert-parallel communication failed */
+};
+
+const char *mg_last_error(void);
+int mg_version(void);
+
+/* ===================================================== kernel level ==== */
+
+/* y[t][r] = sum_c W[r][c] * x[t][c] (+ bias[r]) for t < n_tok; y may also be
+ * accumulated into (accumulate != 0: y += result).  fp32 accumulation.
+ * Replaces wk_matvec (engine/mkern.h:180) followed by wk_addbias
+ * (engine/mkern.h:245), batched over n_tok <= 16 input vectors.
+ * q4g32/mxfp4 need cols % 32 == 0; q8r needs cols % 64 == 0 or falls back to
+ * the generic path; x rows have stride ldx floats, y rows stride ldy. */
+int mg_gemv(int dt, int scale_fmt, const void *w, const void *scales, int64_t rows, int64_t cols,
+            const float *x, int64_t ldx, int n_tok, const float *bias, int accumulate, float *y,
+            int64_t ldy, void *stream);
+
+/* out[i][:] = dequantised row ids[i] of W; replaces wk_row (engine/mkern.h:201). */
+int mg_dequant_rows(int dt, int scale_fmt, const void *w, const void *scales, int64_t rows,
+                    int64_t cols, const int32_t *ids, int n, float *out, void *stream);
+
+/* Re-express power-of-two f16 group scales as ue8m0 bytes (2^(u-127); u = 0
+ * for a zero scale).  *n_inexact (device int, accumulated) counts scales that
+ * are not a positive power of two or zero; those bytes are left 0.  Exact for
+ * every scale the midge converter writes (tools/convert.py:37-53). */
+int mg_scales_to_ue8m0(const uint16_t *f16, uint8_t *ue8m0, int64_t n, int *n_inexact, void *stream);
+
+/* out = x * (1/sqrt(mean(x^2)+eps)) * w per row of n; replaces wk_rmsnorm
+ * (engine/mkern.h:238).  Parallel sum: equal to the reference within fp32
+ * rounding of the sum of squares. */
+int mg_rmsnorm(const float *x, const float *w, float *out, int64_t n, int n_rows, float eps, void *stream);
+
+/* float -> f16 with the reference's subnormal flush (engine/mkern.h:261). */
+int mg_to_f16_ftz(const float *x, uint16_t *out, int64_t n, void *stream);
+
+/* Router for n_tok normed rows xb: logits = Wr * xb + b with the f32 weight
+ * reduced in the reference's AVX2 lane order (engine/mkern.h:85-99), so the
+ * logits and the selected experts are bit-identical to the reference for the
+ * same xb; then top-k and routing weights.  variant 0 = decode top-k
+ * (engine/midge.c:476-486), 1 = batched-prefill top-k (engine/midge.c:410-422);
+ * router_norm as engine/midge.c:423-433.  Outputs: logits [n_tok x E],
+ * sel [n_tok x k] (int32), weights [n_tok x k].  Replaces route_topk
+ * (engine/midge.c:404). */
+int mg_router_topk(const float *xb, int n_tok, const float *rw, const float *rb, int n_experts,
+                   int64_t hidden, int top_k, int router_norm, int variant, float *logits, int32_t *sel,
+                   float *weights, void *stream);
+
+/* Expert geometry of experts.midge (engine/mten.h:136-150). */
+typedef struct {
+    int dt;          /* MG_* dtype of every expert matrix */
+    int scale_fmt;   /* MG_SCALE_* of the 4-bit scales as stored on the device */
+    int64_t hidden, ffn;
+    int64_t off[3][3];   /* [gate,up,down][data,scales,bias] byte offsets within an expert */
+    int64_t expert_stride, layer_stride;
+} mg_expert_layout;
+
+/* Fill an mg_expert_layout exactly as wt_expert_layout (engine/mten.h:136). */
+int mg_expert_layout_init(mg_expert_layout *L, int dt, int64_t hidden, int64_t ffn, int64_t n_experts);
+
+/* Routed-expert FFN for n_tok tokens of one layer (decode form):
+ *   x[t] += sum_i w[t][i] * (down_e(act(gate_e(xb[t]) + bg, up_e(xb[t]) + bu)) + bd),
+ *   e = sel[t][i], summed in top-k rank order as engine/midge.c:514-548.
+ * experts_layer points at layer 0 of the experts blob; layer selects the layer.
+ * act_plain / alpha / limit as engine/midge.c:525-539.  n_tok <= 16.
+ * h_scratch: device buffer of n_tok*top_k*ffn floats. */
+int mg_moe_ffn(const mg_expert_layout *L, const uint8_t *experts, int layer, int n_experts,
+               const float *xb, int n_tok, int top_k, const int32_t *sel, const float *weights,
+               int act_plain, float alpha, float limit, float *h_scratch, float *x, void *stream);
+
+/* ====================================================== model level ==== */
+
+/* The model spec (engine/midge.c:46-63, parsed from the container's embedded
+ * JSON by the host). */
+typedef struct {
+    int64_t hidden, vocab, ffn;
+    int n_layers, n_heads, n_kv_heads, head_dim;
+    int n_experts, top_k;
+    float alpha, limit;
+    int act_plain, router_norm, qk_norm;
+    int sliding_window, sinks;
+    float norm_eps, rope_theta;
+    int yarn;
+    float yarn_factor, yarn_beta_fast, yarn_beta_slow;
+    int yarn_orig_ctx, yarn_truncate;
+    float attn_scale;
+    const int *layer_sliding; /* n_layers entries, copied at create */
+} mg_spec;
+
+typedef struct mg_model mg_model;
+
+/* Create a model for `max_seqs` concurrent sequences of up to `ctx` tokens on
+ * CUDA device `device`.  Replaces the allocation half of model_load
+ * (engine/midge.c:204-294). */
+int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int device, mg_model **out);
+
+/* Upload one dense tensor named as in dense.midge (embed, lm_head,
+ * final_norm, L<i>.attn.q ...; docs/ADDING_MODELS.md naming); host pointers,
+ * copied into HBM.  Vectors: rows = n, cols = 0, dt = MG_F32.  Replaces the
+ * view resolution of model_load (engine/midge.c:229-260). */
+int mg_model_set_dense(mg_model *m, const char *name, int dt, int64_t rows, int64_t cols,
+                       const void *data, const void *scales);
+
+/* Upload the experts.midge data region (all layers, layout of
+ * mg_expert_layout_init) from host memory with pinned staging and
+ * cudaMemcpyAsync; power-of-two f16 scales are re-expressed as ue8m0 in HBM.
+ * Replaces the mmap of experts.midge (engine/midge.c:210-227). */
+int mg_model_set_experts(mg_model *m, int dt, const void *data, uint64_t bytes);
+
+/* Fill the expert blob with seeded synthetic weights directly in HBM (for
+ * benchmarks of shapes whose files would not fit a disk): MXFP4 nibbles
+ * uniform over 0..15, scales 2^k with k uniform in [-8,-4], biases N(0,0.1);
+ * q8r bytes uniform in [-127,127] with power-of-two row scales. */
+int mg_model_synth_experts(mg_model *m, int dt, uint64_t seed);
+
+/* Finish loading (rope tables, KV caches, work buffers).  After this the
+ * model accepts forward calls. */
+int mg_model_ready(mg_model *m);
+
+/* Forget sequence `seq`'s context (position 0). */
+int mg_model_reset(mg_model *m, int seq);
+int mg_model_pos(const mg_model *m, int seq);
+
+/* One token of sequence `seq` through the model: forward
+ * (engine/midge.c:552-566).  logits (host, vocab floats) and/or argmax (host
+ * int32, first maximum wins as engine/midge.c:657-660) may be NULL. */
+int mg_forward(mg_model *m, int seq, int32_t token, float *logits, int32_t *argmax);
+
+/* Expert-major batched prefill of n tokens of sequence `seq`: forward_batch
+ * (engine/midge.c:576-622).  logits_mode 0 = none, 1 = last position,
+ * 2 = every position ([n x vocab]). */
+int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n, int logits_mode, float *logits);
+
+/* One decode step for n_seqs sequences at once (one token each): the
+ * concurrent-sequence form of forward.  logits [n_seqs x vocab] and argmax
+ * [n_seqs] (host) may be NULL. */
+int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, float *logits,
+                   int32_t *argmax);
+
+/* Copy row `row` of the logits the last forward / decode step / prefill
+ * computed (host, vocab floats); the device-resident copy of the reference's
+ * m->logits (engine/midge.c:82). */
+int mg_model_logits(mg_model *m, int row, float *out);
+
+/* usage histogram u32[n_layers x n_experts] (engine/midge.c:283-303) */
+int mg_model_get_usage(mg_model *m, uint32_t *usage);
+int mg_model_set_usage(mg_model *m, const uint32_t *usage);
+uint64_t mg_model_expert_loads(const mg_model *m);
+
+/* Device pointers for benches/tests that drive kernel-level calls on the
+ * model's resident weights. */
+const uint8_t *mg_model_experts_device(const mg_model *m, mg_expert_layout *layout);
+void *mg_model_stream(const mg_model *m);
+
+int mg_model_free(mg_model *m);
+
+/* Weight-streaming microbench of one dequant-GEMV on device `device`: a
+ * [rows x cols] matrix of dtype dt (seeded data, f16 scales re-expressed as
+ * ue8m0 for mxfp4) times n_tok vectors, repeated over enough copies to exceed
+ * L2, for at least `seconds`.  *gbps = (weight + scale bytes) per call / time,
+ * in GiB/s like run_bench (engine/midge.c:687-720), the device replacement of
+ * midged --bench. */
+int mg_bench_gemv(int dt, int64_t rows, int64_t cols, int n_tok, double seconds, int device, double *gbps);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MIDGECUDA_H */

@@ -1,0 +1,55 @@
+// mg_kernels.h -- host-side launchers shared by the C ABI and the model.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "midgecuda.h"
+
+namespace mg {
+
+void set_error(const char *fmt, ...);
+
+int gemv(int dt, int scale_fmt, const void *w, const void *scales, int64_t rows, int64_t cols, const float *x,
+         int64_t ldx, int n_tok, const float *bias, int accumulate, float *y, int64_t ldy, cudaStream_t st);
+size_t gemv_smem_bytes(int cols, int mt, int nt);
+int dequant_rows(int dt, int scale_fmt, const void *w, const void *scales, int64_t rows, int64_t cols,
+                 const int32_t *ids, int n, float *out, cudaStream_t st);
+int scales_to_ue8m0(const uint16_t *f16, uint8_t *ue8m0, int64_t n, int *n_inexact, cudaStream_t st);
+int rmsnorm(const float *x, const float *w, float *out, int64_t n, int n_rows, float eps, cudaStream_t st);
+int to_f16_ftz(const float *x, uint16_t *out, int64_t n, cudaStream_t st);
+
+// router: norm (optional) + AVX2-order f32 logits + top-k + weights + usage
+struct RouterArgs {
+    const float *x;        // [n_tok x hidden] residual rows (normed here if norm_w != null)
+    const float *norm_w;   // mlp norm weight or null (then x is already normed)
+    float eps;
+    float *xb_out;         // normed rows out (may be null when norm_w == null)
+    const float *rw, *rb;  // router weight [E x hidden] f32, bias [E]
+    int n_experts, top_k, router_norm, variant;
+    int64_t hidden;
+    int n_tok;
+    float *logits;         // [n_tok x E] (may be null)
+    int32_t *sel;          // [n_tok x top_k]
+    float *weights;        // [n_tok x top_k]
+    uint32_t *usage;       // [E] counters of this layer, or null
+};
+int router(const RouterArgs &a, cudaStream_t st);
+
+// decode MoE FFN (gate/up + activation, then down + rank-order combine)
+struct MoeArgs {
+    mg_expert_layout L;            // by value: read on the device
+    const uint8_t *experts_layer;  // this layer's first expert
+    int n_experts;
+    const float *xb;  // [n_tok x hidden] normed inputs
+    int n_tok, top_k;
+    const int32_t *sel;
+    const float *weights;
+    int act_plain;
+    float alpha, limit;
+    float *h;  // [n_tok*top_k x ffn] scratch
+    float *x;  // [n_tok x hidden] residual, accumulated into
+    int64_t ldx;
+};
+int moe_decode(const MoeArgs &a, cudaStream_t st);
+
+}  // namespace mg

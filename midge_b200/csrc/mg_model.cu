@@ -1,0 +1,792 @@
+// mg_model.cu -- the model behind mg_model: HBM-resident trunk and experts,
+// f16 KV cache, and the decode / expert-major prefill passes built from the
+// kernels of mg_gemv.cu, mg_moe.cu and mg_attn.cu.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "mg_attn.h"
+#include "mg_common.cuh"
+#include "mg_kernels.h"
+#include "mg_model.h"
+
+using mg::DevMat;
+
+namespace mg {
+
+// ----------------------------------------------------------- small kernels
+// first maximum of each row (engine/midge.c:657-660: strict >, so ties keep
+// the lowest index; a NaN never compares greater)
+__global__ void k_argmax(const float *__restrict__ logits, int64_t V, int32_t *out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float *l = logits + (int64_t)blockIdx.x * V;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+        float v = l[i];
+        if (v > bv || (bi == 0x7fffffff && !(v != v))) { bv = v; bi = (int)i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) { sv[w] = bv; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        int nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
+            // the reference starts from element 0: a NaN there is never replaced
+            float l0 = l[0];
+            out[blockIdx.x] = (l0 != l0 || bi == 0x7fffffff) ? 0 : bi;
+        }
+    }
+}
+
+// Sliding layers after a prefill chunk: the last min(n, cap) tokens' f16 K/V
+// go to their ring slots.
+__global__ void k_ring_store(const uint16_t *__restrict__ tk, const uint16_t *__restrict__ tv, int n, int pos0,
+                             int cap, int kv_dim, uint16_t *kc, uint16_t *vc) {
+    int first = n > cap ? n - cap : 0;
+    int t = first + blockIdx.x;
+    if (t >= n) return;
+    int slot = (pos0 + t) % cap;
+    for (int i = threadIdx.x; i < kv_dim; i += blockDim.x) {
+        kc[(int64_t)slot * kv_dim + i] = tk[(int64_t)t * kv_dim + i];
+        vc[(int64_t)slot * kv_dim + i] = tv[(int64_t)t * kv_dim + i];
+    }
+}
+
+// ---- seeded synthetic expert weights (benchmarks of shapes too big for a file)
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ float gauss(uint64_t h) {  // Box-Muller from one hash
+    float u1 = ((uint32_t)(h >> 40) + 1) * (1.0f / 16777217.0f);
+    float u2 = (uint32_t)(h & 0xffffff) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+// part: 0 = data, 1 = scales, 2 = bias of matrix `mat`, for every (layer, expert)
+__global__ void k_synth_part(uint8_t *base, int64_t expert_stride, int64_t n_le, int64_t off, int64_t bytes, int part,
+                             int dt, int64_t rows, int64_t cols, uint64_t seed) {
+    for (int64_t le = blockIdx.y; le < n_le; le += gridDim.y) {
+        uint8_t *p = base + le * expert_stride + off;
+        uint64_t s0 = mix64(seed ^ (uint64_t)(le * 9 + part * 3 + off));
+        if (part == 0) {
+            for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; i < bytes;
+                 i += (int64_t)gridDim.x * blockDim.x * 8) {
+                uint64_t h = mix64(s0 + (uint64_t)i);
+                if (dt == MG_Q8R) {  // int8 uniform in [-127, 127]
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        uint32_t r = (uint32_t)((h >> (8 * j)) & 0xff);
+                        int v = (int)((r * 255u) >> 8) - 127;  // 0..254 -> -127..127
+                        if (i + j < bytes) p[i + j] = (uint8_t)(int8_t)v;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (i + j < bytes) p[i + j] = (uint8_t)(h >> (8 * j));
+                }
+            }
+        } else if (part == 1) {
+            if (dt == MG_Q8R) {  // f32 row scales: 2^round(log2(1/(127 sqrt(cols))))
+                float s = exp2f(rintf(log2f(1.0f / (127.0f * sqrtf((float)cols)))));
+                for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += (int64_t)gridDim.x * blockDim.x)
+                    reinterpret_cast<float *>(p)[i] = s;
+            } else {  // f16 2^k, k uniform in [-8, -4]
+                for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes / 2;
+                     i += (int64_t)gridDim.x * blockDim.x) {
+                    uint64_t h = mix64(s0 + (uint64_t)i);
+                    int k = -8 + (int)(h % 5);
+                    reinterpret_cast<uint16_t *>(p)[i] = (uint16_t)((k + 15) << 10);
+                }
+            }
+        } else {
+            for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += (int64_t)gridDim.x * blockDim.x)
+                reinterpret_cast<float *>(p)[i] = 0.1f * gauss(mix64(s0 + (uint64_t)i));
+        }
+    }
+}
+
+// Re-express one layer's scale blobs: pass over (expert, mat) blobs into a
+// temp, then copy back into the first half of each blob.
+__global__ void k_layer_scales(uint8_t *layer, int64_t expert_stride, int n_experts, int64_t off0, int64_t n0,
+                               int64_t off1, int64_t n1, int64_t off2, int64_t n2, uint8_t *tmp, int to_tmp,
+                               int *bad) {
+    int e = blockIdx.y;
+    int64_t tot = n0 + n1 + n2;
+    uint8_t *eb = layer + (int64_t)e * expert_stride;
+    uint8_t *te = tmp + (int64_t)e * tot;
+    int local_bad = 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tot; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t off, j;
+        if (i < n0) { off = off0; j = i; }
+        else if (i < n0 + n1) { off = off1; j = i - n0; }
+        else { off = off2; j = i - n0 - n1; }
+        if (to_tmp) {
+            uint32_t hb = reinterpret_cast<const uint16_t *>(eb + off)[j];
+            uint32_t ex = (hb >> 10) & 31u, man = hb & 1023u;
+            uint8_t u = 0;
+            if (hb == 0) u = 0;
+            else if (hb & 0x8000u) local_bad++;
+            else if (ex == 0) { if (__popc(man) == 1) u = (uint8_t)(103 + (31 - __clz(man))); else local_bad++; }
+            else if (ex == 31 || man != 0) local_bad++;
+            else u = (uint8_t)(ex + 112);
+            te[i] = u;
+        } else {
+            eb[off + j] = te[i];
+        }
+    }
+    if (to_tmp && local_bad) atomicAdd(bad, local_bad);
+}
+
+// Check only: count scales that are not a zero or positive power of two.
+__global__ void k_layer_scales_check(const uint8_t *base, int64_t expert_stride, int64_t n_le, int64_t off, int64_t n,
+                                     int *bad) {
+    int local_bad = 0;
+    for (int64_t le = blockIdx.y; le < n_le; le += gridDim.y) {
+        const uint16_t *s = reinterpret_cast<const uint16_t *>(base + le * expert_stride + off);
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+            uint32_t hb = s[i], ex = (hb >> 10) & 31u, man = hb & 1023u;
+            bool ok = hb == 0 || (!(hb & 0x8000u) && ((ex == 0 && __popc(man) == 1) || (ex != 0 && ex != 31 && man == 0)));
+            local_bad += !ok;
+        }
+    }
+    if (local_bad) atomicAdd(bad, local_bad);
+}
+
+}  // namespace mg
+
+// ===================================================================== model
+using namespace mg;
+
+template <typename T>
+static int dalloc(mg_model *m, T **p, size_t bytes) {
+    void *q = nullptr;
+    cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        set_error("cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+        return MG_ERR_OOM;
+    }
+    m->allocs.push_back(q);
+    *p = reinterpret_cast<T *>(q);
+    return MG_OK;
+}
+
+#define TRY(expr)                     \
+    do {                              \
+        int _rc = (expr);             \
+        if (_rc != MG_OK) return _rc; \
+    } while (0)
+
+extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int device, mg_model **out) {
+    MG_REQUIRE(spec && out, MG_ERR_ARG, "model_create: null argument");
+    *out = nullptr;
+    const mg_spec &s = *spec;
+    MG_REQUIRE(s.hidden > 0 && s.vocab > 0 && s.n_layers > 0 && s.ffn > 0 && s.n_experts > 0 && s.top_k > 0,
+               MG_ERR_SPEC, "invalid spec");  // engine/midge.c:135-137
+    MG_REQUIRE(s.top_k <= 16 && s.top_k <= s.n_experts, MG_ERR_SPEC, "top_k %d unsupported", s.top_k);
+    MG_REQUIRE(s.n_heads > 0 && s.n_kv_heads > 0 && s.n_heads % s.n_kv_heads == 0 && s.head_dim > 0 &&
+                   s.head_dim % 2 == 0,
+               MG_ERR_SPEC, "invalid attention shape");
+    MG_REQUIRE(ctx > 0 && max_seqs >= 1 && max_seqs <= 64, MG_ERR_ARG, "bad ctx %d / max_seqs %d", ctx, max_seqs);
+    MG_CUDA(cudaSetDevice(device));
+    mg_model *m = new mg_model();
+    m->spec = s;
+    m->layer_sliding.assign(s.layer_sliding, s.layer_sliding ? s.layer_sliding + s.n_layers : nullptr);
+    if (!s.layer_sliding) m->layer_sliding.assign(s.n_layers, 0);
+    m->spec.layer_sliding = m->layer_sliding.data();
+    m->ctx = ctx;
+    m->max_seqs = max_seqs;
+    m->device = device;
+    cudaError_t e = cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete m;
+        set_error("stream create: %s", cudaGetErrorString(e));
+        return MG_ERR_CUDA;
+    }
+    int L = s.n_layers;
+    m->wq.resize(L); m->wk.resize(L); m->wv.resize(L); m->wo.resize(L); m->router_w.resize(L);
+    for (auto *vec : {&m->bq, &m->bk, &m->bv, &m->bo, &m->router_b, &m->attn_norm, &m->mlp_norm, &m->sinks, &m->qn, &m->kn})
+        vec->assign(L, nullptr);
+    m->pos.assign(max_seqs, 0);
+    const char *ng = getenv("MIDGE_NO_GRAPH");
+    m->use_graphs = !(ng && *ng && *ng != '0');
+    *out = m;
+    return MG_OK;
+}
+
+static int upload(mg_model *m, void **dst, const void *src, size_t bytes) {
+    TRY(dalloc(m, dst, bytes));
+    MG_CUDA(cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice));
+    return MG_OK;
+}
+
+extern "C" int mg_model_set_dense(mg_model *m, const char *name, int dt, int64_t rows, int64_t cols, const void *data,
+                                  const void *scales) {
+    MG_REQUIRE(m && name && data && rows > 0, MG_ERR_ARG, "set_dense: bad arguments");
+    MG_CUDA(cudaSetDevice(m->device));
+    DevMat d;
+    d.dt = dt;
+    d.rows = rows;
+    d.cols = cols;
+    size_t db = 0, sb = 0;
+    if (cols == 0) {
+        MG_REQUIRE(dt == MG_F32, MG_ERR_SPEC, "tensor %s must be f32", name);  // engine/midge.c:196
+        db = (size_t)rows * 4;
+    } else {
+        switch (dt) {
+        case MG_F32: db = (size_t)rows * cols * 4; break;
+        case MG_Q8R: db = (size_t)rows * cols; sb = (size_t)rows * 4; break;
+        case MG_Q4G32:
+        case MG_MXFP4:
+            MG_REQUIRE(cols % 32 == 0, MG_ERR_SPEC, "tensor %s: cols %% 32 != 0", name);
+            db = (size_t)rows * cols / 2;
+            sb = (size_t)rows * (cols / 32) * 2;
+            break;
+        default: set_error("tensor %s: unknown dtype %d", name, dt); return MG_ERR_SPEC;
+        }
+        MG_REQUIRE(sb == 0 || scales, MG_ERR_ARG, "tensor %s: scales missing", name);
+    }
+    TRY(upload(m, &d.data, data, db));
+    if (sb) TRY(upload(m, &d.scales, scales, sb));
+    std::string n(name);
+    if (n == "embed") { m->embed = d; return MG_OK; }
+    if (n == "lm_head") { m->lm_head = d; return MG_OK; }
+    if (n == "final_norm") { m->final_norm = (float *)d.data; return MG_OK; }
+    int layer = -1;
+    char rest[64] = {0};
+    if (sscanf(name, "L%d.%63s", &layer, rest) != 2 || layer < 0 || layer >= m->spec.n_layers) {
+        return MG_OK;  // unknown tensors are ignored, as the reference never looks them up
+    }
+    std::string r(rest);
+    if (r == "attn.q") m->wq[layer] = d;
+    else if (r == "attn.k") m->wk[layer] = d;
+    else if (r == "attn.v") m->wv[layer] = d;
+    else if (r == "attn.o") m->wo[layer] = d;
+    else if (r == "router.w") {
+        MG_REQUIRE(dt == MG_F32, MG_ERR_SPEC, "router %s must be f32", name);
+        m->router_w[layer] = d;
+    } else if (r == "attn.q_b") m->bq[layer] = (float *)d.data;
+    else if (r == "attn.k_b") m->bk[layer] = (float *)d.data;
+    else if (r == "attn.v_b") m->bv[layer] = (float *)d.data;
+    else if (r == "attn.o_b") m->bo[layer] = (float *)d.data;
+    else if (r == "router.b") m->router_b[layer] = (float *)d.data;
+    else if (r == "attn.norm") m->attn_norm[layer] = (float *)d.data;
+    else if (r == "mlp.norm") m->mlp_norm[layer] = (float *)d.data;
+    else if (r == "attn.sinks") m->sinks[layer] = (float *)d.data;
+    else if (r == "attn.q_norm") m->qn[layer] = (float *)d.data;
+    else if (r == "attn.k_norm") m->kn[layer] = (float *)d.data;
+    return MG_OK;
+}
+
+static int convert_expert_scales(mg_model *m) {
+    mg_expert_layout &L = m->el;
+    L.scale_fmt = MG_SCALE_F16;
+    if (L.dt != MG_MXFP4 && L.dt != MG_Q4G32) return MG_OK;
+    const char *keep = getenv("MIDGE_F16_SCALES");
+    if (keep && *keep && *keep != '0') return MG_OK;
+    int64_t ns[3];
+    for (int mt = 0; mt < 3; mt++) {
+        int64_t rows = mt == 2 ? L.hidden : L.ffn, cols = mt == 2 ? L.ffn : L.hidden;
+        ns[mt] = rows * (cols / 32);
+    }
+    int *bad = nullptr;
+    TRY(dalloc(m, &bad, sizeof(int)));
+    MG_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), m->st));
+    int64_t n_le = (int64_t)m->spec.n_layers * m->spec.n_experts;
+    for (int mt = 0; mt < 3; mt++) {
+        dim3 g(64, (unsigned)(n_le < 4096 ? n_le : 4096));
+        k_layer_scales_check<<<g, 256, 0, m->st>>>(m->experts, L.expert_stride, n_le, L.off[mt][1], ns[mt], bad);
+        MG_CHECK_LAUNCH();
+    }
+    int h_bad = 0;
+    MG_CUDA(cudaMemcpyAsync(&h_bad, bad, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+    MG_CUDA(cudaStreamSynchronize(m->st));
+    if (h_bad) {
+        fprintf(stderr, "# %d expert scales are not powers of two: keeping f16 scales\n", h_bad);
+        return MG_OK;
+    }
+    int64_t per_expert = ns[0] + ns[1] + ns[2];
+    uint8_t *tmp = nullptr;
+    void *tmpv = nullptr;
+    MG_CUDA(cudaMalloc(&tmpv, (size_t)per_expert * m->spec.n_experts));
+    tmp = (uint8_t *)tmpv;
+    for (int layer = 0; layer < m->spec.n_layers; layer++) {
+        uint8_t *lb = m->experts + (int64_t)layer * L.layer_stride;
+        dim3 g(32, m->spec.n_experts);
+        for (int pass = 1; pass >= 0; pass--) {
+            k_layer_scales<<<g, 256, 0, m->st>>>(lb, L.expert_stride, m->spec.n_experts, L.off[0][1], ns[0], L.off[1][1],
+                                                 ns[1], L.off[2][1], ns[2], tmp, pass, bad);
+        }
+    }
+    cudaError_t e = cudaGetLastError();
+    cudaError_t e2 = cudaStreamSynchronize(m->st);
+    cudaFree(tmpv);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        set_error("scale re-expression failed: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+        return MG_ERR_CUDA;
+    }
+    L.scale_fmt = MG_SCALE_UE8M0;
+    return MG_OK;
+}
+
+static int experts_alloc(mg_model *m, int dt) {
+    const mg_spec &s = m->spec;
+    TRY(mg_expert_layout_init(&m->el, dt, s.hidden, s.ffn, s.n_experts));
+    m->experts_bytes = (size_t)s.n_layers * m->el.layer_stride;
+    MG_REQUIRE(!m->experts, MG_ERR_STATE, "experts already loaded");
+    TRY(dalloc(m, &m->experts, m->experts_bytes));
+    return MG_OK;
+}
+
+extern "C" int mg_model_set_experts(mg_model *m, int dt, const void *data, uint64_t bytes) {
+    MG_REQUIRE(m && data, MG_ERR_ARG, "set_experts: bad arguments");
+    MG_CUDA(cudaSetDevice(m->device));
+    TRY(experts_alloc(m, dt));
+    MG_REQUIRE(bytes >= m->experts_bytes, MG_ERR_SPEC, "experts.midge too small: need %zu data bytes",
+               m->experts_bytes);  // engine/midge.c:224-227
+    // pinned double-buffered staging; the host copy into a stage overlaps the
+    // DMA of the other
+    const size_t CH = 64ull << 20;
+    void *stage[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    int rc = MG_OK;
+    for (int i = 0; i < 2 && rc == MG_OK; i++) {
+        if (cudaHostAlloc(&stage[i], CH, cudaHostAllocDefault) != cudaSuccess ||
+            cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming) != cudaSuccess) {
+            set_error("pinned staging allocation failed");
+            rc = MG_ERR_OOM;
+        }
+    }
+    const uint8_t *src = (const uint8_t *)data;
+    size_t off = 0;
+    int b = 0;
+    while (rc == MG_OK && off < m->experts_bytes) {
+        size_t n = m->experts_bytes - off < CH ? m->experts_bytes - off : CH;
+        if (cudaEventSynchronize(done[b]) != cudaSuccess) { rc = MG_ERR_CUDA; break; }
+        memcpy(stage[b], src + off, n);
+        if (cudaMemcpyAsync(m->experts + off, stage[b], n, cudaMemcpyHostToDevice, m->st) != cudaSuccess ||
+            cudaEventRecord(done[b], m->st) != cudaSuccess) {
+            set_error("expert upload failed");
+            rc = MG_ERR_CUDA;
+            break;
+        }
+        off += n;
+        b ^= 1;
+    }
+    cudaStreamSynchronize(m->st);
+    for (int i = 0; i < 2; i++) {
+        if (stage[i]) cudaFreeHost(stage[i]);
+        if (done[i]) cudaEventDestroy(done[i]);
+    }
+    if (rc != MG_OK) return rc;
+    return convert_expert_scales(m);
+}
+
+extern "C" int mg_model_synth_experts(mg_model *m, int dt, uint64_t seed) {
+    MG_REQUIRE(m, MG_ERR_ARG, "synth_experts: null model");
+    MG_REQUIRE(dt == MG_MXFP4 || dt == MG_Q8R || dt == MG_Q4G32, MG_ERR_ARG, "synth_experts: dtype %d unsupported", dt);
+    MG_CUDA(cudaSetDevice(m->device));
+    TRY(experts_alloc(m, dt));
+    const mg_expert_layout &L = m->el;
+    int64_t n_le = (int64_t)m->spec.n_layers * m->spec.n_experts;
+    for (int mt = 0; mt < 3; mt++) {
+        int64_t rows = mt == 2 ? L.hidden : L.ffn, cols = mt == 2 ? L.ffn : L.hidden;
+        int64_t db = dt == MG_Q8R ? rows * cols : rows * cols / 2;
+        int64_t sb = dt == MG_Q8R ? rows * 4 : rows * (cols / 32) * 2;
+        int64_t bb = rows * 4;
+        int64_t sizes[3] = {db, sb, bb};
+        for (int part = 0; part < 3; part++) {
+            dim3 g(16, (unsigned)(n_le < 8192 ? n_le : 8192));
+            k_synth_part<<<g, 256, 0, m->st>>>(m->experts, L.expert_stride, n_le, L.off[mt][part], sizes[part], part, dt,
+                                               rows, cols, seed + (uint64_t)mt * 7919u);
+            MG_CHECK_LAUNCH();
+        }
+    }
+    MG_CUDA(cudaStreamSynchronize(m->st));
+    return convert_expert_scales(m);
+}
+
+// YaRN rope tables in double precision, the arithmetic of engine/midge.c:141-176
+static void rope_tables(const mg_spec &s, int ctx, std::vector<float> &co, std::vector<float> &si) {
+    int hd = s.head_dim, half = hd / 2;
+    std::vector<double> inv(half);
+    double mscale = 1.0;
+    for (int i = 0; i < half; i++) inv[i] = 1.0 / pow((double)s.rope_theta, (double)(2 * i) / hd);
+    if (s.yarn) {
+        double f = s.yarn_factor, base = s.rope_theta, orig = s.yarn_orig_ctx;
+        double low = hd * log(orig / (s.yarn_beta_fast * 2.0 * M_PI)) / (2.0 * log(base));
+        double high = hd * log(orig / (s.yarn_beta_slow * 2.0 * M_PI)) / (2.0 * log(base));
+        if (s.yarn_truncate) { low = floor(low); high = ceil(high); }
+        if (low < 0) low = 0;
+        if (high > hd - 1) high = hd - 1;
+        if (high == low) high = low + 0.001;
+        for (int i = 0; i < half; i++) {
+            double ramp = ((double)i - low) / (high - low);
+            ramp = ramp < 0 ? 0 : ramp > 1 ? 1 : ramp;
+            double keep = 1.0 - ramp;  // 1 keeps the unscaled (high-frequency) rate
+            inv[i] = (inv[i] / f) * (1.0 - keep) + inv[i] * keep;
+        }
+        mscale = 0.1 * log(f) + 1.0;
+    }
+    co.resize((size_t)ctx * half);
+    si.resize((size_t)ctx * half);
+    for (int p = 0; p < ctx; p++)
+        for (int i = 0; i < half; i++) {
+            double a = (double)p * inv[i];
+            co[(size_t)p * half + i] = (float)(cos(a) * mscale);
+            si[(size_t)p * half + i] = (float)(sin(a) * mscale);
+        }
+}
+
+extern "C" int mg_model_ready(mg_model *m) {
+    MG_REQUIRE(m, MG_ERR_ARG, "ready: null model");
+    MG_CUDA(cudaSetDevice(m->device));
+    const mg_spec &s = m->spec;
+    // every tensor the reference requires (engine/midge.c:229-260)
+    MG_REQUIRE(m->embed.data && m->lm_head.data && m->final_norm, MG_ERR_SPEC, "missing embed/lm_head/final_norm");
+    MG_REQUIRE(m->experts, MG_ERR_SPEC, "experts not loaded");
+    for (int l = 0; l < s.n_layers; l++) {
+        MG_REQUIRE(m->wq[l].data && m->wk[l].data && m->wv[l].data && m->wo[l].data && m->router_w[l].data,
+                   MG_ERR_SPEC, "missing tensor L%d.attn.{q,k,v,o} / router.w", l);
+        MG_REQUIRE(m->bq[l] && m->bk[l] && m->bv[l] && m->bo[l] && m->router_b[l] && m->attn_norm[l] && m->mlp_norm[l],
+                   MG_ERR_SPEC, "missing tensor L%d bias/norm", l);
+        MG_REQUIRE(!s.sinks || m->sinks[l], MG_ERR_SPEC, "missing tensor L%d.attn.sinks", l);
+        MG_REQUIRE(!s.qk_norm || (m->qn[l] && m->kn[l]), MG_ERR_SPEC, "missing tensor L%d.attn.q_norm/k_norm", l);
+        MG_REQUIRE(m->router_w[l].rows == s.n_experts && m->router_w[l].cols == s.hidden, MG_ERR_SPEC,
+                   "router L%d shape", l);
+    }
+    std::vector<float> co, si;
+    rope_tables(s, m->ctx, co, si);
+    TRY(upload(m, (void **)&m->rope_cos, co.data(), co.size() * 4));
+    TRY(upload(m, (void **)&m->rope_sin, si.data(), si.size() * 4));
+    const int kv_dim = s.n_kv_heads * s.head_dim, q_dim = s.n_heads * s.head_dim;
+    m->kc.resize(s.n_layers);
+    m->vc.resize(s.n_layers);
+    m->cap.resize(s.n_layers);
+    for (int l = 0; l < s.n_layers; l++) {  // engine/midge.c:268-273
+        int c = m->layer_sliding[l] && s.sliding_window > 0 && s.sliding_window < m->ctx ? s.sliding_window : m->ctx;
+        m->cap[l] = c;
+        TRY(dalloc(m, &m->kc[l], (size_t)m->max_seqs * c * kv_dim * 2));
+        TRY(dalloc(m, &m->vc[l], (size_t)m->max_seqs * c * kv_dim * 2));
+        MG_CUDA(cudaMemset(m->kc[l], 0, (size_t)m->max_seqs * c * kv_dim * 2));
+        MG_CUDA(cudaMemset(m->vc[l], 0, (size_t)m->max_seqs * c * kv_dim * 2));
+    }
+    const int R = PF_CHUNK > DEC_MAX ? PF_CHUNK : DEC_MAX;
+    m->rows_max = R;
+    const int64_t H = s.hidden;
+    TRY(dalloc(m, &m->x, (size_t)R * H * 4));
+    TRY(dalloc(m, &m->xb, (size_t)R * H * 4));
+    TRY(dalloc(m, &m->q, (size_t)R * q_dim * 4));
+    TRY(dalloc(m, &m->k, (size_t)R * kv_dim * 4));
+    TRY(dalloc(m, &m->v, (size_t)R * kv_dim * 4));
+    TRY(dalloc(m, &m->ao, (size_t)R * q_dim * 4));
+    TRY(dalloc(m, &m->h, (size_t)R * s.top_k * s.ffn * 4));
+    TRY(dalloc(m, &m->logits, (size_t)DEC_MAX * s.vocab * 4));
+    TRY(dalloc(m, &m->wts, (size_t)R * s.top_k * 4));
+    TRY(dalloc(m, &m->sel, (size_t)R * s.top_k * 4));
+    TRY(dalloc(m, &m->tok_pos, (size_t)R * 4));
+    TRY(dalloc(m, &m->tok_seq, (size_t)R * 4));
+    TRY(dalloc(m, &m->toks, (size_t)R * 4));
+    TRY(dalloc(m, &m->amax, (size_t)DEC_MAX * 4));
+    TRY(dalloc(m, &m->tmp_k, (size_t)R * kv_dim * 2));
+    TRY(dalloc(m, &m->tmp_v, (size_t)R * kv_dim * 2));
+    TRY(dalloc(m, &m->usage, (size_t)s.n_layers * s.n_experts * 4));
+    MG_CUDA(cudaMemset(m->usage, 0, (size_t)s.n_layers * s.n_experts * 4));
+    m->attn_max_splits = (m->ctx + m->attn_split - 1) / m->attn_split;
+    TRY(dalloc(m, &m->attn_part, (size_t)DEC_MAX * s.n_heads * m->attn_max_splits * (s.head_dim + 2) * 4));
+    MG_CUDA(cudaHostAlloc(&m->h_toks, R * 4, cudaHostAllocDefault));
+    MG_CUDA(cudaHostAlloc(&m->h_pos, R * 4, cudaHostAllocDefault));
+    MG_CUDA(cudaHostAlloc(&m->h_seq, R * 4, cudaHostAllocDefault));
+    MG_CUDA(cudaHostAlloc(&m->h_amax, DEC_MAX * 4, cudaHostAllocDefault));
+    m->ready = true;
+    return MG_OK;
+}
+
+// ------------------------------------------------------------ forward passes
+static int gemv_rows(mg_model *m, const DevMat &w, const float *x, int64_t ldx, int n, const float *bias, int acc,
+                     float *y, int64_t ldy) {
+    for (int r0 = 0; r0 < n; r0 += 16) {
+        int nn = n - r0 < 16 ? n - r0 : 16;
+        TRY(gemv(w.dt, MG_SCALE_F16, w.data, w.scales, w.rows, w.cols, x + (int64_t)r0 * ldx, ldx, nn, bias, acc,
+                 y + (int64_t)r0 * ldy, ldy, m->st));
+    }
+    return MG_OK;
+}
+
+// The per-layer body shared by decode (n rows = sequences, one token each)
+// and prefill (n rows = consecutive tokens of one sequence).
+static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int pos0) {
+    const mg_spec &s = m->spec;
+    const int64_t H = s.hidden;
+    const int hd = s.head_dim, q_dim = s.n_heads * hd, kv_dim = s.n_kv_heads * hd;
+    cudaStream_t st = m->st;
+    // attention (engine/midge.c:341-400)
+    TRY(rmsnorm(m->x, m->attn_norm[layer], m->xb, H, n, s.norm_eps, st));
+    TRY(gemv_rows(m, m->wq[layer], m->xb, H, n, m->bq[layer], 0, m->q, q_dim));
+    TRY(gemv_rows(m, m->wk[layer], m->xb, H, n, m->bk[layer], 0, m->k, kv_dim));
+    TRY(gemv_rows(m, m->wv[layer], m->xb, H, n, m->bv[layer], 0, m->v, kv_dim));
+    const int cap = m->cap[layer];
+    const bool sliding = cap < m->ctx;
+    QkvPostArgs qa{};
+    qa.q = m->q; qa.k = m->k; qa.v = m->v; qa.ldq = q_dim; qa.ldk = kv_dim;
+    qa.n_heads = s.n_heads; qa.n_kv_heads = s.n_kv_heads; qa.head_dim = hd;
+    qa.qn = s.qk_norm ? m->qn[layer] : nullptr; qa.kn = s.qk_norm ? m->kn[layer] : nullptr;
+    qa.eps = s.norm_eps; qa.rope_cos = m->rope_cos; qa.rope_sin = m->rope_sin;
+    qa.tok_pos = m->tok_pos; qa.tok_seq = m->tok_seq;
+    qa.write_cache = prefill ? !sliding : 1;
+    qa.kc = m->kc[layer]; qa.vc = m->vc[layer]; qa.cap = cap;
+    qa.tmp_k = prefill ? m->tmp_k : nullptr; qa.tmp_v = prefill ? m->tmp_v : nullptr;
+    TRY(qkv_post(qa, n, st));
+    if (prefill) {
+        AttnPrefillArgs pa{};
+        pa.q = m->q; pa.ldq = q_dim; pa.tmp_k = m->tmp_k; pa.tmp_v = m->tmp_v;
+        pa.kc = m->kc[layer]; pa.vc = m->vc[layer];
+        pa.seq = seq; pa.pos0 = pos0; pa.n = n; pa.cap = cap;
+        pa.n_heads = s.n_heads; pa.n_kv_heads = s.n_kv_heads; pa.head_dim = hd;
+        pa.scale = s.attn_scale; pa.sinks = s.sinks ? m->sinks[layer] : nullptr;
+        pa.out = m->ao; pa.ldo = q_dim;
+        TRY(attn_prefill(pa, st));
+        if (sliding) {
+            int nst = n < cap ? n : cap;
+            uint16_t *kcs = m->kc[layer] + (int64_t)seq * cap * kv_dim, *vcs = m->vc[layer] + (int64_t)seq * cap * kv_dim;
+            k_ring_store<<<nst, 128, 0, st>>>(m->tmp_k, m->tmp_v, n, pos0, cap, kv_dim, kcs, vcs);
+            MG_CHECK_LAUNCH();
+        }
+    } else {
+        AttnDecodeArgs da{};
+        da.q = m->q; da.ldq = q_dim; da.seq_ids = m->tok_seq; da.pos = m->tok_pos;
+        da.kc = m->kc[layer]; da.vc = m->vc[layer]; da.cap = cap;
+        da.n_heads = s.n_heads; da.n_kv_heads = s.n_kv_heads; da.head_dim = hd;
+        da.scale = s.attn_scale; da.sinks = s.sinks ? m->sinks[layer] : nullptr;
+        da.split_len = m->attn_split;
+        da.max_splits = (cap + m->attn_split - 1) / m->attn_split;
+        da.partial = m->attn_part; da.out = m->ao; da.ldo = q_dim;
+        TRY(attn_decode(da, n, st));
+    }
+    TRY(gemv_rows(m, m->wo[layer], m->ao, q_dim, n, m->bo[layer], 1, m->x, H));
+    // MoE (engine/midge.c:469-549; prefill routing engine/midge.c:404-434)
+    RouterArgs ra{};
+    ra.x = m->x; ra.norm_w = m->mlp_norm[layer]; ra.eps = s.norm_eps; ra.xb_out = m->xb;
+    ra.rw = (const float *)m->router_w[layer].data; ra.rb = m->router_b[layer];
+    ra.n_experts = s.n_experts; ra.top_k = s.top_k; ra.router_norm = s.router_norm; ra.variant = prefill ? 1 : 0;
+    ra.hidden = H; ra.n_tok = n; ra.logits = nullptr; ra.sel = m->sel; ra.weights = m->wts;
+    ra.usage = m->usage + (int64_t)layer * s.n_experts;
+    TRY(router(ra, st));
+    const uint8_t *lb = m->experts + (int64_t)layer * m->el.layer_stride;
+    for (int r0 = 0; r0 < n; r0 += DEC_MAX) {
+        int nn = n - r0 < DEC_MAX ? n - r0 : DEC_MAX;
+        MoeArgs ma{};
+        ma.L = m->el;
+        ma.experts_layer = lb; ma.n_experts = s.n_experts;
+        ma.xb = m->xb + (int64_t)r0 * H; ma.n_tok = nn; ma.top_k = s.top_k;
+        ma.sel = m->sel + (int64_t)r0 * s.top_k; ma.weights = m->wts + (int64_t)r0 * s.top_k;
+        ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit;
+        ma.h = m->h; ma.x = m->x + (int64_t)r0 * H; ma.ldx = H;
+        TRY(moe_decode(ma, st));
+    }
+    return MG_OK;
+}
+
+static int logits_rows(mg_model *m, const float *x, int n) {
+    const mg_spec &s = m->spec;
+    TRY(rmsnorm(x, m->final_norm, m->xb, s.hidden, n, s.norm_eps, m->st));
+    TRY(gemv_rows(m, m->lm_head, m->xb, s.hidden, n, nullptr, 0, m->logits, s.vocab));
+    return MG_OK;
+}
+
+// decode body for n sequences whose tokens/positions are already in the
+// pinned staging arrays; everything stream-ordered (graph-capturable)
+static int decode_body(mg_model *m, int n) {
+    const mg_spec &s = m->spec;
+    cudaStream_t st = m->st;
+    MG_CUDA(cudaMemcpyAsync(m->toks, m->h_toks, n * 4, cudaMemcpyHostToDevice, st));
+    MG_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_pos, n * 4, cudaMemcpyHostToDevice, st));
+    MG_CUDA(cudaMemcpyAsync(m->tok_seq, m->h_seq, n * 4, cudaMemcpyHostToDevice, st));
+    TRY(dequant_rows(m->embed.dt, MG_SCALE_F16, m->embed.data, m->embed.scales, m->embed.rows, m->embed.cols, m->toks, n,
+                     m->x, st));
+    for (int l = 0; l < s.n_layers; l++) TRY(layer_pass(m, l, n, false, 0, 0));
+    TRY(logits_rows(m, m->x, n));
+    k_argmax<<<n, 1024, 0, st>>>(m->logits, s.vocab, m->amax);
+    MG_CHECK_LAUNCH();
+    MG_CUDA(cudaMemcpyAsync(m->h_amax, m->amax, n * 4, cudaMemcpyDeviceToHost, st));
+    return MG_OK;
+}
+
+static int run_decode(mg_model *m, int n) {
+    if (!m->use_graphs) return decode_body(m, n);
+    auto it = m->dec_graphs.find(n);
+    if (it != m->dec_graphs.end()) {
+        MG_CUDA(cudaGraphLaunch(it->second.exec, m->st));
+        return MG_OK;
+    }
+    // First step with this many sequences: run it eagerly (which also sets
+    // every kernel's launch attributes), then capture the same stream-ordered
+    // body for the following steps.  Capture executes nothing.
+    TRY(decode_body(m, n));
+    MG_CUDA(cudaStreamSynchronize(m->st));
+    cudaGraph_t g = nullptr;
+    MG_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    int rc = decode_body(m, n);
+    cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+    if (rc != MG_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    MG_REQUIRE(ce == cudaSuccess, MG_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(ce));
+    Graph gr;
+    cudaError_t ie = cudaGraphInstantiate(&gr.exec, g, 0);
+    cudaGraphDestroy(g);
+    MG_REQUIRE(ie == cudaSuccess, MG_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(ie));
+    m->dec_graphs[n] = gr;
+    return MG_OK;
+}
+
+extern "C" int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, float *logits,
+                              int32_t *argmax) {
+    MG_REQUIRE(m && m->ready, MG_ERR_STATE, "decode: model not ready");
+    MG_REQUIRE(n_seqs >= 1 && n_seqs <= DEC_MAX && n_seqs <= m->max_seqs && toks, MG_ERR_ARG, "decode: bad n_seqs %d",
+               n_seqs);
+    MG_CUDA(cudaSetDevice(m->device));
+    const mg_spec &s = m->spec;
+    for (int i = 0; i < n_seqs; i++) {
+        int sq = seq_ids ? seq_ids[i] : i;
+        MG_REQUIRE(sq >= 0 && sq < m->max_seqs, MG_ERR_ARG, "decode: sequence %d out of range", sq);
+        for (int j = 0; j < i; j++) MG_REQUIRE((seq_ids ? seq_ids[j] : j) != sq, MG_ERR_ARG, "decode: duplicate sequence");
+        MG_REQUIRE(m->pos[sq] < m->ctx, MG_ERR_RANGE, "context full (%d)", m->ctx);          // engine/midge.c:554
+        MG_REQUIRE(toks[i] >= 0 && toks[i] < s.vocab, MG_ERR_RANGE, "token %d out of range", toks[i]);  // :555
+        m->h_toks[i] = toks[i];
+        m->h_pos[i] = m->pos[sq];
+        m->h_seq[i] = sq;
+    }
+    TRY(run_decode(m, n_seqs));
+    if (logits)
+        MG_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)n_seqs * s.vocab * 4, cudaMemcpyDeviceToHost, m->st));
+    MG_CUDA(cudaStreamSynchronize(m->st));
+    for (int i = 0; i < n_seqs; i++) m->pos[m->h_seq[i]]++;
+    m->expert_loads += (uint64_t)n_seqs * s.top_k * s.n_layers;
+    if (argmax) memcpy(argmax, m->h_amax, n_seqs * 4);
+    return MG_OK;
+}
+
+extern "C" int mg_forward(mg_model *m, int seq, int32_t token, float *logits, int32_t *argmax) {
+    int32_t sq = seq;
+    return mg_decode_step(m, 1, &sq, &token, logits, argmax);
+}
+
+extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n, int logits_mode, float *logits) {
+    MG_REQUIRE(m && m->ready, MG_ERR_STATE, "forward_batch: model not ready");
+    MG_REQUIRE(seq >= 0 && seq < m->max_seqs && n >= 0 && (n == 0 || toks), MG_ERR_ARG, "forward_batch: bad arguments");
+    MG_REQUIRE(logits_mode >= 0 && logits_mode <= 2 && (logits_mode == 0 || logits), MG_ERR_ARG,
+               "forward_batch: bad logits mode");
+    MG_CUDA(cudaSetDevice(m->device));
+    const mg_spec &s = m->spec;
+    for (int t = 0; t < n; t++) {  // engine/midge.c:580-583
+        MG_REQUIRE(m->pos[seq] + t < m->ctx, MG_ERR_RANGE, "context full (%d)", m->ctx);
+        MG_REQUIRE(toks[t] >= 0 && toks[t] < s.vocab, MG_ERR_RANGE, "token %d out of range", toks[t]);
+    }
+    for (int c0 = 0; c0 < n; c0 += PF_CHUNK) {
+        int nc = n - c0 < PF_CHUNK ? n - c0 : PF_CHUNK;
+        int pos0 = m->pos[seq];
+        for (int t = 0; t < nc; t++) {
+            m->h_toks[t] = toks[c0 + t];
+            m->h_pos[t] = pos0 + t;
+            m->h_seq[t] = seq;
+        }
+        cudaStream_t st = m->st;
+        MG_CUDA(cudaMemcpyAsync(m->toks, m->h_toks, nc * 4, cudaMemcpyHostToDevice, st));
+        MG_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_pos, nc * 4, cudaMemcpyHostToDevice, st));
+        MG_CUDA(cudaMemcpyAsync(m->tok_seq, m->h_seq, nc * 4, cudaMemcpyHostToDevice, st));
+        TRY(dequant_rows(m->embed.dt, MG_SCALE_F16, m->embed.data, m->embed.scales, m->embed.rows, m->embed.cols, m->toks,
+                         nc, m->x, st));
+        for (int l = 0; l < s.n_layers; l++) TRY(layer_pass(m, l, nc, true, seq, pos0));
+        const bool last_chunk = c0 + nc == n;
+        if (logits_mode == 2) {
+            for (int r0 = 0; r0 < nc; r0 += DEC_MAX) {
+                int nn = nc - r0 < DEC_MAX ? nc - r0 : DEC_MAX;
+                TRY(logits_rows(m, m->x + (int64_t)r0 * s.hidden, nn));
+                MG_CUDA(cudaMemcpyAsync(logits + (int64_t)(c0 + r0) * s.vocab, m->logits, (size_t)nn * s.vocab * 4,
+                                        cudaMemcpyDeviceToHost, st));
+            }
+        } else if (logits_mode == 1 && last_chunk) {
+            TRY(logits_rows(m, m->x + (int64_t)(nc - 1) * s.hidden, 1));
+            MG_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)s.vocab * 4, cudaMemcpyDeviceToHost, st));
+        }
+        MG_CUDA(cudaStreamSynchronize(st));
+        m->pos[seq] += nc;
+        m->expert_loads += (uint64_t)nc * s.top_k * s.n_layers;
+    }
+    return MG_OK;
+}
+
+extern "C" int mg_model_logits(mg_model *m, int row, float *out) {
+    MG_REQUIRE(m && m->ready && out && row >= 0 && row < DEC_MAX, MG_ERR_ARG, "logits: bad arguments");
+    MG_CUDA(cudaSetDevice(m->device));
+    MG_CUDA(cudaMemcpy(out, m->logits + (int64_t)row * m->spec.vocab, (size_t)m->spec.vocab * 4, cudaMemcpyDeviceToHost));
+    return MG_OK;
+}
+
+extern "C" int mg_model_reset(mg_model *m, int seq) {
+    MG_REQUIRE(m && seq >= 0 && seq < m->max_seqs, MG_ERR_ARG, "reset: bad sequence");
+    m->pos[seq] = 0;
+    return MG_OK;
+}
+
+extern "C" int mg_model_pos(const mg_model *m, int seq) {
+    if (!m || seq < 0 || seq >= m->max_seqs) return MG_ERR_ARG;
+    return m->pos[seq];
+}
+
+extern "C" int mg_model_get_usage(mg_model *m, uint32_t *usage) {
+    MG_REQUIRE(m && m->ready && usage, MG_ERR_ARG, "get_usage: bad arguments");
+    MG_CUDA(cudaSetDevice(m->device));
+    MG_CUDA(cudaMemcpy(usage, m->usage, (size_t)m->spec.n_layers * m->spec.n_experts * 4, cudaMemcpyDeviceToHost));
+    return MG_OK;
+}
+
+extern "C" int mg_model_set_usage(mg_model *m, const uint32_t *usage) {
+    MG_REQUIRE(m && m->ready && usage, MG_ERR_ARG, "set_usage: bad arguments");
+    MG_CUDA(cudaSetDevice(m->device));
+    MG_CUDA(cudaMemcpy(m->usage, usage, (size_t)m->spec.n_layers * m->spec.n_experts * 4, cudaMemcpyHostToDevice));
+    return MG_OK;
+}
+
+extern "C" uint64_t mg_model_expert_loads(const mg_model *m) { return m ? m->expert_loads : 0; }
+
+extern "C" const uint8_t *mg_model_experts_device(const mg_model *m, mg_expert_layout *layout) {
+    if (!m) return nullptr;
+    if (layout) *layout = m->el;
+    return m->experts;
+}
+
+extern "C" void *mg_model_stream(const mg_model *m) { return m ? (void *)m->st : nullptr; }
+
+extern "C" int mg_model_free(mg_model *m) {
+    if (!m) return MG_OK;
+    cudaSetDevice(m->device);
+    if (m->st) cudaStreamSynchronize(m->st);
+    for (auto &kv : m->dec_graphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (void *p : m->allocs) cudaFree(p);
+    for (void *p : {(void *)m->h_toks, (void *)m->h_pos, (void *)m->h_seq, (void *)m->h_amax})
+        if (p) cudaFreeHost(p);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+    return MG_OK;
+}

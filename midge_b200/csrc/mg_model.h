@@ -1,0 +1,66 @@
+// mg_model.h -- device-resident model state behind the mg_model handle.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "midgecuda.h"
+
+namespace mg {
+
+struct DevMat {
+    int dt = -1;
+    int64_t rows = 0, cols = 0;
+    void *data = nullptr;
+    void *scales = nullptr;
+};
+
+constexpr int PF_CHUNK = 256;   // tokens per prefill pass through the layers
+constexpr int DEC_MAX = 16;     // sequences per decode step
+
+struct Graph {
+    cudaGraphExec_t exec = nullptr;
+};
+
+}  // namespace mg
+
+struct mg_model {
+    mg_spec spec{};
+    std::vector<int> layer_sliding;
+    int ctx = 0, max_seqs = 0, device = 0;
+    cudaStream_t st = nullptr;
+    std::vector<void *> allocs;
+
+    mg::DevMat embed, lm_head;
+    float *final_norm = nullptr;
+    std::vector<mg::DevMat> wq, wk, wv, wo, router_w;
+    std::vector<float *> bq, bk, bv, bo, router_b, attn_norm, mlp_norm, sinks, qn, kn;
+
+    mg_expert_layout el{};
+    uint8_t *experts = nullptr;
+    size_t experts_bytes = 0;
+
+    std::vector<uint16_t *> kc, vc;
+    std::vector<int> cap;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    std::vector<int> pos;  // per sequence
+
+    // work buffers
+    int rows_max = 0;
+    float *x = nullptr, *xb = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *ao = nullptr;
+    float *h = nullptr, *logits = nullptr, *wts = nullptr, *attn_part = nullptr;
+    int32_t *sel = nullptr, *tok_pos = nullptr, *tok_seq = nullptr, *toks = nullptr, *amax = nullptr;
+    uint16_t *tmp_k = nullptr, *tmp_v = nullptr;
+    uint32_t *usage = nullptr;
+    int attn_split = 256, attn_max_splits = 1;
+
+    // pinned host staging for per-step inputs/outputs
+    int32_t *h_toks = nullptr, *h_pos = nullptr, *h_seq = nullptr, *h_amax = nullptr;
+
+    std::unordered_map<int, mg::Graph> dec_graphs;  // keyed by n_seqs
+    uint64_t expert_loads = 0;
+    bool ready = false;
+    bool use_graphs = true;
+};

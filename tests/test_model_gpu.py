@@ -1,0 +1,133 @@
+"""Model-level parity through the C ABI (host buffers in, host buffers out):
+the GPU engine against the reference midged's golden outputs and the CPU
+oracle.  Bar: logits within max relative error 1e-3
+(the reference's own measure, tools/validate.py:133) and greedy tokens
+identical."""
+import os
+
+import numpy as np
+import pytest
+
+from midge_b200 import abi
+from midge_b200 import container as ct
+from oracle import oracle as orc
+from tests.helpers import GOLDEN, VALIDATE_CASES, load_validate_case, max_rel
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def c1_dir(tmp_path_factory):
+    spec, edt = ct.config_spec("c1_tiny")
+    return ct.write_synthetic_model(str(tmp_path_factory.mktemp("c1")), spec, edt, seed=0)
+
+
+@pytest.mark.parametrize("case", VALIDATE_CASES)
+def test_validate_cases(torch_cuda, case, tmp_path):
+    """tools/validate.py's seven cases: tfall logits at 12 positions (the
+    ctx-64 sliding ring of 8 wraps) and 24 greedy tokens."""
+    md, g = load_validate_case(case, str(tmp_path / "m"))
+    m = abi.Model.from_dir(md, ctx=int(g["ctx"]))
+    lg = m.forward_batch(0, g["ids"], logits_mode=2)
+    worst = max(max_rel(g["tfall"][i], lg[i]) for i in range(len(g["ids"])))
+    assert worst < LOGIT_TOL, worst
+    assert np.allclose(g["tfall"], lg, rtol=2e-3, atol=2e-3)
+    toks = []
+    cur = int(np.argmax(lg[-1]))
+    for _ in range(len(g["gen"])):
+        toks.append(cur)
+        _, cur = m.forward(0, cur, want_logits=False)
+    assert toks == list(g["gen"]), (toks, list(g["gen"]))
+    m.close()
+
+
+def test_c1_tfall_and_greedy_vs_reference(torch_cuda, c1_dir):
+    z = np.load(os.path.join(GOLDEN, "c1_tiny.npz"))
+    ctx = int(z["ctx"])
+    m = abi.Model.from_dir(c1_dir, ctx=ctx)
+    lg = m.forward_batch(0, z["prompt"], logits_mode=2)
+    worst = max(max_rel(z["tfall"][i], lg[i]) for i in range(len(z["prompt"])))
+    assert worst < LOGIT_TOL, worst
+    m.close()
+    m = abi.Model.from_dir(c1_dir, ctx=ctx)
+    last = m.forward_batch(0, z["prompt"], logits_mode=1)
+    cur = int(np.argmax(last))
+    toks = []
+    for _ in range(len(z["gen"])):
+        toks.append(cur)
+        _, cur = m.forward(0, cur, want_logits=False)
+    assert toks == list(z["gen"])
+    m.close()
+
+
+def test_c1_decode_path_vs_oracle(torch_cuda, c1_dir):
+    """Per-token forward (the MIDGE_NO_BATCH path) against the oracle at
+    every position, plus the usage histogram."""
+    m = abi.Model.from_dir(c1_dir, ctx=64)
+    om = orc.OracleModel(c1_dir, 64)
+    rng = np.random.default_rng(9)
+    for t in rng.integers(0, 1024, 40):
+        lg, am = m.forward(0, int(t))
+        want = om.forward(int(t))
+        assert max_rel(want, lg) < LOGIT_TOL
+        assert am == int(np.argmax(lg))
+    assert np.array_equal(m.usage(), om.usage())
+    assert m.expert_loads() == 40 * 2 * 2
+    m.close()
+    om.close()
+
+
+def test_concurrent_sequences_match_single(torch_cuda, c1_dir):
+    """Decoding 4 sequences in one step gives the same logits, bit for bit,
+    as decoding each alone (every token is its own MMA column)."""
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, 1024, n) for n in (5, 9, 3, 12)]
+    multi = abi.Model.from_dir(c1_dir, ctx=64, max_seqs=4)
+    for i, p in enumerate(prompts):
+        multi.forward_batch(i, p, logits_mode=0)
+    toks = [int(p[-1]) for p in prompts]
+    lg_multi, am_multi = multi.decode_step([0, 1, 2, 3], toks, want_logits=True)
+    for i, p in enumerate(prompts):
+        single = abi.Model.from_dir(c1_dir, ctx=64)
+        single.forward_batch(0, p, logits_mode=0)
+        lg, am = single.forward(0, toks[i])
+        assert np.array_equal(lg.view(np.uint32), lg_multi[i].view(np.uint32))
+        assert am == am_multi[i]
+        single.close()
+    multi.close()
+
+
+def test_prefill_chunking_and_long_context(torch_cuda, tmp_path):
+    """A prompt longer than the prefill chunk and the sliding window (ring
+    wrap inside and across chunks) against the oracle's 64-token chunking."""
+    spec, edt = ct.config_spec("c1_tiny")
+    spec["attn"]["sliding_window"] = 40
+    md = ct.write_synthetic_model(str(tmp_path / "m"), spec, edt, seed=4)
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, 1024, 300)
+    m = abi.Model.from_dir(md, ctx=400)
+    lg = m.forward_batch(0, prompt, logits_mode=1)
+    om = orc.OracleModel(md, 400)
+    want = om.prefill(list(prompt))
+    assert max_rel(want, lg) < LOGIT_TOL
+    for t in rng.integers(0, 1024, 10):
+        a, _ = m.forward(0, int(t))
+        b = om.forward(int(t))
+        assert max_rel(b, a) < LOGIT_TOL
+    m.close()
+    om.close()
+
+
+def test_errors_are_status_codes(torch_cuda, c1_dir):
+    m = abi.Model.from_dir(c1_dir, ctx=8)
+    with pytest.raises(abi.MidgeError) as e:
+        m.forward(0, 5000)
+    assert e.value.code == abi.MG_ERR_RANGE
+    m.forward_batch(0, list(range(8)), logits_mode=0)
+    with pytest.raises(abi.MidgeError) as e:
+        m.forward(0, 1)
+    assert e.value.code == abi.MG_ERR_RANGE and b"context full" in abi.lib.mg_last_error()
+    m.reset(0)
+    m.forward(0, 1)
+    m.close()
