@@ -1,0 +1,347 @@
+"""bench.py -- decode / prefill throughput of the gpt-oss-120b-shaped MoE on B200.
+
+Workload ("C4"): a random-init gpt-oss-120b-shaped
+model (36 layers, d_model 2880, 64 q / 8 kv heads of dim 64, sliding-128 /
+full layers, YaRN, 128 MXFP4 experts top-4 of width 2880, int8 trunk, vocab
+201088) serving 8 concurrent sequences: a prompt per sequence, then greedy
+decode steps of all 8 at once.  The trunk is generated on the host with the
+config's distributions and uploaded through the C ABI; the 64.7 GB expert
+blob is generated in HBM with the same distributions (the file would not fit
+the box's disk).  Inputs: seeded synthetic token ids.
+
+One bench "step" = 64 decode steps of the 8 sequences (512 tokens), so
+--warmup 3 --steps 5 covers the workload's 512 decode tokens per sequence.
+  value  = decode tokens/s, device-timed (CUDA events on the model's stream)
+  e2e    = decode tokens/s through mg_decode_step with host buffers (token ids
+           in, argmax ids out, copies inside the timed region)
+  prefill_tok_s = the prompts' prefill through mg_forward_batch (device-timed)
+The decode working set (~15 GB of weights per step) is far larger than L2,
+so no flush is needed between steps.
+
+--impl reference times the reference engine (oracle/_ref/midged, built from
+the reference sources with AVX2 + OpenMP) on the host cores: its per-token
+decode on 1- and 2-layer slices of the same shape, extrapolated to 36 layers.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
+DECODE_PER_STEP = 64
+N_SEQ = 8
+
+
+def peaks():
+    try:
+        with open(MEASURED) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index=0):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                self.samples.append([v.strip() for v in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 3 + i and s[3 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons}
+
+
+def build_model(torch, spec, edt, ctx, max_seqs, device=0, seed=0):
+    from midge_b200 import abi
+    from midge_b200 import container as ct
+
+    m = abi.Model(spec, ctx=ctx, max_seqs=max_seqs, device=device)
+    rng = np.random.default_rng(seed)
+    for (n, dt, shape, d, s) in ct.dense_tensors(spec, rng):
+        rows = shape[0]
+        cols = shape[1] if len(shape) > 1 else 0
+        m.set_dense(n, dt, rows, cols, np.frombuffer(d, np.uint8), np.frombuffer(s, np.uint8) if s else None)
+    m.synth_experts(edt, seed + 1)
+    m.ready()
+    return m
+
+
+def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40):
+    """Time the dominant kernel pair (routed-expert FFN: gate/up+SwiGLU and
+    down+combine) live on the resident 120b experts with decode routing of
+    8 tokens, and count its algorithmic bytes: every distinct routed expert's
+    three matrices (nibbles + ue8m0 scales + f32 bias) once, plus activations."""
+    import ctypes as C
+    from midge_b200 import abi
+
+    base, L = m.experts_device()
+    H, F, E, k = spec["hidden"], spec["moe"]["ffn"], spec["moe"]["experts"], spec["moe"]["top_k"]
+    rng = np.random.default_rng(7)
+    layers = spec["n_layers"]
+    stream = torch.cuda.ExternalStream(m.stream())
+    xb = torch.randn(N_SEQ, H, device="cuda")
+    x = torch.zeros(N_SEQ, H, device="cuda")
+    hbuf = torch.empty(N_SEQ * k * F, device="cuda")
+    sels, nbytes = [], []
+    per_mat = lambda rows, cols: rows * cols // 2 + rows * cols // 32 + rows * 4
+    for _ in range(reps):
+        sel = np.stack([rng.permutation(E)[:k] for _ in range(N_SEQ)]).astype(np.int32)
+        sels.append(torch.from_numpy(sel).cuda())
+        d = len(np.unique(sel))
+        nbytes.append(d * (2 * per_mat(F, H) + per_mat(H, F)) + N_SEQ * (H * 4 * 3 + k * F * 4 * 2))
+    w = torch.full((N_SEQ, k), 1.0 / k, device="cuda")
+    torch.cuda.synchronize()
+
+    def launch(i):
+        abi.check(abi.lib.mg_moe_ffn(C.byref(L), base, i % layers, E, xb.data_ptr(), N_SEQ, k, sels[i].data_ptr(),
+                                     w.data_ptr(), 0, 1.702, 7.0, hbuf.data_ptr(), x.data_ptr(), m.stream()))
+
+    for i in range(5):
+        launch(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        launch(i)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    by = float(np.mean(nbytes))
+    ach = by / (ms * 1e-3) / 1e9
+    return {"kernel": "k_moe_gateup+k_moe_down (8 tokens, top-4 of 128)", "ms": ms, "bytes": by, "achieved_gbs": ach,
+            "frac": ach / hbm_peak}
+
+
+def cpu_reference(spec_name="c4_120b", seconds_budget=20.0, gen=8):
+    """The reference engine on this host: decode seconds per token on 1- and
+    2-layer slices of the config (all experts), extrapolated linearly to the
+    full depth.  Returns (tok_s, cores, sample description)."""
+    from midge_b200 import container as ct
+    from oracle import oracle as orc
+
+    if not os.path.exists(orc.REF_MIDGED):
+        return None
+    cores = os.cpu_count() or 1
+    spec_full, edt = ct.config_spec(spec_name)
+    times = {}
+    tmp = tempfile.mkdtemp(prefix="midge_cpu_")
+    try:
+        for nl in (1, 2):
+            spec, _ = ct.config_spec(spec_name, nl)
+            md = ct.write_synthetic_model(os.path.join(tmp, f"l{nl}"), spec, edt, seed=3)
+            env = dict(os.environ, OMP_NUM_THREADS=str(cores))
+            p = subprocess.Popen([orc.REF_MIDGED, md, "--ctx", "256", "--temp", "0"], stdin=subprocess.PIPE,
+                                 stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True, env=env)
+            while p.stdout.readline().strip() != "READY":
+                pass
+            p.stdin.write("ids: 1 2 3 4 5 6 7 8\n")
+            p.stdin.flush()
+            p.stdout.readline()
+            p.stdin.write(f"gen: {gen}\n")
+            p.stdin.flush()
+            while True:
+                ln = p.stdout.readline()
+                if ln.startswith("DONE"):
+                    times[nl] = float(ln.split()[3]) / gen
+                    break
+            p.stdin.write("quit\n")
+            p.stdin.flush()
+            p.wait(timeout=120)
+            shutil.rmtree(md, ignore_errors=True)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    per_layer = max(times[2] - times[1], 1e-9)
+    t_full = times[1] + (spec_full["n_layers"] - 1) * per_layer
+    sample = (f"reference midged (AVX2+OpenMP, {cores} threads) greedy decode of {gen} tokens on 1- and 2-layer "
+              f"slices of the {spec_name} shape (all experts), extrapolated to {spec_full['n_layers']} layers; "
+              f"one sequence at a time (the reference is single-context)")
+    return 1.0 / t_full, cores, sample
+
+
+def run_ours(args):
+    import torch
+
+    from midge_b200 import abi  # noqa: F401  (fails loudly without the CUDA library)
+    from midge_b200 import container as ct
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    spec, edt = ct.config_spec(args.config)
+    prompt_len = args.prompt
+    ctx = prompt_len + DECODE_PER_STEP * (args.warmup + args.steps) + 8
+    hbm_peak, tc_peak, peak_kind = peaks()
+    t0 = time.time()
+    m = build_model(torch, spec, edt, ctx, N_SEQ, device=local, seed=rank)
+    load_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(m.stream())
+    rng = np.random.default_rng(100 + rank)
+    prompts = [rng.integers(0, spec["vocab"], prompt_len).astype(np.int32) for _ in range(N_SEQ)]
+
+    # prefill of the 8 prompts (device-timed on the model stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    t_pf = time.time()
+    last = []
+    for s in range(N_SEQ):
+        last.append(m.forward_batch(s, prompts[s], logits_mode=1))
+    e1.record(stream)
+    e1.synchronize()
+    pf_wall = time.time() - t_pf
+    pf_ms = e0.elapsed_time(e1)
+    prefill_tok_s = N_SEQ * prompt_len / (pf_ms / 1e3)
+    toks = np.array([int(np.argmax(l)) for l in last], np.int32)
+    seqs = np.arange(N_SEQ, dtype=np.int32)
+
+    def run_steps(nsteps, toks):
+        for _ in range(nsteps * DECODE_PER_STEP):
+            _, toks = m.decode_step(seqs, toks)
+        return toks
+
+    toks = run_steps(args.warmup, toks)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        tw = time.time()
+        toks = run_steps(args.steps, toks)
+        e1.record(stream)
+        e1.synchronize()
+        wall = time.time() - tw
+    dev_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([dev_ms, wall * 1e3], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, wall = float(t[0]), float(t[1]) / 1e3
+    ntok = N_SEQ * DECODE_PER_STEP * args.steps * world
+    value = ntok / (dev_ms / 1e3)
+    e2e = ntok / wall
+    roof = moe_kernel_roofline(torch, m, spec, hbm_peak)
+    cpu = cpu_reference(args.config) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    m.close()
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    line = {
+        "metric": "decode tok/s (gpt-oss-120b shape, 8 concurrent sequences, greedy)",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak" if world > 1 else "weak", "vs_baseline": None, "dtype": "mxfp4/int8 weights, fp32 accumulate",
+        "data": "synthetic (seeded random-init weights and token ids)",
+        "config": {"workload": f"{args.config}: 8 sequences x {prompt_len}-token prompt, "
+                               f"{DECODE_PER_STEP} decode steps per bench step",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "working set (~15 GB/step) >> L2, no flush"},
+        "prefill_tok_s": round(prefill_tok_s, 1), "prefill_wall_s": round(pf_wall, 3),
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": N_SEQ * 12 * DECODE_PER_STEP, "d2h_bytes_per_step": N_SEQ * 4 * DECODE_PER_STEP},
+        "roofline": {"bound": "hbm", "achieved": round(roof["achieved_gbs"], 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(roof["frac"], 4), "traffic": None, "kernel": roof["kernel"],
+                     "peak_kind": peak_kind},
+        "gpu_launches": None,
+        "clocks": clk.summary(),
+        "load_s": round(load_s, 1),
+    }
+    if cpu:
+        line["cpu_baseline"] = {"value": round(cpu[0], 4), "unit": "tok/s", "cores": cpu[1], "kind": "reference",
+                                "sample": cpu[2]}
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    r = cpu_reference(args.config, gen=max(2, args.steps))
+    if r is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/midged was not built (reference tree absent "
+                                                               "when the repository was built)"}))
+        return
+    tok_s, cores, sample = r
+    print(json.dumps({
+        "impl": "reference", "metric": "decode tok/s (gpt-oss-120b shape, 8 concurrent sequences, greedy)",
+        "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "config": {"workload": f"{args.config} (reference CPU engine)"},
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": "tok/s", "cores": cores, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(tok_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c4_120b")
+    ap.add_argument("--prompt", type=int, default=4096)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -83,6 +83,8 @@ def _load():
         "mg_model_experts_device": (vp, [vp, C.POINTER(MgExpertLayout)]),
         "mg_model_stream": (vp, [vp]),
         "mg_model_free": (i32, [vp]),
+        "mg_model_logits": (i32, [vp, i32, vp]),
+        "mg_bench_gemv": (i32, [i32, i64, i64, i32, C.c_double, i32, C.POINTER(C.c_double)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

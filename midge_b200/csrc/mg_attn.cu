@@ -180,15 +180,7 @@ __global__ void k_attn_combine(AttnDecodeArgs a) {
 
 template <typename K>
 static int attn_smem_cfg(K kfn, size_t smem) {
-    static unsigned configured = 0;
-    int dev = 0;
-    MG_CUDA(cudaGetDevice(&dev));
-    if (!(configured & (1u << (dev & 31)))) {
-        MG_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        configured |= 1u << (dev & 31);
-    }
-    MG_REQUIRE(smem <= 200 * 1024, MG_ERR_ARG, "attention: shared memory %zu too large", smem);
-    return MG_OK;
+    return ensure_smem(kfn, smem);
 }
 
 template <int HD>

@@ -101,7 +101,7 @@ __device__ __forceinline__ uint32_t u4pair_minus8_h2(uint32_t w_shifted) {
 
 // D(16x8 f32) += A(16x16 f16) * B(16x8 f16)
 __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -110,19 +110,19 @@ __device__ __forceinline__ void mma_16816(float d[4], const uint32_t a[4], uint3
 
 __device__ __forceinline__ uint32_t ldg_nc_u32(const void *p) {
     uint32_t v;
-    asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    asm("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
 __device__ __forceinline__ uint4 ldg_nc_u128(const void *p) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
 }
 __device__ __forceinline__ uint32_t ldg_u32_l1(const void *p) {
     uint32_t v;
-    asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    asm("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
 
@@ -150,5 +150,17 @@ __device__ __forceinline__ float block_sum(float v, float *scratch) {
 }
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+// Raise a kernel's dynamic shared memory limit once per (kernel, device).
+// Keyed by the kernel's address: template instances of one signature are
+// different kernels.
+int ensure_smem_attr(const void *fn, size_t bytes);
+template <typename K>
+inline int ensure_smem(K kfn, size_t bytes) {
+    return ensure_smem_attr(reinterpret_cast<const void *>(kfn), bytes);
+}
 
 }  // namespace mg

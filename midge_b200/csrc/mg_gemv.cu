@@ -24,39 +24,51 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(const uint8_t *__restrict
     float *red = reinterpret_cast<float *>(smem + (size_t)ncol * xs_stride * 2);
 
     using Tile = GemvTile<DT, SC, MT, NT>;
-    const int64_t rbase = (int64_t)blockIdx.x * 16 * MT;
+    const int64_t ntiles = (rows + 16 * MT - 1) / (16 * MT);
     int c0, c1;
     warp_chunk_range(cols / Tile::CHUNK, c0, c1);
+    if ((int64_t)blockIdx.x < ntiles) {
 #pragma unroll
-    for (int m = 0; m < MT; m++) prefetch_tile<DT, SC>(w, scales, rbase + 16 * m, rows, cols, c0, c1);
+        for (int m = 0; m < MT; m++)
+            prefetch_tile<DT, SC>(w, scales, (int64_t)blockIdx.x * 16 * MT + 16 * m, rows, cols, c0, c1);
+    }
     stage_x<DT>(x, ldx, n_tok, cols, xs, xs_stride);
     __syncthreads();
-
-    const uint8_t *wp[MT];
-    const uint8_t *sp[MT];
-    int64_t r0[MT];
-#pragma unroll
-    for (int m = 0; m < MT; m++) { wp[m] = w; sp[m] = scales; r0[m] = rbase + 16 * m; }
-    float acc[MT][NT][4];
-#pragma unroll
-    for (int m = 0; m < MT; m++)
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[m][nt][i] = 0.f;
     const int nt_active = (n_tok + 3) >> 2;
-    Tile::run(wp, sp, r0, rows, cols, c0, c1, xs, xs_stride, nt_active, acc);
-    gemv_block_reduce<MT, NT>(acc, red);
 
-    for (int j = threadIdx.x; j < 16 * MT * n_tok; j += blockDim.x) {
-        int tok = j / (16 * MT), rl = j - tok * 16 * MT;
-        int64_t r = rbase + rl;
-        if (r >= rows) continue;
-        float v = gemv_out<NT>(red, rl >> 4, rl & 15, tok);
-        if (DT == MG_Q8R) v = v * reinterpret_cast<const float *>(scales)[r];
-        if (bias) v += bias[r];
-        float *yp = y + (int64_t)tok * ldy + r;
-        *yp = accumulate ? *yp + v : v;
+    // persistent over row tiles: the activations are staged once per block
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int64_t rbase = tile * 16 * MT;
+        const int64_t nxt = tile + gridDim.x;
+        if (nxt < ntiles) {
+#pragma unroll
+            for (int m = 0; m < MT; m++) prefetch_tile<DT, SC>(w, scales, nxt * 16 * MT + 16 * m, rows, cols, c0, c1);
+        }
+        const uint8_t *wp[MT];
+        const uint8_t *sp[MT];
+        int64_t r0[MT];
+#pragma unroll
+        for (int m = 0; m < MT; m++) { wp[m] = w; sp[m] = scales; r0[m] = rbase + 16 * m; }
+        float acc[MT][NT][4];
+#pragma unroll
+        for (int m = 0; m < MT; m++)
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[m][nt][i] = 0.f;
+        Tile::run(wp, sp, r0, rows, cols, c0, c1, xs, xs_stride, nt_active, acc);
+        gemv_block_reduce<MT, NT>(acc, red);
+        for (int j = threadIdx.x; j < 16 * MT * n_tok; j += blockDim.x) {
+            int tok = j / (16 * MT), rl = j - tok * 16 * MT;
+            int64_t r = rbase + rl;
+            if (r >= rows) continue;
+            float v = gemv_out<NT>(red, rl >> 4, rl & 15, tok);
+            if (DT == MG_Q8R) v = v * reinterpret_cast<const float *>(scales)[r];
+            if (bias) v += bias[r];
+            float *yp = y + (int64_t)tok * ldy + r;
+            *yp = accumulate ? *yp + v : v;
+        }
+        __syncthreads();  // red is reused by the next tile
     }
 }
 
@@ -100,15 +112,14 @@ static int launch_gemv_t(const uint8_t *w, const uint8_t *s, int64_t rows, int c
                          cudaStream_t st) {
     size_t smem = gemv_smem_bytes(cols, MT, NT);
     auto kfn = k_gemv<DT, SC, MT, NT>;
-    static unsigned configured = 0;  // bit per device, per instantiation
-    int dev = 0;
-    MG_CUDA(cudaGetDevice(&dev));
-    if (!(configured & (1u << (dev & 31)))) {
-        MG_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        configured |= 1u << (dev & 31);
-    }
     MG_REQUIRE(smem <= 200 * 1024, MG_ERR_ARG, "gemv: %d columns x %d tokens exceed shared memory", cols, n_tok);
-    int grid = ceil_div(rows, 16 * MT);
+    int rc = ensure_smem(kfn, smem);
+    if (rc) return rc;
+    int ntiles = ceil_div(rows, 16 * MT);
+    int max_resident = 0;
+    MG_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&max_resident, kfn, GEMV_THREADS, smem));
+    int nsm = num_sms();
+    int grid = max_resident > 0 && ntiles > max_resident * nsm ? max_resident * nsm : ntiles;
     kfn<<<grid, GEMV_THREADS, smem, st>>>(w, s, rows, cols, x, ldx, n_tok, bias, acc, y, ldy);
     MG_CHECK_LAUNCH();
     return MG_OK;

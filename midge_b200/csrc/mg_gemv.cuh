@@ -93,18 +93,122 @@ __device__ __forceinline__ void prefetch_tile(const uint8_t *w, const uint8_t *s
 }
 
 // Per-thread partial sums of one warp over chunk range [c0, c1) for MT row
-// tiles (rows base_row[mt] + 0..15 of matrix w[mt]) and NT n-tiles.
+// tiles (rows row0[mt] + 0..15 of matrix w[mt]) and NT n-tiles.
 // 4-bit: chunk = one 32-column group; q8r: chunk = 64 columns.
-// acc[mt][nt][0..3] follow the m16n8 accumulator layout.
+// acc[mt][nt][0..3] follow the m16n8 accumulator layout.  The loop is
+// software-pipelined: the loads of batch b+1 (U chunks) are issued before the
+// tensor-core work of batch b.
 template <int DT, int SC, int MT, int NT>
 struct GemvTile {
     static constexpr int CHUNK = (DT == MG_Q8R) ? 64 : 32;
-    static constexpr int U = (DT == MG_Q8R) ? 2 : 4;  // chunks whose loads are issued together
+    static constexpr int U = (DT == MG_Q8R) ? 2 : 4;  // chunks per batch
+    static constexpr int WW = (DT == MG_Q8R) ? 4 : 1; // 32-bit words per row per chunk per thread
+
+    struct Batch {
+        uint32_t wa[U][MT][WW], wb[U][MT][WW];
+        float sa[U][MT], sb[U][MT];
+    };
+
+    __device__ __forceinline__ static void load(Batch &bt, const uint8_t *const w[MT], const uint8_t *const sc[MT],
+                                                const int64_t ra[MT], const int64_t rb[MT], const bool va[MT],
+                                                const bool vb[MT], int64_t rowbytes, int gpr, int cb, int c1, int t) {
+#pragma unroll
+        for (int u = 0; u < U; u++)
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                const int c = cb + u;
+                const bool oka = c < c1 && va[m], okb = c < c1 && vb[m];
+                if constexpr (DT == MG_Q8R) {
+                    const uint8_t *pa = w[m] + ra[m] * rowbytes + (int64_t)c * 64 + 16 * t;
+                    const uint8_t *pb = w[m] + rb[m] * rowbytes + (int64_t)c * 64 + 16 * t;
+                    uint4 x = oka ? ldg_nc_u128(pa) : make_uint4(0, 0, 0, 0);
+                    uint4 y = okb ? ldg_nc_u128(pb) : make_uint4(0, 0, 0, 0);
+                    bt.wa[u][m][0] = x.x; bt.wa[u][m][1] = x.y; bt.wa[u][m][2] = x.z; bt.wa[u][m][3] = x.w;
+                    bt.wb[u][m][0] = y.x; bt.wb[u][m][1] = y.y; bt.wb[u][m][2] = y.z; bt.wb[u][m][3] = y.w;
+                } else {
+                    const uint8_t *pa = w[m] + ra[m] * rowbytes + (int64_t)c * 16 + 4 * t;
+                    const uint8_t *pb = w[m] + rb[m] * rowbytes + (int64_t)c * 16 + 4 * t;
+                    bt.wa[u][m][0] = oka ? ldg_u32_l1(pa) : 0u;
+                    bt.wb[u][m][0] = okb ? ldg_u32_l1(pb) : 0u;
+                    if (SC == MG_SCALE_UE8M0) {
+                        bt.sa[u][m] = oka ? ue8m0_to_f32(__ldg(sc[m] + ra[m] * gpr + c)) : 0.f;
+                        bt.sb[u][m] = okb ? ue8m0_to_f32(__ldg(sc[m] + rb[m] * gpr + c)) : 0.f;
+                    } else {
+                        const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sc[m]);
+                        bt.sa[u][m] = oka ? h2f(__ldg(s16 + ra[m] * gpr + c)) : 0.f;
+                        bt.sb[u][m] = okb ? h2f(__ldg(s16 + rb[m] * gpr + c)) : 0.f;
+                    }
+                }
+            }
+    }
+
+    __device__ __forceinline__ static void compute(const Batch &bt, int cb, int c1, const __half *xs, int xs_stride,
+                                                   int nt_active, int g, int t, float acc[MT][NT][4]) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int c = cb + u;
+            if (c >= c1) break;
+            if constexpr (DT == MG_Q8R) {
+                uint32_t fa[MT][4][4];  // [m][k-step][a-register]
+#pragma unroll
+                for (int m = 0; m < MT; m++)
+#pragma unroll
+                    for (int s = 0; s < 4; s++) {
+                        s8x4_to_h2(bt.wa[u][m][s], fa[m][s][0], fa[m][s][2]);
+                        s8x4_to_h2(bt.wb[u][m][s], fa[m][s][1], fa[m][s][3]);
+                    }
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    if (nt >= nt_active) break;
+                    const __half *xp = xs + (nt * 8 + g) * xs_stride + c * 64 + 16 * t;
+                    uint4 x0 = *reinterpret_cast<const uint4 *>(xp);
+                    uint4 x1 = *reinterpret_cast<const uint4 *>(xp + 8);
+                    uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                    for (int m = 0; m < MT; m++)
+#pragma unroll
+                        for (int s = 0; s < 4; s++) mma_16816(acc[m][nt], fa[m][s], bx[2 * s], bx[2 * s + 1]);
+                }
+            } else {
+                uint32_t fa[MT][4], fb[MT][4];
+#pragma unroll
+                for (int m = 0; m < MT; m++) {
+                    if (DT == MG_MXFP4) {
+                        e2m1x8_to_h2(bt.wa[u][m][0], fa[m]);
+                        e2m1x8_to_h2(bt.wb[u][m][0], fb[m]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            fa[m][i] = u4pair_minus8_h2(bt.wa[u][m][0] >> (4 * i));
+                            fb[m][i] = u4pair_minus8_h2(bt.wb[u][m][0] >> (4 * i));
+                        }
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    if (nt >= nt_active) break;
+                    const __half *xp = xs + (nt * 8 + g) * xs_stride + c * 32 + 8 * t;
+                    uint4 bx = *reinterpret_cast<const uint4 *>(xp);
+#pragma unroll
+                    for (int m = 0; m < MT; m++) {
+                        float d[4] = {0.f, 0.f, 0.f, 0.f};
+                        uint32_t a0[4] = {fa[m][0], fb[m][0], fa[m][1], fb[m][1]};
+                        uint32_t a1[4] = {fa[m][2], fb[m][2], fa[m][3], fb[m][3]};
+                        mma_16816(d, a0, bx.x, bx.y);
+                        mma_16816(d, a1, bx.z, bx.w);
+                        acc[m][nt][0] = fmaf(bt.sa[u][m], d[0], acc[m][nt][0]);
+                        acc[m][nt][1] = fmaf(bt.sa[u][m], d[1], acc[m][nt][1]);
+                        acc[m][nt][2] = fmaf(bt.sb[u][m], d[2], acc[m][nt][2]);
+                        acc[m][nt][3] = fmaf(bt.sb[u][m], d[3], acc[m][nt][3]);
+                    }
+                }
+            }
+        }
+    }
 
     __device__ __forceinline__ static void run(const uint8_t *const w[MT], const uint8_t *const sc[MT],
-                                               const int64_t row0[MT], int64_t rows, int cols, int c0,
-                                               int c1, const __half *xs, int xs_stride, int nt_active,
-                                               float acc[MT][NT][4]) {
+                                               const int64_t row0[MT], int64_t rows, int cols, int c0, int c1,
+                                               const __half *xs, int xs_stride, int nt_active, float acc[MT][NT][4]) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
         const int64_t rowbytes = (DT == MG_Q8R) ? cols : cols / 2;
         const int gpr = cols / 32;
@@ -117,109 +221,14 @@ struct GemvTile {
             va[m] = ra[m] < rows;
             vb[m] = rb[m] < rows;
         }
+        if (c0 >= c1) return;
+        Batch cur, nxt;
+        load(cur, w, sc, ra, rb, va, vb, rowbytes, gpr, c0, c1, t);
         for (int cb = c0; cb < c1; cb += U) {
-            if constexpr (DT == MG_Q8R) {
-                uint4 wa[U][MT], wb[U][MT];
-#pragma unroll
-                for (int u = 0; u < U; u++)
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        int c = cb + u;
-                        bool ok = c < c1;
-                        const uint8_t *pa = w[m] + ra[m] * rowbytes + (int64_t)c * 64 + 16 * t;
-                        const uint8_t *pb = w[m] + rb[m] * rowbytes + (int64_t)c * 64 + 16 * t;
-                        wa[u][m] = (ok && va[m]) ? ldg_nc_u128(pa) : make_uint4(0, 0, 0, 0);
-                        wb[u][m] = (ok && vb[m]) ? ldg_nc_u128(pb) : make_uint4(0, 0, 0, 0);
-                    }
-#pragma unroll
-                for (int u = 0; u < U; u++) {
-                    int c = cb + u;
-                    if (c >= c1) break;
-                    uint32_t fa[MT][4][4];  // [m][k-step][a-register]
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        uint32_t wav[4] = {wa[u][m].x, wa[u][m].y, wa[u][m].z, wa[u][m].w};
-                        uint32_t wbv[4] = {wb[u][m].x, wb[u][m].y, wb[u][m].z, wb[u][m].w};
-#pragma unroll
-                        for (int s = 0; s < 4; s++) {
-                            s8x4_to_h2(wav[s], fa[m][s][0], fa[m][s][2]);
-                            s8x4_to_h2(wbv[s], fa[m][s][1], fa[m][s][3]);
-                        }
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        if (nt >= nt_active) break;
-                        const __half *xp = xs + (nt * 8 + g) * xs_stride + c * 64 + 16 * t;
-                        uint4 x0 = *reinterpret_cast<const uint4 *>(xp);
-                        uint4 x1 = *reinterpret_cast<const uint4 *>(xp + 8);
-                        uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-                        for (int m = 0; m < MT; m++)
-#pragma unroll
-                            for (int s = 0; s < 4; s++) mma_16816(acc[m][nt], fa[m][s], bx[2 * s], bx[2 * s + 1]);
-                    }
-                }
-            } else {
-                uint32_t wa[U][MT], wb[U][MT];
-                float sa[U][MT], sb[U][MT];
-#pragma unroll
-                for (int u = 0; u < U; u++)
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        int c = cb + u;
-                        bool ok = c < c1;
-                        const uint8_t *pa = w[m] + ra[m] * rowbytes + (int64_t)c * 16 + 4 * t;
-                        const uint8_t *pb = w[m] + rb[m] * rowbytes + (int64_t)c * 16 + 4 * t;
-                        bool oka = ok && va[m], okb = ok && vb[m];
-                        wa[u][m] = oka ? ldg_u32_l1(pa) : 0u;
-                        wb[u][m] = okb ? ldg_u32_l1(pb) : 0u;
-                        if (SC == MG_SCALE_UE8M0) {
-                            sa[u][m] = oka ? ue8m0_to_f32(sc[m][ra[m] * gpr + c]) : 0.f;
-                            sb[u][m] = okb ? ue8m0_to_f32(sc[m][rb[m] * gpr + c]) : 0.f;
-                        } else {
-                            const uint16_t *s16 = reinterpret_cast<const uint16_t *>(sc[m]);
-                            sa[u][m] = oka ? h2f(s16[ra[m] * gpr + c]) : 0.f;
-                            sb[u][m] = okb ? h2f(s16[rb[m] * gpr + c]) : 0.f;
-                        }
-                    }
-#pragma unroll
-                for (int u = 0; u < U; u++) {
-                    int c = cb + u;
-                    if (c >= c1) break;
-                    uint32_t fa[MT][4], fb[MT][4];
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        if (DT == MG_MXFP4) {
-                            e2m1x8_to_h2(wa[u][m], fa[m]);
-                            e2m1x8_to_h2(wb[u][m], fb[m]);
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < 4; i++) {
-                                fa[m][i] = u4pair_minus8_h2(wa[u][m] >> (4 * i));
-                                fb[m][i] = u4pair_minus8_h2(wb[u][m] >> (4 * i));
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        if (nt >= nt_active) break;
-                        const __half *xp = xs + (nt * 8 + g) * xs_stride + c * 32 + 8 * t;
-                        uint4 bx = *reinterpret_cast<const uint4 *>(xp);
-#pragma unroll
-                        for (int m = 0; m < MT; m++) {
-                            float d[4] = {0.f, 0.f, 0.f, 0.f};
-                            uint32_t a0[4] = {fa[m][0], fb[m][0], fa[m][1], fb[m][1]};
-                            uint32_t a1[4] = {fa[m][2], fb[m][2], fa[m][3], fb[m][3]};
-                            mma_16816(d, a0, bx.x, bx.y);
-                            mma_16816(d, a1, bx.z, bx.w);
-                            acc[m][nt][0] = fmaf(sa[u][m], d[0], acc[m][nt][0]);
-                            acc[m][nt][1] = fmaf(sa[u][m], d[1], acc[m][nt][1]);
-                            acc[m][nt][2] = fmaf(sb[u][m], d[2], acc[m][nt][2]);
-                            acc[m][nt][3] = fmaf(sb[u][m], d[3], acc[m][nt][3]);
-                        }
-                    }
-                }
-            }
+            const bool more = cb + U < c1;
+            if (more) load(nxt, w, sc, ra, rb, va, vb, rowbytes, gpr, cb + U, c1, t);
+            compute(cur, cb, c1, xs, xs_stride, nt_active, g, t, acc);
+            if (more) cur = nxt;
         }
     }
 };

@@ -132,13 +132,8 @@ int router(const RouterArgs &a, cudaStream_t st) {
     if (a.n_tok == 0) return MG_OK;
     size_t smem = (size_t)(a.hidden + a.n_experts) * 4;
     MG_REQUIRE(smem <= 160 * 1024, MG_ERR_ARG, "router: hidden %lld too large", (long long)a.hidden);
-    static unsigned configured = 0;
-    int dev = 0;
-    MG_CUDA(cudaGetDevice(&dev));
-    if (!(configured & (1u << (dev & 31)))) {
-        MG_CUDA(cudaFuncSetAttribute(k_router, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-        configured |= 1u << (dev & 31);
-    }
+    int rc0 = ensure_smem(k_router, smem);
+    if (rc0) return rc0;
     int threads = a.n_experts * 8;
     threads = threads < 256 ? 256 : threads > ROUTER_THREADS ? ROUTER_THREADS : (threads + 31) / 32 * 32;
     k_router<<<a.n_tok, threads, smem, st>>>(a);
@@ -319,19 +314,6 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_moe_down(MoeArgs a) {
         float *xp = a.x + (int64_t)t * a.ldx + r;
         *xp = __fadd_rn(*xp, moe);
     }
-}
-
-template <typename K>
-static int ensure_smem(K kfn, size_t bytes) {
-    static unsigned configured = 0;
-    int dev = 0;
-    MG_CUDA(cudaGetDevice(&dev));
-    if (!(configured & (1u << (dev & 31)))) {
-        MG_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        configured |= 1u << (dev & 31);
-    }
-    MG_REQUIRE(bytes <= 220 * 1024, MG_ERR_ARG, "moe: shared memory %zu too large", bytes);
-    return MG_OK;
 }
 
 template <int DT, int SC, int NT>
