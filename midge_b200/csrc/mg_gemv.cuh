@@ -33,14 +33,14 @@ __device__ __forceinline__ int q4_stage_perm(int p) {  // position p in an 8-col
 // those outputs are never read.  Vector path: 8 columns per step (two 16-byte
 // loads, two 16-byte stores); needs x 16-byte aligned and ldx % 4 == 0.
 template <int DT>
-__device__ __forceinline__ void stage_x(const float *x, int64_t ldx, int n_tok, int cols, __half *xs,
-                                        int xs_stride) {
+__device__ __forceinline__ void stage_x_n(const float *x, int64_t ldx, int n_tok, int cols, __half *xs,
+                                          int xs_stride, int tid, int nthr) {
     const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((ldx & 3) == 0);
     if (vec) {
         const int q = cols >> 3;
         const int total = n_tok * q;
 #pragma unroll 2
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+        for (int i = tid; i < total; i += nthr) {
             const int t = i / q, c8 = (i - t * q) << 3;
             const float4 *src = reinterpret_cast<const float4 *>(x + (int64_t)t * ldx + c8);
             float4 a = __ldg(src), b = __ldg(src + 1);
@@ -56,7 +56,7 @@ __device__ __forceinline__ void stage_x(const float *x, int64_t ldx, int n_tok, 
         }
     } else {
         const int total = n_tok * cols;
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+        for (int i = tid; i < total; i += nthr) {
             const int t = i / cols, c = i - t * cols;
             const int src = DT == MG_Q4G32 ? ((c & ~7) | q4_stage_perm(c & 7)) : c;
             __half hi, lo;
@@ -65,6 +65,12 @@ __device__ __forceinline__ void stage_x(const float *x, int64_t ldx, int n_tok, 
             xs[(2 * t + 1) * xs_stride + c] = lo;
         }
     }
+}
+
+template <int DT>
+__device__ __forceinline__ void stage_x(const float *x, int64_t ldx, int n_tok, int cols, __half *xs,
+                                        int xs_stride) {
+    stage_x_n<DT>(x, ldx, n_tok, cols, xs, xs_stride, threadIdx.x, blockDim.x);
 }
 
 __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {

@@ -18,6 +18,30 @@ int scales_to_ue8m0(const uint16_t *f16, uint8_t *ue8m0, int64_t n, int *n_inexa
 int rmsnorm(const float *x, const float *w, float *out, int64_t n, int n_rows, float eps, cudaStream_t st);
 int to_f16_ftz(const float *x, uint16_t *out, int64_t n, cudaStream_t st);
 
+// streamed (bulk-copy ring) GEMV over up to 3 row-concatenated matrices
+struct StreamMat {
+    const void *w, *scales;
+    const float *bias;
+    int64_t rows;
+    float *y;      // outputs (ksplit == 1) or partial planes (ksplit > 1)
+    int64_t ldy;
+};
+struct StreamGemvArgs {
+    int dt, scale_fmt;
+    StreamMat mat[3];
+    int nmat;
+    int64_t cols;
+    const float *x;
+    int64_t ldx;
+    int n_tok;            // <= 8
+    int accumulate;       // ksplit == 1 only
+    int ksplit;           // K splits (partials written to y + ks*part_stride)
+    int64_t part_stride;
+};
+int stream_gemv(const StreamGemvArgs &a, cudaStream_t st);
+int stream_error_check();
+int stream_prepare();
+
 // router: norm (optional) + AVX2-order f32 logits + top-k + weights + usage
 struct RouterArgs {
     const float *x;        // [n_tok x hidden] residual rows (normed here if norm_w != null)
