@@ -17,6 +17,53 @@ void set_error(const char *fmt, ...) {
     va_end(ap);
 }
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+void *encode_tiled_fn() {
+    static void *fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = p;
+    }
+    return fn;
+}
+
+// byte tensor {row bytes, rows [, experts, layers]}, box 128 B x box_rows, 128-byte swizzle, OOB -> 0
+static int map_weights(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
+                       int box_rows) {
+    EncodeTiledFn fn = reinterpret_cast<EncodeTiledFn>(encode_tiled_fn());
+    MG_REQUIRE(fn, MG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(base) & 15) == 0, MG_ERR_ARG, "weight map: base not 16-byte aligned");
+    for (int i = 0; i < rank - 1; i++)
+        MG_REQUIRE(strides[i] % 16 == 0, MG_ERR_ARG, "weight map: stride %llu not a multiple of 16",
+                   (unsigned long long)strides[i]);
+    cuuint32_t box[4] = {128, (cuuint32_t)box_rows, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)rank, const_cast<void *>(base), dims, strides, box,
+                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    MG_REQUIRE(r == CUDA_SUCCESS, MG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MG_OK;
+}
+
+int map_weights_2d(CUtensorMap *map, const void *base, int64_t rowbytes, int64_t rows, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)rowbytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)rowbytes};
+    return map_weights(map, base, 2, dims, strides, box_rows);
+}
+
+int map_weights_4d(CUtensorMap *map, const void *base, int64_t rowbytes, int64_t rows, int64_t n_experts,
+                   int64_t n_layers, int64_t expert_stride, int64_t layer_stride, int box_rows) {
+    cuuint64_t dims[4] = {(cuuint64_t)rowbytes, (cuuint64_t)rows, (cuuint64_t)n_experts, (cuuint64_t)n_layers};
+    cuuint64_t strides[3] = {(cuuint64_t)rowbytes, (cuuint64_t)expert_stride, (cuuint64_t)layer_stride};
+    return map_weights(map, base, 4, dims, strides, box_rows);
+}
+
 int num_sms() {
     static int cache[64] = {0};
     int dev = 0;

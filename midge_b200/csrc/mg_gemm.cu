@@ -1,0 +1,342 @@
+// mg_gemm.cu -- expert-major grouped GEMM for prefill on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in TMEM, activations by TMA).
+//
+// D[M x N] = W[M x K] . X[N x K]^T per expert, M = weight rows (output
+// features), N = the tokens routed to the expert (expert-major rows), K-major
+// operands in 128-byte-swizzled shared memory:
+//   * W (MXFP4 / q8r) is decoded by four converter warps straight into the
+//     UMMA layout as f16, exactly: e2m1 values times 2^(k - k0) with a
+//     per-matrix rebase k0 (so every group scale folds into f16 without
+//     rounding), int8 values as they are; k0 (or the q8r row scale) is
+//     restored in fp32 in the epilogue;
+//   * X is an fp32 activation split into f16 hi + lo halves (~22 bits); the
+//     two halves are two MMAs into the same accumulator;
+//   * modes: GATEUP (gate and up tiles in two TMEM accumulators, the clamped /
+//     plain SwiGLU in the epilogue, h written back as f16 hi/lo for the down
+//     GEMM), DOWN (y = W h + bias per expert-major row), DENSE (one matrix over
+//     all tokens, y = W x + bias, stored or accumulated: the trunk in prefill).
+// Warp roles: warp 0 issues TMA for X, warp 1 issues the MMAs (one thread) and
+// owns TMEM, warps 2-5 convert W and run the epilogue.  All waits are bounded.
+#include <cuda.h>
+
+#include "mg_gemm.h"
+#include "mg_kernels.h"
+#include "mg_tc.cuh"
+
+namespace mg {
+
+constexpr int XG_M = 128, XG_N = 128, XG_K = 64;
+constexpr int XG_THREADS = 192;
+constexpr int XG_TILE_BYTES = XG_M * XG_K * 2;  // 16 KB: 128 rows x 128 B
+constexpr int XG_ERR = 2;
+
+template <int MODE>
+struct XgCfg {
+    static constexpr int NA = MODE == XG_GATEUP ? 2 : 1;              // A tiles per stage
+    static constexpr int STAGE = (NA + 2) * XG_TILE_BYTES;           // + B hi + B lo
+    static constexpr int STAGES = MODE == XG_GATEUP ? 3 : 4;
+    static constexpr int TMEM_COLS = NA * XG_N;                       // 256 or 128
+};
+
+// f16x2 holding 2^e in both halves (e >= -24), exact
+__device__ __forceinline__ uint32_t pow2_h2(int e) {
+    uint32_t h;
+    if (e >= -14) h = (uint32_t)(e + 15) << 10;
+    else h = 1u << (e + 24);
+    return h | (h << 16);
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+
+// Convert one 128 x 64 weight tile (rows m0.., K columns k0..k0+63 of the
+// matrix at w) into f16 at `dst` in the 128B-swizzled K-major layout.
+// 128 threads, one row each.  Out-of-range rows are written as zeros.
+template <int DT>
+__device__ __forceinline__ void xg_convert_tile(uint8_t *dst, const uint8_t *w, const uint8_t *sc, int64_t rows,
+                                                int64_t cols, int64_t m0, int kt, int rebase, int tid) {
+    const int r = tid;  // 0..127
+    const int64_t row = m0 + r;
+    uint8_t *drow = dst + r * 128;
+    const int sw = r & 7;
+    uint32_t v[32];  // 64 f16 = 32 words
+    if (row < rows) {
+        if constexpr (DT == MG_Q8R) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(w + row * cols + (int64_t)kt * 64);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint4 b = __ldg(src + q);
+                s8x4_to_h2(b.x, v[8 * q + 0], v[8 * q + 1]);
+                s8x4_to_h2(b.y, v[8 * q + 2], v[8 * q + 3]);
+                s8x4_to_h2(b.z, v[8 * q + 4], v[8 * q + 5]);
+                s8x4_to_h2(b.w, v[8 * q + 6], v[8 * q + 7]);
+            }
+        } else {
+            const uint4 *src = reinterpret_cast<const uint4 *>(w + row * (cols / 2) + (int64_t)kt * 32);
+            const int64_t gpr = cols / 32;
+#pragma unroll
+            for (int gi = 0; gi < 2; gi++) {  // two 32-column groups per tile
+                const uint4 b = __ldg(src + gi);
+                const uint32_t u = sc[row * gpr + (int64_t)kt * 2 + gi];
+                const uint32_t f = u ? pow2_h2((int)u - 127 - rebase) : 0u;
+                uint32_t words[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int wd = 0; wd < 4; wd++) {
+                    uint32_t o[4];
+                    e2m1x8_to_h2(words[wd], o);
+#pragma unroll
+                    for (int i = 0; i < 4; i++) v[16 * gi + 4 * wd + i] = hmul2_u32(o[i], f);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = 0u;
+    }
+#pragma unroll
+    for (int c = 0; c < 8; c++)  // 16-byte chunk c of the 128-byte row, swizzled
+        *reinterpret_cast<uint4 *>(drow + ((c ^ sw) << 4)) = make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+}
+
+template <int MODE, int DT>
+__global__ void __launch_bounds__(XG_THREADS, 1)
+    k_xgemm(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo, XgArgs a) {
+    using C = XgCfg<MODE>;
+    extern __shared__ __align__(1024) uint8_t xsm[];
+    uint8_t *base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(xsm) + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t full_a[C::STAGES], full_b[C::STAGES], empty[C::STAGES], acc_full;
+    __shared__ uint32_t tmem_base;
+    __shared__ XgTile tile;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) tile = a.tiles[blockIdx.y];
+    __syncthreads();
+    if ((int)blockIdx.y >= *a.ntiles) return;  // uniform: no TMEM touched yet
+    const int64_t m0 = (int64_t)blockIdx.x * XG_M;
+    if (m0 >= a.M) return;
+    const int e = tile.e;
+    const int64_t grow0 = (int64_t)a.offs[e] + tile.row0;  // first expert-major row of the N tile
+    const int KT = (int)(a.K / XG_K);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            mbar_init(&full_a[s], 128);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&acc_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(&tmem_base, C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+
+    // expert (or dense) weights
+    const uint8_t *wmat[2];
+    const uint8_t *smat[2];
+    int rebase[2] = {0, 0};
+    if (MODE == XG_DENSE) {
+        wmat[0] = a.dense_w;
+        smat[0] = a.dense_s;
+    } else {
+        const uint8_t *eb = a.experts_layer + (int64_t)e * a.L.expert_stride;
+        const int mm0 = MODE == XG_DOWN ? 2 : 0;
+        wmat[0] = eb + a.L.off[mm0][0];
+        smat[0] = eb + a.L.off[mm0][1];
+        wmat[1] = eb + a.L.off[1][0];
+        smat[1] = eb + a.L.off[1][1];
+        if (DT != MG_Q8R) {
+            rebase[0] = a.rebase[e * 3 + mm0];
+            rebase[1] = a.rebase[e * 3 + 1];
+        }
+    }
+    bool ok = true;
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        if (lane == 0) {
+            for (int kt = 0; kt < KT && ok; kt++) {
+                const int s = kt % C::STAGES;
+                if (kt >= C::STAGES) ok = mbar_wait(&empty[s], ((kt / C::STAGES) - 1) & 1);
+                if (!ok) break;
+                uint8_t *st = base + (size_t)s * C::STAGE;
+                mbar_arrive_expect_tx(&full_b[s], 2 * XG_TILE_BYTES);
+                tma_load_2d(st + C::NA * XG_TILE_BYTES, &tm_hi, kt * XG_K, (int)grow0, &full_b[s]);
+                tma_load_2d(st + (C::NA + 1) * XG_TILE_BYTES, &tm_lo, kt * XG_K, (int)grow0, &full_b[s]);
+            }
+            if (!ok) atomicExch(a.err, XG_ERR);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_f16(XG_M, XG_N);
+            for (int kt = 0; kt < KT && ok; kt++) {
+                const int s = kt % C::STAGES;
+                const uint32_t par = (kt / C::STAGES) & 1;
+                ok = mbar_wait(&full_b[s], par) && mbar_wait(&full_a[s], par);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t st = smem_u32(base + (size_t)s * C::STAGE);
+                const uint32_t bh = st + C::NA * XG_TILE_BYTES, bl = st + (C::NA + 1) * XG_TILE_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < XG_K / 16; kk++) {
+                    const uint32_t koff = kk * 32;  // 16 f16 = 32 bytes along K inside the swizzle atom
+                    const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+#pragma unroll
+                    for (int na = 0; na < C::NA; na++) {
+                        const uint64_t ad = umma_desc_sw128(st + na * XG_TILE_BYTES + koff);
+                        const uint32_t td = tmem + na * XG_N;
+                        tc_mma_f16(td, ad, umma_desc_sw128(bh + koff), idesc, acc);
+                        tc_mma_f16(td, ad, umma_desc_sw128(bl + koff), idesc, 1u);
+                    }
+                }
+                tc_commit(&empty[s]);  // stage s free once these MMAs have read it
+            }
+            if (ok) tc_commit(&acc_full);
+            else atomicExch(a.err, XG_ERR);
+        }
+    } else {
+        // ------------------------------------------- converters + epilogue
+        const int tid = threadIdx.x - 64;  // 0..127
+        for (int kt = 0; kt < KT && ok; kt++) {
+            const int s = kt % C::STAGES;
+            if (kt >= C::STAGES) ok = mbar_wait(&empty[s], ((kt / C::STAGES) - 1) & 1);
+            if (!ok) break;
+            uint8_t *st = base + (size_t)s * C::STAGE;
+#pragma unroll
+            for (int na = 0; na < C::NA; na++)
+                xg_convert_tile<DT>(st + na * XG_TILE_BYTES, wmat[na], smat[na], a.M, a.K, m0, kt, rebase[na], tid);
+            fence_proxy_async_smem();
+            mbar_arrive(&full_a[s]);
+        }
+        if (ok) ok = mbar_wait(&acc_full, 0);
+        if (!ok) {
+            if (tid == 0) atomicExch(a.err, XG_ERR);
+        } else {
+            tc_fence_after();
+            const int q = warp & 3;  // TMEM lane quarter this warp may access
+            const int64_t row = m0 + 32 * q + lane;
+            const bool rv = row < a.M;
+            float scale0 = 1.f, scale1 = 1.f, b0 = 0.f, b1 = 0.f;
+            if (rv) {
+                if (DT == MG_Q8R) {
+                    scale0 = reinterpret_cast<const float *>(smat[0])[row];
+                    if (MODE == XG_GATEUP) scale1 = reinterpret_cast<const float *>(smat[1])[row];
+                } else {
+                    scale0 = exp2f((float)rebase[0]);
+                    scale1 = exp2f((float)rebase[1]);
+                }
+                if (MODE == XG_DENSE) {
+                    b0 = a.dense_bias ? a.dense_bias[row] : 0.f;
+                } else {
+                    const uint8_t *eb = a.experts_layer + (int64_t)e * a.L.expert_stride;
+                    const int mm0 = MODE == XG_DOWN ? 2 : 0;
+                    b0 = reinterpret_cast<const float *>(eb + a.L.off[mm0][2])[row];
+                    if (MODE == XG_GATEUP) b1 = reinterpret_cast<const float *>(eb + a.L.off[1][2])[row];
+                }
+            }
+            for (int c0 = 0; c0 < XG_N; c0 += 16) {
+                float vg[16], vu[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c0, vg);
+                if (MODE == XG_GATEUP) tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + XG_N + c0, vu);
+                if (!rv) continue;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int n = c0 + j;
+                    if (n >= tile.nrows) break;
+                    const int64_t p = grow0 + n;
+                    if (MODE == XG_GATEUP) {
+                        float g = __fadd_rn(__fmul_rn(vg[j], scale0), b0);
+                        float u = __fadd_rn(__fmul_rn(vu[j], scale1), b1);
+                        float hv;
+                        if (a.act_plain) {
+                            hv = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+                        } else {
+                            if (g > a.limit) g = a.limit;
+                            if (u > a.limit) u = a.limit;
+                            if (u < -a.limit) u = -a.limit;
+                            hv = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(__fmul_rn(-a.alpha, g)))), __fadd_rn(u, 1.0f));
+                        }
+                        __half hi, lo;
+                        split_f16(hv, hi, lo);
+                        a.out_hi[p * a.M + row] = hi;
+                        a.out_lo[p * a.M + row] = lo;
+                    } else {
+                        const float v = __fadd_rn(__fmul_rn(vg[j], scale0), b0);
+                        float *yp = a.y + p * a.ldy + row;
+                        *yp = (MODE == XG_DENSE && a.accumulate) ? __fadd_rn(*yp, v) : v;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// [rows x K] f16 row-major -> TMA map with a 64 x 128 box, 128-byte swizzle
+static int make_map(CUtensorMap *map, const __half *ptr, int64_t rows, int64_t K) {
+    EncodeTiledFn fn = encode_fn();
+    MG_REQUIRE(fn, MG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    MG_REQUIRE((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (K * 2) % 16 == 0, MG_ERR_ARG,
+               "xgemm: activation buffer misaligned");
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {XG_K, XG_N};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    MG_REQUIRE(r == CUDA_SUCCESS, MG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MG_OK;
+}
+
+template <int MODE, int DT>
+static int launch_xg(const XgLaunch &l, cudaStream_t st) {
+    using C = XgCfg<MODE>;
+    CUtensorMap mh, ml;
+    int rc = make_map(&mh, l.x_hi, l.x_rows, l.args.K);
+    if (rc) return rc;
+    rc = make_map(&ml, l.x_lo, l.x_rows, l.args.K);
+    if (rc) return rc;
+    const size_t smem = (size_t)C::STAGES * C::STAGE + 1024;
+    auto kfn = k_xgemm<MODE, DT>;
+    rc = ensure_smem(kfn, smem);
+    if (rc) return rc;
+    dim3 grid((unsigned)ceil_div(l.args.M, XG_M), (unsigned)l.max_tiles);
+    kfn<<<grid, XG_THREADS, smem, st>>>(mh, ml, l.args);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
+int xgemm(int mode, int dt, const XgLaunch &l, cudaStream_t st) {
+    MG_REQUIRE(l.args.K % XG_K == 0, MG_ERR_ARG, "xgemm: K %lld not a multiple of 64", (long long)l.args.K);
+    MG_REQUIRE(dt == MG_MXFP4 || dt == MG_Q8R, MG_ERR_ARG, "xgemm: dtype %d unsupported", dt);
+    if (l.max_tiles <= 0) return MG_OK;
+    if (mode == XG_GATEUP) return dt == MG_Q8R ? launch_xg<XG_GATEUP, MG_Q8R>(l, st) : launch_xg<XG_GATEUP, MG_MXFP4>(l, st);
+    if (mode == XG_DOWN) return dt == MG_Q8R ? launch_xg<XG_DOWN, MG_Q8R>(l, st) : launch_xg<XG_DOWN, MG_MXFP4>(l, st);
+    return dt == MG_Q8R ? launch_xg<XG_DENSE, MG_Q8R>(l, st) : launch_xg<XG_DENSE, MG_MXFP4>(l, st);
+}
+
+}  // namespace mg

@@ -1,5 +1,6 @@
 // mg_kernels.h -- host-side launchers shared by the C ABI and the model.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,7 +20,14 @@ int rmsnorm(const float *x, const float *w, float *out, int64_t n, int n_rows, f
 int to_f16_ftz(const float *x, uint16_t *out, int64_t n, cudaStream_t st);
 
 // streamed (bulk-copy ring) GEMV over up to 3 row-concatenated matrices
+// TMA tensor maps of weight matrices (row bytes x rows [x experts x layers])
+int map_weights_2d(CUtensorMap *map, const void *base, int64_t rowbytes, int64_t rows, int box_rows);
+int map_weights_4d(CUtensorMap *map, const void *base, int64_t rowbytes, int64_t rows, int64_t n_experts,
+                   int64_t n_layers, int64_t expert_stride, int64_t layer_stride, int box_rows);
+void *encode_tiled_fn();
+
 struct StreamMat {
+    const CUtensorMap *map;  // 2-D map of w (box 128 B x 128 rows); built here when null
     const void *w, *scales;
     const float *bias;
     int64_t rows;
@@ -37,10 +45,48 @@ struct StreamGemvArgs {
     int accumulate;       // ksplit == 1 only
     int ksplit;           // K splits (partials written to y + ks*part_stride)
     int64_t part_stride;
+    unsigned long long *amax;  // optional (ksplit == 1): per-token packed first-maximum of the outputs
 };
 int stream_gemv(const StreamGemvArgs &a, cudaStream_t st);
+
+struct MoeStreamArgs {
+    mg_expert_layout L;
+    const CUtensorMap *maps;  // gate (box 64 rows), up (64), down (128): 4-D over all experts and layers
+    int layer;
+    const uint8_t *experts_layer;
+    int n_experts, n_tok, top_k;
+    const int32_t *sel;
+    const float *xb;      // [n_tok x hidden]
+    int act_plain;
+    float alpha, limit;
+    float *h;             // [n_tok*top_k x ffn]
+    float *y;             // [down_ksplit x n_tok*top_k x hidden]
+    int down_ksplit;      // requested
+    int down_ksplit_out;  // what moe_down_ksplit() returned for it
+};
+int moe_stream(const MoeStreamArgs &a, cudaStream_t st);
+int moe_down_ksplit(const mg_expert_layout &L, int want);
+
+struct CombineNormArgs {
+    const float *x_in;     // residual before the MoE (null: x itself)
+    float *x;              // [n_tok x hidden] residual out (x_in + MoE when y != null)
+    const float *y;        // MoE partials [ksplit x n_tok*top_k x hidden] or null
+    int ksplit;
+    const int32_t *sel;
+    const float *w;
+    int n_tok, top_k, n_experts;
+    int64_t hidden;
+    const float *nw;       // norm weight
+    float eps;
+    float *xb;             // normed output (may be null)
+};
+int combine_norm(const CombineNormArgs &a, cudaStream_t st);
+int sum_parts(const float *part, int ks, int64_t plane, int n_tok, int64_t rows, int64_t ldp, float *out, int64_t ldo,
+              int accumulate, cudaStream_t st);
 int stream_error_check();
 int stream_prepare();
+int *stream_error_word();
+int stream_ksplit(int dt, int64_t cols, int want);  // effective K split for a row of `cols`
 
 // router: norm (optional) + AVX2-order f32 logits + top-k + weights + usage
 struct RouterArgs {
@@ -56,8 +102,13 @@ struct RouterArgs {
     int32_t *sel;          // [n_tok x top_k]
     float *weights;        // [n_tok x top_k]
     uint32_t *usage;       // [E] counters of this layer, or null
+    const float *x_parts;  // if set: the residual is x + sum_ks x_parts[ks]; written to x_out
+    float *x_out;
+    int x_parts_ks;
+    int64_t x_parts_stride;
 };
 int router(const RouterArgs &a, cudaStream_t st);
+int router_split(const RouterArgs &a, float *logits_scratch, cudaStream_t st);  // decode: logits across blocks
 
 // decode MoE FFN (gate/up + activation, then down + rank-order combine)
 struct MoeArgs {

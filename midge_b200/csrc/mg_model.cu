@@ -227,6 +227,8 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     m->pos.assign(max_seqs, 0);
     const char *ng = getenv("MIDGE_NO_GRAPH");
     m->use_graphs = !(ng && *ng && *ng != '0');
+    const char *ns = getenv("MIDGE_DECODE_KERNELS");
+    m->use_stream = !(ns && !strcmp(ns, "tile"));
     *out = m;
     return MG_OK;
 }
@@ -509,6 +511,50 @@ extern "C" int mg_model_ready(mg_model *m) {
     TRY(dalloc(m, &m->tmp_v, (size_t)R * kv_dim * 2));
     TRY(dalloc(m, &m->usage, (size_t)s.n_layers * s.n_experts * 4));
     MG_CUDA(cudaMemset(m->usage, 0, (size_t)s.n_layers * s.n_experts * 4));
+    // streamed decode buffers (K splits sized for ~3 units per SM)
+    const int qkv_dim = q_dim + 2 * kv_dim;
+    m->ks_qkv = stream_ksplit(MG_Q8R, H, 12);
+    m->ks_o = stream_ksplit(MG_Q8R, q_dim, 16);
+    m->ks_down = moe_down_ksplit(m->el, 2);
+    MG_CUDA(cudaHostAlloc(&m->h_err, sizeof(int), cudaHostAllocDefault));
+    *m->h_err = 0;
+    TRY(dalloc(m, &m->qkv, (size_t)DEC_MAX * qkv_dim * 4));
+    TRY(dalloc(m, &m->qkv_part, (size_t)m->ks_qkv * DEC_MAX * qkv_dim * 4));
+    TRY(dalloc(m, &m->o_part, (size_t)m->ks_o * DEC_MAX * H * 4));
+    TRY(dalloc(m, &m->moe_y, (size_t)m->ks_down * DEC_MAX * s.top_k * H * 4));
+    TRY(dalloc(m, &m->rlogits, (size_t)DEC_MAX * s.n_experts * 4));
+    TRY(dalloc(m, &m->xa, (size_t)DEC_MAX * H * 4));
+    TRY(dalloc(m, &m->amax_keys, (size_t)DEC_MAX * 8));
+    MG_CUDA(cudaHostAlloc(&m->h_keys, DEC_MAX * 8, cudaHostAllocDefault));
+    TRY(stream_prepare());
+    // TMA maps for the streamed decode (q8r trunk, any 4-bit/int8 experts)
+    m->maps_ok = false;
+    {
+        bool q8 = m->lm_head.dt == MG_Q8R;
+        for (int l = 0; l < s.n_layers; l++)
+            q8 = q8 && m->wq[l].dt == MG_Q8R && m->wk[l].dt == MG_Q8R && m->wv[l].dt == MG_Q8R && m->wo[l].dt == MG_Q8R;
+        const bool ex = m->el.dt == MG_MXFP4 || m->el.dt == MG_Q4G32 || m->el.dt == MG_Q8R;
+        if (q8 && ex) {
+            m->map_q.resize(s.n_layers); m->map_k.resize(s.n_layers); m->map_v.resize(s.n_layers); m->map_o.resize(s.n_layers);
+            for (int l = 0; l < s.n_layers; l++) {
+                TRY(map_weights_2d(&m->map_q[l], m->wq[l].data, m->wq[l].cols, m->wq[l].rows, 128));
+                TRY(map_weights_2d(&m->map_k[l], m->wk[l].data, m->wk[l].cols, m->wk[l].rows, 128));
+                TRY(map_weights_2d(&m->map_v[l], m->wv[l].data, m->wv[l].cols, m->wv[l].rows, 128));
+                TRY(map_weights_2d(&m->map_o[l], m->wo[l].data, m->wo[l].cols, m->wo[l].rows, 128));
+            }
+            TRY(map_weights_2d(&m->map_lm, m->lm_head.data, m->lm_head.cols, m->lm_head.rows, 128));
+            const mg_expert_layout &L = m->el;
+            const int64_t rb_in = L.dt == MG_Q8R ? L.hidden : L.hidden / 2;
+            const int64_t rb_dn = L.dt == MG_Q8R ? L.ffn : L.ffn / 2;
+            TRY(map_weights_4d(&m->map_ex[0], m->experts + L.off[0][0], rb_in, L.ffn, s.n_experts, s.n_layers,
+                               L.expert_stride, L.layer_stride, 64));
+            TRY(map_weights_4d(&m->map_ex[1], m->experts + L.off[1][0], rb_in, L.ffn, s.n_experts, s.n_layers,
+                               L.expert_stride, L.layer_stride, 64));
+            TRY(map_weights_4d(&m->map_ex[2], m->experts + L.off[2][0], rb_dn, L.hidden, s.n_experts, s.n_layers,
+                               L.expert_stride, L.layer_stride, 128));
+            m->maps_ok = true;
+        }
+    }
     m->attn_max_splits = (m->ctx + m->attn_split - 1) / m->attn_split;
     TRY(dalloc(m, &m->attn_part, (size_t)DEC_MAX * s.n_heads * m->attn_max_splits * (s.head_dim + 2) * 4));
     MG_CUDA(cudaHostAlloc(&m->h_toks, R * 4, cudaHostAllocDefault));
@@ -611,9 +657,122 @@ static int logits_rows(mg_model *m, const float *x, int n) {
     return MG_OK;
 }
 
+// Is the streamed decode path available for this model and batch?
+static bool stream_ok(const mg_model *m, int n) {
+    const mg_spec &s = m->spec;
+    auto q8r_ok = [](const DevMat &d) { return d.dt == MG_Q8R && d.cols % 64 == 0; };
+    bool trunk = true;
+    for (int l = 0; l < s.n_layers; l++)
+        trunk = trunk && q8r_ok(m->wq[l]) && q8r_ok(m->wk[l]) && q8r_ok(m->wv[l]) && q8r_ok(m->wo[l]);
+    const bool ex = (m->el.dt == MG_MXFP4 || m->el.dt == MG_Q4G32 || (m->el.dt == MG_Q8R && s.hidden % 64 == 0 && s.ffn % 64 == 0)) &&
+                    s.hidden % 32 == 0 && s.ffn % 32 == 0;
+    return m->maps_ok && trunk && ex && q8r_ok(m->lm_head) && n <= 8 && n * s.top_k <= 128 && m->el.dt != MG_F32;
+}
+
+// One layer of the streamed decode: combine(previous MoE)+norm, QKV (K-split
+// partials), RoPE/QK-norm/KV store, attention, O (partials folded into the
+// residual by the router), router, streamed MoE.
+static int layer_stream(mg_model *m, int layer, int n) {
+    const mg_spec &s = m->spec;
+    const int64_t H = s.hidden;
+    const int hd = s.head_dim, q_dim = s.n_heads * hd, kv_dim = s.n_kv_heads * hd, qkv_dim = q_dim + 2 * kv_dim;
+    cudaStream_t st = m->st;
+    CombineNormArgs cn{};
+    cn.x_in = layer > 0 ? m->xa : nullptr;
+    cn.x = m->x; cn.y = layer > 0 ? m->moe_y : nullptr; cn.ksplit = m->ks_down;
+    cn.sel = m->sel; cn.w = m->wts; cn.n_tok = n; cn.top_k = s.top_k; cn.n_experts = s.n_experts;
+    cn.hidden = H; cn.nw = m->attn_norm[layer]; cn.eps = s.norm_eps; cn.xb = m->xb;
+    TRY(combine_norm(cn, st));
+    StreamGemvArgs g{};
+    g.dt = MG_Q8R; g.scale_fmt = MG_SCALE_F16; g.nmat = 3; g.cols = H; g.x = m->xb; g.ldx = H; g.n_tok = n;
+    g.ksplit = m->ks_qkv; g.part_stride = (int64_t)n * qkv_dim;  // effective split, computed at ready()
+    const DevMat *mats[3] = {&m->wq[layer], &m->wk[layer], &m->wv[layer]};
+    const float *bias[3] = {m->bq[layer], m->bk[layer], m->bv[layer]};
+    const int64_t off[3] = {0, q_dim, q_dim + kv_dim};
+    const CUtensorMap *maps[3] = {&m->map_q[layer], &m->map_k[layer], &m->map_v[layer]};
+    for (int i = 0; i < 3; i++) {
+        g.mat[i].map = maps[i];
+        g.mat[i].w = mats[i]->data; g.mat[i].scales = mats[i]->scales; g.mat[i].bias = bias[i];
+        g.mat[i].rows = mats[i]->rows; g.mat[i].y = m->qkv_part + off[i]; g.mat[i].ldy = qkv_dim;
+    }
+    TRY(stream_gemv(g, st));
+    TRY(sum_parts(m->qkv_part, m->ks_qkv, (int64_t)n * qkv_dim, n, qkv_dim, qkv_dim, m->qkv, qkv_dim, 0, st));
+    const int cap = m->cap[layer];
+    QkvPostArgs qa{};
+    qa.q = m->qkv; qa.k = m->qkv + q_dim; qa.v = m->qkv + q_dim + kv_dim; qa.ldq = qkv_dim; qa.ldk = qkv_dim;
+    qa.n_heads = s.n_heads; qa.n_kv_heads = s.n_kv_heads; qa.head_dim = hd;
+    qa.qn = s.qk_norm ? m->qn[layer] : nullptr; qa.kn = s.qk_norm ? m->kn[layer] : nullptr;
+    qa.eps = s.norm_eps; qa.rope_cos = m->rope_cos; qa.rope_sin = m->rope_sin;
+    qa.tok_pos = m->tok_pos; qa.tok_seq = m->tok_seq; qa.write_cache = 1;
+    qa.kc = m->kc[layer]; qa.vc = m->vc[layer]; qa.cap = cap;
+    TRY(qkv_post(qa, n, st));
+    AttnDecodeArgs da{};
+    da.q = m->qkv; da.ldq = qkv_dim; da.seq_ids = m->tok_seq; da.pos = m->tok_pos;
+    da.kc = m->kc[layer]; da.vc = m->vc[layer]; da.cap = cap;
+    da.n_heads = s.n_heads; da.n_kv_heads = s.n_kv_heads; da.head_dim = hd;
+    da.scale = s.attn_scale; da.sinks = s.sinks ? m->sinks[layer] : nullptr;
+    da.split_len = m->attn_split; da.max_splits = (cap + m->attn_split - 1) / m->attn_split;
+    da.partial = m->attn_part; da.out = m->ao; da.ldo = q_dim;
+    TRY(attn_decode(da, n, st));
+    StreamGemvArgs go{};
+    go.dt = MG_Q8R; go.scale_fmt = MG_SCALE_F16; go.nmat = 1; go.cols = q_dim; go.x = m->ao; go.ldx = q_dim;
+    go.n_tok = n; go.ksplit = m->ks_o; go.part_stride = (int64_t)n * H;
+    go.mat[0].map = &m->map_o[layer];
+    go.mat[0].w = m->wo[layer].data; go.mat[0].scales = m->wo[layer].scales; go.mat[0].bias = m->bo[layer];
+    go.mat[0].rows = H; go.mat[0].y = m->o_part; go.mat[0].ldy = H;
+    TRY(stream_gemv(go, st));
+    RouterArgs ra{};
+    ra.x = m->x; ra.norm_w = m->mlp_norm[layer]; ra.eps = s.norm_eps; ra.xb_out = m->xb;
+    ra.rw = (const float *)m->router_w[layer].data; ra.rb = m->router_b[layer];
+    ra.n_experts = s.n_experts; ra.top_k = s.top_k; ra.router_norm = s.router_norm; ra.variant = 0;
+    ra.hidden = H; ra.n_tok = n; ra.logits = nullptr; ra.sel = m->sel; ra.weights = m->wts;
+    ra.usage = m->usage + (int64_t)layer * s.n_experts;
+    ra.x_parts = m->o_part; ra.x_parts_ks = m->ks_o; ra.x_parts_stride = (int64_t)n * H; ra.x_out = m->xa;
+    TRY(router_split(ra, m->rlogits, st));
+    MoeStreamArgs ma{};
+    ma.L = m->el; ma.experts_layer = m->experts + (int64_t)layer * m->el.layer_stride;
+    ma.maps = m->map_ex; ma.layer = layer;
+    ma.n_experts = s.n_experts; ma.n_tok = n; ma.top_k = s.top_k; ma.sel = m->sel; ma.xb = m->xb;
+    ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit; ma.h = m->h; ma.y = m->moe_y;
+    ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
+    TRY(moe_stream(ma, st));
+    return MG_OK;
+}
+
+static int decode_body_stream(mg_model *m, int n) {
+    const mg_spec &s = m->spec;
+    cudaStream_t st = m->st;
+    MG_CUDA(cudaMemcpyAsync(m->toks, m->h_toks, n * 4, cudaMemcpyHostToDevice, st));
+    MG_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_pos, n * 4, cudaMemcpyHostToDevice, st));
+    MG_CUDA(cudaMemcpyAsync(m->tok_seq, m->h_seq, n * 4, cudaMemcpyHostToDevice, st));
+    TRY(dequant_rows(m->embed.dt, MG_SCALE_F16, m->embed.data, m->embed.scales, m->embed.rows, m->embed.cols, m->toks, n,
+                     m->x, st));
+    for (int l = 0; l < s.n_layers; l++) TRY(layer_stream(m, l, n));
+    CombineNormArgs cn{};
+    cn.x_in = m->xa;
+    cn.x = m->x; cn.y = m->moe_y; cn.ksplit = m->ks_down; cn.sel = m->sel; cn.w = m->wts; cn.n_tok = n;
+    cn.top_k = s.top_k; cn.n_experts = s.n_experts; cn.hidden = s.hidden; cn.nw = m->final_norm;
+    cn.eps = s.norm_eps; cn.xb = m->xb;
+    TRY(combine_norm(cn, st));
+    StreamGemvArgs g{};
+    g.dt = MG_Q8R; g.scale_fmt = MG_SCALE_F16; g.nmat = 1; g.cols = s.hidden; g.x = m->xb; g.ldx = s.hidden;
+    g.n_tok = n; g.ksplit = 1; g.accumulate = 0;
+    g.mat[0].map = &m->map_lm;
+    g.mat[0].w = m->lm_head.data; g.mat[0].scales = m->lm_head.scales; g.mat[0].bias = nullptr;
+    g.mat[0].rows = m->lm_head.rows; g.mat[0].y = m->logits; g.mat[0].ldy = s.vocab;
+    g.amax = m->amax_keys;
+    MG_CUDA(cudaMemsetAsync(m->amax_keys, 0, (size_t)n * 8, st));
+    TRY(stream_gemv(g, st));
+    MG_CUDA(cudaMemcpyAsync(m->h_keys, m->amax_keys, (size_t)n * 8, cudaMemcpyDeviceToHost, st));
+    MG_CUDA(cudaMemcpyAsync(m->h_err, stream_error_word(), sizeof(int), cudaMemcpyDeviceToHost, st));
+    return MG_OK;
+}
+
 // decode body for n sequences whose tokens/positions are already in the
 // pinned staging arrays; everything stream-ordered (graph-capturable)
 static int decode_body(mg_model *m, int n) {
+    m->last_streamed = m->use_stream && stream_ok(m, n);
+    if (m->last_streamed) return decode_body_stream(m, n);
     const mg_spec &s = m->spec;
     cudaStream_t st = m->st;
     MG_CUDA(cudaMemcpyAsync(m->toks, m->h_toks, n * 4, cudaMemcpyHostToDevice, st));
@@ -679,6 +838,12 @@ extern "C" int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, c
     if (logits)
         MG_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)n_seqs * s.vocab * 4, cudaMemcpyDeviceToHost, m->st));
     MG_CUDA(cudaStreamSynchronize(m->st));
+    if (*m->h_err) {  // a bounded wait in a streamed kernel gave up
+        *m->h_err = 0;
+        return stream_error_check();
+    }
+    if (m->last_streamed)  // argmax came back packed as (ordered value << 32 | ~index)
+        for (int i = 0; i < n_seqs; i++) m->h_amax[i] = (int32_t)(0xffffffffu - (uint32_t)(m->h_keys[i] & 0xffffffffull));
     for (int i = 0; i < n_seqs; i++) m->pos[m->h_seq[i]]++;
     m->expert_loads += (uint64_t)n_seqs * s.top_k * s.n_layers;
     if (argmax) memcpy(argmax, m->h_amax, n_seqs * 4);
@@ -784,7 +949,8 @@ extern "C" int mg_model_free(mg_model *m) {
     for (auto &kv : m->dec_graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     for (void *p : m->allocs) cudaFree(p);
-    for (void *p : {(void *)m->h_toks, (void *)m->h_pos, (void *)m->h_seq, (void *)m->h_amax})
+    for (void *p : {(void *)m->h_toks, (void *)m->h_pos, (void *)m->h_seq, (void *)m->h_amax, (void *)m->h_err,
+                    (void *)m->h_keys})
         if (p) cudaFreeHost(p);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;

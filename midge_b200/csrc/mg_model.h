@@ -1,5 +1,6 @@
 // mg_model.h -- device-resident model state behind the mg_model handle.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <string>
@@ -54,13 +55,26 @@ struct mg_model {
     int32_t *sel = nullptr, *tok_pos = nullptr, *tok_seq = nullptr, *toks = nullptr, *amax = nullptr;
     uint16_t *tmp_k = nullptr, *tmp_v = nullptr;
     uint32_t *usage = nullptr;
+    // streamed decode: K-split partial planes and MoE down partials
+    float *xa = nullptr;  // post-attention residual of the streamed decode
+    float *qkv = nullptr, *qkv_part = nullptr, *o_part = nullptr, *moe_y = nullptr, *rlogits = nullptr;
+    unsigned long long *amax_keys = nullptr, *h_keys = nullptr;
+    int ks_qkv = 1, ks_o = 1, ks_down = 1;
+    // TMA maps of the streamed decode: per layer q, k, v, o; lm_head; experts
+    std::vector<CUtensorMap> map_q, map_k, map_v, map_o;
+    CUtensorMap map_lm;
+    CUtensorMap map_ex[3];
+    bool maps_ok = false;
     int attn_split = 256, attn_max_splits = 1;
 
     // pinned host staging for per-step inputs/outputs
     int32_t *h_toks = nullptr, *h_pos = nullptr, *h_seq = nullptr, *h_amax = nullptr;
+    int *h_err = nullptr;  // error word of the streamed kernels, copied back each step
 
     std::unordered_map<int, mg::Graph> dec_graphs;  // keyed by n_seqs
     uint64_t expert_loads = 0;
     bool ready = false;
     bool use_graphs = true;
+    bool use_stream = true;
+    bool last_streamed = false;  // the last decode step took the streamed path  // streamed decode kernels (MIDGE_DECODE_KERNELS=tile selects the tile kernels)
 };

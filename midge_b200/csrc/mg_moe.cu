@@ -26,6 +26,15 @@ __global__ void __launch_bounds__(ROUTER_THREADS) k_router(RouterArgs a) {
     __shared__ float s_val[MAX_TOPK];
     const int tok = blockIdx.x;
     const float *xr = a.x + (int64_t)tok * H;
+    if (a.x_parts) {  // attention output partials join the residual first
+        float *xw = const_cast<float *>(xr);
+        for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
+            float v = 0.f;
+            for (int k = 0; k < a.x_parts_ks; k++) v += a.x_parts[(int64_t)k * a.x_parts_stride + (int64_t)tok * H + i];
+            xw[i] = __fadd_rn(xw[i], v);
+        }
+        __syncthreads();
+    }
 
     if (a.norm_w) {
         float ss = 0.f;
@@ -122,6 +131,162 @@ __global__ void __launch_bounds__(ROUTER_THREADS) k_router(RouterArgs a) {
             }
         }
     }
+}
+
+// Two-stage router for the decode path.  Stage 1: block (expert group of 8,
+// token) stages its 8 weight rows in shared memory with one bulk copy each,
+// norms the token (adding attention-output partials first when given; the
+// group-0 block writes the updated residual and the normed row back), and
+// computes the 8 logits in the AVX2 lane order.  Stage 2: top-k + weights.
+constexpr int RG = 8;  // experts per logits block
+
+__global__ void __launch_bounds__(256) k_router_logits(RouterArgs a, float *logits) {
+    extern __shared__ __align__(16) float rs_[];
+    __shared__ float scratch[32];
+    __shared__ __align__(8) uint64_t bar;
+    const int64_t H = a.hidden;
+    float *ws = rs_;            // [RG][H]
+    float *xs = rs_ + RG * H;   // [H]
+    const int tok = blockIdx.y, e0 = blockIdx.x * RG;
+    const int ne = min(RG, a.n_experts - e0);
+    const uint32_t rowb = (uint32_t)(H * 4);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, rowb * (uint32_t)ne);
+        for (int j = 0; j < ne; j++) bulk_g2s(ws + j * H, a.rw + (int64_t)(e0 + j) * H, rowb, &bar);
+    }
+    const float *xr = a.x + (int64_t)tok * H;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
+        float v = xr[i];
+        if (a.x_parts) {
+            float p = 0.f;
+            for (int k = 0; k < a.x_parts_ks; k++) p += a.x_parts[(int64_t)k * a.x_parts_stride + (int64_t)tok * H + i];
+            v = __fadd_rn(v, p);
+        }
+        xs[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, scratch);
+    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+    for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
+        const float v = xs[i];
+        const float nv = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
+        xs[i] = nv;
+        if (blockIdx.x == 0) {  // the other blocks of this token still read x: write elsewhere
+            if (a.x_parts) a.x_out[(int64_t)tok * H + i] = v;
+            a.xb_out[(int64_t)tok * H + i] = nv;
+        }
+    }
+    __syncthreads();
+    bool ok = true;
+    if (threadIdx.x == 0) ok = mbar_wait(&bar, 0);
+    if (!__syncthreads_and(ok)) return;  // weights never arrived: logits stay unwritten
+    if (threadIdx.x < RG * 8) {
+        const int j = threadIdx.x >> 3, lane8 = threadIdx.x & 7;
+        const int64_t H8 = H & ~(int64_t)7;
+        float acc = 0.f;
+        if (j < ne) {
+            const float *wr = ws + j * H + lane8, *xr8 = xs + lane8;
+#pragma unroll 8
+            for (int64_t c = 0; c < H8; c += 8) acc = fmaf(wr[c], xr8[c], acc);
+        }
+        float s1 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+        float s2 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
+        float s3 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 1));
+        if (j < ne && lane8 == 0) {
+            float r = s3;
+            for (int64_t c = H8; c < H; c++) r = __fadd_rn(r, __fmul_rn(ws[j * H + c], xs[c]));
+            logits[(int64_t)tok * a.n_experts + e0 + j] = __fadd_rn(r, a.rb[e0 + j]);
+        }
+    }
+}
+
+// top-k by (value desc, index asc) among logits > -1e30, routing weights, usage
+__global__ void k_router_topk(RouterArgs a, const float *logits) {
+    __shared__ int taken[2048 / 32];
+    __shared__ int s_sel[MAX_TOPK];
+    __shared__ float s_val[MAX_TOPK];
+    const int tok = blockIdx.x, lane = threadIdx.x;
+    const float *rl = logits + (int64_t)tok * a.n_experts;
+    for (int i = lane; i < (a.n_experts + 31) / 32; i += 32) taken[i] = 0;
+    __syncwarp();
+    for (int j = 0; j < a.top_k; j++) {
+        float bv = -1e30f;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < a.n_experts; e += 32) {
+            if (taken[e >> 5] & (1 << (e & 31))) continue;
+            const float v = rl[e];
+            if (v > bv) { bv = v; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
+            if (bi != 0x7fffffff && bv > -1e30f) {
+                s_sel[j] = bi;
+                s_val[j] = bv;
+                taken[bi >> 5] |= 1 << (bi & 31);
+            } else {
+                s_sel[j] = a.variant == 0 ? -1 : 0;
+                s_val[j] = -1e30f;
+            }
+        }
+        __syncwarp();
+    }
+    float fmx = 0.f, fden = 0.f;
+    if (!a.router_norm) {
+        float mx = -INFINITY;
+        for (int e = lane; e < a.n_experts; e += 32) mx = fmaxf(mx, rl[e]);
+        fmx = warp_max(mx);
+        float d = 0.f;
+        for (int e = lane; e < a.n_experts; e += 32) d += expf(rl[e] - fmx);
+        fden = warp_sum(d);
+    }
+    if (lane == 0) {
+        float w[MAX_TOPK];
+        const int k = a.top_k;
+        if (a.router_norm) {
+            const float mx = s_val[0];
+            float den = 0.f;
+            for (int i = 0; i < k; i++) { w[i] = expf(s_val[i] - mx); den = __fadd_rn(den, w[i]); }
+            for (int i = 0; i < k; i++) w[i] = __fdiv_rn(w[i], den);
+        } else {
+            for (int i = 0; i < k; i++) w[i] = __fdiv_rn(expf(s_val[i] - fmx), fden);
+        }
+        for (int i = 0; i < k; i++) {
+            a.sel[(int64_t)tok * k + i] = s_sel[i];
+            a.weights[(int64_t)tok * k + i] = w[i];
+            if (a.usage && s_sel[i] >= 0 && s_val[i] > -1e30f) atomicAdd(&a.usage[s_sel[i]], 1u);
+        }
+    }
+}
+
+int router_split(const RouterArgs &a, float *logits_scratch, cudaStream_t st) {
+    MG_REQUIRE(a.x && a.norm_w && a.xb_out && a.rw && a.rb && a.sel && a.weights && logits_scratch &&
+                   (!a.x_parts || (a.x_out && a.x_out != a.x)),
+               MG_ERR_ARG, "router: bad arguments");
+    MG_REQUIRE(a.top_k >= 1 && a.top_k <= MAX_TOPK && a.top_k <= a.n_experts && a.n_experts <= 2048, MG_ERR_ARG,
+               "router: top_k %d / n_experts %d unsupported", a.top_k, a.n_experts);
+    MG_REQUIRE((a.hidden * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.rw) & 15) == 0, MG_ERR_ARG,
+               "router: weight rows must be 16-byte aligned");
+    if (a.n_tok == 0) return MG_OK;
+    const size_t smem = (size_t)(RG + 1) * a.hidden * 4;
+    int rc = ensure_smem(k_router_logits, smem);
+    if (rc) return rc;
+    dim3 g1((a.n_experts + RG - 1) / RG, a.n_tok);
+    k_router_logits<<<g1, 256, smem, st>>>(a, logits_scratch);
+    MG_CHECK_LAUNCH();
+    k_router_topk<<<a.n_tok, 32, 0, st>>>(a, logits_scratch);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
 }
 
 int router(const RouterArgs &a, cudaStream_t st) {

@@ -1,0 +1,52 @@
+// mg_prefill.h -- launchers of the tensor-core prefill path.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "mg_gemm.h"
+#include "midgecuda.h"
+
+namespace mg {
+
+struct MoePrefill {
+    mg_expert_layout L;
+    const uint8_t *experts_layer;
+    const int *rebase;  // this layer's [E x 3] rebase exponents
+    int n, top_k, n_experts;
+    const int32_t *sel;
+    const float *w;
+    const float *xb;    // [n x hidden] normed inputs
+    float *x;           // [n x hidden] residual, accumulated into
+    int act_plain;
+    float alpha, limit;
+    // scratch
+    int *counts, *offs, *cursor, *ntiles, *pos_of_slot, *slot_of_pos;
+    XgTile *tiles;
+    __half *x_hi, *x_lo;  // [n*top_k x hidden]
+    __half *h_hi, *h_lo;  // [n*top_k x ffn]
+    float *y;             // [n*top_k x hidden]
+    int *err;
+};
+int moe_prefill(const MoePrefill &a, cudaStream_t st);
+
+struct DenseGemm {
+    const void *w, *scales;  // q8r matrix [rows x cols], f32 row scales
+    const float *bias;
+    int64_t rows, cols;
+    const __half *x_hi, *x_lo;  // [n x cols]
+    int n;
+    float *y;
+    int64_t ldy;
+    int accumulate;
+    const XgTile *tiles;  // ceil(n/128) tiles {0, 128 i, min(128, n - 128 i)}
+    const int *ntiles;
+    const int *zero_offs;  // one int = 0
+    int *err;
+};
+int dense_gemm(const DenseGemm &d, cudaStream_t st);
+
+int split_rows(const float *x, int64_t ldx, int n, int64_t K, __half *hi, __half *lo, cudaStream_t st);
+int pf_rebase(const uint8_t *experts, const mg_expert_layout &L, int n_layers, int n_experts, int *rebase, int *inexact,
+              cudaStream_t st);
+
+}  // namespace mg

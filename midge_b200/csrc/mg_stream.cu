@@ -1,4 +1,6 @@
 // mg_stream.cu -- launchers of the streamed (bulk-copy ring) decode GEMV.
+#include <cstring>
+
 #include "mg_kernels.h"
 #include "mg_stream.cuh"
 
@@ -31,14 +33,49 @@ int stream_error_check() {
 
 int stream_prepare() { return sw_err_ptr() ? MG_OK : MG_ERR_OOM; }
 
+int *stream_error_word() { return sw_err_ptr(); }
+
+int stream_ksplit(int dt, int64_t cols, int want) {
+    const int64_t segb = SW_SEGB;
+    const int64_t rowbytes = dt == MG_Q8R ? cols : cols / 2;
+    const int64_t nseg = (rowbytes + segb - 1) / segb;
+    int ks = want > 0 ? want : 1;
+    if (ks > nseg) ks = (int)nseg;
+    const int64_t sps = (nseg + ks - 1) / ks;
+    return (int)((nseg + sps - 1) / sps);
+}
+
+template <int DT, class P>
+static int launch_policy(void (*kfn)(SwMaps, P, int, int *), const SwMaps &maps, P &pol, size_t xs_bytes, int grid,
+                         cudaStream_t st) {
+    const size_t budget = 227 * 1024 - 2048 - 1024;  // static shared memory and the alignment slack
+    int nstages = (int)((budget - 1024 - xs_bytes) / SW_STAGE_BYTES);
+    if (nstages > SW_MAX_STAGES) nstages = SW_MAX_STAGES;
+    MG_REQUIRE(nstages >= 2, MG_ERR_ARG, "streamed kernel: activations leave no room for a ring");
+    const size_t smem = 1024 + 1024 + (size_t)nstages * SW_STAGE_BYTES + xs_bytes;
+    int rc = ensure_smem_attr(reinterpret_cast<const void *>(kfn), smem);
+    if (rc) return rc;
+    int *err = sw_err_ptr();
+    MG_REQUIRE(err, MG_ERR_OOM, "streamed kernel: no error word");
+    kfn<<<grid, SW_THREADS, smem, st>>>(maps, pol, nstages, err);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
 template <int DT, int SC, int NT>
 static int launch_stream_gemv(const StreamGemvArgs &a, cudaStream_t st) {
-    using G = SwGeom<DT>;
     PolGemv<DT, SC> pol{};
+    SwMaps maps;
+    memset(&maps, 0, sizeof(maps));
     const int64_t rowbytes = DT == MG_Q8R ? a.cols : a.cols / 2;
     int64_t tiles = 0;
     for (int i = 0; i < a.nmat; i++) {
-        pol.m[i].w = (const uint8_t *)a.mat[i].w;
+        if (a.mat[i].map) {
+            maps.m[i] = *a.mat[i].map;
+        } else {
+            int rc = map_weights_2d(&maps.m[i], a.mat[i].w, rowbytes, a.mat[i].rows, SW_ROWS);
+            if (rc) return rc;
+        }
         pol.m[i].sc = (const uint8_t *)a.mat[i].scales;
         pol.m[i].bias = a.mat[i].bias;
         pol.m[i].rows = a.mat[i].rows;
@@ -50,36 +87,21 @@ static int launch_stream_gemv(const StreamGemvArgs &a, cudaStream_t st) {
     pol.nmat = a.nmat;
     pol.cols = (int)a.cols;
     pol.ntiles = tiles;
-    const int nsm = num_sms();
-    int ks = a.ksplit > 0 ? a.ksplit : 1;
-    const int64_t nseg = (rowbytes + G::SEGB - 1) / G::SEGB;
-    if (ks > nseg) ks = (int)nseg;
-    const int64_t segs_per_split = (nseg + ks - 1) / ks;
-    ks = (int)((nseg + segs_per_split - 1) / segs_per_split);
+    const int ks = stream_ksplit(DT, a.cols, a.ksplit);
+    const int64_t nseg = (rowbytes + SW_SEGB - 1) / SW_SEGB;
     pol.ks_count = ks;
-    pol.kbytes_per_split = segs_per_split * G::SEGB;
+    pol.kbytes_per_split = ((nseg + ks - 1) / ks) * SW_SEGB;
     pol.x = a.x;
     pol.ldx = a.ldx;
     pol.n_tok = a.n_tok;
     pol.accumulate = a.accumulate;
     pol.part_stride = a.part_stride;
+    pol.amax = ks == 1 ? a.amax : nullptr;
     const size_t xs_bytes = (size_t)NT * 8 * (a.cols + XS_PAD) * 2;
-    const size_t budget = 227 * 1024 - 1024;
-    int nstages = (int)((budget - 128 - xs_bytes) / G::STAGE_BYTES);
-    if (nstages > SW_MAX_STAGES) nstages = SW_MAX_STAGES;
-    MG_REQUIRE(nstages >= 2, MG_ERR_ARG, "streamed gemv: %lld columns x %d tokens leave no room for a ring",
-               (long long)a.cols, a.n_tok);
-    const size_t smem = 128 + (size_t)nstages * G::STAGE_BYTES + xs_bytes;
-    auto kfn = k_stream<DT, SC, NT, PolGemv<DT, SC>>;
-    int rc = ensure_smem(kfn, smem);
-    if (rc) return rc;
-    int *err = sw_err_ptr();
-    MG_REQUIRE(err, MG_ERR_OOM, "streamed gemv: no error word");
     const int64_t units = tiles * ks;
-    const int grid = (int)(units < nsm ? units : nsm);
-    kfn<<<grid, SW_THREADS, smem, st>>>(pol, nstages, err);
-    MG_CHECK_LAUNCH();
-    return MG_OK;
+    const int nsm = num_sms();
+    return launch_policy<DT>(k_stream<DT, SC, NT, PolGemv<DT, SC>>, maps, pol, xs_bytes,
+                             (int)(units < nsm ? units : nsm), st);
 }
 
 template <int DT, int SC>
@@ -92,7 +114,7 @@ int stream_gemv(const StreamGemvArgs &a, cudaStream_t st) {
     MG_REQUIRE(a.nmat >= 1 && a.nmat <= 3 && a.x && a.n_tok >= 1 && a.n_tok <= 8 && a.cols > 0, MG_ERR_ARG,
                "streamed gemv: bad arguments");
     for (int i = 0; i < a.nmat; i++)
-        MG_REQUIRE(a.mat[i].w && a.mat[i].y && a.mat[i].rows > 0 && (a.dt == MG_F32 || a.mat[i].scales), MG_ERR_ARG,
+        MG_REQUIRE(a.mat[i].w && a.mat[i].y && a.mat[i].rows > 0 && a.mat[i].scales, MG_ERR_ARG,
                    "streamed gemv: matrix %d incomplete", i);
     MG_REQUIRE(((reinterpret_cast<uintptr_t>(a.x) & 15) == 0) && (a.ldx % 4 == 0), MG_ERR_ARG,
                "streamed gemv: activations must be 16-byte aligned");
@@ -111,6 +133,138 @@ int stream_gemv(const StreamGemvArgs &a, cudaStream_t st) {
     }
     set_error("streamed gemv: dtype %d unsupported", a.dt);
     return MG_ERR_ARG;
+}
+
+// ------------------------------------------------------- routed experts
+template <int DT, int SC, int NT>
+static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
+    const int nsm = num_sms();
+    SwMaps maps;
+    for (int i = 0; i < 3; i++) maps.m[i] = a.maps[i];
+    PolMoeGateUp<DT, SC> pg{};
+    pg.L = a.L;
+    pg.experts_layer = a.experts_layer;
+    pg.layer = a.layer;
+    pg.n_experts = a.n_experts;
+    pg.n_tok = a.n_tok;
+    pg.top_k = a.top_k;
+    pg.sel = a.sel;
+    pg.xb = a.xb;
+    pg.act_plain = a.act_plain;
+    pg.alpha = a.alpha;
+    pg.limit = a.limit;
+    pg.h = a.h;
+    int rc = launch_policy<DT>(k_stream<DT, SC, NT, PolMoeGateUp<DT, SC>>, maps, pg,
+                               (size_t)NT * 8 * (a.L.hidden + XS_PAD) * 2, nsm, st);
+    if (rc) return rc;
+    PolMoeDown<DT, SC> pd{};
+    pd.L = a.L;
+    pd.experts_layer = a.experts_layer;
+    pd.layer = a.layer;
+    pd.n_experts = a.n_experts;
+    pd.n_tok = a.n_tok;
+    pd.top_k = a.top_k;
+    pd.sel = a.sel;
+    pd.h = a.h;
+    pd.y = a.y;
+    const int64_t rowbytes = DT == MG_Q8R ? a.L.ffn : a.L.ffn / 2;
+    const int64_t nseg = (rowbytes + SW_SEGB - 1) / SW_SEGB;
+    const int ks = moe_down_ksplit(a.L, a.down_ksplit);
+    MG_REQUIRE(ks == a.down_ksplit_out, MG_ERR_ARG, "moe stream: down K split %d != caller's %d", ks,
+               a.down_ksplit_out);
+    pd.ks_count = ks;
+    pd.kbytes_per_split = ((nseg + ks - 1) / ks) * SW_SEGB;
+    return launch_policy<DT>(k_stream<DT, SC, NT, PolMoeDown<DT, SC>>, maps, pd,
+                             (size_t)NT * 8 * (a.L.ffn + XS_PAD) * 2, nsm, st);
+}
+
+int moe_down_ksplit(const mg_expert_layout &L, int want) { return stream_ksplit(L.dt, L.ffn, want); }
+
+int moe_stream(const MoeStreamArgs &a, cudaStream_t st) {
+    MG_REQUIRE(a.n_tok >= 1 && a.n_tok <= 8 && a.n_tok * a.top_k <= SW_MAX_SLOTS && a.n_experts <= 2048 && a.maps,
+               MG_ERR_ARG, "moe stream: n_tok %d top_k %d unsupported", a.n_tok, a.top_k);
+    const mg_expert_layout &L = a.L;
+    switch (L.dt) {
+    case MG_MXFP4:
+        if (L.scale_fmt == MG_SCALE_UE8M0)
+            return a.n_tok <= 4 ? moe_stream_t<MG_MXFP4, MG_SCALE_UE8M0, 1>(a, st)
+                                : moe_stream_t<MG_MXFP4, MG_SCALE_UE8M0, 2>(a, st);
+        return a.n_tok <= 4 ? moe_stream_t<MG_MXFP4, MG_SCALE_F16, 1>(a, st)
+                            : moe_stream_t<MG_MXFP4, MG_SCALE_F16, 2>(a, st);
+    case MG_Q4G32:
+        if (L.scale_fmt == MG_SCALE_UE8M0)
+            return a.n_tok <= 4 ? moe_stream_t<MG_Q4G32, MG_SCALE_UE8M0, 1>(a, st)
+                                : moe_stream_t<MG_Q4G32, MG_SCALE_UE8M0, 2>(a, st);
+        return a.n_tok <= 4 ? moe_stream_t<MG_Q4G32, MG_SCALE_F16, 1>(a, st)
+                            : moe_stream_t<MG_Q4G32, MG_SCALE_F16, 2>(a, st);
+    case MG_Q8R:
+        MG_REQUIRE(L.hidden % 64 == 0 && L.ffn % 64 == 0, MG_ERR_ARG, "moe stream: q8r dims %% 64");
+        return a.n_tok <= 4 ? moe_stream_t<MG_Q8R, MG_SCALE_F16, 1>(a, st) : moe_stream_t<MG_Q8R, MG_SCALE_F16, 2>(a, st);
+    }
+    set_error("moe stream: dtype %d unsupported", L.dt);
+    return MG_ERR_ARG;
+}
+
+// ----------------------------------------------- MoE combine + RMSNorm
+// x[t] += sum_i w[t][i] * sum_ks y[ks][t*k+i]   (rank order, engine/midge.c:544-548)
+// then xb[t] = rmsnorm(x[t]) * nw.  One block per token.
+__global__ void k_combine_norm(CombineNormArgs a) {
+    __shared__ float scratch[32];
+    const int t = blockIdx.x;
+    float *x = a.x + (int64_t)t * a.hidden;
+    const float *xi = (a.x_in ? a.x_in : a.x) + (int64_t)t * a.hidden;
+    float ss = 0.f;
+    for (int64_t c = threadIdx.x; c < a.hidden; c += blockDim.x) {
+        float v = xi[c];
+        if (a.y) {
+            float moe = 0.f;
+            for (int i = 0; i < a.top_k; i++) {
+                const int e = a.sel[t * a.top_k + i];
+                if (e < 0 || e >= a.n_experts) continue;
+                float yv = 0.f;
+                for (int ks = 0; ks < a.ksplit; ks++)
+                    yv += a.y[((int64_t)ks * a.n_tok * a.top_k + t * a.top_k + i) * a.hidden + c];
+                moe = __fadd_rn(moe, __fmul_rn(a.w[t * a.top_k + i], yv));
+            }
+            v = __fadd_rn(v, moe);
+            x[c] = v;
+        }
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum(ss, scratch);
+    const float inv = 1.0f / sqrtf(ss / (float)a.hidden + a.eps);
+    if (a.xb)
+        for (int64_t c = threadIdx.x; c < a.hidden; c += blockDim.x)
+            a.xb[(int64_t)t * a.hidden + c] = __fmul_rn(__fmul_rn(x[c], inv), a.nw[c]);
+}
+
+int combine_norm(const CombineNormArgs &a, cudaStream_t st) {
+    if (a.n_tok <= 0) return MG_OK;
+    k_combine_norm<<<a.n_tok, 1024, 0, st>>>(a);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
+// sum K-split partial planes: out[t][r] (=|+=) sum_ks part[ks][t][r]
+__global__ void k_sum_parts(const float *__restrict__ part, int ks, int64_t plane, int n_tok, int64_t rows, int64_t ldp,
+                            float *out, int64_t ldo, int accumulate) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_tok * rows; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / rows, r = i - t * rows;
+        float v = 0.f;
+        for (int k = 0; k < ks; k++) v += part[(int64_t)k * plane + t * ldp + r];
+        float *o = out + t * ldo + r;
+        *o = accumulate ? *o + v : v;
+    }
+}
+
+int sum_parts(const float *part, int ks, int64_t plane, int n_tok, int64_t rows, int64_t ldp, float *out, int64_t ldo,
+              int accumulate, cudaStream_t st) {
+    const int64_t n = (int64_t)n_tok * rows;
+    int grid = ceil_div(n, 256);
+    if (grid > 1184) grid = 1184;
+    k_sum_parts<<<grid, 256, 0, st>>>(part, ks, plane, n_tok, rows, ldp, out, ldo, accumulate);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
 }
 
 }  // namespace mg

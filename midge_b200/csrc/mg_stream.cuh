@@ -17,6 +17,8 @@
 // Every wait is bounded; on timeout a kernel records an error code and stops.
 #pragma once
 #include "mg_common.cuh"
+#include <cuda.h>
+
 #include "mg_gemv.cuh"
 
 namespace mg {
@@ -24,17 +26,25 @@ namespace mg {
 constexpr int SW_CONS = 8;                    // consumer warps
 constexpr int SW_THREADS = (SW_CONS + 1) * 32;
 constexpr int SW_ROWS = SW_CONS * 16;         // MMA rows per stage
-constexpr int SW_MAX_STAGES = 6;
+constexpr int SW_MAX_STAGES = 12;
 constexpr int SW_ERR_TIMEOUT = 1;
+constexpr int SW_SEGB = 128;                  // bytes of each row per stage: one 128-byte swizzle row
+constexpr int SW_STAGE_BYTES = SW_ROWS * SW_SEGB;  // 16 KB: one TMA box of 128 rows x 128 B
 
 template <int DT>
 struct SwGeom {
     static constexpr int CB = DT == MG_Q8R ? 64 : 16;    // bytes of one chunk of one row
     static constexpr int COLS_PER_CHUNK = DT == MG_Q8R ? 64 : 32;
-    static constexpr int SEGB = 256;                      // bytes per row per stage
-    // smem row stride: conflict-free fragment loads (LDS.32 / LDS.128)
-    static constexpr int STRIDE = DT == MG_Q8R ? SEGB + 64 : SEGB + 16;
-    static constexpr int STAGE_BYTES = SW_ROWS * STRIDE;
+};
+
+// byte address of 16-byte piece `p` (0..7) of stage row `r` (128-byte swizzle:
+// piece p of row r lives at piece p ^ (r % 8))
+__device__ __forceinline__ uint32_t sw_addr(int r, int p) { return (uint32_t)(r * 128 + ((p ^ (r & 7)) << 4)); }
+
+// Up to three tensor maps per launch, passed as __grid_constant__ so that TMA
+// reads them from parameter space.
+struct SwMaps {
+    CUtensorMap m[3];
 };
 
 // Shared-memory bookkeeping common to all streamed kernels.
@@ -43,11 +53,6 @@ struct SwShared {
     uint64_t empty[SW_MAX_STAGES];
 };
 
-// -------------------------------------------------------------- producer
-// Policy interface (device):
-//   int64_t units() const
-//   void unit(int64_t u, UnitInfo &ui) const  -> byte range [b0, b1) of each row
-//   const uint8_t *row_ptr(const UnitInfo &, int mma_row) const  (null = no row)
 struct UnitInfo {
     int64_t tile;
     int ks;
@@ -55,61 +60,50 @@ struct UnitInfo {
     int aux;          // policy-defined (e.g. expert index)
 };
 
+// -------------------------------------------------------------- producer
+// Policy interface (device):
+//   int64_t units() const;  void unit(int64_t u, UnitInfo &ui) const;
+//   void issue(const SwMaps &, const UnitInfo &, int64_t b, void *dst, uint64_t *bar) const
+//     -- issues the TMA boxes of row bytes [b, b+128) of the unit's rows into dst
 template <int DT, class P>
-__device__ void sw_producer(const P &pol, int64_t u0, int64_t u1, uint8_t *ring, int nstages, SwShared *sh,
-                            int *err) {
-    using G = SwGeom<DT>;
-    const int lane = threadIdx.x & 31;
+__device__ void sw_producer(const P &pol, const SwMaps &maps, int64_t u0, int64_t u1, uint8_t *ring, int nstages,
+                            SwShared *sh, int *err) {
+    if ((threadIdx.x & 31) != 0) return;
     int64_t it = 0;
     for (int64_t u = u0; u < u1; u++) {
         UnitInfo ui;
         pol.unit(u, ui);
-        const uint8_t *rp[SW_ROWS / 32];
-        int nvalid = 0;
-#pragma unroll
-        for (int j = 0; j < SW_ROWS / 32; j++) {
-            rp[j] = pol.row_ptr(ui, lane + 32 * j);
-            nvalid += __popc(__ballot_sync(0xffffffffu, rp[j] != nullptr));
-        }
-        for (int64_t b = ui.b0; b < ui.b1; b += G::SEGB, it++) {
+        for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
             const int s = (int)(it % nstages);
-            const uint32_t bytes = (uint32_t)min((int64_t)G::SEGB, ui.b1 - b);
-            if (it >= nstages) {  // wait until the consumers released this stage
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&sh->empty[s], (uint32_t)(((it / nstages) - 1) & 1));
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) {
-                    if (lane == 0) atomicExch(err, SW_ERR_TIMEOUT);
-                    return;
-                }
+            if (it >= nstages && !mbar_wait(&sh->empty[s], (uint32_t)(((it / nstages) - 1) & 1))) {
+                atomicExch(err, SW_ERR_TIMEOUT);
+                return;
             }
-            if (lane == 0) mbar_arrive_expect_tx(&sh->full[s], bytes * (uint32_t)nvalid);
-            __syncwarp();
-            uint8_t *st = ring + (size_t)s * G::STAGE_BYTES;
-#pragma unroll
-            for (int j = 0; j < SW_ROWS / 32; j++)
-                if (rp[j]) bulk_g2s(st + (size_t)(lane + 32 * j) * G::STRIDE, rp[j] + b, bytes, &sh->full[s]);
+            mbar_arrive_expect_tx(&sh->full[s], SW_STAGE_BYTES);
+            pol.issue(maps, ui, b, ring + (size_t)s * SW_STAGE_BYTES, &sh->full[s]);
         }
     }
 }
 
 // -------------------------------------------------------------- consumer
-// One warp's share of one segment: 16 MMA rows (stage rows 16w..16w+15),
-// `nch` chunks starting at row byte `b` (column col0 of the activations).
+// One warp's share of one stage: its 16 MMA rows (policy stage_row), the
+// stage's 128 bytes of each, at activation column col0.
 template <int DT, int SC, int NT, class P>
 __device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui, const uint8_t *st, int w, int64_t b,
-                                               int nch, const __half *xs, int xs_stride, int nt_active,
+                                               int nbytes, const __half *xs, int xs_stride, int nt_active,
                                                float acc[NT][4]) {
     using G = SwGeom<DT>;
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const uint8_t *ra = st + (size_t)(16 * w + g) * G::STRIDE;
-    const uint8_t *rb = ra + (size_t)8 * G::STRIDE;
+    const int ra = pol.stage_row(w, g), rb = pol.stage_row(w, g + 8);
     const int64_t col0 = b / G::CB * G::COLS_PER_CHUNK;
+    const int nch = nbytes / G::CB;
     if constexpr (DT == MG_Q8R) {
-#pragma unroll 2
-        for (int c = 0; c < nch; c++) {
-            uint4 wa = *reinterpret_cast<const uint4 *>(ra + c * 64 + 16 * t);
-            uint4 wb = *reinterpret_cast<const uint4 *>(rb + c * 64 + 16 * t);
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            if (c >= nch) break;
+            const int piece = 4 * c + t;
+            uint4 wa = *reinterpret_cast<const uint4 *>(st + sw_addr(ra, piece));
+            uint4 wb = *reinterpret_cast<const uint4 *>(st + sw_addr(rb, piece));
             uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w}, wbv[4] = {wb.x, wb.y, wb.z, wb.w};
             uint32_t fa[4][4];
 #pragma unroll
@@ -129,11 +123,17 @@ __device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui,
             }
         }
     } else {
-        const int64_t gchunk0 = b / G::CB;  // group index of the segment's first chunk
-#pragma unroll 2
-        for (int c = 0; c < nch; c++) {
-            const uint32_t wa = lds32(ra + c * 16 + 4 * t), wb = lds32(rb + c * 16 + 4 * t);
-            const float sa = pol.scale(ui, g, gchunk0 + c), sb = pol.scale(ui, g + 8, gchunk0 + c);
+        const int64_t gchunk0 = b / G::CB;  // group index of the stage's first chunk
+        float sa[8], sb[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            sa[c] = c < nch ? pol.scale(ui, g, gchunk0 + c) : 0.f;
+            sb[c] = c < nch ? pol.scale(ui, g + 8, gchunk0 + c) : 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            if (c >= nch) break;
+            const uint32_t wa = lds32(st + sw_addr(ra, c) + 4 * t), wb = lds32(st + sw_addr(rb, c) + 4 * t);
             uint32_t fa[4], fb[4];
             if (DT == MG_MXFP4) {
                 e2m1x8_to_h2(wa, fa);
@@ -155,24 +155,19 @@ __device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui,
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                 mma_16816(d, a0, bx.x, bx.y);
                 mma_16816(d, a1, bx.z, bx.w);
-                acc[nt][0] = fmaf(sa, d[0], acc[nt][0]);
-                acc[nt][1] = fmaf(sa, d[1], acc[nt][1]);
-                acc[nt][2] = fmaf(sb, d[2], acc[nt][2]);
-                acc[nt][3] = fmaf(sb, d[3], acc[nt][3]);
+                acc[nt][0] = fmaf(sa[c], d[0], acc[nt][0]);
+                acc[nt][1] = fmaf(sa[c], d[1], acc[nt][1]);
+                acc[nt][2] = fmaf(sb[c], d[2], acc[nt][2]);
+                acc[nt][3] = fmaf(sb[c], d[3], acc[nt][3]);
             }
         }
     }
 }
 
-// Consumer warps: per unit, accumulate its segments, then the policy epilogue.
-// Policy:  void stage(int64_t u, ...) is done outside; here:
-//   bool restage(int64_t u)  -> the activations must be re-staged before u
-//   void stage_x(int64_t u, __half *xs, int xs_stride)   (consumer threads, synced by caller)
-//   void epilogue(const UnitInfo&, int warp, const float acc[NT][4])
+// Consumer warps: per unit, accumulate its stages, then the policy epilogue.
 template <int DT, int SC, int NT, class P>
 __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int nstages, SwShared *sh, __half *xs,
                              int xs_stride, int *err) {
-    using G = SwGeom<DT>;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int64_t it = 0;
     for (int64_t u = u0; u < u1; u++) {
@@ -190,9 +185,8 @@ __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int 
 #pragma unroll
             for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
         const bool live = pol.warp_live(ui, w);
-        for (int64_t b = ui.b0; b < ui.b1; b += G::SEGB, it++) {
+        for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
             const int s = (int)(it % nstages);
-            const int64_t bytes = min((int64_t)G::SEGB, ui.b1 - b);
             bool ok = true;
             if (lane == 0) ok = mbar_wait(&sh->full[s], (uint32_t)((it / nstages) & 1));
             ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -201,24 +195,27 @@ __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int 
                 return;
             }
             if (live)
-                sw_consume_seg<DT, SC, NT>(pol, ui, ring + (size_t)s * G::STAGE_BYTES, w, b, (int)(bytes / G::CB), xs,
-                                           xs_stride, nt_active, acc);
+                sw_consume_seg<DT, SC, NT>(pol, ui, ring + (size_t)s * SW_STAGE_BYTES, w, b,
+                                           (int)min((int64_t)SW_SEGB, ui.b1 - b), xs, xs_stride, nt_active, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh->empty[s]);
         }
         if (live) pol.template epilogue<NT>(ui, w, acc);
     }
+    pol.finish();  // all consumer threads
 }
 
 // The kernel shell: barrier setup, block's unit range, role split.
 template <int DT, int SC, int NT, class P>
-__global__ void __launch_bounds__(SW_THREADS, 1) k_stream(P pol, int nstages, int *err) {
-    extern __shared__ __align__(128) uint8_t sw_smem[];
-    using G = SwGeom<DT>;
+__global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant__ SwMaps maps, P pol, int nstages,
+                                                          int *err) {
+    extern __shared__ __align__(1024) uint8_t sw_smem_raw[];
+    uint8_t *sw_smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sw_smem_raw) + 1023) & ~(uintptr_t)1023);
     SwShared *sh = reinterpret_cast<SwShared *>(sw_smem);
-    uint8_t *ring = sw_smem + 128;
-    __half *xs = reinterpret_cast<__half *>(ring + (size_t)nstages * G::STAGE_BYTES);
+    uint8_t *ring = sw_smem + 1024;  // stages 1024-aligned for the 128-byte swizzle
+    __half *xs = reinterpret_cast<__half *>(ring + (size_t)nstages * SW_STAGE_BYTES);
     const int xs_stride = pol.xs_stride();
+    pol.init_shared();  // all threads; ends with __syncthreads
     const int64_t nunits = pol.units();
     const int64_t per = (nunits + gridDim.x - 1) / gridDim.x;
     const int64_t u0 = (int64_t)blockIdx.x * per, u1 = min(nunits, u0 + per);
@@ -233,7 +230,7 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(P pol, int nstages, in
     if (u0 >= u1) return;
     const int w = threadIdx.x >> 5;
     if (w == SW_CONS) {
-        sw_producer<DT>(pol, u0, u1, ring, nstages, sh, err);
+        sw_producer<DT>(pol, maps, u0, u1, ring, nstages, sh, err);
     } else {
         pol.stage_x(u0, xs, xs_stride);
         named_bar_sync(1, SW_CONS * 32);
@@ -241,16 +238,34 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(P pol, int nstages, in
     }
 }
 
+__device__ __forceinline__ void tma_box_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_box_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
+                                           uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ------------------------------------------------------------- policies
 // Plain GEMV over up to 3 row-concatenated matrices sharing cols and the
-// activations; K split KS ways.  Unit = (tile of 128 rows of one matrix, ks).
-// Output: KS == 1 -> y = W x (+bias) (store or accumulate); KS > 1 -> part[ks]
-// holds the partial sums (bias added by ks 0) for a later reduction.
+// activations; K split ks_count ways.  Unit = (tile of 128 rows of one
+// matrix, K split).  maps.m[i] is matrix i as a 2-D byte tensor
+// {row bytes, rows}.  Output: ks_count == 1 -> y = W x (+bias), stored or
+// accumulated; else y + ks*part_stride holds split ks's partial sums (bias in
+// split 0) for a later reduction.
 struct GemvMat {
-    const uint8_t *w, *sc;
+    const uint8_t *sc;
     const float *bias;
     int64_t rows;
-    float *y;      // [n_tok x ldy] (KS == 1) or partials [KS x n_tok x ldy]
+    float *y;
     int64_t ldy;
     int64_t tile0;  // first tile index of this matrix
 };
@@ -261,16 +276,57 @@ struct PolGemv {
     int nmat;
     int cols;
     int ks_count;
-    int64_t kbytes_per_split;  // row bytes per K split (multiple of SEGB)
+    int64_t kbytes_per_split;  // multiple of SW_SEGB
     int64_t ntiles;
     const float *x;
     int64_t ldx;
     int n_tok;
     int accumulate;
-    int64_t part_stride;  // floats between K-split partial planes
+    int64_t part_stride;
+    unsigned long long *amax;  // optional: per-token packed (value, -index) maximum of the outputs
+    float bv[2];               // this lane's best output for tokens t and 4+t
+    int bi[2];
 
     __device__ int64_t rowbytes() const { return DT == MG_Q8R ? cols : cols / 2; }
     __device__ int xs_stride() const { return cols + XS_PAD; }
+    __device__ void init_shared() {
+        bv[0] = bv[1] = -INFINITY;
+        bi[0] = bi[1] = 0x7fffffff;
+        __syncthreads();
+    }
+    // first maximum per token over everything this CTA produced, then one
+    // 64-bit atomic max per token: key = ordered value << 32 | ~index
+    __device__ void finish() {
+        if (!amax) return;
+        __shared__ float sv[SW_CONS][8];
+        __shared__ int si[SW_CONS][8];
+        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, t = lane & 3;
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+            float v = bv[nt];
+            int i = bi[nt];
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+                if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+            }
+            if (lane < 4) { sv[w][nt * 4 + t] = v; si[w][nt * 4 + t] = i; }
+        }
+        named_bar_sync(1, SW_CONS * 32);
+        if (threadIdx.x < n_tok && threadIdx.x < 8) {
+            const int tok = threadIdx.x;
+            float v = -INFINITY;
+            int i = 0x7fffffff;
+            for (int ww = 0; ww < SW_CONS; ww++)
+                if (sv[ww][tok] > v || (sv[ww][tok] == v && si[ww][tok] < i)) { v = sv[ww][tok]; i = si[ww][tok]; }
+            if (i != 0x7fffffff) {
+                uint32_t u = __float_as_uint(v);
+                u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+                atomicMax(&amax[tok], ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i));
+            }
+        }
+    }
     __device__ int64_t units() const { return ntiles * ks_count; }
     __device__ int mat_of(int64_t tile) const {
         int k = 0;
@@ -284,16 +340,15 @@ struct PolGemv {
         ui.b1 = min(rowbytes(), ui.b0 + kbytes_per_split);
         ui.aux = mat_of(ui.tile);
     }
-    __device__ int64_t row_of(const UnitInfo &ui, int r) const { return (ui.tile - m[ui.aux].tile0) * SW_ROWS + r; }
-    __device__ const uint8_t *row_ptr(const UnitInfo &ui, int r) const {
-        const int64_t row = row_of(ui, r);
-        return row < m[ui.aux].rows ? m[ui.aux].w + row * rowbytes() : nullptr;
+    __device__ int64_t row0(const UnitInfo &ui) const { return (ui.tile - m[ui.aux].tile0) * SW_ROWS; }
+    __device__ void issue(const SwMaps &maps, const UnitInfo &ui, int64_t b, void *dst, uint64_t *bar) const {
+        tma_box_2d(dst, &maps.m[ui.aux], (int)b, (int)row0(ui), bar);
     }
-    __device__ bool warp_live(const UnitInfo &ui, int w) const { return row_of(ui, 16 * w) < m[ui.aux].rows; }
+    __device__ int stage_row(int w, int r16) const { return 16 * w + r16; }
+    __device__ bool warp_live(const UnitInfo &ui, int w) const { return row0(ui) + 16 * w < m[ui.aux].rows; }
     __device__ float scale(const UnitInfo &ui, int r16, int64_t grp) const {
-        // r16 = MMA row within this warp's 16 (caller passes g or g+8)
         const int w = threadIdx.x >> 5;
-        const int64_t row = row_of(ui, 16 * w + r16);
+        const int64_t row = row0(ui) + 16 * w + r16;
         if (row >= m[ui.aux].rows) return 0.f;
         const int64_t gpr = cols / 32;
         if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(m[ui.aux].sc + row * gpr + grp));
@@ -305,12 +360,12 @@ struct PolGemv {
         stage_x_n<DT>(x, ldx, n_tok, cols, xs, xs_stride, threadIdx.x, SW_CONS * 32);
     }
     template <int NT>
-    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) const {
+    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
         const GemvMat &mm = m[ui.aux];
 #pragma unroll
         for (int half = 0; half < 2; half++) {
-            const int64_t row = row_of(ui, 16 * w + g + 8 * half);
+            const int64_t row = row0(ui) + 16 * w + g + 8 * half;
             if (row >= mm.rows) continue;
             float rs = 1.f;
             if (DT == MG_Q8R) rs = reinterpret_cast<const float *>(mm.sc)[row];
@@ -325,9 +380,232 @@ struct PolGemv {
                 if (ks_count == 1) {
                     float *yp = mm.y + (int64_t)tok * mm.ldy + row;
                     *yp = accumulate ? *yp + v : v;
+                    if (amax && nt < 2 && (v > bv[nt] || (v == bv[nt] && (int)row < bi[nt]))) {  // NaN never wins
+                        bv[nt] = v;
+                        bi[nt] = (int)row;
+                    }
                 } else {
                     mm.y[(int64_t)ui.ks * part_stride + (int64_t)tok * mm.ldy + row] = v;
                 }
+            }
+        }
+    }
+};
+
+// ------------------------------------------------------ routed experts
+// Decode MoE over the distinct experts of n_tok tokens' top-k selection.
+// maps.m[0..2] = gate, up, down of every expert of every layer as 4-D byte
+// tensors {row bytes, rows, expert, layer}.
+constexpr int SW_MAX_SLOTS = 128;  // n_tok * top_k
+struct MoeShared {
+    int nd;
+    int list[SW_MAX_SLOTS];
+    int ne;                        // slot count of the staged expert (down)
+    int slots[16];
+};
+
+struct MoeCommon {
+    mg_expert_layout L;
+    const uint8_t *experts_layer;
+    int layer;
+    int n_experts, n_tok, top_k;
+    const int32_t *sel;
+    MoeShared *ms;
+
+    __device__ const uint8_t *expert(int e) const { return experts_layer + (int64_t)e * L.expert_stride; }
+    __device__ void build_list() {
+        __shared__ uint32_t bm[64];
+        __shared__ int wpre[65];
+        const int n = n_tok * top_k;
+        for (int i = threadIdx.x; i < 64; i += blockDim.x) bm[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const int e = sel[i];
+            if (e >= 0 && e < n_experts) atomicOr(&bm[e >> 5], 1u << (e & 31));
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int c = 0;
+            for (int wd = 0; wd < 64; wd++) { wpre[wd] = c; c += __popc(bm[wd]); }
+            wpre[64] = c;
+            ms->nd = c;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+            const uint32_t word = bm[e >> 5], bit = 1u << (e & 31);
+            if (word & bit) ms->list[wpre[e >> 5] + __popc(word & (bit - 1))] = e;
+        }
+        __syncthreads();
+    }
+};
+
+// gate/up: a unit is 64 output rows of one expert.  Stage rows 0..63 hold the
+// gate rows and 64..127 the up rows; warp w's MMA rows 0..7 are gate rows
+// 8w..8w+7 and 8..15 the up rows of the same outputs, so each lane holds gate
+// (c0,c1) and up (c2,c3) of one row and applies the activation in registers.
+template <int DT, int SC>
+struct PolMoeGateUp : MoeCommon {
+    const float *xb;
+    int act_plain;
+    float alpha, limit;
+    float *h;
+
+    __device__ int64_t rowbytes() const { return DT == MG_Q8R ? L.hidden : L.hidden / 2; }
+    __device__ int xs_stride() const { return (int)L.hidden + XS_PAD; }
+    __device__ int64_t tpe() const { return (L.ffn + 63) / 64; }
+    __device__ void init_shared() {
+        __shared__ MoeShared s;
+        ms = &s;
+        build_list();
+    }
+    __device__ void finish() {}
+    __device__ int64_t units() const { return (int64_t)ms->nd * tpe(); }
+    __device__ void unit(int64_t u, UnitInfo &ui) const {
+        ui.aux = (int)(u / tpe());
+        ui.tile = u % tpe();
+        ui.ks = 0;
+        ui.b0 = 0;
+        ui.b1 = rowbytes();
+    }
+    __device__ void issue(const SwMaps &maps, const UnitInfo &ui, int64_t b, void *dst, uint64_t *bar) const {
+        const int e = ms->list[ui.aux];
+        tma_box_4d(dst, &maps.m[0], (int)b, (int)(ui.tile * 64), e, layer, bar);
+        tma_box_4d(static_cast<uint8_t *>(dst) + 64 * 128, &maps.m[1], (int)b, (int)(ui.tile * 64), e, layer, bar);
+    }
+    __device__ int stage_row(int w, int r16) const { return r16 < 8 ? 8 * w + r16 : 64 + 8 * w + (r16 - 8); }
+    __device__ bool warp_live(const UnitInfo &ui, int w) const { return ui.tile * 64 + 8 * w < L.ffn; }
+    __device__ float scale(const UnitInfo &ui, int r16, int64_t grp) const {
+        const int w = threadIdx.x >> 5;
+        const int64_t row = ui.tile * 64 + 8 * w + (r16 & 7);
+        if (row >= L.ffn) return 0.f;
+        const uint8_t *sc = expert(ms->list[ui.aux]) + ((r16 & 8) ? L.off[1][1] : L.off[0][1]);
+        const int64_t gpr = L.hidden / 32;
+        if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(sc + row * gpr + grp));
+        return h2f(__ldg(reinterpret_cast<const uint16_t *>(sc) + row * gpr + grp));
+    }
+    __device__ int nt_active(const UnitInfo &) const { return (n_tok + 3) >> 2; }
+    __device__ bool restage(int64_t, int64_t) const { return false; }
+    __device__ void stage_x(int64_t, __half *xs, int xs_stride) const {
+        stage_x_n<DT>(xb, L.hidden, n_tok, (int)L.hidden, xs, xs_stride, threadIdx.x, SW_CONS * 32);
+    }
+    template <int NT>
+    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) const {
+        const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+        const int64_t row = ui.tile * 64 + 8 * w + g;
+        if (row >= L.ffn) return;
+        const int e = ms->list[ui.aux];
+        const uint8_t *eb = expert(e);
+        const float bg = reinterpret_cast<const float *>(eb + L.off[0][2])[row];
+        const float bu = reinterpret_cast<const float *>(eb + L.off[1][2])[row];
+        float sg = 1.f, su = 1.f;
+        if (DT == MG_Q8R) {
+            sg = reinterpret_cast<const float *>(eb + L.off[0][1])[row];
+            su = reinterpret_cast<const float *>(eb + L.off[1][1])[row];
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int tok = nt * 4 + t;
+            if (tok >= n_tok) continue;
+            int slot = -1;
+            for (int i = 0; i < top_k; i++)
+                if (sel[tok * top_k + i] == e) { slot = tok * top_k + i; break; }
+            if (slot < 0) continue;
+            float gv = acc[nt][0] + acc[nt][1], uv = acc[nt][2] + acc[nt][3];
+            if (DT == MG_Q8R) { gv = __fmul_rn(gv, sg); uv = __fmul_rn(uv, su); }
+            gv = __fadd_rn(gv, bg);
+            uv = __fadd_rn(uv, bu);
+            float hv;
+            if (act_plain) {
+                hv = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+            } else {
+                if (gv > limit) gv = limit;
+                if (uv > limit) uv = limit;
+                if (uv < -limit) uv = -limit;
+                hv = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(__fmul_rn(-alpha, gv)))), __fadd_rn(uv, 1.0f));
+            }
+            h[(int64_t)slot * L.ffn + row] = hv;
+        }
+    }
+};
+
+// down: a unit is 128 rows of one expert's down matrix times a K split; the
+// activations are the expert's slots' h rows (re-staged when the expert
+// changes).  Output: y[ks][slot][row] partial sums (+ bias in split 0).
+template <int DT, int SC>
+struct PolMoeDown : MoeCommon {
+    const float *h;
+    float *y;
+    int ks_count;
+    int64_t kbytes_per_split;
+
+    __device__ int64_t rowbytes() const { return DT == MG_Q8R ? L.ffn : L.ffn / 2; }
+    __device__ int xs_stride() const { return (int)L.ffn + XS_PAD; }
+    __device__ int64_t tpe() const { return ((L.hidden + SW_ROWS - 1) / SW_ROWS) * ks_count; }
+    __device__ void init_shared() {
+        __shared__ MoeShared s;
+        ms = &s;
+        build_list();
+    }
+    __device__ void finish() {}
+    __device__ int64_t units() const { return (int64_t)ms->nd * tpe(); }
+    __device__ void unit(int64_t u, UnitInfo &ui) const {
+        ui.aux = (int)(u / tpe());
+        const int64_t r = u % tpe();
+        ui.tile = r / ks_count;
+        ui.ks = (int)(r % ks_count);
+        ui.b0 = (int64_t)ui.ks * kbytes_per_split;
+        ui.b1 = min(rowbytes(), ui.b0 + kbytes_per_split);
+    }
+    __device__ void issue(const SwMaps &maps, const UnitInfo &ui, int64_t b, void *dst, uint64_t *bar) const {
+        tma_box_4d(dst, &maps.m[2], (int)b, (int)(ui.tile * SW_ROWS), ms->list[ui.aux], layer, bar);
+    }
+    __device__ int stage_row(int w, int r16) const { return 16 * w + r16; }
+    __device__ bool warp_live(const UnitInfo &ui, int w) const { return ui.tile * SW_ROWS + 16 * w < L.hidden; }
+    __device__ float scale(const UnitInfo &ui, int r16, int64_t grp) const {
+        const int w = threadIdx.x >> 5;
+        const int64_t row = ui.tile * SW_ROWS + 16 * w + r16;
+        if (row >= L.hidden) return 0.f;
+        const uint8_t *sc = expert(ms->list[ui.aux]) + L.off[2][1];
+        const int64_t gpr = L.ffn / 32;
+        if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(sc + row * gpr + grp));
+        return h2f(__ldg(reinterpret_cast<const uint16_t *>(sc) + row * gpr + grp));
+    }
+    __device__ int nt_active(const UnitInfo &) const { return (ms->ne + 3) >> 2; }
+    __device__ bool restage(int64_t u, int64_t u0) const { return u != u0 && (u / tpe()) != ((u - 1) / tpe()); }
+    __device__ void stage_x(int64_t u, __half *xs, int xs_stride) const {
+        const int e = ms->list[(int)(u / tpe())];
+        if (threadIdx.x == 0) {
+            int k = 0;
+            for (int i = 0; i < n_tok * top_k && k < 16; i++)
+                if (sel[i] == e) ms->slots[k++] = i;
+            ms->ne = k;
+        }
+        named_bar_sync(2, SW_CONS * 32);
+        const int ne = ms->ne;
+        for (int j = 0; j < ne; j++)
+            stage_x_n<DT>(h + (int64_t)ms->slots[j] * L.ffn, L.ffn, 1, (int)L.ffn, xs + 2 * j * xs_stride, xs_stride,
+                          threadIdx.x, SW_CONS * 32);
+    }
+    template <int NT>
+    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) const {
+        const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+        const uint8_t *eb = expert(ms->list[ui.aux]);
+        const int ne = ms->ne;
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            const int64_t row = ui.tile * SW_ROWS + 16 * w + g + 8 * half;
+            if (row >= L.hidden) continue;
+            float rs = 1.f;
+            if (DT == MG_Q8R) rs = reinterpret_cast<const float *>(eb + L.off[2][1])[row];
+            const float bd = ui.ks == 0 ? reinterpret_cast<const float *>(eb + L.off[2][2])[row] : 0.f;
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                const int j = nt * 4 + t;
+                if (j >= ne) continue;
+                float v = acc[nt][2 * half] + acc[nt][2 * half + 1];
+                if (DT == MG_Q8R) v = __fmul_rn(v, rs);
+                v = __fadd_rn(v, bd);
+                y[((int64_t)ui.ks * n_tok * top_k + ms->slots[j]) * L.hidden + row] = v;
             }
         }
     }
