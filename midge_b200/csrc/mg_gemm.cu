@@ -38,11 +38,13 @@ struct XgCfg {
     static constexpr int TMEM_COLS = NA * XG_N;                       // 256 or 128
 };
 
-// f16x2 holding 2^e in both halves (e >= -24), exact
+// f16x2 holding 2^e in both halves (exact for e >= -24; 0 below: such
+// values are counted as inexact when the rebase table is built)
 __device__ __forceinline__ uint32_t pow2_h2(int e) {
     uint32_t h;
     if (e >= -14) h = (uint32_t)(e + 15) << 10;
-    else h = 1u << (e + 24);
+    else if (e >= -24) h = 1u << (e + 24);
+    else h = 0u;
     return h | (h << 16);
 }
 
@@ -51,49 +53,69 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
     return *reinterpret_cast<uint32_t *>(&r);
 }
 
-// Convert one 128 x 64 weight tile (rows m0.., K columns k0..k0+63 of the
-// matrix at w) into f16 at `dst` in the 128B-swizzled K-major layout.
-// 128 threads, one row each.  Out-of-range rows are written as zeros.
+// Raw bytes of one row's slice of a 128 x 64 weight tile, loaded one k-tile
+// ahead of its conversion so the global-load latency overlaps the previous
+// tile's conversion and MMAs.
 template <int DT>
-__device__ __forceinline__ void xg_convert_tile(uint8_t *dst, const uint8_t *w, const uint8_t *sc, int64_t rows,
-                                                int64_t cols, int64_t m0, int kt, int rebase, int tid) {
-    const int r = tid;  // 0..127
-    const int64_t row = m0 + r;
-    uint8_t *drow = dst + r * 128;
-    const int sw = r & 7;
-    uint32_t v[32];  // 64 f16 = 32 words
+struct XgRaw {
+    static constexpr int NW = DT == MG_Q8R ? 4 : 2;  // 16-byte words: 64 int8 or 64 e2m1
+    uint4 w[NW];
+    uint32_t s[2];  // ue8m0 codes of the two 32-column groups (MXFP4)
+};
+
+template <int DT>
+__device__ __forceinline__ void xg_load(XgRaw<DT> &r, const uint8_t *w, const uint8_t *sc, int64_t rows, int64_t cols,
+                                        int64_t row, int kt) {
     if (row < rows) {
         if constexpr (DT == MG_Q8R) {
             const uint4 *src = reinterpret_cast<const uint4 *>(w + row * cols + (int64_t)kt * 64);
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const uint4 b = __ldg(src + q);
-                s8x4_to_h2(b.x, v[8 * q + 0], v[8 * q + 1]);
-                s8x4_to_h2(b.y, v[8 * q + 2], v[8 * q + 3]);
-                s8x4_to_h2(b.z, v[8 * q + 4], v[8 * q + 5]);
-                s8x4_to_h2(b.w, v[8 * q + 6], v[8 * q + 7]);
-            }
+            for (int q = 0; q < 4; q++) r.w[q] = __ldg(src + q);
         } else {
             const uint4 *src = reinterpret_cast<const uint4 *>(w + row * (cols / 2) + (int64_t)kt * 32);
+            r.w[0] = __ldg(src);
+            r.w[1] = __ldg(src + 1);
             const int64_t gpr = cols / 32;
-#pragma unroll
-            for (int gi = 0; gi < 2; gi++) {  // two 32-column groups per tile
-                const uint4 b = __ldg(src + gi);
-                const uint32_t u = sc[row * gpr + (int64_t)kt * 2 + gi];
-                const uint32_t f = u ? pow2_h2((int)u - 127 - rebase) : 0u;
-                uint32_t words[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int wd = 0; wd < 4; wd++) {
-                    uint32_t o[4];
-                    e2m1x8_to_h2(words[wd], o);
-#pragma unroll
-                    for (int i = 0; i < 4; i++) v[16 * gi + 4 * wd + i] = hmul2_u32(o[i], f);
-                }
-            }
+            r.s[0] = sc[row * gpr + (int64_t)kt * 2];
+            r.s[1] = sc[row * gpr + (int64_t)kt * 2 + 1];
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = 0u;
+        for (int q = 0; q < XgRaw<DT>::NW; q++) r.w[q] = make_uint4(0, 0, 0, 0);
+        r.s[0] = r.s[1] = 0;
+    }
+}
+
+// Write one row (thread r of 128) of the tile as f16 at `dst` in the
+// 128B-swizzled K-major layout: e2m1 values times 2^(code - 127 - rebase),
+// int8 values as they are.
+template <int DT>
+__device__ __forceinline__ void xg_store(uint8_t *dst, const XgRaw<DT> &raw, int rebase, int r) {
+    uint8_t *drow = dst + r * 128;
+    const int sw = r & 7;
+    uint32_t v[32];  // 64 f16 = 32 words
+    if constexpr (DT == MG_Q8R) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            s8x4_to_h2(raw.w[q].x, v[8 * q + 0], v[8 * q + 1]);
+            s8x4_to_h2(raw.w[q].y, v[8 * q + 2], v[8 * q + 3]);
+            s8x4_to_h2(raw.w[q].z, v[8 * q + 4], v[8 * q + 5]);
+            s8x4_to_h2(raw.w[q].w, v[8 * q + 6], v[8 * q + 7]);
+        }
+    } else {
+#pragma unroll
+        for (int gi = 0; gi < 2; gi++) {  // two 32-column groups per tile
+            const uint32_t u = raw.s[gi];
+            const uint32_t f = u ? pow2_h2((int)u - 127 - rebase) : 0u;
+            const uint32_t words[4] = {raw.w[gi].x, raw.w[gi].y, raw.w[gi].z, raw.w[gi].w};
+#pragma unroll
+            for (int wd = 0; wd < 4; wd++) {
+                uint32_t o[4];
+                e2m1x8_to_h2(words[wd], o);
+#pragma unroll
+                for (int i = 0; i < 4; i++) v[16 * gi + 4 * wd + i] = hmul2_u32(o[i], f);
+            }
+        }
     }
 #pragma unroll
     for (int c = 0; c < 8; c++)  // 16-byte chunk c of the 128-byte row, swizzled
@@ -158,6 +180,7 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
         if (lane == 0) {
+            int issued = 0;
             for (int kt = 0; kt < KT && ok; kt++) {
                 const int s = kt % C::STAGES;
                 if (kt >= C::STAGES) ok = mbar_wait(&empty[s], ((kt / C::STAGES) - 1) & 1);
@@ -166,8 +189,14 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
                 mbar_arrive_expect_tx(&full_b[s], 2 * XG_TILE_BYTES);
                 tma_load_2d(st + C::NA * XG_TILE_BYTES, &tm_hi, kt * XG_K, (int)grow0, &full_b[s]);
                 tma_load_2d(st + (C::NA + 1) * XG_TILE_BYTES, &tm_lo, kt * XG_K, (int)grow0, &full_b[s]);
+                issued = kt + 1;
             }
             if (!ok) atomicExch(a.err, XG_ERR);
+            // every copy this thread issued has landed before the CTA may exit
+            for (int s = 0; s < C::STAGES && s < issued; s++) {
+                const int kl = s + ((issued - 1 - s) / C::STAGES) * C::STAGES;
+                if (!mbar_wait(&full_b[s], (kl / C::STAGES) & 1)) atomicExch(a.err, XG_ERR);
+            }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------- MMA issuer
@@ -195,24 +224,33 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
                 }
                 tc_commit(&empty[s]);  // stage s free once these MMAs have read it
             }
-            if (ok) tc_commit(&acc_full);
-            else atomicExch(a.err, XG_ERR);
+            tc_commit(&acc_full);  // also on failure: arrives once the MMAs issued so far are done
+            if (!ok) atomicExch(a.err, XG_ERR);
         }
     } else {
         // ------------------------------------------- converters + epilogue
-        const int tid = threadIdx.x - 64;  // 0..127
+        const int tid = threadIdx.x - 64;  // 0..127: the weight row this thread converts
+        XgRaw<DT> cur[C::NA], nxt[C::NA];
+#pragma unroll
+        for (int na = 0; na < C::NA; na++) xg_load<DT>(cur[na], wmat[na], smat[na], a.M, a.K, m0 + tid, 0);
         for (int kt = 0; kt < KT && ok; kt++) {
+            if (kt + 1 < KT) {
+#pragma unroll
+                for (int na = 0; na < C::NA; na++) xg_load<DT>(nxt[na], wmat[na], smat[na], a.M, a.K, m0 + tid, kt + 1);
+            }
             const int s = kt % C::STAGES;
             if (kt >= C::STAGES) ok = mbar_wait(&empty[s], ((kt / C::STAGES) - 1) & 1);
             if (!ok) break;
             uint8_t *st = base + (size_t)s * C::STAGE;
 #pragma unroll
-            for (int na = 0; na < C::NA; na++)
-                xg_convert_tile<DT>(st + na * XG_TILE_BYTES, wmat[na], smat[na], a.M, a.K, m0, kt, rebase[na], tid);
+            for (int na = 0; na < C::NA; na++) xg_store<DT>(st + na * XG_TILE_BYTES, cur[na], rebase[na], tid);
             fence_proxy_async_smem();
             mbar_arrive(&full_a[s]);
+#pragma unroll
+            for (int na = 0; na < C::NA; na++) cur[na] = nxt[na];
         }
-        if (ok) ok = mbar_wait(&acc_full, 0);
+        const bool acc_ok = mbar_wait(&acc_full, 0);  // always: TMEM is freed only after the MMAs
+        ok = ok && acc_ok;
         if (!ok) {
             if (tid == 0) atomicExch(a.err, XG_ERR);
         } else {

@@ -10,6 +10,7 @@
 #include "mg_common.cuh"
 #include "mg_kernels.h"
 #include "mg_model.h"
+#include "mg_prefill.h"
 
 using mg::DevMat;
 
@@ -229,6 +230,13 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     m->use_graphs = !(ng && *ng && *ng != '0');
     const char *ns = getenv("MIDGE_DECODE_KERNELS");
     m->use_stream = !(ns && !strcmp(ns, "tile"));
+    const char *pk = getenv("MIDGE_PREFILL_KERNELS");
+    m->tc_prefill = !(pk && !strcmp(pk, "tile"));
+    const char *pc = getenv("MIDGE_PREFILL_CHUNK");
+    if (pc && *pc) {
+        int v = atoi(pc);
+        m->pf_chunk = v < DEC_MAX ? DEC_MAX : (v > 4096 ? 4096 : v);
+    }
     *out = m;
     return MG_OK;
 }
@@ -457,6 +465,8 @@ static void rope_tables(const mg_spec &s, int ctx, std::vector<float> &co, std::
         }
 }
 
+static int prefill_prepare(mg_model *m);
+
 extern "C" int mg_model_ready(mg_model *m) {
     MG_REQUIRE(m, MG_ERR_ARG, "ready: null model");
     MG_CUDA(cudaSetDevice(m->device));
@@ -490,7 +500,7 @@ extern "C" int mg_model_ready(mg_model *m) {
         MG_CUDA(cudaMemset(m->kc[l], 0, (size_t)m->max_seqs * c * kv_dim * 2));
         MG_CUDA(cudaMemset(m->vc[l], 0, (size_t)m->max_seqs * c * kv_dim * 2));
     }
-    const int R = PF_CHUNK > DEC_MAX ? PF_CHUNK : DEC_MAX;
+    const int R = m->pf_chunk > DEC_MAX ? m->pf_chunk : DEC_MAX;
     m->rows_max = R;
     const int64_t H = s.hidden;
     TRY(dalloc(m, &m->x, (size_t)R * H * 4));
@@ -561,7 +571,50 @@ extern "C" int mg_model_ready(mg_model *m) {
     MG_CUDA(cudaHostAlloc(&m->h_pos, R * 4, cudaHostAllocDefault));
     MG_CUDA(cudaHostAlloc(&m->h_seq, R * 4, cudaHostAllocDefault));
     MG_CUDA(cudaHostAlloc(&m->h_amax, DEC_MAX * 4, cudaHostAllocDefault));
+    TRY(prefill_prepare(m));
     m->ready = true;
+    return MG_OK;
+}
+
+// Tensor-core prefill of the routed experts: MXFP4 with ue8m0 scales (exact
+// in f16 after a per-matrix rebase, checked here) or q8r, dims % 64.
+static int prefill_prepare(mg_model *m) {
+    const mg_spec &s = m->spec;
+    const mg_expert_layout &L = m->el;
+    const int R = m->rows_max, E = s.n_experts;
+    const bool fmt = (L.dt == MG_MXFP4 && L.scale_fmt == MG_SCALE_UE8M0) || L.dt == MG_Q8R;
+    if (!m->tc_prefill || !fmt || L.hidden % 64 || L.ffn % 64) {
+        m->tc_prefill = false;
+        return MG_OK;
+    }
+    const int64_t slots = (int64_t)R * s.top_k;
+    TRY(dalloc(m, &m->pf_counts, (size_t)E * 4));
+    TRY(dalloc(m, &m->pf_offs, (size_t)(E + 1) * 4));
+    TRY(dalloc(m, &m->pf_cursor, (size_t)E * 4));
+    TRY(dalloc(m, &m->pf_ntiles, 16));
+    TRY(dalloc(m, &m->pf_pos, (size_t)slots * 4));
+    TRY(dalloc(m, &m->pf_slot, (size_t)slots * 4));
+    TRY(dalloc(m, (uint8_t **)&m->pf_tiles, (size_t)(slots / 128 + 1 + E) * sizeof(XgTile)));
+    TRY(dalloc(m, &m->pf_xhi, (size_t)slots * L.hidden * 2));
+    TRY(dalloc(m, &m->pf_xlo, (size_t)slots * L.hidden * 2));
+    TRY(dalloc(m, &m->pf_hhi, (size_t)slots * L.ffn * 2));
+    TRY(dalloc(m, &m->pf_hlo, (size_t)slots * L.ffn * 2));
+    TRY(dalloc(m, &m->pf_y, (size_t)slots * L.hidden * 4));
+    TRY(dalloc(m, &m->pf_rebase, (size_t)s.n_layers * E * 3 * 4));
+    MG_CUDA(cudaMemset(m->pf_rebase, 0, (size_t)s.n_layers * E * 3 * 4));
+    if (L.dt == MG_MXFP4) {
+        int *inexact = nullptr;
+        TRY(dalloc(m, &inexact, 4));
+        MG_CUDA(cudaMemsetAsync(inexact, 0, 4, m->st));
+        TRY(pf_rebase(m->experts, L, s.n_layers, E, m->pf_rebase, inexact, m->st));
+        int h = 0;
+        MG_CUDA(cudaMemcpyAsync(&h, inexact, 4, cudaMemcpyDeviceToHost, m->st));
+        MG_CUDA(cudaStreamSynchronize(m->st));
+        if (h) {
+            fprintf(stderr, "# %d expert matrices span more than 35 scale binades: tile prefill kernels\n", h);
+            m->tc_prefill = false;
+        }
+    }
     return MG_OK;
 }
 
@@ -636,6 +689,20 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
     ra.usage = m->usage + (int64_t)layer * s.n_experts;
     TRY(router(ra, st));
     const uint8_t *lb = m->experts + (int64_t)layer * m->el.layer_stride;
+    if (prefill && m->tc_prefill) {
+        MoePrefill pf{};
+        pf.L = m->el;
+        pf.experts_layer = lb;
+        pf.rebase = m->pf_rebase + (int64_t)layer * s.n_experts * 3;
+        pf.n = n; pf.top_k = s.top_k; pf.n_experts = s.n_experts;
+        pf.sel = m->sel; pf.w = m->wts; pf.xb = m->xb; pf.x = m->x;
+        pf.act_plain = s.act_plain; pf.alpha = s.alpha; pf.limit = s.limit;
+        pf.counts = m->pf_counts; pf.offs = m->pf_offs; pf.cursor = m->pf_cursor; pf.ntiles = m->pf_ntiles;
+        pf.pos_of_slot = m->pf_pos; pf.slot_of_pos = m->pf_slot; pf.tiles = (XgTile *)m->pf_tiles;
+        pf.x_hi = m->pf_xhi; pf.x_lo = m->pf_xlo; pf.h_hi = m->pf_hhi; pf.h_lo = m->pf_hlo; pf.y = m->pf_y;
+        pf.err = stream_error_word();
+        return moe_prefill(pf, st);
+    }
     for (int r0 = 0; r0 < n; r0 += DEC_MAX) {
         int nn = n - r0 < DEC_MAX ? n - r0 : DEC_MAX;
         MoeArgs ma{};
@@ -866,8 +933,8 @@ extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n
         MG_REQUIRE(m->pos[seq] + t < m->ctx, MG_ERR_RANGE, "context full (%d)", m->ctx);
         MG_REQUIRE(toks[t] >= 0 && toks[t] < s.vocab, MG_ERR_RANGE, "token %d out of range", toks[t]);
     }
-    for (int c0 = 0; c0 < n; c0 += PF_CHUNK) {
-        int nc = n - c0 < PF_CHUNK ? n - c0 : PF_CHUNK;
+    for (int c0 = 0; c0 < n; c0 += m->pf_chunk) {
+        int nc = n - c0 < m->pf_chunk ? n - c0 : m->pf_chunk;
         int pos0 = m->pos[seq];
         for (int t = 0; t < nc; t++) {
             m->h_toks[t] = toks[c0 + t];
@@ -894,6 +961,7 @@ extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n
             MG_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)s.vocab * 4, cudaMemcpyDeviceToHost, st));
         }
         MG_CUDA(cudaStreamSynchronize(st));
+        if (m->tc_prefill) TRY(stream_error_check());
         m->pos[seq] += nc;
         m->expert_loads += (uint64_t)nc * s.top_k * s.n_layers;
     }

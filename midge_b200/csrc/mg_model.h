@@ -1,6 +1,7 @@
 // mg_model.h -- device-resident model state behind the mg_model handle.
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <string>
@@ -18,7 +19,7 @@ struct DevMat {
     void *scales = nullptr;
 };
 
-constexpr int PF_CHUNK = 256;   // tokens per prefill pass through the layers
+constexpr int PF_CHUNK = 1024;  // default tokens per prefill pass through the layers (MIDGE_PREFILL_CHUNK)
 constexpr int DEC_MAX = 16;     // sequences per decode step
 
 struct Graph {
@@ -70,6 +71,15 @@ struct mg_model {
     // pinned host staging for per-step inputs/outputs
     int32_t *h_toks = nullptr, *h_pos = nullptr, *h_seq = nullptr, *h_amax = nullptr;
     int *h_err = nullptr;  // error word of the streamed kernels, copied back each step
+
+    // tensor-core prefill of the routed experts (expert-major grouped GEMM)
+    int pf_chunk = mg::PF_CHUNK;
+    bool tc_prefill = false;
+    int *pf_counts = nullptr, *pf_offs = nullptr, *pf_cursor = nullptr, *pf_ntiles = nullptr;
+    int *pf_pos = nullptr, *pf_slot = nullptr, *pf_rebase = nullptr;
+    void *pf_tiles = nullptr;  // mg::XgTile[]
+    __half *pf_xhi = nullptr, *pf_xlo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
+    float *pf_y = nullptr;
 
     std::unordered_map<int, mg::Graph> dec_graphs;  // keyed by n_seqs
     uint64_t expert_loads = 0;

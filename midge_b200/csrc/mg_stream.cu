@@ -45,19 +45,26 @@ int stream_ksplit(int dt, int64_t cols, int want) {
     return (int)((nseg + sps - 1) / sps);
 }
 
+// Shared memory: [alignment slack][barriers][ring of nstages][2 scale slots of
+// ssb bytes][partial-sum hand-over][activations].  Scale slots are dropped (ssb = 0: per-lane scale
+// loads) when they would leave fewer than 4 ring stages.
 template <int DT, class P>
-static int launch_policy(void (*kfn)(SwMaps, P, int, int *), const SwMaps &maps, P &pol, size_t xs_bytes, int grid,
-                         cudaStream_t st) {
+static int launch_policy(void (*kfn)(SwMaps, P, int, int, int *), const SwMaps &maps, P &pol, size_t xs_bytes,
+                         size_t ssb, int grid, cudaStream_t st) {
     const size_t budget = 227 * 1024 - 2048 - 1024;  // static shared memory and the alignment slack
-    int nstages = (int)((budget - 1024 - xs_bytes) / SW_STAGE_BYTES);
+    ssb = (ssb + 127) & ~(size_t)127;
+    xs_bytes += SW_RED_BYTES;  // the partial-sum hand-over sits just before the activations
+    if (ssb && budget < 1024 + xs_bytes + 2 * ssb + 4 * (size_t)SW_STAGE_BYTES) ssb = 0;
+    MG_REQUIRE(budget > 1024 + xs_bytes + 2 * ssb, MG_ERR_ARG, "streamed kernel: activations leave no room for a ring");
+    int nstages = (int)((budget - 1024 - xs_bytes - 2 * ssb) / SW_STAGE_BYTES);
     if (nstages > SW_MAX_STAGES) nstages = SW_MAX_STAGES;
     MG_REQUIRE(nstages >= 2, MG_ERR_ARG, "streamed kernel: activations leave no room for a ring");
-    const size_t smem = 1024 + 1024 + (size_t)nstages * SW_STAGE_BYTES + xs_bytes;
+    const size_t smem = 1024 + 1024 + (size_t)nstages * SW_STAGE_BYTES + 2 * ssb + xs_bytes;
     int rc = ensure_smem_attr(reinterpret_cast<const void *>(kfn), smem);
     if (rc) return rc;
     int *err = sw_err_ptr();
     MG_REQUIRE(err, MG_ERR_OOM, "streamed kernel: no error word");
-    kfn<<<grid, SW_THREADS, smem, st>>>(maps, pol, nstages, err);
+    kfn<<<grid, SW_THREADS, smem, st>>>(maps, pol, nstages, (int)ssb, err);
     MG_CHECK_LAUNCH();
     return MG_OK;
 }
@@ -100,7 +107,18 @@ static int launch_stream_gemv(const StreamGemvArgs &a, cudaStream_t st) {
     const size_t xs_bytes = (size_t)NT * 8 * (a.cols + XS_PAD) * 2;
     const int64_t units = tiles * ks;
     const int nsm = num_sms();
-    return launch_policy<DT>(k_stream<DT, SC, NT, PolGemv<DT, SC>>, maps, pol, xs_bytes,
+    // scale slots need every matrix's scale blob 16-byte aligned and a whole
+    // number of 16-byte pieces long (the last tile's copy ends at the blob's end)
+    size_t ssb = 0;
+    if (DT != MG_Q8R) {
+        const int64_t sb = SC == MG_SCALE_UE8M0 ? 1 : 2;
+        bool fits = true;
+        for (int i = 0; i < a.nmat; i++)
+            fits = fits && (reinterpret_cast<uintptr_t>(a.mat[i].scales) & 15) == 0 &&
+                   (a.mat[i].rows * (a.cols / 32) * sb) % 16 == 0;
+        if (fits) ssb = (size_t)SW_ROWS * (a.cols / 32) * sb;
+    }
+    return launch_policy<DT>(k_stream<DT, SC, NT, PolGemv<DT, SC>>, maps, pol, xs_bytes, ssb,
                              (int)(units < nsm ? units : nsm), st);
 }
 
@@ -154,8 +172,13 @@ static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
     pg.alpha = a.alpha;
     pg.limit = a.limit;
     pg.h = a.h;
+    // scale slots: the expert blob's scale regions are 64-byte aligned and
+    // padded, so a copy rounded up to 16 bytes stays inside them
+    const size_t sb = SC == MG_SCALE_UE8M0 ? 1 : 2;
+    const size_t ssb_gu = DT == MG_Q8R ? 0 : 2 * 64 * (size_t)(a.L.hidden / 32) * sb;
+    const size_t ssb_dn = DT == MG_Q8R ? 0 : (size_t)SW_ROWS * (a.L.ffn / 32) * sb;
     int rc = launch_policy<DT>(k_stream<DT, SC, NT, PolMoeGateUp<DT, SC>>, maps, pg,
-                               (size_t)NT * 8 * (a.L.hidden + XS_PAD) * 2, nsm, st);
+                               (size_t)NT * 8 * (a.L.hidden + XS_PAD) * 2, ssb_gu, nsm, st);
     if (rc) return rc;
     PolMoeDown<DT, SC> pd{};
     pd.L = a.L;
@@ -175,7 +198,7 @@ static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
     pd.ks_count = ks;
     pd.kbytes_per_split = ((nseg + ks - 1) / ks) * SW_SEGB;
     return launch_policy<DT>(k_stream<DT, SC, NT, PolMoeDown<DT, SC>>, maps, pd,
-                             (size_t)NT * 8 * (a.L.ffn + XS_PAD) * 2, nsm, st);
+                             (size_t)NT * 8 * (a.L.ffn + XS_PAD) * 2, ssb_dn, nsm, st);
 }
 
 int moe_down_ksplit(const mg_expert_layout &L, int want) { return stream_ksplit(L.dt, L.ffn, want); }

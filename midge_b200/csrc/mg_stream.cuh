@@ -1,6 +1,6 @@
 // mg_stream.cuh -- warp-specialized streamed dequant-GEMV for decode.
 //
-// One CTA = 8 consumer warps + 1 producer warp.  The producer streams weight
+// One CTA = 16 consumer warps + 1 producer warp.  The producer streams weight
 // rows into a ring of shared-memory stages with cp.async.bulk (one bulk copy
 // per row segment, completion counted on an mbarrier); the consumers decode
 // and multiply out of shared memory on the tensor cores (mma.sync, f16 hi/lo
@@ -8,11 +8,13 @@
 // mbarrier.  Memory parallelism is therefore set by the ring depth, not by
 // registers.
 //
-// A stage holds 128 "MMA rows" (16 per consumer warp) x up to SEGB bytes of
+// A stage holds 128 "MMA rows" (8 row groups of 16) x up to SEGB bytes of
 // each row.  Work is a list of units; a unit is a tile of MMA rows times a
 // range of each row's bytes (a K split), streamed as consecutive segments.
-// Each consumer warp accumulates its own 16 rows over the unit's segments and
-// runs the policy's epilogue itself: no cross-warp reduction.
+// Two consumer warps share a row group, each taking half of every stage's
+// bytes (more warps per scheduler to hide the decode and MMA latencies); at
+// the end of a unit the second warp hands its sums to the first through
+// shared memory and the first runs the policy's epilogue.
 //
 // Every wait is bounded; on timeout a kernel records an error code and stops.
 #pragma once
@@ -23,9 +25,13 @@
 
 namespace mg {
 
-constexpr int SW_CONS = 8;                    // consumer warps
+constexpr int SW_RG = 8;                      // row groups of 16 MMA rows per stage
+constexpr int SW_KH = 2;                      // consumer warps per row group (each takes 1/SW_KH of the stage's bytes)
+constexpr int SW_CONS = SW_RG * SW_KH;        // consumer warps
 constexpr int SW_THREADS = (SW_CONS + 1) * 32;
-constexpr int SW_ROWS = SW_CONS * 16;         // MMA rows per stage
+constexpr int SW_ROWS = SW_RG * 16;           // MMA rows per stage
+constexpr int SW_BAR_PAIR0 = 4;               // named barriers 4..11: the two warps of a row group
+constexpr int SW_RED_BYTES = SW_RG * 32 * 8 * 4;  // hand-over of partial sums (NT <= 2)
 constexpr int SW_MAX_STAGES = 12;
 constexpr int SW_ERR_TIMEOUT = 1;
 constexpr int SW_SEGB = 128;                  // bytes of each row per stage: one 128-byte swizzle row
@@ -51,7 +57,21 @@ struct SwMaps {
 struct SwShared {
     uint64_t full[SW_MAX_STAGES];
     uint64_t empty[SW_MAX_STAGES];
+    uint64_t sfull[2], sempty[2];  // the two per-unit scale slots
 };
+
+// Group scales of 4-bit weights: when the launch gives scale slots (ssb > 0),
+// the producer bulk-copies each unit's scales into one of two shared-memory
+// slots ahead of its weight stages, so the consumers never wait on a global
+// load inside a stage.  sb = bytes per scale (1 for ue8m0, 2 for f16).
+template <int SC>
+__device__ __forceinline__ float scale_at(const uint8_t *p) {
+    if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(*p);
+    return h2f(*reinterpret_cast<const uint16_t *>(p));
+}
+__device__ __forceinline__ uint32_t round16(uint32_t v) { return (v + 15u) & ~15u; }
+// row group of the calling consumer warp
+__device__ __forceinline__ int sw_rg() { return (threadIdx.x >> 5) & (SW_RG - 1); }
 
 struct UnitInfo {
     int64_t tile;
@@ -67,39 +87,62 @@ struct UnitInfo {
 //     -- issues the TMA boxes of row bytes [b, b+128) of the unit's rows into dst
 template <int DT, class P>
 __device__ void sw_producer(const P &pol, const SwMaps &maps, int64_t u0, int64_t u1, uint8_t *ring, int nstages,
-                            SwShared *sh, int *err) {
+                            uint8_t *ss, int ssb, SwShared *sh, int *err) {
     if ((threadIdx.x & 31) != 0) return;
-    int64_t it = 0;
-    for (int64_t u = u0; u < u1; u++) {
+    int64_t it = 0, nu = 0;  // stages and scale slots issued
+    bool ok = true;
+    for (int64_t u = u0; u < u1 && ok; u++) {
         UnitInfo ui;
         pol.unit(u, ui);
+        if (ssb) {
+            const int64_t j = u - u0;
+            const int slot = (int)(j & 1);
+            if (j >= 2 && !mbar_wait(&sh->sempty[slot], (uint32_t)(((j >> 1) - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            mbar_arrive_expect_tx(&sh->sfull[slot], pol.scale_bytes(ui));
+            pol.issue_scales(ui, ss + (size_t)slot * ssb, &sh->sfull[slot]);
+            nu = j + 1;
+        }
         for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
             const int s = (int)(it % nstages);
             if (it >= nstages && !mbar_wait(&sh->empty[s], (uint32_t)(((it / nstages) - 1) & 1))) {
-                atomicExch(err, SW_ERR_TIMEOUT);
-                return;
+                ok = false;
+                break;
             }
             mbar_arrive_expect_tx(&sh->full[s], SW_STAGE_BYTES);
             pol.issue(maps, ui, b, ring + (size_t)s * SW_STAGE_BYTES, &sh->full[s]);
         }
     }
+    if (!ok) atomicExch(err, SW_ERR_TIMEOUT);
+    // every copy issued has landed before the CTA may exit (already true on
+    // success: the consumers waited for all of them)
+    for (int64_t k = it - 1; k >= 0 && k >= it - nstages; k--)
+        if (!mbar_wait(&sh->full[k % nstages], (uint32_t)((k / nstages) & 1))) atomicExch(err, SW_ERR_TIMEOUT);
+    for (int64_t j = nu - 1; j >= 0 && j >= nu - 2; j--)
+        if (!mbar_wait(&sh->sfull[j & 1], (uint32_t)((j >> 1) & 1))) atomicExch(err, SW_ERR_TIMEOUT);
 }
 
 // -------------------------------------------------------------- consumer
-// One warp's share of one stage: its 16 MMA rows (policy stage_row), the
-// stage's 128 bytes of each, at activation column col0.
+// One warp's share of one stage: its row group's 16 MMA rows (policy
+// stage_row), chunks [kh*CPW, kh*CPW + CPW) of the stage's 128 bytes of each,
+// at activation column col0.
 template <int DT, int SC, int NT, class P>
-__device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui, const uint8_t *st, int w, int64_t b,
-                                               int nbytes, const __half *xs, int xs_stride, int nt_active,
-                                               float acc[NT][4]) {
+__device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui, const uint8_t *st, int w, int kh,
+                                               int64_t b, int nbytes, const __half *xs, int xs_stride, int nt_active,
+                                               const uint8_t *ss, float acc[NT][4]) {
     using G = SwGeom<DT>;
+    constexpr int CPW = SW_SEGB / G::CB / SW_KH;  // chunks per warp per stage
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int ra = pol.stage_row(w, g), rb = pol.stage_row(w, g + 8);
     const int64_t col0 = b / G::CB * G::COLS_PER_CHUNK;
     const int nch = nbytes / G::CB;
+    const int c0 = kh * CPW;
     if constexpr (DT == MG_Q8R) {
 #pragma unroll
-        for (int c = 0; c < 2; c++) {
+        for (int cc = 0; cc < CPW; cc++) {
+            const int c = c0 + cc;
             if (c >= nch) break;
             const int piece = 4 * c + t;
             uint4 wa = *reinterpret_cast<const uint4 *>(st + sw_addr(ra, piece));
@@ -124,14 +167,27 @@ __device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui,
         }
     } else {
         const int64_t gchunk0 = b / G::CB;  // group index of the stage's first chunk
-        float sa[8], sb[8];
+        float sa[CPW], sb[CPW];
+        if (ss) {
+            const uint8_t *pa = pol.scale_sm(ui, ss, g), *pb = pol.scale_sm(ui, ss, g + 8);
+            constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            sa[c] = c < nch ? pol.scale(ui, g, gchunk0 + c) : 0.f;
-            sb[c] = c < nch ? pol.scale(ui, g + 8, gchunk0 + c) : 0.f;
+            for (int cc = 0; cc < CPW; cc++) {
+                const int c = c0 + cc;
+                sa[cc] = c < nch ? scale_at<SC>(pa + (gchunk0 + c) * SB) : 0.f;
+                sb[cc] = c < nch ? scale_at<SC>(pb + (gchunk0 + c) * SB) : 0.f;
+            }
+        } else {
+#pragma unroll
+            for (int cc = 0; cc < CPW; cc++) {
+                const int c = c0 + cc;
+                sa[cc] = c < nch ? pol.scale(ui, g, gchunk0 + c) : 0.f;
+                sb[cc] = c < nch ? pol.scale(ui, g + 8, gchunk0 + c) : 0.f;
+            }
         }
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
+        for (int cc = 0; cc < CPW; cc++) {
+            const int c = c0 + cc;
             if (c >= nch) break;
             const uint32_t wa = lds32(st + sw_addr(ra, c) + 4 * t), wb = lds32(st + sw_addr(rb, c) + 4 * t);
             uint32_t fa[4], fb[4];
@@ -155,10 +211,10 @@ __device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui,
                 float d[4] = {0.f, 0.f, 0.f, 0.f};
                 mma_16816(d, a0, bx.x, bx.y);
                 mma_16816(d, a1, bx.z, bx.w);
-                acc[nt][0] = fmaf(sa[c], d[0], acc[nt][0]);
-                acc[nt][1] = fmaf(sa[c], d[1], acc[nt][1]);
-                acc[nt][2] = fmaf(sb[c], d[2], acc[nt][2]);
-                acc[nt][3] = fmaf(sb[c], d[3], acc[nt][3]);
+                acc[nt][0] = fmaf(sa[cc], d[0], acc[nt][0]);
+                acc[nt][1] = fmaf(sa[cc], d[1], acc[nt][1]);
+                acc[nt][2] = fmaf(sb[cc], d[2], acc[nt][2]);
+                acc[nt][3] = fmaf(sb[cc], d[3], acc[nt][3]);
             }
         }
     }
@@ -166,10 +222,13 @@ __device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui,
 
 // Consumer warps: per unit, accumulate its stages, then the policy epilogue.
 template <int DT, int SC, int NT, class P>
-__device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int nstages, SwShared *sh, __half *xs,
-                             int xs_stride, int *err) {
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int nstages, uint8_t *ss_base, int ssb,
+                             float *red, SwShared *sh, __half *xs, int xs_stride, int *err) {
+    const int lane = threadIdx.x & 31, w = sw_rg(), kh = (threadIdx.x >> 5) / SW_RG;
     int64_t it = 0;
+    // After a timed-out wait a warp stops waiting and computing but keeps
+    // taking part in the named barriers, so no other warp is left waiting.
+    bool failed = false;
     for (int64_t u = u0; u < u1; u++) {
         if (pol.restage(u, u0)) {
             named_bar_sync(1, SW_CONS * 32);  // everyone is done with the old activations
@@ -185,22 +244,57 @@ __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int 
 #pragma unroll
             for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
         const bool live = pol.warp_live(ui, w);
-        for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
-            const int s = (int)(it % nstages);
+        const uint8_t *ss = nullptr;
+        const int slot = (int)((u - u0) & 1);
+        if (ssb && !failed) {
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(&sh->full[s], (uint32_t)((it / nstages) & 1));
+            if (lane == 0) ok = mbar_wait(&sh->sfull[slot], (uint32_t)(((u - u0) >> 1) & 1));
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
                 if (lane == 0) atomicExch(err, SW_ERR_TIMEOUT);
-                return;
+                failed = true;
             }
-            if (live)
-                sw_consume_seg<DT, SC, NT>(pol, ui, ring + (size_t)s * SW_STAGE_BYTES, w, b,
-                                           (int)min((int64_t)SW_SEGB, ui.b1 - b), xs, xs_stride, nt_active, acc);
+            ss = ss_base + (size_t)slot * ssb;
+        }
+        for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
+            const int s = (int)(it % nstages);
+            if (!failed) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&sh->full[s], (uint32_t)((it / nstages) & 1));
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    if (lane == 0) atomicExch(err, SW_ERR_TIMEOUT);
+                    failed = true;
+                }
+            }
+            if (live && !failed)
+                sw_consume_seg<DT, SC, NT>(pol, ui, ring + (size_t)s * SW_STAGE_BYTES, w, kh, b,
+                                           (int)min((int64_t)SW_SEGB, ui.b1 - b), xs, xs_stride, nt_active, ss, acc);
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh->empty[s]);
         }
-        if (live) pol.template epilogue<NT>(ui, w, acc);
+        if (live) {  // both warps of the row group agree on `live`
+            float *rp = red + ((size_t)w * 32 + lane) * (NT * 4);
+            if (kh == 1) {
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) rp[nt * 4 + i] = acc[nt][i];
+            }
+            named_bar_sync(SW_BAR_PAIR0 + w, 64);
+            if (kh == 0) {
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) acc[nt][i] += rp[nt * 4 + i];
+                if (!failed) pol.template epilogue<NT>(ui, w, acc);
+            }
+            named_bar_sync(SW_BAR_PAIR0 + w, 64);  // the sums are read before the next unit's overwrite them
+        }
+        if (ssb) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh->sempty[slot]);
+        }
     }
     pol.finish();  // all consumer threads
 }
@@ -208,12 +302,14 @@ __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int 
 // The kernel shell: barrier setup, block's unit range, role split.
 template <int DT, int SC, int NT, class P>
 __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant__ SwMaps maps, P pol, int nstages,
-                                                          int *err) {
+                                                          int ssb, int *err) {
     extern __shared__ __align__(1024) uint8_t sw_smem_raw[];
     uint8_t *sw_smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sw_smem_raw) + 1023) & ~(uintptr_t)1023);
     SwShared *sh = reinterpret_cast<SwShared *>(sw_smem);
     uint8_t *ring = sw_smem + 1024;  // stages 1024-aligned for the 128-byte swizzle
-    __half *xs = reinterpret_cast<__half *>(ring + (size_t)nstages * SW_STAGE_BYTES);
+    uint8_t *ss = ring + (size_t)nstages * SW_STAGE_BYTES;  // 2 scale slots of ssb bytes (ssb % 128 == 0)
+    float *red = reinterpret_cast<float *>(ss + 2 * (size_t)ssb);  // SW_RG x 32 lanes x NT*4 partial sums
+    __half *xs = reinterpret_cast<__half *>(reinterpret_cast<uint8_t *>(red) + SW_RED_BYTES);
     const int xs_stride = pol.xs_stride();
     pol.init_shared();  // all threads; ends with __syncthreads
     const int64_t nunits = pol.units();
@@ -224,17 +320,21 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant_
             mbar_init(&sh->full[s], 1);
             mbar_init(&sh->empty[s], SW_CONS);
         }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(&sh->sfull[s], 1);
+            mbar_init(&sh->sempty[s], SW_CONS);
+        }
         fence_mbar_init();
     }
     __syncthreads();
     if (u0 >= u1) return;
     const int w = threadIdx.x >> 5;
     if (w == SW_CONS) {
-        sw_producer<DT>(pol, maps, u0, u1, ring, nstages, sh, err);
+        sw_producer<DT>(pol, maps, u0, u1, ring, nstages, ss, ssb, sh, err);
     } else {
         pol.stage_x(u0, xs, xs_stride);
         named_bar_sync(1, SW_CONS * 32);
-        sw_consumers<DT, SC, NT>(pol, u0, u1, ring, nstages, sh, xs, xs_stride, err);
+        sw_consumers<DT, SC, NT>(pol, u0, u1, ring, nstages, ss, ssb, red, sh, xs, xs_stride, err);
     }
 }
 
@@ -330,7 +430,8 @@ struct PolGemv {
     __device__ int64_t units() const { return ntiles * ks_count; }
     __device__ int mat_of(int64_t tile) const {
         int k = 0;
-        while (k + 1 < nmat && tile >= m[k + 1].tile0) k++;
+        if (nmat > 1 && tile >= m[1].tile0) k = 1;
+        if (nmat > 2 && tile >= m[2].tile0) k = 2;
         return k;
     }
     __device__ void unit(int64_t u, UnitInfo &ui) const {
@@ -340,19 +441,36 @@ struct PolGemv {
         ui.b1 = min(rowbytes(), ui.b0 + kbytes_per_split);
         ui.aux = mat_of(ui.tile);
     }
-    __device__ int64_t row0(const UnitInfo &ui) const { return (ui.tile - m[ui.aux].tile0) * SW_ROWS; }
+    // field of matrix i without dynamic indexing of the parameter array (which
+    // would copy the policy to local memory)
+#define MG_SEL(i, f) ((i) == 0 ? m[0].f : ((i) == 1 ? m[1].f : m[2].f))
+    __device__ int64_t row0(const UnitInfo &ui) const { return (ui.tile - MG_SEL(ui.aux, tile0)) * SW_ROWS; }
     __device__ void issue(const SwMaps &maps, const UnitInfo &ui, int64_t b, void *dst, uint64_t *bar) const {
         tma_box_2d(dst, &maps.m[ui.aux], (int)b, (int)row0(ui), bar);
     }
     __device__ int stage_row(int w, int r16) const { return 16 * w + r16; }
-    __device__ bool warp_live(const UnitInfo &ui, int w) const { return row0(ui) + 16 * w < m[ui.aux].rows; }
+    __device__ bool warp_live(const UnitInfo &ui, int w) const { return row0(ui) + 16 * w < MG_SEL(ui.aux, rows); }
     __device__ float scale(const UnitInfo &ui, int r16, int64_t grp) const {
-        const int w = threadIdx.x >> 5;
+        const int w = sw_rg();
         const int64_t row = row0(ui) + 16 * w + r16;
-        if (row >= m[ui.aux].rows) return 0.f;
+        if (row >= MG_SEL(ui.aux, rows)) return 0.f;
         const int64_t gpr = cols / 32;
-        if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(m[ui.aux].sc + row * gpr + grp));
-        return h2f(__ldg(reinterpret_cast<const uint16_t *>(m[ui.aux].sc) + row * gpr + grp));
+        const uint8_t *sc = MG_SEL(ui.aux, sc);
+        if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(sc + row * gpr + grp));
+        return h2f(__ldg(reinterpret_cast<const uint16_t *>(sc) + row * gpr + grp));
+    }
+    // unit scales: the tile's rows, whole rows (every K split reads all of them)
+    static constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
+    __device__ uint32_t scale_bytes(const UnitInfo &ui) const {
+        const int64_t nr = min((int64_t)SW_ROWS, MG_SEL(ui.aux, rows) - row0(ui));
+        return round16((uint32_t)(nr * (cols / 32) * SB));
+    }
+    __device__ void issue_scales(const UnitInfo &ui, uint8_t *dst, uint64_t *bar) const {
+        bulk_g2s(dst, MG_SEL(ui.aux, sc) + row0(ui) * (cols / 32) * SB, scale_bytes(ui), bar);
+    }
+    __device__ const uint8_t *scale_sm(const UnitInfo &, const uint8_t *ss, int r16) const {
+        const int w = sw_rg();
+        return ss + (int64_t)(16 * w + r16) * (cols / 32) * SB;
     }
     __device__ int nt_active(const UnitInfo &) const { return (n_tok + 3) >> 2; }
     __device__ bool restage(int64_t, int64_t) const { return false; }
@@ -362,14 +480,17 @@ struct PolGemv {
     template <int NT>
     __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-        const GemvMat &mm = m[ui.aux];
+        const int64_t mrows = MG_SEL(ui.aux, rows), mldy = MG_SEL(ui.aux, ldy);
+        const uint8_t *msc = MG_SEL(ui.aux, sc);
+        const float *mbias = MG_SEL(ui.aux, bias);
+        float *my = MG_SEL(ui.aux, y);
 #pragma unroll
         for (int half = 0; half < 2; half++) {
             const int64_t row = row0(ui) + 16 * w + g + 8 * half;
-            if (row >= mm.rows) continue;
+            if (row >= mrows) continue;
             float rs = 1.f;
-            if (DT == MG_Q8R) rs = reinterpret_cast<const float *>(mm.sc)[row];
-            const float bias = (mm.bias && ui.ks == 0) ? mm.bias[row] : 0.f;
+            if (DT == MG_Q8R) rs = reinterpret_cast<const float *>(msc)[row];
+            const float bias = (mbias && ui.ks == 0) ? mbias[row] : 0.f;
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 const int tok = nt * 4 + t;
@@ -378,19 +499,20 @@ struct PolGemv {
                 if (DT == MG_Q8R) v *= rs;
                 v += bias;
                 if (ks_count == 1) {
-                    float *yp = mm.y + (int64_t)tok * mm.ldy + row;
+                    float *yp = my + (int64_t)tok * mldy + row;
                     *yp = accumulate ? *yp + v : v;
                     if (amax && nt < 2 && (v > bv[nt] || (v == bv[nt] && (int)row < bi[nt]))) {  // NaN never wins
                         bv[nt] = v;
                         bi[nt] = (int)row;
                     }
                 } else {
-                    mm.y[(int64_t)ui.ks * part_stride + (int64_t)tok * mm.ldy + row] = v;
+                    my[(int64_t)ui.ks * part_stride + (int64_t)tok * mldy + row] = v;
                 }
             }
         }
     }
 };
+#undef MG_SEL
 
 // ------------------------------------------------------ routed experts
 // Decode MoE over the distinct experts of n_tok tokens' top-k selection.
@@ -475,13 +597,31 @@ struct PolMoeGateUp : MoeCommon {
     __device__ int stage_row(int w, int r16) const { return r16 < 8 ? 8 * w + r16 : 64 + 8 * w + (r16 - 8); }
     __device__ bool warp_live(const UnitInfo &ui, int w) const { return ui.tile * 64 + 8 * w < L.ffn; }
     __device__ float scale(const UnitInfo &ui, int r16, int64_t grp) const {
-        const int w = threadIdx.x >> 5;
+        const int w = sw_rg();
         const int64_t row = ui.tile * 64 + 8 * w + (r16 & 7);
         if (row >= L.ffn) return 0.f;
         const uint8_t *sc = expert(ms->list[ui.aux]) + ((r16 & 8) ? L.off[1][1] : L.off[0][1]);
         const int64_t gpr = L.hidden / 32;
         if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(sc + row * gpr + grp));
         return h2f(__ldg(reinterpret_cast<const uint16_t *>(sc) + row * gpr + grp));
+    }
+    // unit scales: [gate rows tile*64.. +64][up rows], each 64 x hidden/32 scales
+    static constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
+    __device__ uint32_t half_bytes(const UnitInfo &ui) const {
+        const int64_t nr = min((int64_t)64, L.ffn - ui.tile * 64);
+        return round16((uint32_t)(nr * (L.hidden / 32) * SB));
+    }
+    __device__ uint32_t scale_bytes(const UnitInfo &ui) const { return 2 * half_bytes(ui); }
+    __device__ void issue_scales(const UnitInfo &ui, uint8_t *dst, uint64_t *bar) const {
+        const uint8_t *eb = expert(ms->list[ui.aux]);
+        const int64_t off = ui.tile * 64 * (L.hidden / 32) * SB;
+        const uint32_t n = half_bytes(ui);
+        bulk_g2s(dst, eb + L.off[0][1] + off, n, bar);
+        bulk_g2s(dst + 64 * (L.hidden / 32) * SB, eb + L.off[1][1] + off, n, bar);
+    }
+    __device__ const uint8_t *scale_sm(const UnitInfo &, const uint8_t *ss, int r16) const {
+        const int w = sw_rg();
+        return ss + (int64_t)((r16 & 8 ? 64 : 0) + 8 * w + (r16 & 7)) * (L.hidden / 32) * SB;
     }
     __device__ int nt_active(const UnitInfo &) const { return (n_tok + 3) >> 2; }
     __device__ bool restage(int64_t, int64_t) const { return false; }
@@ -562,13 +702,27 @@ struct PolMoeDown : MoeCommon {
     __device__ int stage_row(int w, int r16) const { return 16 * w + r16; }
     __device__ bool warp_live(const UnitInfo &ui, int w) const { return ui.tile * SW_ROWS + 16 * w < L.hidden; }
     __device__ float scale(const UnitInfo &ui, int r16, int64_t grp) const {
-        const int w = threadIdx.x >> 5;
+        const int w = sw_rg();
         const int64_t row = ui.tile * SW_ROWS + 16 * w + r16;
         if (row >= L.hidden) return 0.f;
         const uint8_t *sc = expert(ms->list[ui.aux]) + L.off[2][1];
         const int64_t gpr = L.ffn / 32;
         if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(sc + row * gpr + grp));
         return h2f(__ldg(reinterpret_cast<const uint16_t *>(sc) + row * gpr + grp));
+    }
+    // unit scales: the tile's 128 rows, whole rows (both K splits read all of them)
+    static constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
+    __device__ uint32_t scale_bytes(const UnitInfo &ui) const {
+        const int64_t nr = min((int64_t)SW_ROWS, L.hidden - ui.tile * SW_ROWS);
+        return round16((uint32_t)(nr * (L.ffn / 32) * SB));
+    }
+    __device__ void issue_scales(const UnitInfo &ui, uint8_t *dst, uint64_t *bar) const {
+        const uint8_t *eb = expert(ms->list[ui.aux]);
+        bulk_g2s(dst, eb + L.off[2][1] + ui.tile * SW_ROWS * (L.ffn / 32) * SB, scale_bytes(ui), bar);
+    }
+    __device__ const uint8_t *scale_sm(const UnitInfo &, const uint8_t *ss, int r16) const {
+        const int w = sw_rg();
+        return ss + (int64_t)(16 * w + r16) * (L.ffn / 32) * SB;
     }
     __device__ int nt_active(const UnitInfo &) const { return (ms->ne + 3) >> 2; }
     __device__ bool restage(int64_t u, int64_t u0) const { return u != u0 && (u / tpe()) != ((u - 1) / tpe()); }

@@ -98,9 +98,10 @@ def test_concurrent_sequences_match_single(torch_cuda, c1_dir):
     multi.close()
 
 
-def test_prefill_chunking_and_long_context(torch_cuda, tmp_path):
+def test_prefill_chunking_and_long_context(torch_cuda, tmp_path, monkeypatch):
     """A prompt longer than the prefill chunk and the sliding window (ring
     wrap inside and across chunks) against the oracle's 64-token chunking."""
+    monkeypatch.setenv("MIDGE_PREFILL_CHUNK", "128")
     spec, edt = ct.config_spec("c1_tiny")
     spec["attn"]["sliding_window"] = 40
     md = ct.write_synthetic_model(str(tmp_path / "m"), spec, edt, seed=4)
