@@ -108,6 +108,21 @@ int mg_moe_ffn(const mg_expert_layout *L, const uint8_t *experts, int layer, int
                const float *xb, int n_tok, int top_k, const int32_t *sel, const float *weights,
                int act_plain, float alpha, float limit, float *h_scratch, float *x, void *stream);
 
+/* No counterpart in the reference.  mg_moe_ffn for callers that may not
+ * allocate device memory on the call path (a fixed start-up memory budget,
+ * an allocator owned by another component, a plain C or cgo host without a
+ * device allocator): the gate/up activations live in a fixed device array
+ * inside this library instead of a caller's h_scratch.  Limit:
+ * n_tok * top_k * ffn <= MG_NOALLOC_MAX_H floats, else MG_ERR_RANGE.  The
+ * first call on a device (with that device current) looks up the array and
+ * should come before any stream capture.  Calls that overlap in time on one
+ * device share the array and race; serialise them.  The array needs no
+ * zeroing. */
+#define MG_NOALLOC_MAX_H (1 << 20)
+int mg_moe_ffn_noalloc(const mg_expert_layout *L, const uint8_t *experts, int layer, int n_experts,
+                       const float *xb, int n_tok, int top_k, const int32_t *sel, const float *weights,
+                       int act_plain, float alpha, float limit, float *x, void *stream);
+
 /* ====================================================== model level ==== */
 
 /* The model spec (engine/midge.c:46-63, parsed from the container's embedded

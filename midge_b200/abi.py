@@ -67,6 +67,8 @@ def _load():
         "mg_expert_layout_init": (i32, [C.POINTER(MgExpertLayout), i32, i64, i64, i64]),
         "mg_moe_ffn": (i32, [C.POINTER(MgExpertLayout), vp, i32, i32, vp, i32, i32, vp, vp, i32, f32, f32, vp, vp,
                              vp]),
+        "mg_moe_ffn_noalloc": (i32, [C.POINTER(MgExpertLayout), vp, i32, i32, vp, i32, i32, vp, vp, i32, f32, f32,
+                                     vp, vp]),
         "mg_model_create": (i32, [C.POINTER(MgSpec), i32, i32, i32, C.POINTER(vp)]),
         "mg_model_set_dense": (i32, [vp, C.c_char_p, i32, i64, i64, vp, vp]),
         "mg_model_set_experts": (i32, [vp, i32, vp, C.c_uint64]),
