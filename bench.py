@@ -11,9 +11,12 @@ the box's disk).  Inputs: seeded synthetic token ids.
 
 One bench "step" = 64 decode steps of the 8 sequences (512 tokens), so
 --warmup 3 --steps 5 covers the workload's 512 decode tokens per sequence.
-  value  = decode tokens/s, device-timed (CUDA events on the model's stream)
+  value  = decode tokens/s of greedy decode with the argmax fed back on the
+           device (mg_decode_greedy), device-timed (CUDA events on the
+           model's stream)
   e2e    = decode tokens/s through mg_decode_step with host buffers (token ids
-           in, argmax ids out, copies inside the timed region)
+           in, argmax ids out, copies inside the timed region), the same
+           number of steps continuing the same sequences
   prefill_tok_s = the prompts' prefill through mg_forward_batch (device-timed)
 The decode working set (~15 GB of weights per step) is far larger than L2,
 so no flush is needed between steps.
@@ -41,6 +44,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
+# DRAM bytes (read + write) per routed expert of one gate/up + down launch
+# pair, from the ncu capture summarised in
+# profiles/moe_stream_gateup_down_c4_decode8.md (per-launch traffic =
+# experts routed x this figure)
+TRAFFIC_PER_EXPERT = None
 DECODE_PER_STEP = 64
 N_SEQ = 8
 
@@ -114,34 +122,32 @@ def build_model(torch, spec, edt, ctx, max_seqs, device=0, seed=0):
 
 
 def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40):
-    """Time the dominant kernel pair (routed-expert FFN: gate/up+SwiGLU and
-    down+combine) live on the resident 120b experts with decode routing of
-    8 tokens, and count its algorithmic bytes: every distinct routed expert's
-    three matrices (nibbles + ue8m0 scales + f32 bias) once, plus activations."""
-    import ctypes as C
+    """Time the dominant kernel pair of the decode step live: the streamed
+    routed-expert FFN (gate/up + clamped SwiGLU, then down) that the decode
+    graph runs, on the resident 120b experts with decode routing of 8 tokens
+    (mg_model_moe_stream on the model's stream, CUDA events on that stream).
+    Algorithmic bytes per launch: every distinct routed expert's three
+    matrices once (nibbles + one ue8m0 scale byte per 32 values + f32 bias),
+    plus the activations read and written."""
     from midge_b200 import abi
 
-    base, L = m.experts_device()
     H, F, E, k = spec["hidden"], spec["moe"]["ffn"], spec["moe"]["experts"], spec["moe"]["top_k"]
     rng = np.random.default_rng(7)
     layers = spec["n_layers"]
     stream = torch.cuda.ExternalStream(m.stream())
-    xb = torch.randn(N_SEQ, H, device="cuda")
-    x = torch.zeros(N_SEQ, H, device="cuda")
-    hbuf = torch.empty(N_SEQ * k * F, device="cuda")
-    sels, nbytes = [], []
+    sels, nbytes, nexp = [], [], []
     per_mat = lambda rows, cols: rows * cols // 2 + rows * cols // 32 + rows * 4
     for _ in range(reps):
         sel = np.stack([rng.permutation(E)[:k] for _ in range(N_SEQ)]).astype(np.int32)
         sels.append(torch.from_numpy(sel).cuda())
         d = len(np.unique(sel))
-        nbytes.append(d * (2 * per_mat(F, H) + per_mat(H, F)) + N_SEQ * (H * 4 * 3 + k * F * 4 * 2))
-    w = torch.full((N_SEQ, k), 1.0 / k, device="cuda")
+        nexp.append(d)
+        nbytes.append(d * (2 * per_mat(F, H) + per_mat(H, F)) + N_SEQ * H * 4 + N_SEQ * k * F * 4 * 2
+                      + 2 * N_SEQ * k * H * 4)
     torch.cuda.synchronize()
 
     def launch(i):
-        abi.check(abi.lib.mg_moe_ffn(C.byref(L), base, i % layers, E, xb.data_ptr(), N_SEQ, k, sels[i].data_ptr(),
-                                     w.data_ptr(), 0, 1.702, 7.0, hbuf.data_ptr(), x.data_ptr(), m.stream()))
+        abi.check(abi.lib.mg_model_moe_stream(m.h, i % layers, N_SEQ, sels[i].data_ptr()))
 
     for i in range(5):
         launch(i)
@@ -155,8 +161,8 @@ def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40):
     ms = e0.elapsed_time(e1) / reps
     by = float(np.mean(nbytes))
     ach = by / (ms * 1e-3) / 1e9
-    return {"kernel": "k_moe_gateup+k_moe_down (8 tokens, top-4 of 128)", "ms": ms, "bytes": by, "achieved_gbs": ach,
-            "frac": ach / hbm_peak}
+    return {"kernel": "k_stream<PolMoeGateUp> + k_stream<PolMoeDown> (8 tokens, top-4 of 128 experts)", "ms": ms,
+            "bytes": by, "experts": float(np.mean(nexp)), "achieved_gbs": ach, "frac": ach / hbm_peak}
 
 
 def cpu_reference(spec_name="c4_120b", seconds_budget=20.0, gen=8):
@@ -221,7 +227,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
     spec, edt = ct.config_spec(args.config)
     prompt_len = args.prompt
-    ctx = prompt_len + DECODE_PER_STEP * (args.warmup + args.steps) + 8
+    ctx = prompt_len + DECODE_PER_STEP * (args.warmup + 2 * args.steps) + 8  # value run, then the e2e run
     hbm_peak, tc_peak, peak_kind = peaks()
     t0 = time.time()
     m = build_model(torch, spec, edt, ctx, N_SEQ, device=local, seed=rank)
@@ -246,23 +252,30 @@ def run_ours(args):
     toks = np.array([int(np.argmax(l)) for l in last], np.int32)
     seqs = np.arange(N_SEQ, dtype=np.int32)
 
-    def run_steps(nsteps, toks):
-        for _ in range(nsteps * DECODE_PER_STEP):
-            _, toks = m.decode_step(seqs, toks)
-        return toks
-
-    toks = run_steps(args.warmup, toks)
+    # value: greedy decode fed back on the device (mg_decode_greedy), inputs
+    # resident, no host round trip inside the timed region
+    cur = m.decode_greedy(seqs, toks, args.warmup * DECODE_PER_STEP)[-1]
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    k0 = m.kernel_launches()
     with ClockSampler(local) as clk:
         e0.record(stream)
-        tw = time.time()
-        toks = run_steps(args.steps, toks)
+        out = m.decode_greedy(seqs, cur, args.steps * DECODE_PER_STEP)
         e1.record(stream)
         e1.synchronize()
-        wall = time.time() - tw
+    launches = m.kernel_launches() - k0
     dev_ms = e0.elapsed_time(e1)
+    cur = out[-1]
+    # e2e: the same decode through mg_decode_step with host buffers: token
+    # ids copied in and argmax ids read back every step
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    tw = time.time()
+    for _ in range(args.steps * DECODE_PER_STEP):
+        _, cur = m.decode_step(seqs, cur)
+    wall = time.time() - tw
     if dist:
         t = torch.tensor([dev_ms, wall * 1e3], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -289,11 +302,14 @@ def run_ours(args):
                    "l2": "working set (~15 GB/step) >> L2, no flush"},
         "prefill_tok_s": round(prefill_tok_s, 1), "prefill_wall_s": round(pf_wall, 3),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": N_SEQ * 12 * DECODE_PER_STEP, "d2h_bytes_per_step": N_SEQ * 4 * DECODE_PER_STEP},
+                "h2d_bytes_per_step": N_SEQ * 12 * DECODE_PER_STEP,
+                "d2h_bytes_per_step": (N_SEQ * 8 + 4) * DECODE_PER_STEP},
         "roofline": {"bound": "hbm", "achieved": round(roof["achieved_gbs"], 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(roof["frac"], 4), "traffic": None, "kernel": roof["kernel"],
-                     "peak_kind": peak_kind},
-        "gpu_launches": None,
+                     "frac": round(roof["frac"], 4),
+                     "traffic": round(roof["experts"] * TRAFFIC_PER_EXPERT, 0) if TRAFFIC_PER_EXPERT else None,
+                     "kernel": roof["kernel"], "bytes_per_launch": round(roof["bytes"], 0),
+                     "ms_per_launch": round(roof["ms"], 4), "peak_kind": peak_kind + " (hbm_gbs burst copy)"},
+        "gpu_launches": int(launches),
         "clocks": clk.summary(),
         "load_s": round(load_s, 1),
     }

@@ -149,6 +149,20 @@ typedef struct mg_model mg_model;
  * (engine/midge.c:204-294). */
 int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int device, mg_model **out);
 
+/* Expert parallelism over the GPUs of one box (no counterpart in the
+ * reference, which is one process; its expert-swarm proposal shards experts
+ * the same way).  Rank r of `world` holds experts [r E/world, (r+1) E/world);
+ * tokens, attention, KV cache, router and trunk are replicated, every rank
+ * drives the same calls with the same inputs, and each layer's per-slot
+ * expert outputs are summed over the ranks through NCCL (loaded at run time),
+ * so results equal the one-GPU results bit for bit.  mg_ep_unique_id fills
+ * MG_EP_ID_BYTES bytes on one rank, which the host hands to every rank;
+ * mg_model_set_ep goes between mg_model_create and the experts upload (which
+ * then takes the full blob and keeps this rank's shard). */
+#define MG_EP_ID_BYTES 128
+int mg_ep_unique_id(void *id);
+int mg_model_set_ep(mg_model *m, int rank, int world, const void *id);
+
 /* Upload one dense tensor named as in dense.midge (embed, lm_head,
  * final_norm, L<i>.attn.q ...; docs/ADDING_MODELS.md naming); host pointers,
  * copied into HBM.  Vectors: rows = n, cols = 0, dt = MG_F32.  Replaces the
@@ -191,6 +205,27 @@ int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n, int logit
  * [n_seqs] (host) may be NULL. */
 int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, float *logits,
                    int32_t *argmax);
+
+/* Greedy decode of n_steps tokens for n_seqs sequences without host round
+ * trips: the concurrent-sequence form of midged's gen: loop
+ * (engine/midge.c:812-826, argmax as engine/midge.c:657-660).  Step k's
+ * input is step k-1's argmax, fed on the device; out_toks (host,
+ * [n_steps x n_seqs]) receives every step's argmax, exactly what n_steps
+ * calls of mg_decode_step with argmax feedback return.  n_steps <= 4096. */
+int mg_decode_greedy(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, int n_steps,
+                     int32_t *out_toks);
+
+/* Kernels launched so far by the decode entry points of this model (graph
+ * replays counted by their kernel nodes). */
+uint64_t mg_model_kernel_launches(const mg_model *m);
+
+/* Measurement hook, no counterpart in the reference: the routed-expert FFN
+ * kernels of the streamed decode (gate/up + clamped SwiGLU, then down) for
+ * n_tok tokens routed by sel (device, [n_tok x top_k]) on the model's
+ * resident experts of `layer`, reading the model's current normed rows and
+ * writing its scratch.  Asynchronous on mg_model_stream(m), unlike the other
+ * model-level calls, so that a caller can time it with stream events. */
+int mg_model_moe_stream(mg_model *m, int layer, int n_tok, const int32_t *sel);
 
 /* Copy row `row` of the logits the last forward / decode step / prefill
  * computed (host, vocab floats); the device-resident copy of the reference's

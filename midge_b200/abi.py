@@ -18,6 +18,8 @@ LIB_PATH = os.path.join(PKG, "libmidgecuda.so")
 MG_F32, MG_Q8R, MG_Q4G32, MG_MXFP4 = 0, 1, 2, 3
 MG_SCALE_F16, MG_SCALE_UE8M0 = 0, 1
 MG_OK, MG_ERR_ARG, MG_ERR_CUDA, MG_ERR_OOM, MG_ERR_STATE, MG_ERR_RANGE, MG_ERR_SPEC = 0, -1, -2, -3, -4, -5, -6
+MG_ERR_COMM = -9
+EP_ID_BYTES = 128
 
 i64, i32, f32, vp = C.c_int64, C.c_int, C.c_float, C.c_void_p
 
@@ -82,6 +84,11 @@ def _load():
         "mg_model_get_usage": (i32, [vp, vp]),
         "mg_model_set_usage": (i32, [vp, vp]),
         "mg_model_expert_loads": (C.c_uint64, [vp]),
+        "mg_decode_greedy": (i32, [vp, i32, vp, vp, i32, vp]),
+        "mg_model_kernel_launches": (C.c_uint64, [vp]),
+        "mg_model_moe_stream": (i32, [vp, i32, i32, vp]),
+        "mg_ep_unique_id": (i32, [vp]),
+        "mg_model_set_ep": (i32, [vp, i32, i32, vp]),
         "mg_model_experts_device": (vp, [vp, C.POINTER(MgExpertLayout)]),
         "mg_model_stream": (vp, [vp]),
         "mg_model_free": (i32, [vp]),
@@ -126,7 +133,8 @@ def ptr(a):
 class Model:
     """A model resident on one GPU, driven through the C ABI with host buffers."""
 
-    def __init__(self, spec: dict, ctx: int, max_seqs: int = 1, device: int = 0):
+    def __init__(self, spec: dict, ctx: int, max_seqs: int = 1, device: int = 0, ep=None):
+        """ep: (rank, world, id bytes) for expert parallelism (midge_b200.ep)."""
         self.spec = spec
         self._cspec, self._arr = make_spec(spec)
         h = vp()
@@ -134,11 +142,15 @@ class Model:
         self.h = h
         self.vocab = int(spec["vocab"])
         self.ctx = ctx
+        if ep is not None:
+            rank, world, uid = ep
+            buf = C.create_string_buffer(bytes(uid), EP_ID_BYTES)
+            check(lib.mg_model_set_ep(self.h, int(rank), int(world), buf))
 
     @classmethod
-    def from_dir(cls, path: str, ctx: int, max_seqs: int = 1, device: int = 0):
+    def from_dir(cls, path: str, ctx: int, max_seqs: int = 1, device: int = 0, ep=None):
         md = ModelDir(path)
-        m = cls(md.spec, ctx, max_seqs, device)
+        m = cls(md.spec, ctx, max_seqs, device, ep=ep)
         try:
             for name, dt, rows, cols, d, s in md.tensors():
                 m.set_dense(name, dt, rows, cols, d, s)
@@ -201,6 +213,18 @@ class Model:
 
     def expert_loads(self):
         return int(lib.mg_model_expert_loads(self.h))
+
+    def decode_greedy(self, seqs, toks, n_steps):
+        """n_steps greedy tokens for each sequence, fed back on the device:
+        returns int32 [n_steps x len(seqs)]."""
+        s = np.ascontiguousarray(seqs, dtype=np.int32)
+        t = np.ascontiguousarray(toks, dtype=np.int32)
+        out = np.zeros((n_steps, len(s)), np.int32)
+        check(lib.mg_decode_greedy(self.h, len(s), ptr(s), ptr(t), n_steps, ptr(out)))
+        return out
+
+    def kernel_launches(self):
+        return int(lib.mg_model_kernel_launches(self.h))
 
     def experts_device(self):
         L = MgExpertLayout()

@@ -38,21 +38,6 @@ struct XgCfg {
     static constexpr int TMEM_COLS = NA * XG_N;                       // 256 or 128
 };
 
-// f16x2 holding 2^e in both halves (exact for e >= -24; 0 below: such
-// values are counted as inexact when the rebase table is built)
-__device__ __forceinline__ uint32_t pow2_h2(int e) {
-    uint32_t h;
-    if (e >= -14) h = (uint32_t)(e + 15) << 10;
-    else if (e >= -24) h = 1u << (e + 24);
-    else h = 0u;
-    return h | (h << 16);
-}
-
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-    __half2 r = __hmul2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
-    return *reinterpret_cast<uint32_t *>(&r);
-}
-
 // Raw bytes of one row's slice of a 128 x 64 weight tile, loaded one k-tile
 // ahead of its conversion so the global-load latency overlaps the previous
 // tile's conversion and MMAs.
@@ -133,13 +118,20 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
     __shared__ XgTile tile;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) tile = a.tiles[blockIdx.y];
-    __syncthreads();
-    if ((int)blockIdx.y >= *a.ntiles) return;  // uniform: no TMEM touched yet
+    if (MODE == XG_DENSE) {
+        if (threadIdx.x == 0) tile = XgTile{0, (int)blockIdx.y * XG_N, min(XG_N, a.n_rows - (int)blockIdx.y * XG_N)};
+        __syncthreads();
+        if (tile.nrows <= 0) return;
+    } else {
+        if (threadIdx.x == 0) tile = a.tiles[blockIdx.y];
+        __syncthreads();
+        if ((int)blockIdx.y >= *a.ntiles) return;  // uniform: no TMEM touched yet
+    }
     const int64_t m0 = (int64_t)blockIdx.x * XG_M;
     if (m0 >= a.M) return;
     const int e = tile.e;
-    const int64_t grow0 = (int64_t)a.offs[e] + tile.row0;  // first expert-major row of the N tile
+    // first (expert-major) activation row of the N tile
+    const int64_t grow0 = (MODE == XG_DENSE ? 0 : (int64_t)a.offs[e]) + tile.row0;
     const int KT = (int)(a.K / XG_K);
 
     if (threadIdx.x == 0) {
@@ -304,7 +296,8 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
                         a.out_lo[p * a.M + row] = lo;
                     } else {
                         const float v = __fadd_rn(__fmul_rn(vg[j], scale0), b0);
-                        float *yp = a.y + p * a.ldy + row;
+                        const int64_t yr = MODE == XG_DOWN ? (int64_t)a.slot_of_pos[p] : p;
+                        float *yp = a.y + yr * a.ldy + row;
                         *yp = (MODE == XG_DENSE && a.accumulate) ? __fadd_rn(*yp, v) : v;
                     }
                 }

@@ -25,11 +25,13 @@ struct XgArgs {
     const XgTile *tiles;
     const int *ntiles;                 // device count of valid tiles
     const int *offs;                   // first expert-major row of each expert
+    const int *slot_of_pos;            // DOWN: (token, rank) slot of each expert-major row: y is slot-major
     const int *rebase;                 // [E x 3] MXFP4 scale rebase exponents of this layer
     __half *out_hi, *out_lo;           // GATEUP output [P x M]
     float *y;                          // DOWN / DENSE output
     int64_t ldy;
     int accumulate;                    // DENSE: y += result
+    int n_rows;                        // DENSE: activation rows (tile i = rows 128 i ..), no tile list
     int act_plain;
     float alpha, limit;
     int *err;

@@ -54,6 +54,7 @@ struct MoeStreamArgs {
     const CUtensorMap *maps;  // gate (box 64 rows), up (64), down (128): 4-D over all experts and layers
     int layer;
     const uint8_t *experts_layer;
+    int e0;  // global id of local expert 0 (sel holds global ids)
     int n_experts, n_tok, top_k;
     const int32_t *sel;
     const float *xb;      // [n_tok x hidden]
@@ -63,8 +64,12 @@ struct MoeStreamArgs {
     float *y;             // [down_ksplit x n_tok*top_k x hidden]
     int down_ksplit;      // requested
     int down_ksplit_out;  // what moe_down_ksplit() returned for it
+    const int *rebase;    // MXFP4: this layer's [n_experts x 3] f16 rebase exponents (null: none)
+    int use_tc;           // run the tensor-core kernels when the format allows
 };
 int moe_stream(const MoeStreamArgs &a, cudaStream_t st);
+bool tmoe_supported(const mg_expert_layout &L, const int *rebase);
+int moe_tmoe(const MoeStreamArgs &a, const int *rebase, cudaStream_t st);
 int moe_down_ksplit(const mg_expert_layout &L, int want);
 
 struct CombineNormArgs {
@@ -106,9 +111,10 @@ struct RouterArgs {
     float *x_out;
     int x_parts_ks;
     int64_t x_parts_stride;
+    int *err;              // decode router: error word set when a bounded wait gives up (may be null)
 };
 int router(const RouterArgs &a, cudaStream_t st);
-int router_split(const RouterArgs &a, float *logits_scratch, cudaStream_t st);  // decode: logits across blocks
+int router_split(const RouterArgs &a, float *logits_scratch, unsigned *ticket, cudaStream_t st);  // decode
 
 // decode MoE FFN (gate/up + activation, then down + rank-order combine)
 struct MoeArgs {

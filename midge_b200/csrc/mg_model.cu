@@ -1,6 +1,7 @@
 // mg_model.cu -- the model behind mg_model: HBM-resident trunk and experts,
 // f16 KV cache, and the decode / expert-major prefill passes built from the
 // kernels of mg_gemv.cu, mg_moe.cu and mg_attn.cu.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -56,6 +57,30 @@ __global__ void k_argmax(const float *__restrict__ logits, int64_t V, int32_t *o
 
 // Sliding layers after a prefill chunk: the last min(n, cap) tokens' f16 K/V
 // go to their ring slots.
+// Greedy chaining on the device: the argmax of the step just run becomes
+// the next step's token (recorded in out[step]); positions advance by one.
+// keys: the fused lm_head argmax (value << 32 | ~index, 0 = no finite
+// maximum -> token 0); else amax holds the indices.
+__global__ void k_advance(const unsigned long long *keys, const int32_t *amax, int n, int32_t *toks, int32_t *tok_pos,
+                          int32_t *out, int32_t *step) {
+    const int i = threadIdx.x;
+    const int s = *step;
+    if (i < n) {
+        int32_t t;
+        if (keys) {
+            const unsigned long long k = keys[i];
+            t = k ? (int32_t)(0xffffffffu - (uint32_t)(k & 0xffffffffull)) : 0;
+        } else {
+            t = amax[i];
+        }
+        toks[i] = t;
+        tok_pos[i] += 1;
+        out[(int64_t)s * n + i] = t;
+    }
+    __syncthreads();
+    if (i == 0) *step = s + 1;
+}
+
 __global__ void k_ring_store(const uint16_t *__restrict__ tk, const uint16_t *__restrict__ tv, int n, int pos0,
                              int cap, int kv_dim, uint16_t *kc, uint16_t *vc) {
     int first = n > cap ? n - cap : 0;
@@ -82,11 +107,15 @@ __device__ __forceinline__ float gauss(uint64_t h) {  // Box-Muller from one has
 }
 
 // part: 0 = data, 1 = scales, 2 = bias of matrix `mat`, for every (layer, expert)
+// le runs over the local blob (n_local experts per layer); the seed uses the
+// global (layer, expert) index so that every rank of an expert-parallel run
+// holds exactly its shard of the same model
 __global__ void k_synth_part(uint8_t *base, int64_t expert_stride, int64_t n_le, int64_t off, int64_t bytes, int part,
-                             int dt, int64_t rows, int64_t cols, uint64_t seed) {
+                             int dt, int64_t rows, int64_t cols, uint64_t seed, int n_local, int e0, int n_experts) {
     for (int64_t le = blockIdx.y; le < n_le; le += gridDim.y) {
         uint8_t *p = base + le * expert_stride + off;
-        uint64_t s0 = mix64(seed ^ (uint64_t)(le * 9 + part * 3 + off));
+        const int64_t lg = (le / n_local) * n_experts + e0 + le % n_local;
+        uint64_t s0 = mix64(seed ^ (uint64_t)(lg * 9 + part * 3 + off));
         if (part == 0) {
             for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; i < bytes;
                  i += (int64_t)gridDim.x * blockDim.x * 8) {
@@ -226,10 +255,14 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     for (auto *vec : {&m->bq, &m->bk, &m->bv, &m->bo, &m->router_b, &m->attn_norm, &m->mlp_norm, &m->sinks, &m->qn, &m->kn})
         vec->assign(L, nullptr);
     m->pos.assign(max_seqs, 0);
+    m->e0 = 0;
+    m->n_local = s.n_experts;
     const char *ng = getenv("MIDGE_NO_GRAPH");
     m->use_graphs = !(ng && *ng && *ng != '0');
     const char *ns = getenv("MIDGE_DECODE_KERNELS");
     m->use_stream = !(ns && !strcmp(ns, "tile"));
+    const char *mk = getenv("MIDGE_MOE_KERNELS");
+    m->tc_moe = mk && !strcmp(mk, "tc");
     const char *pk = getenv("MIDGE_PREFILL_KERNELS");
     m->tc_prefill = !(pk && !strcmp(pk, "tile"));
     const char *pc = getenv("MIDGE_PREFILL_CHUNK");
@@ -319,7 +352,7 @@ static int convert_expert_scales(mg_model *m) {
     int *bad = nullptr;
     TRY(dalloc(m, &bad, sizeof(int)));
     MG_CUDA(cudaMemsetAsync(bad, 0, sizeof(int), m->st));
-    int64_t n_le = (int64_t)m->spec.n_layers * m->spec.n_experts;
+    int64_t n_le = (int64_t)m->spec.n_layers * m->n_local;
     for (int mt = 0; mt < 3; mt++) {
         dim3 g(64, (unsigned)(n_le < 4096 ? n_le : 4096));
         k_layer_scales_check<<<g, 256, 0, m->st>>>(m->experts, L.expert_stride, n_le, L.off[mt][1], ns[mt], bad);
@@ -335,13 +368,13 @@ static int convert_expert_scales(mg_model *m) {
     int64_t per_expert = ns[0] + ns[1] + ns[2];
     uint8_t *tmp = nullptr;
     void *tmpv = nullptr;
-    MG_CUDA(cudaMalloc(&tmpv, (size_t)per_expert * m->spec.n_experts));
+    MG_CUDA(cudaMalloc(&tmpv, (size_t)per_expert * m->n_local));
     tmp = (uint8_t *)tmpv;
     for (int layer = 0; layer < m->spec.n_layers; layer++) {
         uint8_t *lb = m->experts + (int64_t)layer * L.layer_stride;
-        dim3 g(32, m->spec.n_experts);
+        dim3 g(32, m->n_local);
         for (int pass = 1; pass >= 0; pass--) {
-            k_layer_scales<<<g, 256, 0, m->st>>>(lb, L.expert_stride, m->spec.n_experts, L.off[0][1], ns[0], L.off[1][1],
+            k_layer_scales<<<g, 256, 0, m->st>>>(lb, L.expert_stride, m->n_local, L.off[0][1], ns[0], L.off[1][1],
                                                  ns[1], L.off[2][1], ns[2], tmp, pass, bad);
         }
     }
@@ -358,10 +391,23 @@ static int convert_expert_scales(mg_model *m) {
 
 static int experts_alloc(mg_model *m, int dt) {
     const mg_spec &s = m->spec;
-    TRY(mg_expert_layout_init(&m->el, dt, s.hidden, s.ffn, s.n_experts));
+    TRY(mg_expert_layout_init(&m->el, dt, s.hidden, s.ffn, m->n_local));
     m->experts_bytes = (size_t)s.n_layers * m->el.layer_stride;
     MG_REQUIRE(!m->experts, MG_ERR_STATE, "experts already loaded");
     TRY(dalloc(m, &m->experts, m->experts_bytes));
+    return MG_OK;
+}
+
+extern "C" int mg_ep_unique_id(void *id) { return ep_unique_id(id); }
+
+extern "C" int mg_model_set_ep(mg_model *m, int rank, int world, const void *id) {
+    MG_REQUIRE(m && !m->experts && !m->ready, MG_ERR_STATE, "set_ep: call after create, before the experts");
+    MG_REQUIRE(world >= 1 && rank >= 0 && rank < world && (world == 1 || id), MG_ERR_ARG, "set_ep: bad arguments");
+    MG_REQUIRE(m->spec.n_experts % world == 0, MG_ERR_SPEC, "set_ep: %d experts do not split over %d ranks",
+               m->spec.n_experts, world);
+    MG_CUDA(cudaSetDevice(m->device));
+    TRY(ep_init(&m->ep, rank, world, id));
+    ep_range(m->spec.n_experts, world, rank, &m->e0, &m->n_local);
     return MG_OK;
 }
 
@@ -369,8 +415,16 @@ extern "C" int mg_model_set_experts(mg_model *m, int dt, const void *data, uint6
     MG_REQUIRE(m && data, MG_ERR_ARG, "set_experts: bad arguments");
     MG_CUDA(cudaSetDevice(m->device));
     TRY(experts_alloc(m, dt));
-    MG_REQUIRE(bytes >= m->experts_bytes, MG_ERR_SPEC, "experts.midge too small: need %zu data bytes",
-               m->experts_bytes);  // engine/midge.c:224-227
+    // the blob holds every expert; this rank uploads its shard of each layer
+    const int64_t full_layer = m->el.expert_stride * m->spec.n_experts;
+    const size_t full_bytes = (size_t)m->spec.n_layers * full_layer;
+    MG_REQUIRE(bytes >= full_bytes, MG_ERR_SPEC, "experts.midge too small: need %zu data bytes",
+               full_bytes);  // engine/midge.c:224-227
+    const size_t seg = (size_t)m->el.layer_stride;  // local bytes per layer
+    auto src_of = [&](size_t dst_off) {
+        const size_t layer = dst_off / seg, in = dst_off % seg;
+        return (size_t)layer * full_layer + (size_t)m->e0 * m->el.expert_stride + in;
+    };
     // pinned double-buffered staging; the host copy into a stage overlaps the
     // DMA of the other
     const size_t CH = 64ull << 20;
@@ -389,8 +443,9 @@ extern "C" int mg_model_set_experts(mg_model *m, int dt, const void *data, uint6
     int b = 0;
     while (rc == MG_OK && off < m->experts_bytes) {
         size_t n = m->experts_bytes - off < CH ? m->experts_bytes - off : CH;
+        if (n > seg - off % seg) n = seg - off % seg;  // a copy never crosses a layer of the local blob
         if (cudaEventSynchronize(done[b]) != cudaSuccess) { rc = MG_ERR_CUDA; break; }
-        memcpy(stage[b], src + off, n);
+        memcpy(stage[b], src + src_of(off), n);
         if (cudaMemcpyAsync(m->experts + off, stage[b], n, cudaMemcpyHostToDevice, m->st) != cudaSuccess ||
             cudaEventRecord(done[b], m->st) != cudaSuccess) {
             set_error("expert upload failed");
@@ -415,7 +470,7 @@ extern "C" int mg_model_synth_experts(mg_model *m, int dt, uint64_t seed) {
     MG_CUDA(cudaSetDevice(m->device));
     TRY(experts_alloc(m, dt));
     const mg_expert_layout &L = m->el;
-    int64_t n_le = (int64_t)m->spec.n_layers * m->spec.n_experts;
+    int64_t n_le = (int64_t)m->spec.n_layers * m->n_local;
     for (int mt = 0; mt < 3; mt++) {
         int64_t rows = mt == 2 ? L.hidden : L.ffn, cols = mt == 2 ? L.ffn : L.hidden;
         int64_t db = dt == MG_Q8R ? rows * cols : rows * cols / 2;
@@ -425,7 +480,8 @@ extern "C" int mg_model_synth_experts(mg_model *m, int dt, uint64_t seed) {
         for (int part = 0; part < 3; part++) {
             dim3 g(16, (unsigned)(n_le < 8192 ? n_le : 8192));
             k_synth_part<<<g, 256, 0, m->st>>>(m->experts, L.expert_stride, n_le, L.off[mt][part], sizes[part], part, dt,
-                                               rows, cols, seed + (uint64_t)mt * 7919u);
+                                               rows, cols, seed + (uint64_t)mt * 7919u, m->n_local, m->e0,
+                                               m->spec.n_experts);
             MG_CHECK_LAUNCH();
         }
     }
@@ -466,6 +522,7 @@ static void rope_tables(const mg_spec &s, int ctx, std::vector<float> &co, std::
 }
 
 static int prefill_prepare(mg_model *m);
+static int rebase_prepare(mg_model *m);
 
 extern "C" int mg_model_ready(mg_model *m) {
     MG_REQUIRE(m, MG_ERR_ARG, "ready: null model");
@@ -524,7 +581,7 @@ extern "C" int mg_model_ready(mg_model *m) {
     // streamed decode buffers (K splits sized for ~3 units per SM)
     const int qkv_dim = q_dim + 2 * kv_dim;
     m->ks_qkv = stream_ksplit(MG_Q8R, H, 12);
-    m->ks_o = stream_ksplit(MG_Q8R, q_dim, 16);
+    m->ks_o = stream_ksplit(MG_Q8R, q_dim, 6);
     m->ks_down = moe_down_ksplit(m->el, 2);
     MG_CUDA(cudaHostAlloc(&m->h_err, sizeof(int), cudaHostAllocDefault));
     *m->h_err = 0;
@@ -533,6 +590,8 @@ extern "C" int mg_model_ready(mg_model *m) {
     TRY(dalloc(m, &m->o_part, (size_t)m->ks_o * DEC_MAX * H * 4));
     TRY(dalloc(m, &m->moe_y, (size_t)m->ks_down * DEC_MAX * s.top_k * H * 4));
     TRY(dalloc(m, &m->rlogits, (size_t)DEC_MAX * s.n_experts * 4));
+    TRY(dalloc(m, &m->rticket, 16));
+    MG_CUDA(cudaMemset(m->rticket, 0, 16));
     TRY(dalloc(m, &m->xa, (size_t)DEC_MAX * H * 4));
     TRY(dalloc(m, &m->amax_keys, (size_t)DEC_MAX * 8));
     MG_CUDA(cudaHostAlloc(&m->h_keys, DEC_MAX * 8, cudaHostAllocDefault));
@@ -556,11 +615,11 @@ extern "C" int mg_model_ready(mg_model *m) {
             const mg_expert_layout &L = m->el;
             const int64_t rb_in = L.dt == MG_Q8R ? L.hidden : L.hidden / 2;
             const int64_t rb_dn = L.dt == MG_Q8R ? L.ffn : L.ffn / 2;
-            TRY(map_weights_4d(&m->map_ex[0], m->experts + L.off[0][0], rb_in, L.ffn, s.n_experts, s.n_layers,
+            TRY(map_weights_4d(&m->map_ex[0], m->experts + L.off[0][0], rb_in, L.ffn, m->n_local, s.n_layers,
                                L.expert_stride, L.layer_stride, 64));
-            TRY(map_weights_4d(&m->map_ex[1], m->experts + L.off[1][0], rb_in, L.ffn, s.n_experts, s.n_layers,
+            TRY(map_weights_4d(&m->map_ex[1], m->experts + L.off[1][0], rb_in, L.ffn, m->n_local, s.n_layers,
                                L.expert_stride, L.layer_stride, 64));
-            TRY(map_weights_4d(&m->map_ex[2], m->experts + L.off[2][0], rb_dn, L.hidden, s.n_experts, s.n_layers,
+            TRY(map_weights_4d(&m->map_ex[2], m->experts + L.off[2][0], rb_dn, L.hidden, m->n_local, s.n_layers,
                                L.expert_stride, L.layer_stride, 128));
             m->maps_ok = true;
         }
@@ -571,7 +630,16 @@ extern "C" int mg_model_ready(mg_model *m) {
     MG_CUDA(cudaHostAlloc(&m->h_pos, R * 4, cudaHostAllocDefault));
     MG_CUDA(cudaHostAlloc(&m->h_seq, R * 4, cudaHostAllocDefault));
     MG_CUDA(cudaHostAlloc(&m->h_amax, DEC_MAX * 4, cudaHostAllocDefault));
+    if (m->ep.world > 1) {  // the collectives are placed in the streamed decode and tensor-core prefill
+        MG_REQUIRE(m->maps_ok && m->use_stream, MG_ERR_SPEC,
+                   "expert parallelism needs the streamed decode kernels (q8r trunk, 4-bit/int8 experts)");
+    }
+    TRY(dalloc(m, &m->greedy_out, (size_t)GREEDY_MAX * DEC_MAX * 4));
+    TRY(dalloc(m, &m->greedy_step, 16));
+    TRY(rebase_prepare(m));
     TRY(prefill_prepare(m));
+    MG_REQUIRE(m->ep.world == 1 || m->tc_prefill, MG_ERR_SPEC,
+               "expert parallelism needs the tensor-core prefill (MXFP4 with power-of-two scales or q8r experts)");
     m->ready = true;
     return MG_OK;
 }
@@ -581,13 +649,21 @@ extern "C" int mg_model_ready(mg_model *m) {
 static int prefill_prepare(mg_model *m) {
     const mg_spec &s = m->spec;
     const mg_expert_layout &L = m->el;
-    const int R = m->rows_max, E = s.n_experts;
+    const int R = m->rows_max, E = m->n_local;
     const bool fmt = (L.dt == MG_MXFP4 && L.scale_fmt == MG_SCALE_UE8M0) || L.dt == MG_Q8R;
-    if (!m->tc_prefill || !fmt || L.hidden % 64 || L.ffn % 64) {
-        m->tc_prefill = false;
-        return MG_OK;
-    }
+    const int q_dim = s.n_heads * s.head_dim;
+    // trunk projections on the tensor cores: q8r matrices, reduction dims % 64
+    bool dense = m->tc_prefill && s.hidden % 64 == 0 && q_dim % 64 == 0;
+    for (int l = 0; l < s.n_layers && dense; l++)
+        dense = m->wq[l].dt == MG_Q8R && m->wk[l].dt == MG_Q8R && m->wv[l].dt == MG_Q8R && m->wo[l].dt == MG_Q8R;
+    m->tc_dense = dense;
+    if (!m->tc_prefill || !fmt || L.hidden % 64 || L.ffn % 64) m->tc_prefill = false;
+    if (!m->tc_prefill && !m->tc_dense) return MG_OK;
     const int64_t slots = (int64_t)R * s.top_k;
+    const int64_t xrow = std::max((int64_t)slots * L.hidden, (int64_t)R * std::max<int64_t>(s.hidden, q_dim));
+    TRY(dalloc(m, &m->pf_xhi, (size_t)xrow * 2));
+    TRY(dalloc(m, &m->pf_xlo, (size_t)xrow * 2));
+    if (!m->tc_prefill) return MG_OK;
     TRY(dalloc(m, &m->pf_counts, (size_t)E * 4));
     TRY(dalloc(m, &m->pf_offs, (size_t)(E + 1) * 4));
     TRY(dalloc(m, &m->pf_cursor, (size_t)E * 4));
@@ -595,30 +671,49 @@ static int prefill_prepare(mg_model *m) {
     TRY(dalloc(m, &m->pf_pos, (size_t)slots * 4));
     TRY(dalloc(m, &m->pf_slot, (size_t)slots * 4));
     TRY(dalloc(m, (uint8_t **)&m->pf_tiles, (size_t)(slots / 128 + 1 + E) * sizeof(XgTile)));
-    TRY(dalloc(m, &m->pf_xhi, (size_t)slots * L.hidden * 2));
-    TRY(dalloc(m, &m->pf_xlo, (size_t)slots * L.hidden * 2));
     TRY(dalloc(m, &m->pf_hhi, (size_t)slots * L.ffn * 2));
     TRY(dalloc(m, &m->pf_hlo, (size_t)slots * L.ffn * 2));
     TRY(dalloc(m, &m->pf_y, (size_t)slots * L.hidden * 4));
-    TRY(dalloc(m, &m->pf_rebase, (size_t)s.n_layers * E * 3 * 4));
-    MG_CUDA(cudaMemset(m->pf_rebase, 0, (size_t)s.n_layers * E * 3 * 4));
-    if (L.dt == MG_MXFP4) {
-        int *inexact = nullptr;
-        TRY(dalloc(m, &inexact, 4));
-        MG_CUDA(cudaMemsetAsync(inexact, 0, 4, m->st));
-        TRY(pf_rebase(m->experts, L, s.n_layers, E, m->pf_rebase, inexact, m->st));
-        int h = 0;
-        MG_CUDA(cudaMemcpyAsync(&h, inexact, 4, cudaMemcpyDeviceToHost, m->st));
-        MG_CUDA(cudaStreamSynchronize(m->st));
-        if (h) {
-            fprintf(stderr, "# %d expert matrices span more than 35 scale binades: tile prefill kernels\n", h);
-            m->tc_prefill = false;
-        }
+    if (L.dt == MG_MXFP4 && !m->rebase_ok) {
+        fprintf(stderr, "# expert matrices span more than 35 scale binades: tile prefill kernels\n");
+        m->tc_prefill = false;
     }
     return MG_OK;
 }
 
+// Per-(layer, expert, matrix) rebase exponents of MXFP4 experts with ue8m0
+// scales: e2m1 x 2^(code - 127 - k0) is exact in f16 for every matrix whose
+// codes span at most 35 binades (the tensor-core kernels' weight operand).
+static int rebase_prepare(mg_model *m) {
+    const mg_spec &s = m->spec;
+    const mg_expert_layout &L = m->el;
+    m->rebase_ok = false;
+    if (L.dt != MG_MXFP4 || L.scale_fmt != MG_SCALE_UE8M0) return MG_OK;
+    const int E = m->n_local;
+    TRY(dalloc(m, &m->pf_rebase, (size_t)s.n_layers * E * 3 * 4));
+    MG_CUDA(cudaMemset(m->pf_rebase, 0, (size_t)s.n_layers * E * 3 * 4));
+    int *inexact = nullptr;
+    TRY(dalloc(m, &inexact, 4));
+    MG_CUDA(cudaMemsetAsync(inexact, 0, 4, m->st));
+    TRY(pf_rebase(m->experts, L, s.n_layers, E, m->pf_rebase, inexact, m->st));
+    int h = 0;
+    MG_CUDA(cudaMemcpyAsync(&h, inexact, 4, cudaMemcpyDeviceToHost, m->st));
+    MG_CUDA(cudaStreamSynchronize(m->st));
+    m->rebase_ok = h == 0;
+    return MG_OK;
+}
+
 // ------------------------------------------------------------ forward passes
+// y[n x w.rows] (=|+=) W x + bias for the n activation rows already split
+// into m->pf_xhi / pf_xlo (tcgen05 dense GEMM)
+static int dense_rows(mg_model *m, const DevMat &w, int n, const float *bias, int acc, float *y, int64_t ldy) {
+    DenseGemm d{};
+    d.w = w.data; d.scales = w.scales; d.bias = bias; d.rows = w.rows; d.cols = w.cols;
+    d.x_hi = m->pf_xhi; d.x_lo = m->pf_xlo; d.n = n;
+    d.y = y; d.ldy = ldy; d.accumulate = acc; d.err = stream_error_word();
+    return dense_gemm(d, m->st);
+}
+
 static int gemv_rows(mg_model *m, const DevMat &w, const float *x, int64_t ldx, int n, const float *bias, int acc,
                      float *y, int64_t ldy) {
     for (int r0 = 0; r0 < n; r0 += 16) {
@@ -638,9 +733,17 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
     cudaStream_t st = m->st;
     // attention (engine/midge.c:341-400)
     TRY(rmsnorm(m->x, m->attn_norm[layer], m->xb, H, n, s.norm_eps, st));
-    TRY(gemv_rows(m, m->wq[layer], m->xb, H, n, m->bq[layer], 0, m->q, q_dim));
-    TRY(gemv_rows(m, m->wk[layer], m->xb, H, n, m->bk[layer], 0, m->k, kv_dim));
-    TRY(gemv_rows(m, m->wv[layer], m->xb, H, n, m->bv[layer], 0, m->v, kv_dim));
+    const bool dense = prefill && m->tc_dense;
+    if (dense) {
+        TRY(split_rows(m->xb, H, n, H, m->pf_xhi, m->pf_xlo, st));
+        TRY(dense_rows(m, m->wq[layer], n, m->bq[layer], 0, m->q, q_dim));
+        TRY(dense_rows(m, m->wk[layer], n, m->bk[layer], 0, m->k, kv_dim));
+        TRY(dense_rows(m, m->wv[layer], n, m->bv[layer], 0, m->v, kv_dim));
+    } else {
+        TRY(gemv_rows(m, m->wq[layer], m->xb, H, n, m->bq[layer], 0, m->q, q_dim));
+        TRY(gemv_rows(m, m->wk[layer], m->xb, H, n, m->bk[layer], 0, m->k, kv_dim));
+        TRY(gemv_rows(m, m->wv[layer], m->xb, H, n, m->bv[layer], 0, m->v, kv_dim));
+    }
     const int cap = m->cap[layer];
     const bool sliding = cap < m->ctx;
     QkvPostArgs qa{};
@@ -679,7 +782,12 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
         da.partial = m->attn_part; da.out = m->ao; da.ldo = q_dim;
         TRY(attn_decode(da, n, st));
     }
-    TRY(gemv_rows(m, m->wo[layer], m->ao, q_dim, n, m->bo[layer], 1, m->x, H));
+    if (dense) {
+        TRY(split_rows(m->ao, q_dim, n, q_dim, m->pf_xhi, m->pf_xlo, st));
+        TRY(dense_rows(m, m->wo[layer], n, m->bo[layer], 1, m->x, H));
+    } else {
+        TRY(gemv_rows(m, m->wo[layer], m->ao, q_dim, n, m->bo[layer], 1, m->x, H));
+    }
     // MoE (engine/midge.c:469-549; prefill routing engine/midge.c:404-434)
     RouterArgs ra{};
     ra.x = m->x; ra.norm_w = m->mlp_norm[layer]; ra.eps = s.norm_eps; ra.xb_out = m->xb;
@@ -693,8 +801,9 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
         MoePrefill pf{};
         pf.L = m->el;
         pf.experts_layer = lb;
-        pf.rebase = m->pf_rebase + (int64_t)layer * s.n_experts * 3;
-        pf.n = n; pf.top_k = s.top_k; pf.n_experts = s.n_experts;
+        pf.rebase = m->pf_rebase + (int64_t)layer * m->n_local * 3;
+        pf.n = n; pf.top_k = s.top_k; pf.n_experts = s.n_experts; pf.e0 = m->e0; pf.n_local = m->n_local;
+        pf.ep = &m->ep;
         pf.sel = m->sel; pf.w = m->wts; pf.xb = m->xb; pf.x = m->x;
         pf.act_plain = s.act_plain; pf.alpha = s.alpha; pf.limit = s.limit;
         pf.counts = m->pf_counts; pf.offs = m->pf_offs; pf.cursor = m->pf_cursor; pf.ntiles = m->pf_ntiles;
@@ -795,23 +904,28 @@ static int layer_stream(mg_model *m, int layer, int n) {
     ra.hidden = H; ra.n_tok = n; ra.logits = nullptr; ra.sel = m->sel; ra.weights = m->wts;
     ra.usage = m->usage + (int64_t)layer * s.n_experts;
     ra.x_parts = m->o_part; ra.x_parts_ks = m->ks_o; ra.x_parts_stride = (int64_t)n * H; ra.x_out = m->xa;
-    TRY(router_split(ra, m->rlogits, st));
+    ra.err = stream_error_word();
+    TRY(router_split(ra, m->rlogits, m->rticket, st));
     MoeStreamArgs ma{};
     ma.L = m->el; ma.experts_layer = m->experts + (int64_t)layer * m->el.layer_stride;
     ma.maps = m->map_ex; ma.layer = layer;
-    ma.n_experts = s.n_experts; ma.n_tok = n; ma.top_k = s.top_k; ma.sel = m->sel; ma.xb = m->xb;
+    ma.n_experts = m->n_local; ma.e0 = m->e0; ma.n_tok = n; ma.top_k = s.top_k; ma.sel = m->sel; ma.xb = m->xb;
     ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit; ma.h = m->h; ma.y = m->moe_y;
     ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
+    ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
+    ma.use_tc = m->tc_moe;
+    const size_t ycount = (size_t)m->ks_down * n * s.top_k * H;
+    if (m->ep.world > 1)  // slots of other ranks' experts stay zero, then the sum over ranks fills them exactly
+        MG_CUDA(cudaMemsetAsync(m->moe_y, 0, ycount * 4, st));
     TRY(moe_stream(ma, st));
+    TRY(ep_allreduce_sum(m->ep, m->moe_y, ycount, st));
     return MG_OK;
 }
 
-static int decode_body_stream(mg_model *m, int n) {
+// embedding -> logits and argmax keys, device only (tokens/positions in m->toks / tok_pos)
+static int decode_core_stream(mg_model *m, int n) {
     const mg_spec &s = m->spec;
     cudaStream_t st = m->st;
-    MG_CUDA(cudaMemcpyAsync(m->toks, m->h_toks, n * 4, cudaMemcpyHostToDevice, st));
-    MG_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_pos, n * 4, cudaMemcpyHostToDevice, st));
-    MG_CUDA(cudaMemcpyAsync(m->tok_seq, m->h_seq, n * 4, cudaMemcpyHostToDevice, st));
     TRY(dequant_rows(m->embed.dt, MG_SCALE_F16, m->embed.data, m->embed.scales, m->embed.rows, m->embed.cols, m->toks, n,
                      m->x, st));
     for (int l = 0; l < s.n_layers; l++) TRY(layer_stream(m, l, n));
@@ -830,8 +944,19 @@ static int decode_body_stream(mg_model *m, int n) {
     g.amax = m->amax_keys;
     MG_CUDA(cudaMemsetAsync(m->amax_keys, 0, (size_t)n * 8, st));
     TRY(stream_gemv(g, st));
-    MG_CUDA(cudaMemcpyAsync(m->h_keys, m->amax_keys, (size_t)n * 8, cudaMemcpyDeviceToHost, st));
-    MG_CUDA(cudaMemcpyAsync(m->h_err, stream_error_word(), sizeof(int), cudaMemcpyDeviceToHost, st));
+    return MG_OK;
+}
+
+// embedding -> logits and argmax (tile kernels), device only
+static int decode_core_tile(mg_model *m, int n) {
+    const mg_spec &s = m->spec;
+    cudaStream_t st = m->st;
+    TRY(dequant_rows(m->embed.dt, MG_SCALE_F16, m->embed.data, m->embed.scales, m->embed.rows, m->embed.cols, m->toks, n,
+                     m->x, st));
+    for (int l = 0; l < s.n_layers; l++) TRY(layer_pass(m, l, n, false, 0, 0));
+    TRY(logits_rows(m, m->x, n));
+    k_argmax<<<n, 1024, 0, st>>>(m->logits, s.vocab, m->amax);
+    MG_CHECK_LAUNCH();
     return MG_OK;
 }
 
@@ -839,37 +964,60 @@ static int decode_body_stream(mg_model *m, int n) {
 // pinned staging arrays; everything stream-ordered (graph-capturable)
 static int decode_body(mg_model *m, int n) {
     m->last_streamed = m->use_stream && stream_ok(m, n);
-    if (m->last_streamed) return decode_body_stream(m, n);
-    const mg_spec &s = m->spec;
     cudaStream_t st = m->st;
     MG_CUDA(cudaMemcpyAsync(m->toks, m->h_toks, n * 4, cudaMemcpyHostToDevice, st));
     MG_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_pos, n * 4, cudaMemcpyHostToDevice, st));
     MG_CUDA(cudaMemcpyAsync(m->tok_seq, m->h_seq, n * 4, cudaMemcpyHostToDevice, st));
-    TRY(dequant_rows(m->embed.dt, MG_SCALE_F16, m->embed.data, m->embed.scales, m->embed.rows, m->embed.cols, m->toks, n,
-                     m->x, st));
-    for (int l = 0; l < s.n_layers; l++) TRY(layer_pass(m, l, n, false, 0, 0));
-    TRY(logits_rows(m, m->x, n));
-    k_argmax<<<n, 1024, 0, st>>>(m->logits, s.vocab, m->amax);
-    MG_CHECK_LAUNCH();
-    MG_CUDA(cudaMemcpyAsync(m->h_amax, m->amax, n * 4, cudaMemcpyDeviceToHost, st));
+    if (m->last_streamed) {
+        TRY(decode_core_stream(m, n));
+        MG_CUDA(cudaMemcpyAsync(m->h_keys, m->amax_keys, (size_t)n * 8, cudaMemcpyDeviceToHost, st));
+        MG_CUDA(cudaMemcpyAsync(m->h_err, stream_error_word(), sizeof(int), cudaMemcpyDeviceToHost, st));
+    } else {
+        TRY(decode_core_tile(m, n));
+        MG_CUDA(cudaMemcpyAsync(m->h_amax, m->amax, n * 4, cudaMemcpyDeviceToHost, st));
+    }
     return MG_OK;
 }
 
-static int run_decode(mg_model *m, int n) {
-    if (!m->use_graphs) return decode_body(m, n);
-    auto it = m->dec_graphs.find(n);
-    if (it != m->dec_graphs.end()) {
+// one greedy step fed from the previous step's argmax, device only
+static int decode_chain_body(mg_model *m, int n) {
+    const bool streamed = m->use_stream && stream_ok(m, n);
+    k_advance<<<1, 32, 0, m->st>>>(streamed ? m->amax_keys : nullptr, m->amax, n, m->toks, m->tok_pos, m->greedy_out,
+                                   m->greedy_step);
+    MG_CHECK_LAUNCH();
+    return streamed ? decode_core_stream(m, n) : decode_core_tile(m, n);
+}
+
+static int graph_kernels(cudaGraph_t g) {
+    size_t nn = 0;
+    if (cudaGraphGetNodes(g, nullptr, &nn) != cudaSuccess || nn == 0) return 0;
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (cudaGraphGetNodes(g, nodes.data(), &nn) != cudaSuccess) return 0;
+    int k = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+    }
+    return k;
+}
+
+// Run body(m, n) from a CUDA graph kept in tab[n].  The first run with this
+// many sequences is eager (which also sets every kernel's launch attributes);
+// the same stream-ordered body is then captured for the following runs
+// (capture executes nothing).  Counts the kernels launched.
+static int graph_run(mg_model *m, std::unordered_map<int, Graph> &tab, int n, int (*body)(mg_model *, int)) {
+    if (!m->use_graphs) return body(m, n);  // eager-only runs are not counted
+    auto it = tab.find(n);
+    if (it != tab.end()) {
         MG_CUDA(cudaGraphLaunch(it->second.exec, m->st));
+        m->kernel_launches += (uint64_t)it->second.kernels;
         return MG_OK;
     }
-    // First step with this many sequences: run it eagerly (which also sets
-    // every kernel's launch attributes), then capture the same stream-ordered
-    // body for the following steps.  Capture executes nothing.
-    TRY(decode_body(m, n));
+    TRY(body(m, n));
     MG_CUDA(cudaStreamSynchronize(m->st));
     cudaGraph_t g = nullptr;
     MG_CUDA(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
-    int rc = decode_body(m, n);
+    int rc = body(m, n);
     cudaError_t ce = cudaStreamEndCapture(m->st, &g);
     if (rc != MG_OK) {
         if (g) cudaGraphDestroy(g);
@@ -877,12 +1025,16 @@ static int run_decode(mg_model *m, int n) {
     }
     MG_REQUIRE(ce == cudaSuccess, MG_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(ce));
     Graph gr;
+    gr.kernels = graph_kernels(g);
     cudaError_t ie = cudaGraphInstantiate(&gr.exec, g, 0);
     cudaGraphDestroy(g);
     MG_REQUIRE(ie == cudaSuccess, MG_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(ie));
-    m->dec_graphs[n] = gr;
+    tab[n] = gr;
+    m->kernel_launches += (uint64_t)gr.kernels;  // the eager run launched the same kernels
     return MG_OK;
 }
+
+static int run_decode(mg_model *m, int n) { return graph_run(m, m->dec_graphs, n, decode_body); }
 
 extern "C" int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, float *logits,
                               int32_t *argmax) {
@@ -909,12 +1061,68 @@ extern "C" int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, c
         *m->h_err = 0;
         return stream_error_check();
     }
-    if (m->last_streamed)  // argmax came back packed as (ordered value << 32 | ~index)
-        for (int i = 0; i < n_seqs; i++) m->h_amax[i] = (int32_t)(0xffffffffu - (uint32_t)(m->h_keys[i] & 0xffffffffull));
+    if (m->last_streamed)  // argmax came back packed as (ordered value << 32 | ~index); 0: no finite maximum
+        for (int i = 0; i < n_seqs; i++)
+            m->h_amax[i] = m->h_keys[i] ? (int32_t)(0xffffffffu - (uint32_t)(m->h_keys[i] & 0xffffffffull)) : 0;
     for (int i = 0; i < n_seqs; i++) m->pos[m->h_seq[i]]++;
     m->expert_loads += (uint64_t)n_seqs * s.top_k * s.n_layers;
     if (argmax) memcpy(argmax, m->h_amax, n_seqs * 4);
     return MG_OK;
+}
+
+extern "C" int mg_decode_greedy(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, int n_steps,
+                                int32_t *out_toks) {
+    MG_REQUIRE(m && m->ready, MG_ERR_STATE, "greedy: model not ready");
+    MG_REQUIRE(n_seqs >= 1 && n_seqs <= DEC_MAX && n_seqs <= m->max_seqs && toks && out_toks, MG_ERR_ARG,
+               "greedy: bad arguments");
+    MG_REQUIRE(n_steps >= 1 && n_steps <= GREEDY_MAX, MG_ERR_ARG, "greedy: n_steps %d not in [1, %d]", n_steps,
+               GREEDY_MAX);
+    MG_CUDA(cudaSetDevice(m->device));
+    const mg_spec &s = m->spec;
+    for (int i = 0; i < n_seqs; i++) {
+        int sq = seq_ids ? seq_ids[i] : i;
+        MG_REQUIRE(sq >= 0 && sq < m->max_seqs, MG_ERR_ARG, "greedy: sequence %d out of range", sq);
+        for (int j = 0; j < i; j++) MG_REQUIRE((seq_ids ? seq_ids[j] : j) != sq, MG_ERR_ARG, "greedy: duplicate sequence");
+        MG_REQUIRE(m->pos[sq] + n_steps <= m->ctx, MG_ERR_RANGE, "context full (%d)", m->ctx);
+        MG_REQUIRE(toks[i] >= 0 && toks[i] < s.vocab, MG_ERR_RANGE, "token %d out of range", toks[i]);
+        m->h_toks[i] = toks[i];
+        m->h_pos[i] = m->pos[sq];
+        m->h_seq[i] = sq;
+    }
+    cudaStream_t st = m->st;
+    MG_CUDA(cudaMemsetAsync(m->greedy_step, 0, 4, st));
+    TRY(run_decode(m, n_seqs));
+    for (int k = 1; k < n_steps; k++) TRY(graph_run(m, m->chain_graphs, n_seqs, decode_chain_body));
+    const bool streamed = m->use_stream && stream_ok(m, n_seqs);
+    k_advance<<<1, 32, 0, st>>>(streamed ? m->amax_keys : nullptr, m->amax, n_seqs, m->toks, m->tok_pos, m->greedy_out,
+                                m->greedy_step);
+    MG_CHECK_LAUNCH();
+    m->kernel_launches += 1;
+    MG_CUDA(cudaMemcpyAsync(out_toks, m->greedy_out, (size_t)n_steps * n_seqs * 4, cudaMemcpyDeviceToHost, st));
+    MG_CUDA(cudaStreamSynchronize(st));
+    *m->h_err = 0;
+    TRY(stream_error_check());
+    for (int i = 0; i < n_seqs; i++) m->pos[m->h_seq[i]] += n_steps;
+    m->expert_loads += (uint64_t)n_seqs * s.top_k * s.n_layers * n_steps;
+    return MG_OK;
+}
+
+extern "C" uint64_t mg_model_kernel_launches(const mg_model *m) { return m ? m->kernel_launches : 0; }
+
+extern "C" int mg_model_moe_stream(mg_model *m, int layer, int n_tok, const int32_t *sel) {
+    MG_REQUIRE(m && m->ready && sel && layer >= 0 && layer < m->spec.n_layers, MG_ERR_ARG, "moe_stream: bad arguments");
+    MG_REQUIRE(m->use_stream && stream_ok(m, n_tok), MG_ERR_STATE, "moe_stream: the streamed kernels do not apply");
+    MG_CUDA(cudaSetDevice(m->device));
+    const mg_spec &s = m->spec;
+    MoeStreamArgs ma{};
+    ma.L = m->el; ma.experts_layer = m->experts + (int64_t)layer * m->el.layer_stride;
+    ma.maps = m->map_ex; ma.layer = layer;
+    ma.n_experts = m->n_local; ma.e0 = m->e0; ma.n_tok = n_tok; ma.top_k = s.top_k; ma.sel = sel; ma.xb = m->xb;
+    ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit; ma.h = m->h; ma.y = m->moe_y;
+    ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
+    ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
+    ma.use_tc = m->tc_moe;
+    return moe_stream(ma, m->st);
 }
 
 extern "C" int mg_forward(mg_model *m, int seq, int32_t token, float *logits, int32_t *argmax) {
@@ -961,7 +1169,7 @@ extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n
             MG_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)s.vocab * 4, cudaMemcpyDeviceToHost, st));
         }
         MG_CUDA(cudaStreamSynchronize(st));
-        if (m->tc_prefill) TRY(stream_error_check());
+        if (m->tc_prefill || m->tc_dense) TRY(stream_error_check());
         m->pos[seq] += nc;
         m->expert_loads += (uint64_t)nc * s.top_k * s.n_layers;
     }
@@ -1014,8 +1222,10 @@ extern "C" int mg_model_free(mg_model *m) {
     if (!m) return MG_OK;
     cudaSetDevice(m->device);
     if (m->st) cudaStreamSynchronize(m->st);
-    for (auto &kv : m->dec_graphs)
-        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (auto *tab : {&m->dec_graphs, &m->chain_graphs})  // graphs holding collectives go before the communicator
+        for (auto &kv : *tab)
+            if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    ep_destroy(&m->ep);
     for (void *p : m->allocs) cudaFree(p);
     for (void *p : {(void *)m->h_toks, (void *)m->h_pos, (void *)m->h_seq, (void *)m->h_amax, (void *)m->h_err,
                     (void *)m->h_keys})

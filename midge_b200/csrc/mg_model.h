@@ -8,6 +8,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "mg_ep.h"
 #include "midgecuda.h"
 
 namespace mg {
@@ -22,8 +23,11 @@ struct DevMat {
 constexpr int PF_CHUNK = 1024;  // default tokens per prefill pass through the layers (MIDGE_PREFILL_CHUNK)
 constexpr int DEC_MAX = 16;     // sequences per decode step
 
+constexpr int GREEDY_MAX = 4096;  // steps per mg_decode_greedy call
+
 struct Graph {
     cudaGraphExec_t exec = nullptr;
+    int kernels = 0;  // kernel nodes in the graph
 };
 
 }  // namespace mg
@@ -40,7 +44,9 @@ struct mg_model {
     std::vector<mg::DevMat> wq, wk, wv, wo, router_w;
     std::vector<float *> bq, bk, bv, bo, router_b, attn_norm, mlp_norm, sinks, qn, kn;
 
-    mg_expert_layout el{};
+    mg_expert_layout el{};  // layout of the local blob: layer_stride = n_local experts
+    int e0 = 0, n_local = 0;  // this rank's experts [e0, e0 + n_local) (expert parallelism)
+    mg::EpComm ep;
     uint8_t *experts = nullptr;
     size_t experts_bytes = 0;
 
@@ -60,6 +66,7 @@ struct mg_model {
     float *xa = nullptr;  // post-attention residual of the streamed decode
     float *qkv = nullptr, *qkv_part = nullptr, *o_part = nullptr, *moe_y = nullptr, *rlogits = nullptr;
     unsigned long long *amax_keys = nullptr, *h_keys = nullptr;
+    unsigned *rticket = nullptr;  // last-block ticket of the decode router
     int ks_qkv = 1, ks_o = 1, ks_down = 1;
     // TMA maps of the streamed decode: per layer q, k, v, o; lm_head; experts
     std::vector<CUtensorMap> map_q, map_k, map_v, map_o;
@@ -75,13 +82,19 @@ struct mg_model {
     // tensor-core prefill of the routed experts (expert-major grouped GEMM)
     int pf_chunk = mg::PF_CHUNK;
     bool tc_prefill = false;
+    bool tc_dense = false;  // trunk q/k/v/o of prefill on the tensor cores
+    bool tc_moe = false;    // decode MoE on tcgen05 (MIDGE_MOE_KERNELS=tc); default: the mma.sync kernels
+    bool rebase_ok = false; // pf_rebase holds exact f16 rebase exponents of every expert matrix
     int *pf_counts = nullptr, *pf_offs = nullptr, *pf_cursor = nullptr, *pf_ntiles = nullptr;
     int *pf_pos = nullptr, *pf_slot = nullptr, *pf_rebase = nullptr;
     void *pf_tiles = nullptr;  // mg::XgTile[]
     __half *pf_xhi = nullptr, *pf_xlo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
     float *pf_y = nullptr;
 
-    std::unordered_map<int, mg::Graph> dec_graphs;  // keyed by n_seqs
+    std::unordered_map<int, mg::Graph> dec_graphs;    // keyed by n_seqs
+    std::unordered_map<int, mg::Graph> chain_graphs;  // device-fed greedy steps, keyed by n_seqs
+    int32_t *greedy_out = nullptr, *greedy_step = nullptr;  // [GREEDY_MAX x DEC_MAX] tokens, step counter
+    uint64_t kernel_launches = 0;  // kernels launched by the decode paths
     uint64_t expert_loads = 0;
     bool ready = false;
     bool use_graphs = true;

@@ -133,86 +133,72 @@ __global__ void __launch_bounds__(ROUTER_THREADS) k_router(RouterArgs a) {
     }
 }
 
-// Two-stage router for the decode path.  Stage 1: block (expert group of 8,
-// token) stages its 8 weight rows in shared memory with one bulk copy each,
-// norms the token (adding attention-output partials first when given; the
-// group-0 block writes the updated residual and the normed row back), and
-// computes the 8 logits in the AVX2 lane order.  Stage 2: top-k + weights.
+// Decode router in two launches.
+//   k_router_prep (block per token): residual = x + the attention-output
+//   K-split partials (summed in plane order), written to x_out; its RMS norm
+//   -> xb_out.
+//   k_router_logits (block per 8 experts, all tokens): the 8 weight rows and
+//   the tokens' normed rows are bulk-copied into shared memory (row stride
+//   padded so the 8-lane groups of a warp hit distinct banks) and every logit
+//   is reduced in the AVX2 lane order (engine/mkern.h:85-99); the last block
+//   to finish (atomic ticket) runs the top-k, routing weights and usage for
+//   all tokens.
 constexpr int RG = 8;  // experts per logits block
 
-__global__ void __launch_bounds__(256) k_router_logits(RouterArgs a, float *logits) {
-    extern __shared__ __align__(16) float rs_[];
+__global__ void __launch_bounds__(1024) k_router_prep(RouterArgs a) {
     __shared__ float scratch[32];
-    __shared__ __align__(8) uint64_t bar;
     const int64_t H = a.hidden;
-    float *ws = rs_;            // [RG][H]
-    float *xs = rs_ + RG * H;   // [H]
-    const int tok = blockIdx.y, e0 = blockIdx.x * RG;
-    const int ne = min(RG, a.n_experts - e0);
-    const uint32_t rowb = (uint32_t)(H * 4);
-    if (threadIdx.x == 0) {
-        mbar_init(&bar, 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(&bar, rowb * (uint32_t)ne);
-        for (int j = 0; j < ne; j++) bulk_g2s(ws + j * H, a.rw + (int64_t)(e0 + j) * H, rowb, &bar);
-    }
+    const int tok = blockIdx.x;
     const float *xr = a.x + (int64_t)tok * H;
+    constexpr int PER = 4;  // elements per thread per pass (loads issued together)
+    float v[PER];
     float ss = 0.f;
-    for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
-        float v = xr[i];
-        if (a.x_parts) {
-            float p = 0.f;
-            for (int k = 0; k < a.x_parts_ks; k++) p += a.x_parts[(int64_t)k * a.x_parts_stride + (int64_t)tok * H + i];
-            v = __fadd_rn(v, p);
+    for (int64_t c0 = threadIdx.x; c0 < H; c0 += (int64_t)blockDim.x * PER) {
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = c0 + (int64_t)j * blockDim.x;
+            v[j] = c < H ? xr[c] : 0.f;
         }
-        xs[i] = v;
-        ss = fmaf(v, v, ss);
+        if (a.x_parts) {
+            float p[PER] = {0.f, 0.f, 0.f, 0.f};
+            for (int k = 0; k < a.x_parts_ks; k++) {
+                const float *pp = a.x_parts + (int64_t)k * a.x_parts_stride + (int64_t)tok * H;
+#pragma unroll
+                for (int j = 0; j < PER; j++) {
+                    const int64_t c = c0 + (int64_t)j * blockDim.x;
+                    if (c < H) p[j] += pp[c];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const int64_t c = c0 + (int64_t)j * blockDim.x;
+                v[j] = __fadd_rn(v[j], p[j]);
+                if (c < H) a.x_out[(int64_t)tok * H + c] = v[j];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = c0 + (int64_t)j * blockDim.x;
+            if (c < H) {
+                ss = fmaf(v[j], v[j], ss);
+                a.xb_out[(int64_t)tok * H + c] = v[j];  // raw for now, scaled below
+            }
+        }
     }
     ss = block_sum(ss, scratch);
     const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
-    for (int64_t i = threadIdx.x; i < H; i += blockDim.x) {
-        const float v = xs[i];
-        const float nv = __fmul_rn(__fmul_rn(v, inv), a.norm_w[i]);
-        xs[i] = nv;
-        if (blockIdx.x == 0) {  // the other blocks of this token still read x: write elsewhere
-            if (a.x_parts) a.x_out[(int64_t)tok * H + i] = v;
-            a.xb_out[(int64_t)tok * H + i] = nv;
-        }
-    }
     __syncthreads();
-    bool ok = true;
-    if (threadIdx.x == 0) ok = mbar_wait(&bar, 0);
-    if (!__syncthreads_and(ok)) return;  // weights never arrived: logits stay unwritten
-    if (threadIdx.x < RG * 8) {
-        const int j = threadIdx.x >> 3, lane8 = threadIdx.x & 7;
-        const int64_t H8 = H & ~(int64_t)7;
-        float acc = 0.f;
-        if (j < ne) {
-            const float *wr = ws + j * H + lane8, *xr8 = xs + lane8;
-#pragma unroll 8
-            for (int64_t c = 0; c < H8; c += 8) acc = fmaf(wr[c], xr8[c], acc);
-        }
-        float s1 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
-        float s2 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
-        float s3 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 1));
-        if (j < ne && lane8 == 0) {
-            float r = s3;
-            for (int64_t c = H8; c < H; c++) r = __fadd_rn(r, __fmul_rn(ws[j * H + c], xs[c]));
-            logits[(int64_t)tok * a.n_experts + e0 + j] = __fadd_rn(r, a.rb[e0 + j]);
-        }
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
+        const int64_t o = (int64_t)tok * H + c;
+        a.xb_out[o] = __fmul_rn(__fmul_rn(a.xb_out[o], inv), a.norm_w[c]);
     }
 }
 
-// top-k by (value desc, index asc) among logits > -1e30, routing weights, usage
-__global__ void k_router_topk(RouterArgs a, const float *logits) {
-    __shared__ int taken[2048 / 32];
-    __shared__ int s_sel[MAX_TOPK];
-    __shared__ float s_val[MAX_TOPK];
-    const int tok = blockIdx.x, lane = threadIdx.x;
-    const float *rl = logits + (int64_t)tok * a.n_experts;
+// top-k by (value desc, index asc) among logits > -1e30, routing weights and
+// usage for token `tok`; one warp
+__device__ void router_topk_warp(const RouterArgs &a, const float *rl, int tok, int *taken, int *s_sel,
+                                 float *s_val) {
+    const int lane = threadIdx.x & 31;
     for (int i = lane; i < (a.n_experts + 31) / 32; i += 32) taken[i] = 0;
     __syncwarp();
     for (int j = 0; j < a.top_k; j++) {
@@ -267,26 +253,111 @@ __global__ void k_router_topk(RouterArgs a, const float *logits) {
             if (a.usage && s_sel[i] >= 0 && s_val[i] > -1e30f) atomicAdd(&a.usage[s_sel[i]], 1u);
         }
     }
+    __syncwarp();
 }
 
-int router_split(const RouterArgs &a, float *logits_scratch, cudaStream_t st) {
-    MG_REQUIRE(a.x && a.norm_w && a.xb_out && a.rw && a.rb && a.sel && a.weights && logits_scratch &&
+__global__ void k_router_topk(RouterArgs a, const float *logits) {
+    __shared__ int taken[2048 / 32];
+    __shared__ int s_sel[MAX_TOPK];
+    __shared__ float s_val[MAX_TOPK];
+    router_topk_warp(a, logits + (int64_t)blockIdx.x * a.n_experts, blockIdx.x, taken, s_sel, s_val);
+}
+
+constexpr int RL_THREADS = 512;  // 64 groups of 8 lanes: 8 experts x 8 tokens
+
+__global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, float *logits, unsigned *ticket) {
+    extern __shared__ __align__(16) float rs_[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ unsigned s_last;
+    __shared__ int taken[16][2048 / 32];
+    __shared__ int s_sel[16][MAX_TOPK];
+    __shared__ float s_val[16][MAX_TOPK];
+    const int64_t H = a.hidden;
+    const int64_t ld = ((H + 31) / 32) * 32 + 8;  // row stride: 8-lane groups of a warp in distinct banks
+    float *ws = rs_;                 // [RG][ld]
+    float *xs = rs_ + RG * ld;       // [n_tok][ld]
+    const int e0 = blockIdx.x * RG;
+    const int ne = min(RG, a.n_experts - e0);
+    const uint32_t rowb = (uint32_t)(H * 4);
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, rowb * (uint32_t)(ne + a.n_tok));
+        for (int j = 0; j < ne; j++) bulk_g2s(ws + j * ld, a.rw + (int64_t)(e0 + j) * H, rowb, &bar);
+        for (int t = 0; t < a.n_tok; t++) bulk_g2s(xs + t * ld, a.xb_out + (int64_t)t * H, rowb, &bar);
+    }
+    bool ok = true;
+    if (threadIdx.x == 0) ok = mbar_wait(&bar, 0);
+    if (!__syncthreads_and(ok)) {  // rows never arrived: report; the experts of this step are stale
+        if (threadIdx.x == 0 && a.err) atomicExch(a.err, 3);
+        return;
+    }
+    const int gi = threadIdx.x >> 3, lane8 = threadIdx.x & 7;
+    const int j = gi & 7, t = gi >> 3;
+    const int64_t H8 = H & ~(int64_t)7;
+    float acc = 0.f;
+    const bool live = j < ne && t < a.n_tok;
+    if (live) {
+        const float *wr = ws + j * ld + lane8, *xr8 = xs + t * ld + lane8;
+#pragma unroll 8
+        for (int64_t c = 0; c < H8; c += 8) acc = fmaf(wr[c], xr8[c], acc);
+    }
+    const float s1 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+    const float s2 = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
+    const float s3 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, 1));
+    if (live && lane8 == 0) {
+        float r = s3;
+        for (int64_t c = H8; c < H; c++) r = __fadd_rn(r, __fmul_rn(ws[j * ld + c], xs[t * ld + c]));
+        logits[(int64_t)t * a.n_experts + e0 + j] = __fadd_rn(r, a.rb[e0 + j]);
+    }
+    // the last block to finish selects the experts of every token
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(ticket, 1u) % gridDim.x == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int w = threadIdx.x >> 5;
+    for (int tok = w; tok < a.n_tok; tok += RL_THREADS / 32)
+        router_topk_warp(a, logits + (int64_t)tok * a.n_experts, tok, taken[w], s_sel[w], s_val[w]);
+    if (threadIdx.x == 0) *ticket = 0;  // ready for the next launch
+}
+
+int router_split(const RouterArgs &a, float *logits_scratch, unsigned *ticket, cudaStream_t st) {
+    MG_REQUIRE(a.x && a.norm_w && a.xb_out && a.rw && a.rb && a.sel && a.weights && logits_scratch && ticket &&
                    (!a.x_parts || (a.x_out && a.x_out != a.x)),
                MG_ERR_ARG, "router: bad arguments");
-    MG_REQUIRE(a.top_k >= 1 && a.top_k <= MAX_TOPK && a.top_k <= a.n_experts && a.n_experts <= 2048, MG_ERR_ARG,
-               "router: top_k %d / n_experts %d unsupported", a.top_k, a.n_experts);
-    MG_REQUIRE((a.hidden * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.rw) & 15) == 0, MG_ERR_ARG,
-               "router: weight rows must be 16-byte aligned");
+    MG_REQUIRE(a.top_k >= 1 && a.top_k <= MAX_TOPK && a.top_k <= a.n_experts && a.n_experts <= 2048 &&
+                   a.n_tok <= 16,
+               MG_ERR_ARG, "router: top_k %d / n_experts %d / n_tok %d unsupported", a.top_k, a.n_experts, a.n_tok);
+    MG_REQUIRE((a.hidden * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.rw) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.xb_out) & 15) == 0,
+               MG_ERR_ARG, "router: rows must be 16-byte aligned");
     if (a.n_tok == 0) return MG_OK;
-    const size_t smem = (size_t)(RG + 1) * a.hidden * 4;
-    int rc = ensure_smem(k_router_logits, smem);
-    if (rc) return rc;
-    dim3 g1((a.n_experts + RG - 1) / RG, a.n_tok);
-    k_router_logits<<<g1, 256, smem, st>>>(a, logits_scratch);
+    k_router_prep<<<a.n_tok, 1024, 0, st>>>(a);
     MG_CHECK_LAUNCH();
-    k_router_topk<<<a.n_tok, 32, 0, st>>>(a, logits_scratch);
-    MG_CHECK_LAUNCH();
-    return MG_OK;
+    const int64_t ld = ((a.hidden + 31) / 32) * 32 + 8;
+    if (a.n_tok <= 8) {
+        const size_t smem = (size_t)(RG + a.n_tok) * ld * 4;
+        if (smem <= 200 * 1024) {
+            int rc = ensure_smem(k_router_logits, smem);
+            if (rc) return rc;
+            k_router_logits<<<(a.n_experts + RG - 1) / RG, RL_THREADS, smem, st>>>(a, logits_scratch, ticket);
+            MG_CHECK_LAUNCH();
+            return MG_OK;
+        }
+    }
+    // more tokens than one block's groups: logits per token through the
+    // one-block-per-token router on the normed rows
+    RouterArgs b = a;
+    b.x = a.xb_out;
+    b.norm_w = nullptr;
+    b.x_parts = nullptr;
+    b.logits = nullptr;
+    return router(b, st);
 }
 
 int router(const RouterArgs &a, cudaStream_t st) {

@@ -13,10 +13,11 @@ namespace mg {
 
 constexpr int PF_TILE_N = 128;
 
-__global__ void k_pf_count(const int32_t *__restrict__ sel, int nslots, int n_experts, int *counts) {
+// histogram of the slots over this rank's experts (local index e - e0)
+__global__ void k_pf_count(const int32_t *__restrict__ sel, int nslots, int e0, int n_local, int *counts) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nslots; i += gridDim.x * blockDim.x) {
-        const int e = sel[i];
-        if (e >= 0 && e < n_experts) atomicAdd(&counts[e], 1);
+        const int e = sel[i] - e0;
+        if (e >= 0 && e < n_local) atomicAdd(&counts[e], 1);
     }
 }
 
@@ -38,11 +39,11 @@ __global__ void k_pf_tiles(const int *counts, int n_experts, int *offs, int *cur
 
 // expert-major position of every slot (order inside an expert is arbitrary:
 // every row of a GEMM tile is computed independently of the others)
-__global__ void k_pf_scatter(const int32_t *__restrict__ sel, int nslots, int n_experts, const int *offs, int *cursor,
-                             int *pos_of_slot, int *slot_of_pos) {
+__global__ void k_pf_scatter(const int32_t *__restrict__ sel, int nslots, int e0, int n_local, const int *offs,
+                             int *cursor, int *pos_of_slot, int *slot_of_pos) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nslots; i += gridDim.x * blockDim.x) {
-        const int e = sel[i];
-        if (e >= 0 && e < n_experts) {
+        const int e = sel[i] - e0;
+        if (e >= 0 && e < n_local) {
             const int p = offs[e] + atomicAdd(&cursor[e], 1);
             pos_of_slot[i] = p;
             slot_of_pos[p] = i;
@@ -88,9 +89,10 @@ __global__ void k_split_rows(const float *__restrict__ x, int64_t ldx, int n, in
     }
 }
 
-// x[t] += w * y per routed expert in ascending expert id (engine/midge.c:595-611, :466)
+// x[t] += w * y per routed expert in ascending expert id (engine/midge.c:595-611, :466);
+// Y is slot-major (row t*top_k + i)
 __global__ void k_pf_combine(float *x, int64_t H, const int32_t *__restrict__ sel, const float *__restrict__ w,
-                             int top_k, int n_experts, const int *__restrict__ pos_of_slot, const float *__restrict__ Y) {
+                             int top_k, int n_experts, const float *__restrict__ Y) {
     const int t = blockIdx.x;
     int ord[16];
     int k = 0;
@@ -106,8 +108,7 @@ __global__ void k_pf_combine(float *x, int64_t H, const int32_t *__restrict__ se
         float acc = xr[c];
         for (int j = 0; j < k; j++) {
             const int i = ord[j];
-            const int p = pos_of_slot[t * top_k + i];
-            acc = __fadd_rn(acc, __fmul_rn(w[t * top_k + i], Y[(int64_t)p * H + c]));
+            acc = __fadd_rn(acc, __fmul_rn(w[t * top_k + i], Y[(int64_t)(t * top_k + i) * H + c]));
         }
         xr[c] = acc;
     }
@@ -166,9 +167,7 @@ int dense_gemm(const DenseGemm &d, cudaStream_t st) {
     l.args.dense_bias = d.bias;
     l.args.M = d.rows;
     l.args.K = d.cols;
-    l.args.tiles = d.tiles;
-    l.args.ntiles = d.ntiles;
-    l.args.offs = d.zero_offs;
+    l.args.n_rows = d.n;
     l.args.y = d.y;
     l.args.ldy = d.ldy;
     l.args.accumulate = d.accumulate;
@@ -182,15 +181,16 @@ int dense_gemm(const DenseGemm &d, cudaStream_t st) {
 
 int moe_prefill(const MoePrefill &a, cudaStream_t st) {
     const int nslots = a.n * a.top_k;
-    const int E = a.n_experts;
+    const int E = a.n_local;
+    const bool ep = a.ep && a.ep->world > 1;
     MG_CUDA(cudaMemsetAsync(a.counts, 0, (size_t)E * sizeof(int), st));
     int g = ceil_div(nslots, 256);
-    k_pf_count<<<g, 256, 0, st>>>(a.sel, nslots, E, a.counts);
+    k_pf_count<<<g, 256, 0, st>>>(a.sel, nslots, a.e0, E, a.counts);
     MG_CHECK_LAUNCH();
     const int max_tiles = (nslots + PF_TILE_N - 1) / PF_TILE_N + E;
     k_pf_tiles<<<1, 32, 0, st>>>(a.counts, E, a.offs, a.cursor, a.tiles, a.ntiles, max_tiles);
     MG_CHECK_LAUNCH();
-    k_pf_scatter<<<g, 256, 0, st>>>(a.sel, nslots, E, a.offs, a.cursor, a.pos_of_slot, a.slot_of_pos);
+    k_pf_scatter<<<g, 256, 0, st>>>(a.sel, nslots, a.e0, E, a.offs, a.cursor, a.pos_of_slot, a.slot_of_pos);
     MG_CHECK_LAUNCH();
     int gg = ceil_div((int64_t)nslots * (a.L.hidden / 8), 256);
     if (gg > 148 * 16) gg = 148 * 16;
@@ -218,16 +218,22 @@ int moe_prefill(const MoePrefill &a, cudaStream_t st) {
     l.x_rows = nslots;
     int rc = xgemm(XG_GATEUP, a.L.dt, l, st);
     if (rc) return rc;
-    // down -> y
+    // down -> y (slot-major); slots of other ranks' experts stay zero
+    if (ep) MG_CUDA(cudaMemsetAsync(a.y, 0, (size_t)nslots * a.L.hidden * sizeof(float), st));
     l.args.M = a.L.hidden;
     l.args.K = a.L.ffn;
+    l.args.slot_of_pos = a.slot_of_pos;
     l.args.y = a.y;
     l.args.ldy = a.L.hidden;
     l.x_hi = a.h_hi;
     l.x_lo = a.h_lo;
     rc = xgemm(XG_DOWN, a.L.dt, l, st);
     if (rc) return rc;
-    k_pf_combine<<<a.n, 256, 0, st>>>(a.x, a.L.hidden, a.sel, a.w, a.top_k, E, a.pos_of_slot, a.y);
+    if (ep) {  // every slot's output on every rank: exact, each slot is nonzero on one rank only
+        rc = ep_allreduce_sum(*a.ep, a.y, (size_t)nslots * a.L.hidden, st);
+        if (rc) return rc;
+    }
+    k_pf_combine<<<a.n, 256, 0, st>>>(a.x, a.L.hidden, a.sel, a.w, a.top_k, a.n_experts, a.y);
     MG_CHECK_LAUNCH();
     return MG_OK;
 }

@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "mg_ep.h"
 #include "mg_gemm.h"
 #include "midgecuda.h"
 
@@ -12,7 +13,9 @@ struct MoePrefill {
     mg_expert_layout L;
     const uint8_t *experts_layer;
     const int *rebase;  // this layer's [E x 3] rebase exponents
-    int n, top_k, n_experts;
+    int n, top_k, n_experts;  // n_experts: all experts (sel holds global ids)
+    int e0, n_local;          // this rank's experts [e0, e0 + n_local), the ones in experts_layer
+    const EpComm *ep;         // sums the slot outputs over the ranks (null or world 1: local only)
     const int32_t *sel;
     const float *w;
     const float *xb;    // [n x hidden] normed inputs
@@ -24,7 +27,7 @@ struct MoePrefill {
     XgTile *tiles;
     __half *x_hi, *x_lo;  // [n*top_k x hidden]
     __half *h_hi, *h_lo;  // [n*top_k x ffn]
-    float *y;             // [n*top_k x hidden]
+    float *y;             // [n*top_k x hidden], slot-major
     int *err;
 };
 int moe_prefill(const MoePrefill &a, cudaStream_t st);
@@ -38,9 +41,6 @@ struct DenseGemm {
     float *y;
     int64_t ldy;
     int accumulate;
-    const XgTile *tiles;  // ceil(n/128) tiles {0, 128 i, min(128, n - 128 i)}
-    const int *ntiles;
-    const int *zero_offs;  // one int = 0
     int *err;
 };
 int dense_gemm(const DenseGemm &d, cudaStream_t st);

@@ -104,7 +104,7 @@ static int launch_stream_gemv(const StreamGemvArgs &a, cudaStream_t st) {
     pol.accumulate = a.accumulate;
     pol.part_stride = a.part_stride;
     pol.amax = ks == 1 ? a.amax : nullptr;
-    const size_t xs_bytes = (size_t)NT * 8 * (a.cols + XS_PAD) * 2;
+    const size_t xs_bytes = (size_t)NT * 8 * sw_xs_stride<DT>(a.cols) * 2;
     const int64_t units = tiles * ks;
     const int nsm = num_sms();
     // scale slots need every matrix's scale blob 16-byte aligned and a whole
@@ -163,6 +163,7 @@ static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
     pg.L = a.L;
     pg.experts_layer = a.experts_layer;
     pg.layer = a.layer;
+    pg.e0 = a.e0;
     pg.n_experts = a.n_experts;
     pg.n_tok = a.n_tok;
     pg.top_k = a.top_k;
@@ -178,12 +179,13 @@ static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
     const size_t ssb_gu = DT == MG_Q8R ? 0 : 2 * 64 * (size_t)(a.L.hidden / 32) * sb;
     const size_t ssb_dn = DT == MG_Q8R ? 0 : (size_t)SW_ROWS * (a.L.ffn / 32) * sb;
     int rc = launch_policy<DT>(k_stream<DT, SC, NT, PolMoeGateUp<DT, SC>>, maps, pg,
-                               (size_t)NT * 8 * (a.L.hidden + XS_PAD) * 2, ssb_gu, nsm, st);
+                               (size_t)NT * 8 * sw_xs_stride<DT>(a.L.hidden) * 2, ssb_gu, nsm, st);
     if (rc) return rc;
     PolMoeDown<DT, SC> pd{};
     pd.L = a.L;
     pd.experts_layer = a.experts_layer;
     pd.layer = a.layer;
+    pd.e0 = a.e0;
     pd.n_experts = a.n_experts;
     pd.n_tok = a.n_tok;
     pd.top_k = a.top_k;
@@ -198,7 +200,7 @@ static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
     pd.ks_count = ks;
     pd.kbytes_per_split = ((nseg + ks - 1) / ks) * SW_SEGB;
     return launch_policy<DT>(k_stream<DT, SC, NT, PolMoeDown<DT, SC>>, maps, pd,
-                             (size_t)NT * 8 * (a.L.ffn + XS_PAD) * 2, ssb_dn, nsm, st);
+                             (size_t)NT * 8 * sw_xs_stride<DT>(a.L.ffn) * 2, ssb_dn, nsm, st);
 }
 
 int moe_down_ksplit(const mg_expert_layout &L, int want) { return stream_ksplit(L.dt, L.ffn, want); }
@@ -207,6 +209,7 @@ int moe_stream(const MoeStreamArgs &a, cudaStream_t st) {
     MG_REQUIRE(a.n_tok >= 1 && a.n_tok <= 8 && a.n_tok * a.top_k <= SW_MAX_SLOTS && a.n_experts <= 2048 && a.maps,
                MG_ERR_ARG, "moe stream: n_tok %d top_k %d unsupported", a.n_tok, a.top_k);
     const mg_expert_layout &L = a.L;
+    if (a.use_tc && tmoe_supported(L, a.rebase)) return moe_tmoe(a, a.rebase, st);
     switch (L.dt) {
     case MG_MXFP4:
         if (L.scale_fmt == MG_SCALE_UE8M0)
@@ -231,23 +234,39 @@ int moe_stream(const MoeStreamArgs &a, cudaStream_t st) {
 // ----------------------------------------------- MoE combine + RMSNorm
 // x[t] += sum_i w[t][i] * sum_ks y[ks][t*k+i]   (rank order, engine/midge.c:544-548)
 // then xb[t] = rmsnorm(x[t]) * nw.  One block per token.
-__global__ void k_combine_norm(CombineNormArgs a) {
+__global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
     __shared__ float scratch[32];
+    __shared__ float s_w[16];
+    __shared__ int s_slot[16], s_k;
     const int t = blockIdx.x;
-    float *x = a.x + (int64_t)t * a.hidden;
-    const float *xi = (a.x_in ? a.x_in : a.x) + (int64_t)t * a.hidden;
+    const int64_t H = a.hidden;
+    float *x = a.x + (int64_t)t * H;
+    const float *xi = (a.x_in ? a.x_in : a.x) + (int64_t)t * H;
+    if (threadIdx.x == 0) {  // this token's valid routing slots, rank order
+        int k = 0;
+        if (a.y)
+            for (int i = 0; i < a.top_k && i < 16; i++) {
+                const int e = a.sel[t * a.top_k + i];
+                if (e < 0 || e >= a.n_experts) continue;
+                s_slot[k] = t * a.top_k + i;
+                s_w[k] = a.w[t * a.top_k + i];
+                k++;
+            }
+        s_k = k;
+    }
+    __syncthreads();
+    const int nk = s_k;
+    const int64_t plane = (int64_t)a.n_tok * a.top_k * H;
     float ss = 0.f;
-    for (int64_t c = threadIdx.x; c < a.hidden; c += blockDim.x) {
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
         float v = xi[c];
         if (a.y) {
             float moe = 0.f;
-            for (int i = 0; i < a.top_k; i++) {
-                const int e = a.sel[t * a.top_k + i];
-                if (e < 0 || e >= a.n_experts) continue;
+            for (int i = 0; i < nk; i++) {
+                const float *yp = a.y + (int64_t)s_slot[i] * H + c;
                 float yv = 0.f;
-                for (int ks = 0; ks < a.ksplit; ks++)
-                    yv += a.y[((int64_t)ks * a.n_tok * a.top_k + t * a.top_k + i) * a.hidden + c];
-                moe = __fadd_rn(moe, __fmul_rn(a.w[t * a.top_k + i], yv));
+                for (int ks = 0; ks < a.ksplit; ks++) yv += yp[ks * plane];
+                moe = __fadd_rn(moe, __fmul_rn(s_w[i], yv));
             }
             v = __fadd_rn(v, moe);
             x[c] = v;
@@ -255,10 +274,10 @@ __global__ void k_combine_norm(CombineNormArgs a) {
         ss = fmaf(v, v, ss);
     }
     ss = block_sum(ss, scratch);
-    const float inv = 1.0f / sqrtf(ss / (float)a.hidden + a.eps);
+    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
     if (a.xb)
-        for (int64_t c = threadIdx.x; c < a.hidden; c += blockDim.x)
-            a.xb[(int64_t)t * a.hidden + c] = __fmul_rn(__fmul_rn(x[c], inv), a.nw[c]);
+        for (int64_t c = threadIdx.x; c < H; c += blockDim.x)
+            a.xb[(int64_t)t * H + c] = __fmul_rn(__fmul_rn(x[c], inv), a.nw[c]);
 }
 
 int combine_norm(const CombineNormArgs &a, cudaStream_t st) {

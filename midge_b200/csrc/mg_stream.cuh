@@ -11,10 +11,10 @@
 // A stage holds 128 "MMA rows" (8 row groups of 16) x up to SEGB bytes of
 // each row.  Work is a list of units; a unit is a tile of MMA rows times a
 // range of each row's bytes (a K split), streamed as consecutive segments.
-// Two consumer warps share a row group, each taking half of every stage's
-// bytes (more warps per scheduler to hide the decode and MMA latencies); at
-// the end of a unit the second warp hands its sums to the first through
-// shared memory and the first runs the policy's epilogue.
+// Two consumer warps share a row group and take the unit's stages in turn
+// (more warps per scheduler to hide the decode and MMA latencies); at the
+// end of a unit the second warp hands its sums to the first through shared
+// memory and the first runs the policy's epilogue.
 //
 // Every wait is bounded; on timeout a kernel records an error code and stops.
 #pragma once
@@ -26,7 +26,7 @@
 namespace mg {
 
 constexpr int SW_RG = 8;                      // row groups of 16 MMA rows per stage
-constexpr int SW_KH = 2;                      // consumer warps per row group (each takes 1/SW_KH of the stage's bytes)
+constexpr int SW_KH = 2;                      // consumer warps per row group (taking alternate stages)
 constexpr int SW_CONS = SW_RG * SW_KH;        // consumer warps
 constexpr int SW_THREADS = (SW_CONS + 1) * 32;
 constexpr int SW_ROWS = SW_RG * 16;           // MMA rows per stage
@@ -125,71 +125,99 @@ __device__ void sw_producer(const P &pol, const SwMaps &maps, int64_t u0, int64_
 }
 
 // -------------------------------------------------------------- consumer
-// One warp's share of one stage: its row group's 16 MMA rows (policy
-// stage_row), chunks [kh*CPW, kh*CPW + CPW) of the stage's 128 bytes of each,
-// at activation column col0.
-template <int DT, int SC, int NT, class P>
-__device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui, const uint8_t *st, int w, int kh,
-                                               int64_t b, int nbytes, const __half *xs, int xs_stride, int nt_active,
-                                               const uint8_t *ss, float acc[NT][4]) {
-    using G = SwGeom<DT>;
-    constexpr int CPW = SW_SEGB / G::CB / SW_KH;  // chunks per warp per stage
+// Activation row stride (halves) of the streamed kernels, chosen so that the
+// 16-byte activation loads of a quarter-warp (rows g, g+1, 4 lanes t each)
+// fall in distinct bank groups: row stride = 64 B mod 128 for the 4-bit
+// layout (lanes t at 16 t), 16 B mod 32 for int8 (lanes t at 32 t).
+template <int DT>
+__host__ __device__ __forceinline__ int sw_xs_stride(int64_t cols) {
+    return (int)(((cols + 63) / 64) * 64 + (DT == MG_Q8R ? 8 : 32));
+}
+
+__device__ __forceinline__ void mma_16816_z(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// Per-lane constants of a consumer warp, fixed for the kernel: the byte
+// offsets (within a stage) of the lane's two MMA rows ra = stage_row(w, g),
+// rb = stage_row(w, g + 8), pre-XORed with their swizzle keys so that chunk c
+// is at off ^ (c << 4) (4-bit: 16-byte chunks, lane word 4t) or off ^ (c << 6)
+// (int8: 64-byte chunks, lane piece 4c + t); and the lane's activation byte
+// offset (row g of the staged activations, column piece t).
+struct SwLane {
+    uint32_t offA, offB, xoff;
+};
+
+template <int DT, class P>
+__device__ __forceinline__ SwLane sw_lane(const P &pol, int w, int xs_stride) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int ra = pol.stage_row(w, g), rb = pol.stage_row(w, g + 8);
-    const int64_t col0 = b / G::CB * G::COLS_PER_CHUNK;
-    const int nch = nbytes / G::CB;
-    const int c0 = kh * CPW;
+    SwLane L;
+    if (DT == MG_Q8R) {
+        L.offA = (uint32_t)(ra * 128 + (((t ^ (ra & 7))) << 4));
+        L.offB = (uint32_t)(rb * 128 + (((t ^ (rb & 7))) << 4));
+        L.xoff = (uint32_t)(g * xs_stride * 2 + 32 * t);
+    } else {
+        L.offA = (uint32_t)((ra * 128 + 4 * t) ^ ((ra & 7) << 4));
+        L.offB = (uint32_t)((rb * 128 + 4 * t) ^ ((rb & 7) << 4));
+        L.xoff = (uint32_t)(g * xs_stride * 2 + 16 * t);
+    }
+    return L;
+}
+
+// One warp's pass over one stage: its row group's 16 MMA rows times the
+// stage's bytes [b, b + nbytes) of each row (all chunks when FULL).
+//   st: the stage; xs8: staged activations (bytes); xs8_nt: byte distance
+//   between the two token groups (8 rows); pa, pb: the lane's rows' scales
+//   in the unit's scale slot (4-bit, when ss is used).
+template <int DT, int SC, int NT, bool FULL, class P>
+__device__ __forceinline__ void sw_stage(const P &pol, const UnitInfo &ui, const SwLane &ln, const uint8_t *st,
+                                         int64_t b, int nbytes, const uint8_t *xs8, uint32_t xs8_nt, int nt_active,
+                                         const uint8_t *pa, const uint8_t *pb, float acc[NT][4]) {
+    using G = SwGeom<DT>;
+    constexpr int CPS = SW_SEGB / G::CB;  // chunks per stage
+    const int nch = FULL ? CPS : nbytes / G::CB;
+    const int lane = threadIdx.x & 31, g = lane >> 2;
     if constexpr (DT == MG_Q8R) {
+        const uint8_t *xb = xs8 + ln.xoff + b * 2;  // column b (1 byte per column), 2 bytes per half
 #pragma unroll
-        for (int cc = 0; cc < CPW; cc++) {
-            const int c = c0 + cc;
-            if (c >= nch) break;
-            const int piece = 4 * c + t;
-            uint4 wa = *reinterpret_cast<const uint4 *>(st + sw_addr(ra, piece));
-            uint4 wb = *reinterpret_cast<const uint4 *>(st + sw_addr(rb, piece));
-            uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w}, wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+        for (int c = 0; c < CPS; c++) {
+            if (!FULL && c >= nch) break;
+            const uint4 wa = *reinterpret_cast<const uint4 *>(st + (ln.offA ^ (c << 6)));
+            const uint4 wb = *reinterpret_cast<const uint4 *>(st + (ln.offB ^ (c << 6)));
+            const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w}, wbv[4] = {wb.x, wb.y, wb.z, wb.w};
             uint32_t fa[4][4];
 #pragma unroll
-            for (int s = 0; s < 4; s++) {
-                s8x4_to_h2(wav[s], fa[s][0], fa[s][2]);
-                s8x4_to_h2(wbv[s], fa[s][1], fa[s][3]);
+            for (int q = 0; q < 4; q++) {
+                s8x4_to_h2(wav[q], fa[q][0], fa[q][2]);
+                s8x4_to_h2(wbv[q], fa[q][1], fa[q][3]);
             }
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 if (nt >= nt_active) break;
-                const __half *xp = xs + (nt * 8 + g) * xs_stride + col0 + c * 64 + 16 * t;
-                uint4 x0 = *reinterpret_cast<const uint4 *>(xp);
-                uint4 x1 = *reinterpret_cast<const uint4 *>(xp + 8);
-                uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const uint8_t *xp = xb + nt * xs8_nt + c * 128;
+                const uint4 x0 = *reinterpret_cast<const uint4 *>(xp);
+                const uint4 x1 = *reinterpret_cast<const uint4 *>(xp + 16);
+                const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-                for (int s = 0; s < 4; s++) mma_16816(acc[nt], fa[s], bx[2 * s], bx[2 * s + 1]);
+                for (int q = 0; q < 4; q++) mma_16816(acc[nt], fa[q], bx[2 * q], bx[2 * q + 1]);
             }
         }
     } else {
-        const int64_t gchunk0 = b / G::CB;  // group index of the stage's first chunk
-        float sa[CPW], sb[CPW];
-        if (ss) {
-            const uint8_t *pa = pol.scale_sm(ui, ss, g), *pb = pol.scale_sm(ui, ss, g + 8);
-            constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
+        constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
+        const int64_t gchunk0 = b / G::CB;          // group index of the stage's first chunk
+        const uint8_t *xb = xs8 + ln.xoff + b * 4;   // column 2b, 2 bytes per half
+        const uint8_t *psa = pa ? pa + gchunk0 * SB : nullptr, *psb = pb ? pb + gchunk0 * SB : nullptr;
 #pragma unroll
-            for (int cc = 0; cc < CPW; cc++) {
-                const int c = c0 + cc;
-                sa[cc] = c < nch ? scale_at<SC>(pa + (gchunk0 + c) * SB) : 0.f;
-                sb[cc] = c < nch ? scale_at<SC>(pb + (gchunk0 + c) * SB) : 0.f;
-            }
-        } else {
-#pragma unroll
-            for (int cc = 0; cc < CPW; cc++) {
-                const int c = c0 + cc;
-                sa[cc] = c < nch ? pol.scale(ui, g, gchunk0 + c) : 0.f;
-                sb[cc] = c < nch ? pol.scale(ui, g + 8, gchunk0 + c) : 0.f;
-            }
-        }
-#pragma unroll
-        for (int cc = 0; cc < CPW; cc++) {
-            const int c = c0 + cc;
-            if (c >= nch) break;
-            const uint32_t wa = lds32(st + sw_addr(ra, c) + 4 * t), wb = lds32(st + sw_addr(rb, c) + 4 * t);
+        for (int c = 0; c < CPS; c++) {
+            if (!FULL && c >= nch) break;
+            const uint32_t wa = *reinterpret_cast<const uint32_t *>(st + (ln.offA ^ (c << 4)));
+            const uint32_t wb = *reinterpret_cast<const uint32_t *>(st + (ln.offB ^ (c << 4)));
+            const float sa = psa ? scale_at<SC>(psa + c * SB) : pol.scale(ui, g, gchunk0 + c);
+            const float sb = psb ? scale_at<SC>(psb + c * SB) : pol.scale(ui, g + 8, gchunk0 + c);
             uint32_t fa[4], fb[4];
             if (DT == MG_MXFP4) {
                 e2m1x8_to_h2(wa, fa);
@@ -206,25 +234,32 @@ __device__ __forceinline__ void sw_consume_seg(const P &pol, const UnitInfo &ui,
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 if (nt >= nt_active) break;
-                const uint4 bx =
-                    *reinterpret_cast<const uint4 *>(xs + (nt * 8 + g) * xs_stride + col0 + c * 32 + 8 * t);
-                float d[4] = {0.f, 0.f, 0.f, 0.f};
-                mma_16816(d, a0, bx.x, bx.y);
+                const uint4 bx = *reinterpret_cast<const uint4 *>(xb + nt * xs8_nt + c * 64);
+                float d[4];
+                mma_16816_z(d, a0, bx.x, bx.y);
                 mma_16816(d, a1, bx.z, bx.w);
-                acc[nt][0] = fmaf(sa[cc], d[0], acc[nt][0]);
-                acc[nt][1] = fmaf(sa[cc], d[1], acc[nt][1]);
-                acc[nt][2] = fmaf(sb[cc], d[2], acc[nt][2]);
-                acc[nt][3] = fmaf(sb[cc], d[3], acc[nt][3]);
+                acc[nt][0] = fmaf(sa, d[0], acc[nt][0]);
+                acc[nt][1] = fmaf(sa, d[1], acc[nt][1]);
+                acc[nt][2] = fmaf(sb, d[2], acc[nt][2]);
+                acc[nt][3] = fmaf(sb, d[3], acc[nt][3]);
             }
         }
     }
 }
 
-// Consumer warps: per unit, accumulate its stages, then the policy epilogue.
+// Consumer warps.  The two warps of a row group take a unit's stages in
+// turn (warp kh takes the stages whose running index has parity kh), each
+// accumulating its row group's sums; at the end of the unit the second warp
+// hands its sums to the first, which runs the policy epilogue.
 template <int DT, int SC, int NT, class P>
-__device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int nstages, uint8_t *ss_base, int ssb,
-                             float *red, SwShared *sh, __half *xs, int xs_stride, int *err) {
+__device__ __forceinline__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int nstages,
+                                             uint8_t *ss_base, int ssb, float *red, SwShared *sh, __half *xs,
+                                             int xs_stride, int *err) {
     const int lane = threadIdx.x & 31, w = sw_rg(), kh = (threadIdx.x >> 5) / SW_RG;
+    const int g = lane >> 2;
+    const SwLane ln = sw_lane<DT>(pol, w, xs_stride);
+    const uint8_t *xs8 = reinterpret_cast<const uint8_t *>(xs);
+    const uint32_t xs8_nt = (uint32_t)(8 * xs_stride * 2);
     int64_t it = 0;
     // After a timed-out wait a warp stops waiting and computing but keeps
     // taking part in the named barriers, so no other warp is left waiting.
@@ -244,7 +279,7 @@ __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int 
 #pragma unroll
             for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
         const bool live = pol.warp_live(ui, w);
-        const uint8_t *ss = nullptr;
+        const uint8_t *pa = nullptr, *pb = nullptr;
         const int slot = (int)((u - u0) & 1);
         if (ssb && !failed) {
             bool ok = true;
@@ -254,9 +289,12 @@ __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int 
                 if (lane == 0) atomicExch(err, SW_ERR_TIMEOUT);
                 failed = true;
             }
-            ss = ss_base + (size_t)slot * ssb;
+            const uint8_t *ss = ss_base + (size_t)slot * ssb;
+            pa = pol.scale_sm(ui, ss, g);
+            pb = pol.scale_sm(ui, ss, g + 8);
         }
         for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
+            if ((int)(it & 1) != kh) continue;  // the other warp of the row group takes this stage
             const int s = (int)(it % nstages);
             if (!failed) {
                 bool ok = true;
@@ -267,9 +305,14 @@ __device__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uint8_t *ring, int 
                     failed = true;
                 }
             }
-            if (live && !failed)
-                sw_consume_seg<DT, SC, NT>(pol, ui, ring + (size_t)s * SW_STAGE_BYTES, w, kh, b,
-                                           (int)min((int64_t)SW_SEGB, ui.b1 - b), xs, xs_stride, nt_active, ss, acc);
+            if (live && !failed) {
+                const uint8_t *st = ring + (size_t)s * SW_STAGE_BYTES;
+                const int nbytes = (int)min((int64_t)SW_SEGB, ui.b1 - b);
+                if (nbytes == SW_SEGB)
+                    sw_stage<DT, SC, NT, true>(pol, ui, ln, st, b, nbytes, xs8, xs8_nt, nt_active, pa, pb, acc);
+                else
+                    sw_stage<DT, SC, NT, false>(pol, ui, ln, st, b, nbytes, xs8, xs8_nt, nt_active, pa, pb, acc);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh->empty[s]);
         }
@@ -318,7 +361,7 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant_
     if (threadIdx.x == 0) {
         for (int s = 0; s < nstages; s++) {
             mbar_init(&sh->full[s], 1);
-            mbar_init(&sh->empty[s], SW_CONS);
+            mbar_init(&sh->empty[s], SW_RG);  // the row-group warps that took the stage
         }
         for (int s = 0; s < 2; s++) {
             mbar_init(&sh->sfull[s], 1);
@@ -388,7 +431,7 @@ struct PolGemv {
     int bi[2];
 
     __device__ int64_t rowbytes() const { return DT == MG_Q8R ? cols : cols / 2; }
-    __device__ int xs_stride() const { return cols + XS_PAD; }
+    __device__ int xs_stride() const { return sw_xs_stride<DT>(cols); }
     __device__ void init_shared() {
         bv[0] = bv[1] = -INFINITY;
         bi[0] = bi[1] = 0x7fffffff;
@@ -505,6 +548,9 @@ struct PolGemv {
                         bv[nt] = v;
                         bi[nt] = (int)row;
                     }
+                    // the reference's scan starts from element 0 and never replaces a NaN there
+                    // (engine/midge.c:657-660): that token's argmax is 0
+                    if (amax && row == 0 && v != v) atomicMax(&amax[tok], ~0ull);
                 } else {
                     my[(int64_t)ui.ks * part_stride + (int64_t)tok * mldy + row] = v;
                 }
@@ -530,6 +576,7 @@ struct MoeCommon {
     mg_expert_layout L;
     const uint8_t *experts_layer;
     int layer;
+    int e0;  // sel holds global expert ids; this blob holds experts [e0, e0 + n_experts)
     int n_experts, n_tok, top_k;
     const int32_t *sel;
     MoeShared *ms;
@@ -542,7 +589,7 @@ struct MoeCommon {
         for (int i = threadIdx.x; i < 64; i += blockDim.x) bm[i] = 0;
         __syncthreads();
         for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            const int e = sel[i];
+            const int e = sel[i] - e0;  // local index; other ranks' experts fall outside
             if (e >= 0 && e < n_experts) atomicOr(&bm[e >> 5], 1u << (e & 31));
         }
         __syncthreads();
@@ -573,7 +620,7 @@ struct PolMoeGateUp : MoeCommon {
     float *h;
 
     __device__ int64_t rowbytes() const { return DT == MG_Q8R ? L.hidden : L.hidden / 2; }
-    __device__ int xs_stride() const { return (int)L.hidden + XS_PAD; }
+    __device__ int xs_stride() const { return sw_xs_stride<DT>(L.hidden); }
     __device__ int64_t tpe() const { return (L.ffn + 63) / 64; }
     __device__ void init_shared() {
         __shared__ MoeShared s;
@@ -648,7 +695,7 @@ struct PolMoeGateUp : MoeCommon {
             if (tok >= n_tok) continue;
             int slot = -1;
             for (int i = 0; i < top_k; i++)
-                if (sel[tok * top_k + i] == e) { slot = tok * top_k + i; break; }
+                if (sel[tok * top_k + i] == e + e0) { slot = tok * top_k + i; break; }
             if (slot < 0) continue;
             float gv = acc[nt][0] + acc[nt][1], uv = acc[nt][2] + acc[nt][3];
             if (DT == MG_Q8R) { gv = __fmul_rn(gv, sg); uv = __fmul_rn(uv, su); }
@@ -679,7 +726,7 @@ struct PolMoeDown : MoeCommon {
     int64_t kbytes_per_split;
 
     __device__ int64_t rowbytes() const { return DT == MG_Q8R ? L.ffn : L.ffn / 2; }
-    __device__ int xs_stride() const { return (int)L.ffn + XS_PAD; }
+    __device__ int xs_stride() const { return sw_xs_stride<DT>(L.ffn); }
     __device__ int64_t tpe() const { return ((L.hidden + SW_ROWS - 1) / SW_ROWS) * ks_count; }
     __device__ void init_shared() {
         __shared__ MoeShared s;
@@ -731,7 +778,7 @@ struct PolMoeDown : MoeCommon {
         if (threadIdx.x == 0) {
             int k = 0;
             for (int i = 0; i < n_tok * top_k && k < 16; i++)
-                if (sel[i] == e) ms->slots[k++] = i;
+                if (sel[i] == e + e0) ms->slots[k++] = i;
             ms->ne = k;
         }
         named_bar_sync(2, SW_CONS * 32);

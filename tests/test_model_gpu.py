@@ -132,3 +132,64 @@ def test_errors_are_status_codes(torch_cuda, c1_dir):
     m.reset(0)
     m.forward(0, 1)
     m.close()
+
+
+@pytest.mark.parametrize("kernels", ["stream", "tile"])
+def test_decode_greedy_matches_step_loop(torch_cuda, c1_dir, monkeypatch, kernels):
+    """mg_decode_greedy (argmax fed back on the device) gives exactly the
+    tokens of the host loop over mg_decode_step, for concurrent sequences."""
+    if kernels == "tile":
+        monkeypatch.setenv("MIDGE_DECODE_KERNELS", "tile")
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, 1024, 10 + 3 * i) for i in range(5)]
+    seqs = np.arange(5, dtype=np.int32)
+
+    def prefilled():
+        m = abi.Model.from_dir(c1_dir, ctx=96, max_seqs=5)
+        first = [int(np.argmax(m.forward_batch(i, p, logits_mode=1))) for i, p in enumerate(prompts)]
+        return m, np.array(first, np.int32)
+
+    a, toks = prefilled()
+    want = []
+    cur = toks.copy()
+    for _ in range(24):
+        _, cur = a.decode_step(seqs, cur)
+        want.append(np.asarray(cur, np.int32).copy())
+    u_loop = a.usage()
+    a.close()
+    b, toks_b = prefilled()
+    assert np.array_equal(toks, toks_b)
+    got = b.decode_greedy(seqs, toks_b, 24)
+    assert np.array_equal(np.stack(want), got)
+    assert np.array_equal(b.usage(), u_loop)
+    assert b.kernel_launches() > 0
+    # the sequences continue where the greedy run left them
+    _, nxt = b.decode_step(seqs, got[-1])
+    b.close()
+    a, _ = prefilled()
+    cur = toks.copy()
+    for _ in range(25):
+        _, cur = a.decode_step(seqs, cur)
+    assert np.array_equal(np.asarray(cur), np.asarray(nxt))
+    a.close()
+
+
+@pytest.mark.parametrize("moe", ["tc", "mma"])
+def test_decode_moe_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, moe):
+    """Both decode expert kernels (tcgen05 with the weights in tensor memory,
+    and the mma.sync streamed kernels) against the oracle, 8 concurrent
+    sequences, and bit-identical across the two greedy entry points."""
+    monkeypatch.setenv("MIDGE_MOE_KERNELS", moe)
+    rng = np.random.default_rng(41)
+    prompts = [rng.integers(0, 1024, 6 + i).astype(np.int32) for i in range(8)]
+    m = abi.Model.from_dir(c1_dir, ctx=64, max_seqs=8)
+    first = np.array([int(np.argmax(m.forward_batch(i, p, logits_mode=1))) for i, p in enumerate(prompts)], np.int32)
+    seqs = np.arange(8, dtype=np.int32)
+    lg, nxt = m.decode_step(seqs, first, want_logits=True)
+    for i, p in enumerate(prompts):
+        om = orc.OracleModel(c1_dir, 64)
+        om.prefill(list(p))
+        want = om.forward(int(first[i]))
+        om.close()
+        assert max_rel(want, lg[i]) < LOGIT_TOL
+    m.close()
