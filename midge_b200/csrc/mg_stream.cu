@@ -234,6 +234,7 @@ int moe_stream(const MoeStreamArgs &a, cudaStream_t st) {
 // ----------------------------------------------- MoE combine + RMSNorm
 // x[t] += sum_i w[t][i] * sum_ks y[ks][t*k+i]   (rank order, engine/midge.c:544-548)
 // then xb[t] = rmsnorm(x[t]) * nw.  One block per token.
+template <int KS>  // K-split planes of the expert outputs (compile time so their loads issue together)
 __global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
     __shared__ float scratch[32];
     __shared__ float s_w[16];
@@ -261,12 +262,31 @@ __global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
     for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
         float v = xi[c];
         if (a.y) {
+            // all of this element's plane values first (independent loads), then the
+            // reference's order: per slot the planes in order, slots in rank order
             float moe = 0.f;
-            for (int i = 0; i < nk; i++) {
-                const float *yp = a.y + (int64_t)s_slot[i] * H + c;
-                float yv = 0.f;
-                for (int ks = 0; ks < a.ksplit; ks++) yv += yp[ks * plane];
-                moe = __fadd_rn(moe, __fmul_rn(s_w[i], yv));
+            if (nk <= 8) {
+                float yv[8][KS];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float *yp = a.y + (int64_t)s_slot[i < nk ? i : 0] * H + c;
+#pragma unroll
+                    for (int ks = 0; ks < KS; ks++) yv[i][ks] = i < nk ? yp[ks * plane] : 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    float yy = 0.f;
+#pragma unroll
+                    for (int ks = 0; ks < KS; ks++) yy += yv[i][ks];
+                    if (i < nk) moe = __fadd_rn(moe, __fmul_rn(s_w[i], yy));
+                }
+            } else {
+                for (int i = 0; i < nk; i++) {
+                    const float *yp = a.y + (int64_t)s_slot[i] * H + c;
+                    float yy = 0.f;
+                    for (int ks = 0; ks < KS; ks++) yy += yp[ks * plane];
+                    moe = __fadd_rn(moe, __fmul_rn(s_w[i], yy));
+                }
             }
             v = __fadd_rn(v, moe);
             x[c] = v;
@@ -282,7 +302,13 @@ __global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
 
 int combine_norm(const CombineNormArgs &a, cudaStream_t st) {
     if (a.n_tok <= 0) return MG_OK;
-    k_combine_norm<<<a.n_tok, 1024, 0, st>>>(a);
+    switch (a.y ? a.ksplit : 1) {
+    case 1: k_combine_norm<1><<<a.n_tok, 1024, 0, st>>>(a); break;
+    case 2: k_combine_norm<2><<<a.n_tok, 1024, 0, st>>>(a); break;
+    case 3: k_combine_norm<3><<<a.n_tok, 1024, 0, st>>>(a); break;
+    case 4: k_combine_norm<4><<<a.n_tok, 1024, 0, st>>>(a); break;
+    default: set_error("combine_norm: %d K-split planes unsupported", a.ksplit); return MG_ERR_ARG;
+    }
     MG_CHECK_LAUNCH();
     return MG_OK;
 }
