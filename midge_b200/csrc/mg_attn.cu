@@ -292,6 +292,237 @@ __global__ void __launch_bounds__(PF_Q *(HD > 64 ? 2 : 1)) k_attn_prefill(AttnPr
     for (int i = 0; i < DPT; i++) a.out[(int64_t)qi * a.ldo + (int64_t)h * HD + part * DPT + i] = acc[i] * corr * inv;
 }
 
+// ---------------------------------------------- prefill attention, tensor cores
+// Flash-attention form on mma.sync (head_dim 64): block = 64 queries of one
+// head, 4 warps x 16 query rows; 64-key tiles of K and V (f16, exactly as
+// cached) double-buffered in 128-byte-swizzled shared memory by cp.async.
+//   S = Q K^T with Q split into f16 hi + lo (products exact, fp32 sums), the
+//   scale, the causal / sliding-window mask, online softmax in fp32 (row max
+//   and sum over the quad of lanes holding a row), then O += P V with P split
+//   into hi + lo the same way.  The sink joins the normaliser at the end, as
+//   engine/midge.c:376-398 does.  Agrees with the fp32 scalar kernel to ~1e-6.
+constexpr int TCA_Q = 64, TCA_K = 64, TCA_THREADS = 128;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {  // (lo -> low half, hi -> high half)
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+// f16 hi/lo pair of two values: hi = f16(v), lo = f16(v - hi)
+__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+    __half2 H = __halves2half2(ha, hb), L = __halves2half2(la, lb);
+    hi = *reinterpret_cast<uint32_t *>(&H);
+    lo = *reinterpret_cast<uint32_t *>(&L);
+}
+
+__global__ void __launch_bounds__(TCA_THREADS) k_attn_prefill_tc(AttnPrefillArgs a) {
+    constexpr int HD = 64;
+    __shared__ __align__(128) uint16_t kv_s[2][2][TCA_K * HD];  // [buffer][K, V][key][dim], swizzled
+    const int kv_dim = a.n_kv_heads * HD;
+    const int h = blockIdx.y, kh = h / (a.n_heads / a.n_kv_heads);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int q0 = blockIdx.x * TCA_Q;  // first query (chunk index) of the block
+    const int qr0 = q0 + warp * 16 + g, qr1 = qr0 + 8;
+    const bool act0 = qr0 < a.n, act1 = qr1 < a.n;
+    const int p0 = a.pos0 + qr0, p1 = a.pos0 + qr1;
+    // Q fragments (rows qr0, qr1; 4 k-steps of 16 dims), hi and lo
+    uint32_t qh[4][4], ql[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ks++) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = (i & 1) ? qr1 : qr0;
+            const bool ok = (i & 1) ? act1 : act0;
+            const int d = ks * 16 + 2 * t + (i >> 1) * 8;
+            const float *qp = a.q + (int64_t)(ok ? r : 0) * a.ldq + (int64_t)h * HD + d;
+            v[2 * i] = ok ? qp[0] : 0.f;
+            v[2 * i + 1] = ok ? qp[1] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) split2(v[2 * i], v[2 * i + 1], qh[ks][i], ql[ks][i]);
+    }
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) o[i][j] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+    const int p_first = a.pos0 + q0;
+    const int p_last = a.pos0 + min(a.n, q0 + TCA_Q) - 1;
+    const int j_lo = max(0, p_first - a.cap + 1);
+    const int ntile = (p_last - j_lo) / TCA_K + 1;
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(&kv_s[0][0][0]);
+    auto swz = [](int key, int chunk) { return (uint32_t)(key * 128 + ((chunk ^ (key & 7)) << 4)); };
+    auto load_tile = [&](int tile, int buf) {
+        const int jb = j_lo + tile * TCA_K;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int c = threadIdx.x + TCA_THREADS * i;  // 512 chunks of 16 bytes per matrix
+            const int key = c >> 3, part = c & 7;
+            const int j = jb + key;
+            const uint32_t dk = sbase + (uint32_t)((buf * 2 + 0) * TCA_K * HD * 2) + swz(key, part);
+            const uint32_t dv = sbase + (uint32_t)((buf * 2 + 1) * TCA_K * HD * 2) + swz(key, part);
+            if (j <= p_last) {
+                const uint16_t *kr, *vr;
+                if (j >= a.pos0) {
+                    kr = a.tmp_k + (int64_t)(j - a.pos0) * kv_dim;
+                    vr = a.tmp_v + (int64_t)(j - a.pos0) * kv_dim;
+                } else {
+                    const int slot = j % a.cap;
+                    kr = a.kc + ((int64_t)a.seq * a.cap + slot) * kv_dim;
+                    vr = a.vc + ((int64_t)a.seq * a.cap + slot) * kv_dim;
+                }
+                cp_async16(dk, kr + kh * HD + part * 8);
+                cp_async16(dv, vr + kh * HD + part * 8);
+            } else {  // beyond the block's last key: zeros (their P is 0, V must be finite)
+                asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dk), "r"(0) : "memory");
+                asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dv), "r"(0) : "memory");
+            }
+        }
+        cp_async_commit();
+    };
+    load_tile(0, 0);
+    for (int tile = 0; tile < ntile; tile++) {
+        const int buf = tile & 1;
+        if (tile + 1 < ntile) {
+            load_tile(tile + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const int jb = j_lo + tile * TCA_K;
+        const uint32_t kb = sbase + (uint32_t)((buf * 2 + 0) * TCA_K * HD * 2);
+        const uint32_t vb = sbase + (uint32_t)((buf * 2 + 1) * TCA_K * HD * 2);
+        // S = Q K^T: 8 n-tiles of 8 keys
+        float sc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll
+        for (int np = 0; np < 4; np++) {      // keys 16 np .. 16 np + 15
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {  // dims 16 ks .. 16 ks + 15
+                // matrices: (keys +0..7, dims +0..7), (keys +0..7, dims +8..15), (keys +8..15, dims +0..7), (+8..15, +8..15)
+                const int mi = lane >> 3, rr = lane & 7;
+                const int key = np * 16 + (mi >> 1) * 8 + rr, chunk = ks * 2 + (mi & 1);
+                uint32_t b00, b01, b10, b11;
+                ldsm_x4(kb + swz(key, chunk), b00, b01, b10, b11);
+                mma_16816(sc[2 * np], qh[ks], b00, b01);
+                mma_16816(sc[2 * np], ql[ks], b00, b01);
+                mma_16816(sc[2 * np + 1], qh[ks], b10, b11);
+                mma_16816(sc[2 * np + 1], ql[ks], b10, b11);
+            }
+        }
+        // scale, mask, online softmax (row g: elements 0,1; row g + 8: elements 2,3)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int j = jb + nt * 8 + 2 * t + (e & 1);
+                const int p = (e < 2) ? p0 : p1;
+                const bool ok = ((e < 2) ? act0 : act1) && j <= p && j > p - a.cap;
+                const float v = ok ? sc[nt][e] * a.scale : -INFINITY;
+                sc[nt][e] = v;
+                if (e < 2) mx0 = fmaxf(mx0, v);
+                else mx1 = fmaxf(mx1, v);
+            }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float c0 = mn0 == -INFINITY ? 1.f : expf(m0 - mn0), c1 = mn1 == -INFINITY ? 1.f : expf(m1 - mn1);
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float mref = e < 2 ? mn0 : mn1;
+                const float pv = sc[nt][e] == -INFINITY ? 0.f : expf(sc[nt][e] - mref);
+                sc[nt][e] = pv;
+                if (e < 2) s0 += pv;
+                else s1 += pv;
+            }
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+        s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+        l0 = l0 * c0 + s0;
+        l1 = l1 * c1 + s1;
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int dt = 0; dt < 8; dt++) {
+            o[dt][0] *= c0;
+            o[dt][1] *= c0;
+            o[dt][2] *= c1;
+            o[dt][3] *= c1;
+        }
+        // O += P V: k-steps of 16 keys, 8 n-tiles of 8 dims
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            uint32_t ph[4], pl[4];
+            split2(sc[2 * kk][0], sc[2 * kk][1], ph[0], pl[0]);
+            split2(sc[2 * kk][2], sc[2 * kk][3], ph[1], pl[1]);
+            split2(sc[2 * kk + 1][0], sc[2 * kk + 1][1], ph[2], pl[2]);
+            split2(sc[2 * kk + 1][2], sc[2 * kk + 1][3], ph[3], pl[3]);
+#pragma unroll
+            for (int dp = 0; dp < 4; dp++) {  // dims 16 dp .. 16 dp + 15
+                // transposed matrices: (keys +0..7, dims +0..7), (keys +8..15, dims +0..7), (keys +0..7, dims +8..15), (+8.., +8..)
+                const int mi = lane >> 3, rr = lane & 7;
+                const int key = kk * 16 + (mi & 1) * 8 + rr, chunk = dp * 2 + (mi >> 1);
+                uint32_t b00, b01, b10, b11;
+                ldsm_x4_t(vb + swz(key, chunk), b00, b01, b10, b11);
+                mma_16816(o[2 * dp], ph, b00, b01);
+                mma_16816(o[2 * dp], pl, b00, b01);
+                mma_16816(o[2 * dp + 1], ph, b10, b11);
+                mma_16816(o[2 * dp + 1], pl, b10, b11);
+            }
+        }
+        __syncthreads();  // the buffer is refilled by the next iteration's prefetch
+    }
+    const float sink = a.sinks ? a.sinks[h] : -INFINITY;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const bool ok = half ? act1 : act0;
+        if (!ok) continue;
+        const float m = half ? m1 : m0, l = half ? l1 : l0;
+        const float M = fmaxf(m, sink);
+        const float corr = expf(m - M);
+        const float L = l * corr + (a.sinks ? expf(sink - M) : 0.f);
+        const float inv = 1.0f / L;
+        const int r = half ? qr1 : qr0;
+        float *op = a.out + (int64_t)r * a.ldo + (int64_t)h * HD;
+#pragma unroll
+        for (int dt = 0; dt < 8; dt++) {
+            const int d = dt * 8 + 2 * t;
+            op[d] = o[dt][2 * half] * corr * inv;
+            op[d + 1] = o[dt][2 * half + 1] * corr * inv;
+        }
+    }
+}
+
 template <int HD>
 static int attn_prefill_t(const AttnPrefillArgs &a, cudaStream_t st) {
     constexpr int TPR = HD > 64 ? 2 : 1;
@@ -309,7 +540,14 @@ int attn_prefill(const AttnPrefillArgs &a, cudaStream_t st) {
     switch (a.head_dim) {
     case 16: return attn_prefill_t<16>(a, st);
     case 32: return attn_prefill_t<32>(a, st);
-    case 64: return attn_prefill_t<64>(a, st);
+    case 64:
+        if (a.use_tc) {
+            dim3 grid(ceil_div(a.n, TCA_Q), a.n_heads);
+            k_attn_prefill_tc<<<grid, TCA_THREADS, 0, st>>>(a);
+            MG_CHECK_LAUNCH();
+            return MG_OK;
+        }
+        return attn_prefill_t<64>(a, st);
     case 128: return attn_prefill_t<128>(a, st);
     }
     set_error("prefill attention: head_dim %d unsupported (16/32/64/128)", a.head_dim);

@@ -47,6 +47,7 @@ struct AttnPrefillArgs {
     const float *sinks;
     float *out;
     int64_t ldo;
+    int use_tc;  // head_dim 64: the tensor-core kernel
 };
 int attn_prefill(const AttnPrefillArgs &a, cudaStream_t st);
 

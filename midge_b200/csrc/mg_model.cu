@@ -261,6 +261,8 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     m->use_graphs = !(ng && *ng && *ng != '0');
     const char *ns = getenv("MIDGE_DECODE_KERNELS");
     m->use_stream = !(ns && !strcmp(ns, "tile"));
+    const char *ak = getenv("MIDGE_ATTN_KERNELS");
+    m->tc_attn = !(ak && !strcmp(ak, "scalar"));
     const char *mk = getenv("MIDGE_MOE_KERNELS");
     m->tc_moe = mk && !strcmp(mk, "tc");
     const char *pk = getenv("MIDGE_PREFILL_KERNELS");
@@ -763,7 +765,7 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
         pa.seq = seq; pa.pos0 = pos0; pa.n = n; pa.cap = cap;
         pa.n_heads = s.n_heads; pa.n_kv_heads = s.n_kv_heads; pa.head_dim = hd;
         pa.scale = s.attn_scale; pa.sinks = s.sinks ? m->sinks[layer] : nullptr;
-        pa.out = m->ao; pa.ldo = q_dim;
+        pa.out = m->ao; pa.ldo = q_dim; pa.use_tc = m->tc_attn;
         TRY(attn_prefill(pa, st));
         if (sliding) {
             int nst = n < cap ? n : cap;

@@ -83,6 +83,7 @@ struct mg_model {
     int pf_chunk = mg::PF_CHUNK;
     bool tc_prefill = false;
     bool tc_dense = false;  // trunk q/k/v/o of prefill on the tensor cores
+    bool tc_attn = true;    // prefill attention on the tensor cores (MIDGE_ATTN_KERNELS=scalar: fp32 kernel)
     bool tc_moe = false;    // decode MoE on tcgen05 (MIDGE_MOE_KERNELS=tc); default: the mma.sync kernels
     bool rebase_ok = false; // pf_rebase holds exact f16 rebase exponents of every expert matrix
     int *pf_counts = nullptr, *pf_offs = nullptr, *pf_cursor = nullptr, *pf_ntiles = nullptr;

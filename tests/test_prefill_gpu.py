@@ -64,3 +64,29 @@ def test_tc_prefill_chunks(torch_cuda, tmp_path, monkeypatch):
     chunked = m.forward_batch(0, prompt, logits_mode=2)
     m.close()
     assert np.array_equal(one.view(np.uint32), chunked.view(np.uint32))
+
+
+@pytest.mark.parametrize("window", [0, 40])
+def test_tc_attention_matches_scalar(torch_cuda, tmp_path, monkeypatch, window):
+    """Prefill attention on the tensor cores (Q and P split into f16 hi/lo)
+    against the fp32 kernel and the oracle: long prompt over several chunks,
+    full and sliding-window layers."""
+    spec, edt = ct.config_spec("c1_tiny")
+    spec["attn"]["sliding_window"] = window
+    if window:
+        spec["attn"]["layer_types"] = ["sliding_attention", "full_attention"]
+    md = ct.write_synthetic_model(str(tmp_path / "m"), spec, edt, seed=17)
+    prompt = np.random.default_rng(18).integers(0, 1024, 333)
+    monkeypatch.setenv("MIDGE_PREFILL_CHUNK", "128")
+    m = abi.Model.from_dir(md, ctx=400)
+    tc = m.forward_batch(0, prompt, logits_mode=2)
+    m.close()
+    monkeypatch.setenv("MIDGE_ATTN_KERNELS", "scalar")
+    m = abi.Model.from_dir(md, ctx=400)
+    sc = m.forward_batch(0, prompt, logits_mode=2)
+    m.close()
+    assert max(max_rel(sc[i], tc[i]) for i in range(0, len(prompt), 5)) < 1e-4
+    om = orc.OracleModel(md, 400)
+    want = om.prefill(list(prompt))
+    om.close()
+    assert max_rel(want, tc[-1]) < LOGIT_TOL
