@@ -115,6 +115,7 @@ struct RouterArgs {
 };
 int router(const RouterArgs &a, cudaStream_t st);
 int router_split(const RouterArgs &a, float *logits_scratch, unsigned *ticket, cudaStream_t st);  // decode
+int router_batch(const RouterArgs &a, float *logits_scratch, cudaStream_t st);                     // prefill
 
 // decode MoE FFN (gate/up + activation, then down + rank-order combine)
 struct MoeArgs {

@@ -559,7 +559,9 @@ extern "C" int mg_model_ready(mg_model *m) {
         MG_CUDA(cudaMemset(m->kc[l], 0, (size_t)m->max_seqs * c * kv_dim * 2));
         MG_CUDA(cudaMemset(m->vc[l], 0, (size_t)m->max_seqs * c * kv_dim * 2));
     }
-    const int R = m->pf_chunk > DEC_MAX ? m->pf_chunk : DEC_MAX;
+    if (m->pf_chunk > m->ctx) m->pf_chunk = m->ctx;  // a chunk never exceeds the context
+    if (m->pf_chunk < DEC_MAX) m->pf_chunk = DEC_MAX;
+    const int R = m->pf_chunk;
     m->rows_max = R;
     const int64_t H = s.hidden;
     TRY(dalloc(m, &m->x, (size_t)R * H * 4));
@@ -591,7 +593,7 @@ extern "C" int mg_model_ready(mg_model *m) {
     TRY(dalloc(m, &m->qkv_part, (size_t)m->ks_qkv * DEC_MAX * qkv_dim * 4));
     TRY(dalloc(m, &m->o_part, (size_t)m->ks_o * DEC_MAX * H * 4));
     TRY(dalloc(m, &m->moe_y, (size_t)m->ks_down * DEC_MAX * s.top_k * H * 4));
-    TRY(dalloc(m, &m->rlogits, (size_t)DEC_MAX * s.n_experts * 4));
+    TRY(dalloc(m, &m->rlogits, (size_t)R * s.n_experts * 4));  // decode and prefill router logits
     TRY(dalloc(m, &m->rticket, 16));
     MG_CUDA(cudaMemset(m->rticket, 0, 16));
     TRY(dalloc(m, &m->xa, (size_t)DEC_MAX * H * 4));
@@ -797,7 +799,8 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
     ra.n_experts = s.n_experts; ra.top_k = s.top_k; ra.router_norm = s.router_norm; ra.variant = prefill ? 1 : 0;
     ra.hidden = H; ra.n_tok = n; ra.logits = nullptr; ra.sel = m->sel; ra.weights = m->wts;
     ra.usage = m->usage + (int64_t)layer * s.n_experts;
-    TRY(router(ra, st));
+    if (prefill) TRY(router_batch(ra, m->rlogits, st));
+    else TRY(router(ra, st));
     const uint8_t *lb = m->experts + (int64_t)layer * m->el.layer_stride;
     if (prefill && m->tc_prefill) {
         MoePrefill pf{};

@@ -20,7 +20,7 @@ struct DevMat {
     void *scales = nullptr;
 };
 
-constexpr int PF_CHUNK = 1024;  // default tokens per prefill pass through the layers (MIDGE_PREFILL_CHUNK)
+constexpr int PF_CHUNK = 4096;  // default tokens per prefill pass through the layers (MIDGE_PREFILL_CHUNK)
 constexpr int DEC_MAX = 16;     // sequences per decode step
 
 constexpr int GREEDY_MAX = 4096;  // steps per mg_decode_greedy call

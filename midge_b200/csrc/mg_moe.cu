@@ -265,6 +265,8 @@ __global__ void k_router_topk(RouterArgs a, const float *logits) {
 
 constexpr int RL_THREADS = 512;  // 64 groups of 8 lanes: 8 experts x 8 tokens
 
+// blockIdx.y: group of 8 tokens; ticket null: no top-k here (a separate
+// per-token kernel runs it)
 __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, float *logits, unsigned *ticket) {
     extern __shared__ __align__(16) float rs_[];
     __shared__ __align__(8) uint64_t bar;
@@ -278,6 +280,7 @@ __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, floa
     float *xs = rs_ + RG * ld;       // [n_tok][ld]
     const int e0 = blockIdx.x * RG;
     const int ne = min(RG, a.n_experts - e0);
+    const int tok0 = blockIdx.y * 8, ntk = min(8, a.n_tok - tok0);
     const uint32_t rowb = (uint32_t)(H * 4);
     if (threadIdx.x == 0) {
         mbar_init(&bar, 1);
@@ -285,9 +288,9 @@ __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, floa
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        mbar_arrive_expect_tx(&bar, rowb * (uint32_t)(ne + a.n_tok));
+        mbar_arrive_expect_tx(&bar, rowb * (uint32_t)(ne + ntk));
         for (int j = 0; j < ne; j++) bulk_g2s(ws + j * ld, a.rw + (int64_t)(e0 + j) * H, rowb, &bar);
-        for (int t = 0; t < a.n_tok; t++) bulk_g2s(xs + t * ld, a.xb_out + (int64_t)t * H, rowb, &bar);
+        for (int t = 0; t < ntk; t++) bulk_g2s(xs + t * ld, a.xb_out + (int64_t)(tok0 + t) * H, rowb, &bar);
     }
     bool ok = true;
     if (threadIdx.x == 0) ok = mbar_wait(&bar, 0);
@@ -299,7 +302,7 @@ __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, floa
     const int j = gi & 7, t = gi >> 3;
     const int64_t H8 = H & ~(int64_t)7;
     float acc = 0.f;
-    const bool live = j < ne && t < a.n_tok;
+    const bool live = j < ne && t < ntk;
     if (live) {
         const float *wr = ws + j * ld + lane8, *xr8 = xs + t * ld + lane8;
 #pragma unroll 8
@@ -311,8 +314,9 @@ __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, floa
     if (live && lane8 == 0) {
         float r = s3;
         for (int64_t c = H8; c < H; c++) r = __fadd_rn(r, __fmul_rn(ws[j * ld + c], xs[t * ld + c]));
-        logits[(int64_t)t * a.n_experts + e0 + j] = __fadd_rn(r, a.rb[e0 + j]);
+        logits[(int64_t)(tok0 + t) * a.n_experts + e0 + j] = __fadd_rn(r, a.rb[e0 + j]);
     }
+    if (!ticket) return;
     // the last block to finish selects the experts of every token
     __threadfence();
     __syncthreads();
@@ -358,6 +362,33 @@ int router_split(const RouterArgs &a, float *logits_scratch, unsigned *ticket, c
     b.x_parts = nullptr;
     b.logits = nullptr;
     return router(b, st);
+}
+
+// Prefill router: norm (block per token), logits (8 experts x 8 tokens per
+// block, the AVX2 lane order), top-k per token with the prefill insertion
+// variant.  logits_scratch: [n_tok x E].
+int router_batch(const RouterArgs &a, float *logits_scratch, cudaStream_t st) {
+    MG_REQUIRE(a.x && a.norm_w && a.xb_out && a.rw && a.rb && a.sel && a.weights && logits_scratch && !a.x_parts,
+               MG_ERR_ARG, "router: bad arguments");
+    MG_REQUIRE(a.top_k >= 1 && a.top_k <= MAX_TOPK && a.top_k <= a.n_experts && a.n_experts <= 2048, MG_ERR_ARG,
+               "router: top_k %d / n_experts %d unsupported", a.top_k, a.n_experts);
+    MG_REQUIRE((a.hidden * 4) % 16 == 0 && (reinterpret_cast<uintptr_t>(a.rw) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.xb_out) & 15) == 0,
+               MG_ERR_ARG, "router: rows must be 16-byte aligned");
+    if (a.n_tok == 0) return MG_OK;
+    const int64_t ld = ((a.hidden + 31) / 32) * 32 + 8;
+    const size_t smem = (size_t)(RG + 8) * ld * 4;
+    if (smem > 200 * 1024) return router(a, st);
+    k_router_prep<<<a.n_tok, 1024, 0, st>>>(a);
+    MG_CHECK_LAUNCH();
+    int rc = ensure_smem(k_router_logits, smem);
+    if (rc) return rc;
+    dim3 g((a.n_experts + RG - 1) / RG, (a.n_tok + 7) / 8);
+    k_router_logits<<<g, RL_THREADS, smem, st>>>(a, logits_scratch, nullptr);
+    MG_CHECK_LAUNCH();
+    k_router_topk<<<a.n_tok, 32, 0, st>>>(a, logits_scratch);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
 }
 
 int router(const RouterArgs &a, cudaStream_t st) {
