@@ -21,6 +21,11 @@ One bench "step" = 64 decode steps of the 8 sequences (512 tokens), so
 The decode working set (~15 GB of weights per step) is far larger than L2,
 so no flush is needed between steps.
 
+--gpus N (torchrun, one rank per GPU): expert parallel -- every rank holds
+1/N of the experts and serves the same 8 sequences (trunk, attention and KV
+replicated), so value is the 8 sequences' tokens/s over the max of the ranks'
+times ("scaling": "strong").
+
 --impl reference times the reference engine (oracle/_ref/midged, built from
 the reference sources with AVX2 + OpenMP) on the host cores: its per-token
 decode on 1- and 2-layer slices of the same shape, extrapolated to 36 layers.
@@ -48,7 +53,7 @@ MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # pair, from the ncu capture summarised in
 # profiles/moe_stream_gateup_down_c4_decode8.md (per-launch traffic =
 # experts routed x this figure)
-TRAFFIC_PER_EXPERT = None
+TRAFFIC_PER_EXPERT = 13456832
 DECODE_PER_STEP = 64
 N_SEQ = 8
 
@@ -106,11 +111,11 @@ class ClockSampler:
                 "reasons": reasons}
 
 
-def build_model(torch, spec, edt, ctx, max_seqs, device=0, seed=0):
+def build_model(torch, spec, edt, ctx, max_seqs, device=0, seed=0, ep=None):
     from midge_b200 import abi
     from midge_b200 import container as ct
 
-    m = abi.Model(spec, ctx=ctx, max_seqs=max_seqs, device=device)
+    m = abi.Model(spec, ctx=ctx, max_seqs=max_seqs, device=device, ep=ep)
     rng = np.random.default_rng(seed)
     for (n, dt, shape, d, s) in ct.dense_tensors(spec, rng):
         rows = shape[0]
@@ -121,7 +126,7 @@ def build_model(torch, spec, edt, ctx, max_seqs, device=0, seed=0):
     return m
 
 
-def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40):
+def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40, rank=0, world=1):
     """Time the dominant kernel pair of the decode step live: the streamed
     routed-expert FFN (gate/up + clamped SwiGLU, then down) that the decode
     graph runs, on the resident 120b experts with decode routing of 8 tokens
@@ -140,7 +145,8 @@ def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40):
     for _ in range(reps):
         sel = np.stack([rng.permutation(E)[:k] for _ in range(N_SEQ)]).astype(np.int32)
         sels.append(torch.from_numpy(sel).cuda())
-        d = len(np.unique(sel))
+        per = E // world  # this rank's experts (expert parallel): only they are read
+        d = len([e for e in np.unique(sel) if rank * per <= e < (rank + 1) * per])
         nexp.append(d)
         nbytes.append(d * (2 * per_mat(F, H) + per_mat(H, F)) + N_SEQ * H * 4 + N_SEQ * k * F * 4 * 2
                       + 2 * N_SEQ * k * H * 4)
@@ -230,10 +236,15 @@ def run_ours(args):
     ctx = prompt_len + DECODE_PER_STEP * (args.warmup + 2 * args.steps) + 8  # value run, then the e2e run
     hbm_peak, tc_peak, peak_kind = peaks()
     t0 = time.time()
-    m = build_model(torch, spec, edt, ctx, N_SEQ, device=local, seed=rank)
+    ep_arg = None
+    if world > 1:  # expert parallel: the same model and inputs on every rank, experts sharded
+        from midge_b200 import ep as mep
+
+        ep_arg = (rank, world, mep.exchange_id(rank, world))
+    m = build_model(torch, spec, edt, ctx, N_SEQ, device=local, seed=0, ep=ep_arg)
     load_s = time.time() - t0
     stream = torch.cuda.ExternalStream(m.stream())
-    rng = np.random.default_rng(100 + rank)
+    rng = np.random.default_rng(100)
     prompts = [rng.integers(0, spec["vocab"], prompt_len).astype(np.int32) for _ in range(N_SEQ)]
 
     # prefill of the 8 prompts (device-timed on the model stream)
@@ -280,10 +291,10 @@ def run_ours(args):
         t = torch.tensor([dev_ms, wall * 1e3], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms, wall = float(t[0]), float(t[1]) / 1e3
-    ntok = N_SEQ * DECODE_PER_STEP * args.steps * world
+    ntok = N_SEQ * DECODE_PER_STEP * args.steps  # every rank serves the same 8 sequences
     value = ntok / (dev_ms / 1e3)
     e2e = ntok / wall
-    roof = moe_kernel_roofline(torch, m, spec, hbm_peak)
+    roof = moe_kernel_roofline(torch, m, spec, hbm_peak, rank=rank, world=world)
     cpu = cpu_reference(args.config) if (rank == 0 and world == 1 and not args.no_cpu) else None
     m.close()
     if rank != 0:
@@ -294,11 +305,11 @@ def run_ours(args):
         "metric": "decode tok/s (gpt-oss-120b shape, 8 concurrent sequences, greedy)",
         "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak" if world > 1 else "weak", "vs_baseline": None, "dtype": "mxfp4/int8 weights, fp32 accumulate",
+        "scaling": "strong", "vs_baseline": None, "dtype": "mxfp4/int8 weights, fp32 accumulate",
         "data": "synthetic (seeded random-init weights and token ids)",
         "config": {"workload": f"{args.config}: 8 sequences x {prompt_len}-token prompt, "
                                f"{DECODE_PER_STEP} decode steps per bench step",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": f"expert-parallel ep{world} (trunk replicated)" if world > 1 else "single GPU",
                    "l2": "working set (~15 GB/step) >> L2, no flush"},
         "prefill_tok_s": round(prefill_tok_s, 1), "prefill_wall_s": round(pf_wall, 3),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s",
@@ -350,7 +361,11 @@ def main():
     ap.add_argument("--config", default="c4_120b")
     ap.add_argument("--prompt", type=int, default=4096)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--decode-per-step", type=int, default=DECODE_PER_STEP,
+                    help="decode steps per bench step (64: the workload's 512 tokens over --steps 5 --warmup 3)")
     args = ap.parse_args()
+    global DECODE_PER_STEP
+    DECODE_PER_STEP = max(1, args.decode_per_step)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
