@@ -353,6 +353,7 @@ def run_reference(args):
 
 
 def main():
+    global DECODE_PER_STEP
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -364,7 +365,6 @@ def main():
     ap.add_argument("--decode-per-step", type=int, default=DECODE_PER_STEP,
                     help="decode steps per bench step (64: the workload's 512 tokens over --steps 5 --warmup 3)")
     args = ap.parse_args()
-    global DECODE_PER_STEP
     DECODE_PER_STEP = max(1, args.decode_per_step)
     if args.warmup < 3:
         args.warmup = 3
