@@ -231,7 +231,7 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
-    spec, edt = ct.config_spec(args.config)
+    spec, edt = ct.config_spec(args.config, args.layers)
     prompt_len = args.prompt
     ctx = prompt_len + DECODE_PER_STEP * (args.warmup + 2 * args.steps) + 8  # value run, then the e2e run
     hbm_peak, tc_peak, peak_kind = peaks()
@@ -307,7 +307,7 @@ def run_ours(args):
         "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "mxfp4/int8 weights, fp32 accumulate",
         "data": "synthetic (seeded random-init weights and token ids)",
-        "config": {"workload": f"{args.config}: 8 sequences x {prompt_len}-token prompt, "
+        "config": {"workload": f"{args.config}{'' if args.layers is None else f' ({args.layers} layers)'}: 8 sequences x {prompt_len}-token prompt, "
                                f"{DECODE_PER_STEP} decode steps per bench step",
                    "parallelism": f"expert-parallel ep{world} (trunk replicated)" if world > 1 else "single GPU",
                    "l2": "working set (~15 GB/step) >> L2, no flush"},
@@ -362,6 +362,8 @@ def main():
     ap.add_argument("--config", default="c4_120b")
     ap.add_argument("--prompt", type=int, default=4096)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="depth-reduced slice of the config (profiling captures); default: the full depth")
     ap.add_argument("--decode-per-step", type=int, default=DECODE_PER_STEP,
                     help="decode steps per bench step (64: the workload's 512 tokens over --steps 5 --warmup 3)")
     args = ap.parse_args()
