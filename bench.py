@@ -53,7 +53,7 @@ MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # pair, from the ncu capture summarised in
 # profiles/moe_stream_gateup_down_c4_decode8.md (per-launch traffic =
 # experts routed x this figure)
-TRAFFIC_PER_EXPERT = 13456832
+TRAFFIC_PER_EXPERT = 13640000
 DECODE_PER_STEP = 64
 N_SEQ = 8
 
