@@ -77,6 +77,35 @@ int qkv_post(const QkvPostArgs &a, int n_tok, cudaStream_t st) {
 // position, its K row held in registers), then each thread accumulates
 // (head, dim) outputs over the split.  Partials (max, sum, acc[hd]) go to
 // scratch for the combine.
+// ---- shared helpers of the tensor-core attention kernels
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {  // (lo -> low half, hi -> high half)
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+// f16 hi/lo pair of two values: hi = f16(v), lo = f16(v - hi)
+__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+    __half2 H = __halves2half2(ha, hb), L = __halves2half2(la, lb);
+    hi = *reinterpret_cast<uint32_t *>(&H);
+    lo = *reinterpret_cast<uint32_t *>(&L);
+}
+
 constexpr int ATTN_THREADS = 128;
 
 template <int HD>
@@ -157,6 +186,150 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnDecodeArgs a) 
     }
 }
 
+// Decode attention on the tensor cores (head_dim 64, up to 8 query heads per
+// KV head).  Block = one warp = (kv head, sequence, split of 64 positions).
+// The A operand of every MMA stacks the f16 hi halves of the group's query
+// rows (rows 0..7) over their lo halves (rows 8..15), so D rows g and g + 8
+// are the two halves of the same (head, position) and sum exactly in fp32:
+//   S = [q_hi; q_lo] K^T, softmax pieces in fp32, O = [P_hi; P_lo] V.
+// K and V tiles (64 positions x 64 dims of f16, as cached) come in by
+// cp.async into 128-byte-swizzled shared memory, read with ldmatrix.  Writes
+// the same per-split partials (max, sum, acc) as k_attn_decode.
+constexpr int TCD_POS = 64;
+
+__global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
+    constexpr int HD = 64;
+    __shared__ __align__(128) uint16_t kv[2][TCD_POS * HD];
+    const int kh = blockIdx.x, si = blockIdx.y, sp = blockIdx.z;
+    const int seq = a.seq_ids[si];
+    const int gq = a.n_heads / a.n_kv_heads, kv_dim = a.n_kv_heads * HD;
+    const int pos = a.pos[si];
+    const int nctx = pos + 1 < a.cap ? pos + 1 : a.cap;
+    const int t0 = sp * TCD_POS;
+    const int np = min(TCD_POS, nctx - t0);
+    const int lane = threadIdx.x, g = lane >> 2, t = lane & 3;
+    const int64_t pstride = (int64_t)a.max_splits * (HD + 2);
+    float *part = a.partial + ((int64_t)si * a.n_heads + kh * gq) * pstride + (int64_t)sp * (HD + 2);
+    if (np <= 0) {
+        if (lane < gq) {
+            part[lane * pstride + 0] = -INFINITY;
+            part[lane * pstride + 1] = 0.f;
+        }
+        return;
+    }
+    // positions [t0, t0 + np) of the ring, rows beyond np zero-filled
+    const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&kv[0][0]);
+    auto swz = [](int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); };
+    const uint16_t *kc = a.kc + (int64_t)seq * a.cap * kv_dim + (int64_t)kh * HD;
+    const uint16_t *vc = a.vc + (int64_t)seq * a.cap * kv_dim + (int64_t)kh * HD;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {  // 512 chunks of 16 bytes per matrix, 16 per lane
+        const int c = lane + 32 * i, r = c >> 3, part8 = c & 7;
+        const uint32_t dk = sb + swz(r, part8), dv = sb + (uint32_t)(TCD_POS * HD * 2) + swz(r, part8);
+        if (r < np) {
+            cp_async16(dk, kc + (int64_t)(t0 + r) * kv_dim + part8 * 8);
+            cp_async16(dv, vc + (int64_t)(t0 + r) * kv_dim + part8 * 8);
+        } else {
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dk), "r"(0) : "memory");
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dv), "r"(0) : "memory");
+        }
+    }
+    cp_async_commit();
+    // A fragments of [q_hi; q_lo] for the 4 k-steps (row g = head g)
+    uint32_t qa[4][4];
+    {
+        const bool hv = g < gq;
+        const float *qp = a.q + (int64_t)si * a.ldq + (int64_t)(kh * gq + (hv ? g : 0)) * HD;
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+            const int d0 = ks * 16 + 2 * t, d1 = d0 + 8;
+            const float x0 = hv ? qp[d0] : 0.f, x1 = hv ? qp[d0 + 1] : 0.f;
+            const float x2 = hv ? qp[d1] : 0.f, x3 = hv ? qp[d1 + 1] : 0.f;
+            split2(x0, x1, qa[ks][0], qa[ks][1]);  // a0: row g (hi), a1: row g + 8 (lo)
+            split2(x2, x3, qa[ks][2], qa[ks][3]);
+        }
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+    const uint32_t kb = sb, vb = sb + (uint32_t)(TCD_POS * HD * 2);
+    float sc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll
+    for (int np2 = 0; np2 < 4; np2++) {
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+            const int mi = lane >> 3, rr = lane & 7;
+            const int r = np2 * 16 + (mi >> 1) * 8 + rr, chunk = ks * 2 + (mi & 1);
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4(kb + swz(r, chunk), b00, b01, b10, b11);
+            mma_16816(sc[2 * np2], qa[ks], b00, b01);
+            mma_16816(sc[2 * np2 + 1], qa[ks], b10, b11);
+        }
+    }
+    // head g's scores at positions 8 nt + 2t (+1): hi part in c0/c1, lo part in c2/c3
+    float sv[8][2];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int p = nt * 8 + 2 * t + e;
+            const float v = p < np ? __fadd_rn(sc[nt][e], sc[nt][2 + e]) * a.scale : -INFINITY;
+            sv[nt][e] = v;
+            mx = fmaxf(mx, v);
+        }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    float sum = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const float pv = sv[nt][e] == -INFINITY ? 0.f : expf(sv[nt][e] - mx);
+            sv[nt][e] = pv;
+            sum += pv;
+        }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    // O = [P_hi; P_lo] V
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) o[i][j] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {  // positions 16 kk .. 16 kk + 15
+        uint32_t pa[4];
+        split2(sv[2 * kk][0], sv[2 * kk][1], pa[0], pa[1]);
+        split2(sv[2 * kk + 1][0], sv[2 * kk + 1][1], pa[2], pa[3]);
+#pragma unroll
+        for (int dp = 0; dp < 4; dp++) {
+            const int mi = lane >> 3, rr = lane & 7;
+            const int r = kk * 16 + (mi & 1) * 8 + rr, chunk = dp * 2 + (mi >> 1);
+            uint32_t b00, b01, b10, b11;
+            ldsm_x4_t(vb + swz(r, chunk), b00, b01, b10, b11);
+            mma_16816(o[2 * dp], pa, b00, b01);
+            mma_16816(o[2 * dp + 1], pa, b10, b11);
+        }
+    }
+    if (g < gq) {
+        float *ph = part + (int64_t)g * pstride;
+        if (t == 0) {
+            ph[0] = mx;
+            ph[1] = sum;
+        }
+#pragma unroll
+        for (int dt = 0; dt < 8; dt++) {
+            const int d = dt * 8 + 2 * t;
+            ph[2 + d] = __fadd_rn(o[dt][0], o[dt][2]);
+            ph[2 + d + 1] = __fadd_rn(o[dt][1], o[dt][3]);
+        }
+    }
+}
+
 // Combine splits and the sink:
 //   out = sum_s acc_s e^(m_s-M) / (e^(sink-M) + sum_s l_s e^(m_s-M)),  M = max(sink, m_s)
 __global__ void k_attn_combine(AttnDecodeArgs a) {
@@ -186,6 +359,15 @@ static int attn_smem_cfg(K kfn, size_t smem) {
 template <int HD>
 static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     int gq = a.n_heads / a.n_kv_heads;
+    if (HD == 64 && a.use_tc && gq <= 8 && a.split_len == TCD_POS) {
+        dim3 g1(a.n_kv_heads, n_seqs, a.max_splits);
+        k_attn_decode_tc<<<g1, 32, 0, st>>>(a);
+        MG_CHECK_LAUNCH();
+        dim3 g2(a.n_heads, n_seqs);
+        k_attn_combine<<<g2, 64, 0, st>>>(a);
+        MG_CHECK_LAUNCH();
+        return MG_OK;
+    }
     size_t smem = (size_t)(gq * HD + gq * a.split_len) * 4;
     int rc = attn_smem_cfg(k_attn_decode<HD>, smem);
     if (rc) return rc;
@@ -302,34 +484,6 @@ __global__ void __launch_bounds__(PF_Q *(HD > 64 ? 2 : 1)) k_attn_prefill(AttnPr
 //   into hi + lo the same way.  The sink joins the normaliser at the end, as
 //   engine/midge.c:376-398 does.  Agrees with the fp32 scalar kernel to ~1e-6.
 constexpr int TCA_Q = 64, TCA_K = 64, TCA_THREADS = 128;
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {  // (lo -> low half, hi -> high half)
-    __half2 h = __floats2half2_rn(lo, hi);
-    return *reinterpret_cast<uint32_t *>(&h);
-}
-// f16 hi/lo pair of two values: hi = f16(v), lo = f16(v - hi)
-__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
-    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
-    __half2 H = __halves2half2(ha, hb), L = __halves2half2(la, lb);
-    hi = *reinterpret_cast<uint32_t *>(&H);
-    lo = *reinterpret_cast<uint32_t *>(&L);
-}
 
 __global__ void __launch_bounds__(TCA_THREADS) k_attn_prefill_tc(AttnPrefillArgs a) {
     constexpr int HD = 64;

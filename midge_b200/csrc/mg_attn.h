@@ -34,6 +34,7 @@ struct AttnDecodeArgs {
     float *partial;      // [n_seqs x n_heads x max_splits x (hd+2)]
     float *out;          // [n_seqs x ldo]
     int64_t ldo;
+    int use_tc;          // head_dim 64, split_len 64: the tensor-core kernel
 };
 int attn_decode(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st);
 

@@ -783,6 +783,7 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
         da.scale = s.attn_scale; da.sinks = s.sinks ? m->sinks[layer] : nullptr;
         da.split_len = m->attn_split;
         da.max_splits = (cap + m->attn_split - 1) / m->attn_split;
+        da.use_tc = m->tc_attn;
         da.partial = m->attn_part; da.out = m->ao; da.ldo = q_dim;
         TRY(attn_decode(da, n, st));
     }
@@ -893,6 +894,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     da.n_heads = s.n_heads; da.n_kv_heads = s.n_kv_heads; da.head_dim = hd;
     da.scale = s.attn_scale; da.sinks = s.sinks ? m->sinks[layer] : nullptr;
     da.split_len = m->attn_split; da.max_splits = (cap + m->attn_split - 1) / m->attn_split;
+    da.use_tc = m->tc_attn;
     da.partial = m->attn_part; da.out = m->ao; da.ldo = q_dim;
     TRY(attn_decode(da, n, st));
     StreamGemvArgs go{};

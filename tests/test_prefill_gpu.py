@@ -78,14 +78,20 @@ def test_tc_attention_matches_scalar(torch_cuda, tmp_path, monkeypatch, window):
     md = ct.write_synthetic_model(str(tmp_path / "m"), spec, edt, seed=17)
     prompt = np.random.default_rng(18).integers(0, 1024, 333)
     monkeypatch.setenv("MIDGE_PREFILL_CHUNK", "128")
-    m = abi.Model.from_dir(md, ctx=400)
-    tc = m.forward_batch(0, prompt, logits_mode=2)
-    m.close()
+    nxt = np.random.default_rng(19).integers(0, 1024, 6)
+
+    def run():
+        m = abi.Model.from_dir(md, ctx=400)
+        lg = m.forward_batch(0, prompt, logits_mode=2)
+        dec = [m.forward(0, int(t))[0] for t in nxt]  # decode attention over the long context
+        m.close()
+        return lg, dec
+
+    tc, tc_dec = run()
     monkeypatch.setenv("MIDGE_ATTN_KERNELS", "scalar")
-    m = abi.Model.from_dir(md, ctx=400)
-    sc = m.forward_batch(0, prompt, logits_mode=2)
-    m.close()
+    sc, sc_dec = run()
     assert max(max_rel(sc[i], tc[i]) for i in range(0, len(prompt), 5)) < 1e-4
+    assert max(max_rel(a, b) for a, b in zip(sc_dec, tc_dec)) < 1e-4
     om = orc.OracleModel(md, 400)
     want = om.prefill(list(prompt))
     om.close()
