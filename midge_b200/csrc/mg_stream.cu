@@ -176,8 +176,12 @@ static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
     // scale slots: the expert blob's scale regions are 64-byte aligned and
     // padded, so a copy rounded up to 16 bytes stays inside them
     const size_t sb = SC == MG_SCALE_UE8M0 ? 1 : 2;
-    const size_t ssb_gu = DT == MG_Q8R ? 0 : 2 * 64 * (size_t)(a.L.hidden / 32) * sb;
-    const size_t ssb_dn = DT == MG_Q8R ? 0 : (size_t)SW_ROWS * (a.L.ffn / 32) * sb;
+    // (+ the tile's biases, whose runs are whole 16-byte pieces when the row
+    // counts are multiples of 4)
+    pg.bias_ss = DT != MG_Q8R && a.L.ffn % 4 == 0;
+    const size_t ssb_gu = DT == MG_Q8R ? 0 : 2 * 64 * (size_t)(a.L.hidden / 32) * sb + (pg.bias_ss ? 512 : 0);
+    const size_t ssb_dn =
+        DT == MG_Q8R ? 0 : (size_t)SW_ROWS * (a.L.ffn / 32) * sb + (a.L.hidden % 4 == 0 ? SW_ROWS * 4 : 0);
     int rc = launch_policy<DT>(k_stream<DT, SC, NT, PolMoeGateUp<DT, SC>>, maps, pg,
                                (size_t)NT * 8 * sw_xs_stride<DT>(a.L.hidden) * 2, ssb_gu, nsm, st);
     if (rc) return rc;
@@ -192,6 +196,7 @@ static int moe_stream_t(const MoeStreamArgs &a, cudaStream_t st) {
     pd.sel = a.sel;
     pd.h = a.h;
     pd.y = a.y;
+    pd.bias_ss = DT != MG_Q8R && a.L.hidden % 4 == 0;
     const int64_t rowbytes = DT == MG_Q8R ? a.L.ffn : a.L.ffn / 2;
     const int64_t nseg = (rowbytes + SW_SEGB - 1) / SW_SEGB;
     const int ks = moe_down_ksplit(a.L, a.down_ksplit);

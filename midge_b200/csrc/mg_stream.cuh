@@ -90,6 +90,8 @@ __device__ void sw_producer(const P &pol, const SwMaps &maps, int64_t u0, int64_
                             uint8_t *ss, int ssb, SwShared *sh, int *err) {
     if ((threadIdx.x & 31) != 0) return;
     int64_t it = 0, nu = 0;  // stages and scale slots issued
+    int s = 0;               // it % nstages
+    uint32_t ph = 0;         // (it / nstages) & 1
     bool ok = true;
     for (int64_t u = u0; u < u1 && ok; u++) {
         UnitInfo ui;
@@ -106,13 +108,13 @@ __device__ void sw_producer(const P &pol, const SwMaps &maps, int64_t u0, int64_
             nu = j + 1;
         }
         for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
-            const int s = (int)(it % nstages);
-            if (it >= nstages && !mbar_wait(&sh->empty[s], (uint32_t)(((it / nstages) - 1) & 1))) {
+            if (it >= nstages && !mbar_wait(&sh->empty[s], ph ^ 1u)) {
                 ok = false;
                 break;
             }
             mbar_arrive_expect_tx(&sh->full[s], SW_STAGE_BYTES);
             pol.issue(maps, ui, b, ring + (size_t)s * SW_STAGE_BYTES, &sh->full[s]);
+            if (++s == nstages) { s = 0; ph ^= 1u; }
         }
     }
     if (!ok) atomicExch(err, SW_ERR_TIMEOUT);
@@ -169,20 +171,21 @@ __device__ __forceinline__ SwLane sw_lane(const P &pol, int w, int xs_stride) {
 }
 
 // One warp's pass over one stage: its row group's 16 MMA rows times the
-// stage's bytes [b, b + nbytes) of each row (all chunks when FULL).
-//   st: the stage; xs8: staged activations (bytes); xs8_nt: byte distance
-//   between the two token groups (8 rows); pa, pb: the lane's rows' scales
-//   in the unit's scale slot (4-bit, when ss is used).
-template <int DT, int SC, int NT, bool FULL, class P>
+// stage's bytes [b, b + nbytes) of each row (all chunks when FULL), for the
+// first NTA of the NT token groups.
+//   st: the stage; xs8: staged activations (bytes); xo[nt]: the lane's byte
+//   offset in xs8 of token group nt (its activation row, column piece t);
+//   pa, pb: the lane's rows' scales in the unit's scale slot (4-bit, SS).
+template <int DT, int SC, int NT, int NTA, bool FULL, bool SS, class P>
 __device__ __forceinline__ void sw_stage(const P &pol, const UnitInfo &ui, const SwLane &ln, const uint8_t *st,
-                                         int64_t b, int nbytes, const uint8_t *xs8, uint32_t xs8_nt, int nt_active,
+                                         int64_t b, int nbytes, const uint8_t *xs8, const uint32_t xo[NT],
                                          const uint8_t *pa, const uint8_t *pb, float acc[NT][4]) {
     using G = SwGeom<DT>;
     constexpr int CPS = SW_SEGB / G::CB;  // chunks per stage
     const int nch = FULL ? CPS : nbytes / G::CB;
     const int lane = threadIdx.x & 31, g = lane >> 2;
     if constexpr (DT == MG_Q8R) {
-        const uint8_t *xb = xs8 + ln.xoff + b * 2;  // column b (1 byte per column), 2 bytes per half
+        const uint8_t *xb = xs8 + b * 2;  // column b (1 byte per column), 2 bytes per half
 #pragma unroll
         for (int c = 0; c < CPS; c++) {
             if (!FULL && c >= nch) break;
@@ -196,9 +199,8 @@ __device__ __forceinline__ void sw_stage(const P &pol, const UnitInfo &ui, const
                 s8x4_to_h2(wbv[q], fa[q][1], fa[q][3]);
             }
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                if (nt >= nt_active) break;
-                const uint8_t *xp = xb + nt * xs8_nt + c * 128;
+            for (int nt = 0; nt < NTA; nt++) {
+                const uint8_t *xp = xb + xo[nt] + c * 128;
                 const uint4 x0 = *reinterpret_cast<const uint4 *>(xp);
                 const uint4 x1 = *reinterpret_cast<const uint4 *>(xp + 16);
                 const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -209,15 +211,15 @@ __device__ __forceinline__ void sw_stage(const P &pol, const UnitInfo &ui, const
     } else {
         constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
         const int64_t gchunk0 = b / G::CB;          // group index of the stage's first chunk
-        const uint8_t *xb = xs8 + ln.xoff + b * 4;   // column 2b, 2 bytes per half
-        const uint8_t *psa = pa ? pa + gchunk0 * SB : nullptr, *psb = pb ? pb + gchunk0 * SB : nullptr;
+        const uint8_t *xb = xs8 + b * 4;   // column 2b, 2 bytes per half
+        const uint8_t *psa = SS ? pa + gchunk0 * SB : nullptr, *psb = SS ? pb + gchunk0 * SB : nullptr;
 #pragma unroll
         for (int c = 0; c < CPS; c++) {
             if (!FULL && c >= nch) break;
             const uint32_t wa = *reinterpret_cast<const uint32_t *>(st + (ln.offA ^ (c << 4)));
             const uint32_t wb = *reinterpret_cast<const uint32_t *>(st + (ln.offB ^ (c << 4)));
-            const float sa = psa ? scale_at<SC>(psa + c * SB) : pol.scale(ui, g, gchunk0 + c);
-            const float sb = psb ? scale_at<SC>(psb + c * SB) : pol.scale(ui, g + 8, gchunk0 + c);
+            const float sa = SS ? scale_at<SC>(psa + c * SB) : pol.scale(ui, g, gchunk0 + c);
+            const float sb = SS ? scale_at<SC>(psb + c * SB) : pol.scale(ui, g + 8, gchunk0 + c);
             uint32_t fa[4], fb[4];
             if (DT == MG_MXFP4) {
                 e2m1x8_to_h2(wa, fa);
@@ -232,9 +234,8 @@ __device__ __forceinline__ void sw_stage(const P &pol, const UnitInfo &ui, const
             const uint32_t a0[4] = {fa[0], fb[0], fa[1], fb[1]};
             const uint32_t a1[4] = {fa[2], fb[2], fa[3], fb[3]};
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                if (nt >= nt_active) break;
-                const uint4 bx = *reinterpret_cast<const uint4 *>(xb + nt * xs8_nt + c * 64);
+            for (int nt = 0; nt < NTA; nt++) {
+                const uint4 bx = *reinterpret_cast<const uint4 *>(xb + xo[nt] + c * 64);
                 float d[4];
                 mma_16816_z(d, a0, bx.x, bx.y);
                 mma_16816(d, a1, bx.z, bx.w);
@@ -245,6 +246,39 @@ __device__ __forceinline__ void sw_stage(const P &pol, const UnitInfo &ui, const
             }
         }
     }
+}
+
+// sw_stage with the unit's active token-group count and scale-slot use as
+// compile-time constants (no per-chunk branches)
+template <int DT, int SC, int NT, bool FULL, bool SS, class P>
+__device__ __forceinline__ void sw_stage_nt(const P &pol, const UnitInfo &ui, const SwLane &ln, const uint8_t *st,
+                                            int64_t b, int nbytes, const uint8_t *xs8, const uint32_t xo[NT],
+                                            int nt_active, const uint8_t *pa, const uint8_t *pb, float acc[NT][4]) {
+    if constexpr (NT >= 4)
+        if (nt_active >= 4) return sw_stage<DT, SC, NT, 4, FULL, SS>(pol, ui, ln, st, b, nbytes, xs8, xo, pa, pb, acc);
+    if constexpr (NT >= 3)
+        if (nt_active == 3) return sw_stage<DT, SC, NT, 3, FULL, SS>(pol, ui, ln, st, b, nbytes, xs8, xo, pa, pb, acc);
+    if constexpr (NT >= 2)
+        if (nt_active == 2) return sw_stage<DT, SC, NT, 2, FULL, SS>(pol, ui, ln, st, b, nbytes, xs8, xo, pa, pb, acc);
+    sw_stage<DT, SC, NT, 1, FULL, SS>(pol, ui, ln, st, b, nbytes, xs8, xo, pa, pb, acc);
+}
+
+template <int DT, int SC, int NT, bool SS, class P>
+__device__ __forceinline__ void sw_stage_any(const P &pol, const UnitInfo &ui, const SwLane &ln, const uint8_t *st,
+                                             int64_t b, int nbytes, const uint8_t *xs8, const uint32_t xo[NT],
+                                             int nt_active, const uint8_t *pa, const uint8_t *pb, float acc[NT][4]) {
+    if (nbytes == SW_SEGB)
+        sw_stage_nt<DT, SC, NT, true, SS>(pol, ui, ln, st, b, nbytes, xs8, xo, nt_active, pa, pb, acc);
+    else
+        sw_stage_nt<DT, SC, NT, false, SS>(pol, ui, ln, st, b, nbytes, xs8, xo, nt_active, pa, pb, acc);
+}
+
+// Default activation rows of the consumers: token group nt is staged rows
+// 8 nt .. 8 nt + 7 (token 4 nt + r/2, half r%2)
+template <int NT>
+__device__ __forceinline__ void sw_x_rows(const SwLane &ln, uint32_t xs8_nt, uint32_t xo[NT]) {
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) xo[nt] = ln.xoff + nt * xs8_nt;
 }
 
 // Consumer warps.  The two warps of a row group take a unit's stages in
@@ -260,7 +294,9 @@ __device__ __forceinline__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uin
     const SwLane ln = sw_lane<DT>(pol, w, xs_stride);
     const uint8_t *xs8 = reinterpret_cast<const uint8_t *>(xs);
     const uint32_t xs8_nt = (uint32_t)(8 * xs_stride * 2);
-    int64_t it = 0;
+    uint32_t it = 0;  // running stage index (its parity picks the warp)
+    int s = 0;        // it % nstages
+    uint32_t ph = 0;  // (it / nstages) & 1
     // After a timed-out wait a warp stops waiting and computing but keeps
     // taking part in the named barriers, so no other warp is left waiting.
     bool failed = false;
@@ -272,7 +308,8 @@ __device__ __forceinline__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uin
         }
         UnitInfo ui;
         pol.unit(u, ui);
-        const int nt_active = pol.nt_active(ui);
+        uint32_t xo[NT];
+        const int nt_active = pol.template x_rows<NT>(ui, ln, xs8_nt, xs_stride, xo);
         float acc[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; nt++)
@@ -294,11 +331,13 @@ __device__ __forceinline__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uin
             pb = pol.scale_sm(ui, ss, g + 8);
         }
         for (int64_t b = ui.b0; b < ui.b1; b += SW_SEGB, it++) {
-            if ((int)(it & 1) != kh) continue;  // the other warp of the row group takes this stage
-            const int s = (int)(it % nstages);
+            const int sc = s;
+            const uint32_t phc = ph;
+            if (++s == nstages) { s = 0; ph ^= 1u; }
+            if ((int)(it & 1u) != kh) continue;  // the other warp of the row group takes this stage
             if (!failed) {
                 bool ok = true;
-                if (lane == 0) ok = mbar_wait(&sh->full[s], (uint32_t)((it / nstages) & 1));
+                if (lane == 0) ok = mbar_wait(&sh->full[sc], phc);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) {
                     if (lane == 0) atomicExch(err, SW_ERR_TIMEOUT);
@@ -306,15 +345,15 @@ __device__ __forceinline__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uin
                 }
             }
             if (live && !failed) {
-                const uint8_t *st = ring + (size_t)s * SW_STAGE_BYTES;
+                const uint8_t *st = ring + (size_t)sc * SW_STAGE_BYTES;
                 const int nbytes = (int)min((int64_t)SW_SEGB, ui.b1 - b);
-                if (nbytes == SW_SEGB)
-                    sw_stage<DT, SC, NT, true>(pol, ui, ln, st, b, nbytes, xs8, xs8_nt, nt_active, pa, pb, acc);
+                if (DT == MG_Q8R || pa)
+                    sw_stage_any<DT, SC, NT, true>(pol, ui, ln, st, b, nbytes, xs8, xo, nt_active, pa, pb, acc);
                 else
-                    sw_stage<DT, SC, NT, false>(pol, ui, ln, st, b, nbytes, xs8, xs8_nt, nt_active, pa, pb, acc);
+                    sw_stage_any<DT, SC, NT, false>(pol, ui, ln, st, b, nbytes, xs8, xo, nt_active, pa, pb, acc);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sh->empty[s]);
+            if (lane == 0) mbar_arrive(&sh->empty[sc]);
         }
         if (live) {  // both warps of the row group agree on `live`
             float *rp = red + ((size_t)w * 32 + lane) * (NT * 4);
@@ -330,7 +369,7 @@ __device__ __forceinline__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uin
                 for (int nt = 0; nt < NT; nt++)
 #pragma unroll
                     for (int i = 0; i < 4; i++) acc[nt][i] += rp[nt * 4 + i];
-                if (!failed) pol.template epilogue<NT>(ui, w, acc);
+                if (!failed) pol.template epilogue<NT>(ui, w, acc, ssb ? ss_base + (size_t)slot * ssb : nullptr);
             }
             named_bar_sync(SW_BAR_PAIR0 + w, 64);  // the sums are read before the next unit's overwrite them
         }
@@ -515,13 +554,17 @@ struct PolGemv {
         const int w = sw_rg();
         return ss + (int64_t)(16 * w + r16) * (cols / 32) * SB;
     }
-    __device__ int nt_active(const UnitInfo &) const { return (n_tok + 3) >> 2; }
+    template <int NT>
+    __device__ int x_rows(const UnitInfo &, const SwLane &ln, uint32_t xs8_nt, int, uint32_t xo[NT]) const {
+        sw_x_rows<NT>(ln, xs8_nt, xo);
+        return (n_tok + 3) >> 2;
+    }
     __device__ bool restage(int64_t, int64_t) const { return false; }
     __device__ void stage_x(int64_t, __half *xs, int xs_stride) const {
         stage_x_n<DT>(x, ldx, n_tok, cols, xs, xs_stride, threadIdx.x, SW_CONS * 32);
     }
     template <int NT>
-    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) {
+    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4], const uint8_t *) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
         const int64_t mrows = MG_SEL(ui.aux, rows), mldy = MG_SEL(ui.aux, ldy);
         const uint8_t *msc = MG_SEL(ui.aux, sc);
@@ -582,6 +625,23 @@ struct MoeCommon {
     MoeShared *ms;
 
     __device__ const uint8_t *expert(int e) const { return experts_layer + (int64_t)e * L.expert_stride; }
+    // Warp-collective: the j-th (from 0, in slot order) of the n_tok x top_k
+    // routing slots that chose local expert e, or -1; *count (if given) gets
+    // the number of such slots.  Slot order is token order (a token picks an
+    // expert at most once).
+    __device__ int nth_slot(int e, int j, int *count) const {
+        const int n = n_tok * top_k, lane = threadIdx.x & 31;
+        int res = -1, total = 0;
+        for (int base = 0; base < n; base += 32) {
+            const int i = base + lane;
+            const unsigned m = __ballot_sync(0xffffffffu, i < n && sel[i] == e + e0);
+            const int c = __popc(m);
+            if (res < 0 && j >= total && j < total + c) res = base + (int)__fns(m, 0, j - total + 1);
+            total += c;
+        }
+        if (count) *count = total;
+        return res;
+    }
     __device__ void build_list() {
         __shared__ uint32_t bm[64];
         __shared__ int wpre[65];
@@ -615,6 +675,7 @@ struct MoeCommon {
 template <int DT, int SC>
 struct PolMoeGateUp : MoeCommon {
     const float *xb;
+    int bias_ss;  // the scale slot carries the unit's biases
     int act_plain;
     float alpha, limit;
     float *h;
@@ -658,32 +719,68 @@ struct PolMoeGateUp : MoeCommon {
         const int64_t nr = min((int64_t)64, L.ffn - ui.tile * 64);
         return round16((uint32_t)(nr * (L.hidden / 32) * SB));
     }
-    __device__ uint32_t scale_bytes(const UnitInfo &ui) const { return 2 * half_bytes(ui); }
+    // then the tile's gate biases and up biases (64 floats each) when bias_ss
+    // (ffn % 4 == 0: every tile's bias run is a multiple of 16 bytes)
+    __device__ uint32_t bias_off() const { return (uint32_t)(2 * 64 * (L.hidden / 32) * SB); }
+    __device__ uint32_t bias_bytes(const UnitInfo &ui) const {
+        return bias_ss ? (uint32_t)(min((int64_t)64, L.ffn - ui.tile * 64) * 4) : 0u;
+    }
+    __device__ uint32_t scale_bytes(const UnitInfo &ui) const { return 2 * half_bytes(ui) + 2 * bias_bytes(ui); }
     __device__ void issue_scales(const UnitInfo &ui, uint8_t *dst, uint64_t *bar) const {
         const uint8_t *eb = expert(ms->list[ui.aux]);
         const int64_t off = ui.tile * 64 * (L.hidden / 32) * SB;
         const uint32_t n = half_bytes(ui);
         bulk_g2s(dst, eb + L.off[0][1] + off, n, bar);
         bulk_g2s(dst + 64 * (L.hidden / 32) * SB, eb + L.off[1][1] + off, n, bar);
+        if (bias_ss) {
+            const uint32_t nb = bias_bytes(ui);
+            bulk_g2s(dst + bias_off(), eb + L.off[0][2] + ui.tile * 64 * 4, nb, bar);
+            bulk_g2s(dst + bias_off() + 256, eb + L.off[1][2] + ui.tile * 64 * 4, nb, bar);
+        }
     }
     __device__ const uint8_t *scale_sm(const UnitInfo &, const uint8_t *ss, int r16) const {
         const int w = sw_rg();
         return ss + (int64_t)((r16 & 8 ? 64 : 0) + 8 * w + (r16 & 7)) * (L.hidden / 32) * SB;
     }
-    __device__ int nt_active(const UnitInfo &) const { return (n_tok + 3) >> 2; }
+    // All tokens are staged once; a unit multiplies only the expert's own
+    // tokens: MMA column n of token group nt is the expert's token 4 nt + n/2
+    // (its activation rows 2 tok + n%2), columns past the expert's count read
+    // token 0 and are dropped by the epilogue.
+    template <int NT>
+    __device__ int x_rows(const UnitInfo &ui, const SwLane &ln, uint32_t, int xs_stride, uint32_t xo[NT]) const {
+        const int g = (threadIdx.x & 31) >> 2;
+        const int e = ms->list[ui.aux];
+        int ne = 0;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int slot = nth_slot(e, nt * 4 + (g >> 1), nt == 0 ? &ne : nullptr);
+            const int tok = slot >= 0 ? slot / top_k : 0;
+            xo[nt] = (uint32_t)((2 * tok + (g & 1)) * xs_stride * 2) + (ln.xoff - (uint32_t)(g * xs_stride * 2));
+        }
+        return (ne + 3) >> 2;
+    }
     __device__ bool restage(int64_t, int64_t) const { return false; }
     __device__ void stage_x(int64_t, __half *xs, int xs_stride) const {
         stage_x_n<DT>(xb, L.hidden, n_tok, (int)L.hidden, xs, xs_stride, threadIdx.x, SW_CONS * 32);
     }
     template <int NT>
-    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) const {
+    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4], const uint8_t *ss) const {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+        const int e = ms->list[ui.aux];
+        int slots[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) slots[nt] = nth_slot(e, nt * 4 + t, nullptr);  // warp-collective
         const int64_t row = ui.tile * 64 + 8 * w + g;
         if (row >= L.ffn) return;
-        const int e = ms->list[ui.aux];
         const uint8_t *eb = expert(e);
-        const float bg = reinterpret_cast<const float *>(eb + L.off[0][2])[row];
-        const float bu = reinterpret_cast<const float *>(eb + L.off[1][2])[row];
+        float bg, bu;
+        if (bias_ss && ss) {
+            bg = reinterpret_cast<const float *>(ss + bias_off())[8 * w + g];
+            bu = reinterpret_cast<const float *>(ss + bias_off())[64 + 8 * w + g];
+        } else {
+            bg = reinterpret_cast<const float *>(eb + L.off[0][2])[row];
+            bu = reinterpret_cast<const float *>(eb + L.off[1][2])[row];
+        }
         float sg = 1.f, su = 1.f;
         if (DT == MG_Q8R) {
             sg = reinterpret_cast<const float *>(eb + L.off[0][1])[row];
@@ -691,11 +788,7 @@ struct PolMoeGateUp : MoeCommon {
         }
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            const int tok = nt * 4 + t;
-            if (tok >= n_tok) continue;
-            int slot = -1;
-            for (int i = 0; i < top_k; i++)
-                if (sel[tok * top_k + i] == e + e0) { slot = tok * top_k + i; break; }
+            const int slot = slots[nt];  // MMA columns 2t, 2t+1: the expert's token 4 nt + t
             if (slot < 0) continue;
             float gv = acc[nt][0] + acc[nt][1], uv = acc[nt][2] + acc[nt][3];
             if (DT == MG_Q8R) { gv = __fmul_rn(gv, sg); uv = __fmul_rn(uv, su); }
@@ -722,6 +815,7 @@ template <int DT, int SC>
 struct PolMoeDown : MoeCommon {
     const float *h;
     float *y;
+    int bias_ss;  // the scale slot carries the unit's biases
     int ks_count;
     int64_t kbytes_per_split;
 
@@ -759,19 +853,30 @@ struct PolMoeDown : MoeCommon {
     }
     // unit scales: the tile's 128 rows, whole rows (both K splits read all of them)
     static constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
-    __device__ uint32_t scale_bytes(const UnitInfo &ui) const {
+    // then the tile's biases (128 floats) when bias_ss (hidden % 4 == 0)
+    __device__ uint32_t bias_off() const { return (uint32_t)(SW_ROWS * (L.ffn / 32) * SB); }
+    __device__ uint32_t scale_part(const UnitInfo &ui) const {
         const int64_t nr = min((int64_t)SW_ROWS, L.hidden - ui.tile * SW_ROWS);
         return round16((uint32_t)(nr * (L.ffn / 32) * SB));
     }
+    __device__ uint32_t bias_bytes(const UnitInfo &ui) const {
+        return bias_ss ? (uint32_t)(min((int64_t)SW_ROWS, L.hidden - ui.tile * SW_ROWS) * 4) : 0u;
+    }
+    __device__ uint32_t scale_bytes(const UnitInfo &ui) const { return scale_part(ui) + bias_bytes(ui); }
     __device__ void issue_scales(const UnitInfo &ui, uint8_t *dst, uint64_t *bar) const {
         const uint8_t *eb = expert(ms->list[ui.aux]);
-        bulk_g2s(dst, eb + L.off[2][1] + ui.tile * SW_ROWS * (L.ffn / 32) * SB, scale_bytes(ui), bar);
+        bulk_g2s(dst, eb + L.off[2][1] + ui.tile * SW_ROWS * (L.ffn / 32) * SB, scale_part(ui), bar);
+        if (bias_ss) bulk_g2s(dst + bias_off(), eb + L.off[2][2] + ui.tile * SW_ROWS * 4, bias_bytes(ui), bar);
     }
     __device__ const uint8_t *scale_sm(const UnitInfo &, const uint8_t *ss, int r16) const {
         const int w = sw_rg();
         return ss + (int64_t)(16 * w + r16) * (L.ffn / 32) * SB;
     }
-    __device__ int nt_active(const UnitInfo &) const { return (ms->ne + 3) >> 2; }
+    template <int NT>
+    __device__ int x_rows(const UnitInfo &, const SwLane &ln, uint32_t xs8_nt, int, uint32_t xo[NT]) const {
+        sw_x_rows<NT>(ln, xs8_nt, xo);
+        return (ms->ne + 3) >> 2;
+    }
     __device__ bool restage(int64_t u, int64_t u0) const { return u != u0 && (u / tpe()) != ((u - 1) / tpe()); }
     __device__ void stage_x(int64_t u, __half *xs, int xs_stride) const {
         const int e = ms->list[(int)(u / tpe())];
@@ -788,7 +893,7 @@ struct PolMoeDown : MoeCommon {
                           threadIdx.x, SW_CONS * 32);
     }
     template <int NT>
-    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4]) const {
+    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4], const uint8_t *ss) const {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
         const uint8_t *eb = expert(ms->list[ui.aux]);
         const int ne = ms->ne;
@@ -798,7 +903,9 @@ struct PolMoeDown : MoeCommon {
             if (row >= L.hidden) continue;
             float rs = 1.f;
             if (DT == MG_Q8R) rs = reinterpret_cast<const float *>(eb + L.off[2][1])[row];
-            const float bd = ui.ks == 0 ? reinterpret_cast<const float *>(eb + L.off[2][2])[row] : 0.f;
+            const float bd = ui.ks != 0 ? 0.f
+                             : (bias_ss && ss) ? reinterpret_cast<const float *>(ss + bias_off())[16 * w + g + 8 * half]
+                                               : reinterpret_cast<const float *>(eb + L.off[2][2])[row];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 const int j = nt * 4 + t;
