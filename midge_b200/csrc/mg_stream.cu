@@ -51,7 +51,9 @@ int stream_ksplit(int dt, int64_t cols, int want) {
 template <int DT, class P>
 static int launch_policy(void (*kfn)(SwMaps, P, int, int, int *), const SwMaps &maps, P &pol, size_t xs_bytes,
                          size_t ssb, int grid, cudaStream_t st) {
-    const size_t budget = 227 * 1024 - 2048 - 1024;  // static shared memory and the alignment slack
+    cudaFuncAttributes fa{};
+    MG_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(kfn)));
+    const size_t budget = 227 * 1024 - fa.sharedSizeBytes - 1024;  // static shared memory and the alignment slack
     ssb = (ssb + 127) & ~(size_t)127;
     xs_bytes += SW_RED_BYTES;  // the partial-sum hand-over sits just before the activations
     if (ssb && budget < 1024 + xs_bytes + 2 * ssb + 4 * (size_t)SW_STAGE_BYTES) ssb = 0;

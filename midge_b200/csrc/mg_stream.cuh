@@ -608,11 +608,12 @@ struct PolGemv {
 // maps.m[0..2] = gate, up, down of every expert of every layer as 4-D byte
 // tensors {row bytes, rows, expert, layer}.
 constexpr int SW_MAX_SLOTS = 128;  // n_tok * top_k
+constexpr int SW_MAX_TOK = 8;      // tokens per launch (a token picks an expert at most once)
 struct MoeShared {
-    int nd;
-    int list[SW_MAX_SLOTS];
-    int ne;                        // slot count of the staged expert (down)
-    int slots[16];
+    int nd;                                    // distinct local experts routed to
+    uint16_t list[SW_MAX_SLOTS];               // their local ids, ascending
+    int ecount[SW_MAX_SLOTS];                  // routing slots of list[d]
+    uint8_t eslot[SW_MAX_SLOTS][SW_MAX_TOK];   // those slots (any fixed order)
 };
 
 struct MoeCommon {
@@ -625,28 +626,17 @@ struct MoeCommon {
     MoeShared *ms;
 
     __device__ const uint8_t *expert(int e) const { return experts_layer + (int64_t)e * L.expert_stride; }
-    // Warp-collective: the j-th (from 0, in slot order) of the n_tok x top_k
-    // routing slots that chose local expert e, or -1; *count (if given) gets
-    // the number of such slots.  Slot order is token order (a token picks an
-    // expert at most once).
-    __device__ int nth_slot(int e, int j, int *count) const {
-        const int n = n_tok * top_k, lane = threadIdx.x & 31;
-        int res = -1, total = 0;
-        for (int base = 0; base < n; base += 32) {
-            const int i = base + lane;
-            const unsigned m = __ballot_sync(0xffffffffu, i < n && sel[i] == e + e0);
-            const int c = __popc(m);
-            if (res < 0 && j >= total && j < total + c) res = base + (int)__fns(m, 0, j - total + 1);
-            total += c;
-        }
-        if (count) *count = total;
-        return res;
-    }
+    // the j-th routing slot of listed expert d, or -1
+    __device__ int nth_slot(int d, int j) const { return j < ms->ecount[d] ? (int)ms->eslot[d][j] : -1; }
+    // Experts routed to (ascending local ids) and, per expert, its routing
+    // slots; the order of an expert's slots is immaterial (each is an
+    // independent MMA column and output row).
     __device__ void build_list() {
         __shared__ uint32_t bm[64];
         __shared__ int wpre[65];
         const int n = n_tok * top_k;
         for (int i = threadIdx.x; i < 64; i += blockDim.x) bm[i] = 0;
+        for (int i = threadIdx.x; i < SW_MAX_SLOTS; i += blockDim.x) ms->ecount[i] = 0;
         __syncthreads();
         for (int i = threadIdx.x; i < n; i += blockDim.x) {
             const int e = sel[i] - e0;  // local index; other ranks' experts fall outside
@@ -662,7 +652,15 @@ struct MoeCommon {
         __syncthreads();
         for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
             const uint32_t word = bm[e >> 5], bit = 1u << (e & 31);
-            if (word & bit) ms->list[wpre[e >> 5] + __popc(word & (bit - 1))] = e;
+            if (word & bit) ms->list[wpre[e >> 5] + __popc(word & (bit - 1))] = (uint16_t)e;
+        }
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const int e = sel[i] - e0;
+            if (e >= 0 && e < n_experts) {
+                const int d = wpre[e >> 5] + __popc(bm[e >> 5] & ((1u << (e & 31)) - 1u));
+                const int k = atomicAdd(&ms->ecount[d], 1);
+                if (k < SW_MAX_TOK) ms->eslot[d][k] = (uint8_t)i;
+            }
         }
         __syncthreads();
     }
@@ -691,8 +689,9 @@ struct PolMoeGateUp : MoeCommon {
     __device__ void finish() {}
     __device__ int64_t units() const { return (int64_t)ms->nd * tpe(); }
     __device__ void unit(int64_t u, UnitInfo &ui) const {
-        ui.aux = (int)(u / tpe());
-        ui.tile = u % tpe();
+        const int tp = (int)tpe();
+        ui.aux = (int)u / tp;
+        ui.tile = (int)u - ui.aux * tp;
         ui.ks = 0;
         ui.b0 = 0;
         ui.b1 = rowbytes();
@@ -749,11 +748,10 @@ struct PolMoeGateUp : MoeCommon {
     template <int NT>
     __device__ int x_rows(const UnitInfo &ui, const SwLane &ln, uint32_t, int xs_stride, uint32_t xo[NT]) const {
         const int g = (threadIdx.x & 31) >> 2;
-        const int e = ms->list[ui.aux];
-        int ne = 0;
+        const int ne = min(ms->ecount[ui.aux], SW_MAX_TOK);
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            const int slot = nth_slot(e, nt * 4 + (g >> 1), nt == 0 ? &ne : nullptr);
+            const int slot = nth_slot(ui.aux, nt * 4 + (g >> 1));
             const int tok = slot >= 0 ? slot / top_k : 0;
             xo[nt] = (uint32_t)((2 * tok + (g & 1)) * xs_stride * 2) + (ln.xoff - (uint32_t)(g * xs_stride * 2));
         }
@@ -767,9 +765,6 @@ struct PolMoeGateUp : MoeCommon {
     __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4], const uint8_t *ss) const {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
         const int e = ms->list[ui.aux];
-        int slots[NT];
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++) slots[nt] = nth_slot(e, nt * 4 + t, nullptr);  // warp-collective
         const int64_t row = ui.tile * 64 + 8 * w + g;
         if (row >= L.ffn) return;
         const uint8_t *eb = expert(e);
@@ -788,7 +783,7 @@ struct PolMoeGateUp : MoeCommon {
         }
 #pragma unroll
         for (int nt = 0; nt < NT; nt++) {
-            const int slot = slots[nt];  // MMA columns 2t, 2t+1: the expert's token 4 nt + t
+            const int slot = nth_slot(ui.aux, nt * 4 + t);  // MMA columns 2t, 2t+1: the expert's slot 4 nt + t
             if (slot < 0) continue;
             float gv = acc[nt][0] + acc[nt][1], uv = acc[nt][2] + acc[nt][3];
             if (DT == MG_Q8R) { gv = __fmul_rn(gv, sg); uv = __fmul_rn(uv, su); }
@@ -830,10 +825,11 @@ struct PolMoeDown : MoeCommon {
     __device__ void finish() {}
     __device__ int64_t units() const { return (int64_t)ms->nd * tpe(); }
     __device__ void unit(int64_t u, UnitInfo &ui) const {
-        ui.aux = (int)(u / tpe());
-        const int64_t r = u % tpe();
+        const int tp = (int)tpe();
+        ui.aux = (int)u / tp;
+        const int r = (int)u - ui.aux * tp;
         ui.tile = r / ks_count;
-        ui.ks = (int)(r % ks_count);
+        ui.ks = r - (r / ks_count) * ks_count;
         ui.b0 = (int64_t)ui.ks * kbytes_per_split;
         ui.b1 = min(rowbytes(), ui.b0 + kbytes_per_split);
     }
@@ -873,30 +869,23 @@ struct PolMoeDown : MoeCommon {
         return ss + (int64_t)(16 * w + r16) * (L.ffn / 32) * SB;
     }
     template <int NT>
-    __device__ int x_rows(const UnitInfo &, const SwLane &ln, uint32_t xs8_nt, int, uint32_t xo[NT]) const {
+    __device__ int x_rows(const UnitInfo &ui, const SwLane &ln, uint32_t xs8_nt, int, uint32_t xo[NT]) const {
         sw_x_rows<NT>(ln, xs8_nt, xo);
-        return (ms->ne + 3) >> 2;
+        return (min(ms->ecount[ui.aux], SW_MAX_TOK) + 3) >> 2;
     }
-    __device__ bool restage(int64_t u, int64_t u0) const { return u != u0 && (u / tpe()) != ((u - 1) / tpe()); }
+    __device__ bool restage(int64_t u, int64_t u0) const { return u != u0 && unit_expert(u) != unit_expert(u - 1); }
+    __device__ int unit_expert(int64_t u) const { return (int)u / (int)tpe(); }
+    // the expert's slots' h rows: slot j at activation rows 2j, 2j + 1
     __device__ void stage_x(int64_t u, __half *xs, int xs_stride) const {
-        const int e = ms->list[(int)(u / tpe())];
-        if (threadIdx.x == 0) {
-            int k = 0;
-            for (int i = 0; i < n_tok * top_k && k < 16; i++)
-                if (sel[i] == e + e0) ms->slots[k++] = i;
-            ms->ne = k;
-        }
-        named_bar_sync(2, SW_CONS * 32);
-        const int ne = ms->ne;
+        const int d = unit_expert(u), ne = min(ms->ecount[d], SW_MAX_TOK);
         for (int j = 0; j < ne; j++)
-            stage_x_n<DT>(h + (int64_t)ms->slots[j] * L.ffn, L.ffn, 1, (int)L.ffn, xs + 2 * j * xs_stride, xs_stride,
-                          threadIdx.x, SW_CONS * 32);
+            stage_x_n<DT>(h + (int64_t)ms->eslot[d][j] * L.ffn, L.ffn, 1, (int)L.ffn, xs + 2 * j * xs_stride,
+                          xs_stride, threadIdx.x, SW_CONS * 32);
     }
     template <int NT>
     __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4], const uint8_t *ss) const {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
         const uint8_t *eb = expert(ms->list[ui.aux]);
-        const int ne = ms->ne;
 #pragma unroll
         for (int half = 0; half < 2; half++) {
             const int64_t row = ui.tile * SW_ROWS + 16 * w + g + 8 * half;
@@ -908,12 +897,12 @@ struct PolMoeDown : MoeCommon {
                                                : reinterpret_cast<const float *>(eb + L.off[2][2])[row];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                const int j = nt * 4 + t;
-                if (j >= ne) continue;
+                const int slot = nth_slot(ui.aux, nt * 4 + t);
+                if (slot < 0) continue;
                 float v = acc[nt][2 * half] + acc[nt][2 * half + 1];
                 if (DT == MG_Q8R) v = __fmul_rn(v, rs);
                 v = __fadd_rn(v, bd);
-                y[((int64_t)ui.ks * n_tok * top_k + ms->slots[j]) * L.hidden + row] = v;
+                y[((int64_t)ui.ks * n_tok * top_k + slot) * L.hidden + row] = v;
             }
         }
     }
