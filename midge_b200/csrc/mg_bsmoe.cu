@@ -1,0 +1,606 @@
+// mg_bsmoe.cu -- decode-time routed experts (MXFP4, ue8m0 group scales) on
+// block-scaled tcgen05 MMAs: tcgen05.mma.kind::mxf4.block_scale.block32.
+//
+// The tensor core reads the e2m1 weights and their ue8m0 group scales as
+// they are stored (engine/mten.h:136 expert layout; the scale of 32 weights
+// is 2^(code - 127), the reference's dequant), so no SM instruction is spent
+// per weight:
+//   * A (weights): TMA copies each K-stage of 128 bytes (256 packed e2m1
+//     values) of 128 rows from HBM into shared memory (128-byte swizzle,
+//     K-major); gate/up stages hold 64 gate rows then the 64 up rows of the
+//     same outputs, down stages 128 rows.  The ragged end of a row is
+//     zero-filled by the TMA bounds.
+//   * B (activations): each activation row x is written as 12 e2m1 limbs,
+//     x = sum_l q_l 2^(c_l,b - 127), with one ue8m0 code per limb and block of
+//     32 values: limb l quantises the residual of limbs < l at a scale 4x
+//     below limb l-1's (round-to-nearest leaves less than half a step, so the
+//     scaled residual stays below 4 and never saturates), i.e. 2 bits per
+//     limb, 24 bits below the block maximum.  A token owns 16 B rows (MMA
+//     columns); rows 12..15 stay zero.
+//   * scale factors: per stage the 128 A rows x 8 blocks and the B rows x 8
+//     blocks are laid out as 32 x 16-byte atoms (4 blocks each) and copied
+//     into TMEM with tcgen05.cp.32x128b.warpx4; an MMA (K = 64) reads two
+//     blocks, selected by its scale-factor id (0 or 2).
+//   * D (fp32, TMEM): 128 output rows x 16 columns per token; the epilogue
+//     sums each token's 16 limb columns.
+// Each unit multiplies one expert's weight tile by up to 4 of its routed
+// tokens (the MMA cost does not depend on N up to 64 columns); an expert with
+// more routed tokens takes a second token group.
+//
+// Warp roles (320 threads, one CTA per SM, persistent over the units):
+//   warp 0     producer: per unit the 128 rows' scales and the group's B
+//              scale words by bulk copy into one of two slots; per stage the
+//              A box(es) and the group's B rows by TMA into a ring
+//   warp 1     MMA issuer (one thread): per stage tcgen05.cp of the four
+//              scale atoms, 4 MMAs of K = 64, commit -> the stage is free;
+//              per unit commit -> accumulator buffer ready (2 buffers)
+//   warps 2-5  scale-factor atoms: per stage the A atoms (from the unit's
+//              slot; blocks past K get code 127) and the B atoms
+//   warps 6-9  epilogue (TMEM lane quadrant = warp % 4): limb sums; gate/up:
+//              bias, clamped SwiGLU (engine/midge.c:386-392) and the h values
+//              re-encoded as 12 limbs for the down pass; down: bias in split
+//              0 and the per-slot partial sums y[ks][slot][row]
+// Every wait is bounded: a timed-out wait sets the error word and the role
+// stops; the producer waits for its copies in flight and the MMA issuer for
+// its MMAs before the CTA exits.
+#include "mg_bsmoe.h"
+#include "mg_stream.cuh"
+#include "mg_tc.cuh"
+
+namespace mg {
+
+#define BS_TRY(expr)                  \
+    do {                              \
+        int _rc = (expr);             \
+        if (_rc != MG_OK) return _rc; \
+    } while (0)
+
+typedef CUresult (*BsEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                               const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+constexpr int BS_LIMBS = 16;                           // B rows (MMA columns) per token
+constexpr int BS_LQ = 12;                              // of which encoded limbs
+constexpr int BS_KE = 256;                             // K values per stage (128 packed bytes)
+constexpr int BS_TOKG = 4;                             // tokens per unit
+constexpr int BS_A_BYTES = 128 * 128;                  // A stage: 128 rows x 128 B
+constexpr int BS_B_TOK = BS_LIMBS * 128;               // B rows of one token per stage: 16 x 128 B
+constexpr int BS_B_BYTES = BS_TOKG * BS_B_TOK;
+constexpr int BS_STAGE = BS_A_BYTES + BS_B_BYTES;      // 24 KB, 1024-aligned
+constexpr int BS_ATOMS = 2048;                         // 2 A atoms + 2 B atoms per stage
+constexpr int BS_MAX_STAGES = 8;
+constexpr int BS_THREADS = 320;
+constexpr int BS_TMEM_COLS = 256;                      // 2 accumulators x 64 columns + 8 stages x 16 scale columns
+constexpr int BS_SF_COL0 = 128;
+constexpr int BS_MAX_V = 2 * SW_MAX_SLOTS;             // token groups (experts x up to 2)
+constexpr int BS_ERR_TIMEOUT = 1;
+
+struct BsBars {
+    uint64_t full[BS_MAX_STAGES], empty[BS_MAX_STAGES], sfready[BS_MAX_STAGES];
+    uint64_t sfull[2], sempty[2], accfull[2], accempty[2];
+    uint64_t done;  // the MMA issuer's last commit: no MMA is in flight when TMEM is released
+    uint32_t tmem;
+};
+
+struct BsMapsK {
+    CUtensorMap a0, a1, b;  // gate/up: gate, up, x limbs; down: down, (unused), h limbs
+};
+
+// shared-memory matrix descriptor, no swizzle (the scale atoms: 8-row core
+// matrices of 16-byte rows, 128 B apart; one core matrix along K)
+__device__ __forceinline__ uint64_t umma_desc_plain(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+}
+// instruction descriptor, kind::mxf4 block-scaled: A and B e2m1 (1), ue8m0
+// scales (bit 23), K-major A and B, K = 64, D f32; scale-factor ids in bits
+// 4-5 (B) and 29-30 (A)
+__device__ __forceinline__ uint32_t bs_idesc(int N, uint32_t sf_id) {
+    return (sf_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+           ((uint32_t)(128 >> 4) << 24) | (sf_id << 29);
+}
+__device__ __forceinline__ void bs_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                       uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+__device__ __forceinline__ void bs_cp_atom(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// ---------------------------------------------------------- limb encoding
+// e2m1 nibble of v (|v| < 4 here: no saturation) and its exact value
+__device__ __forceinline__ uint32_t e2m1_rn(float v, float &back) {
+    uint32_t byte;
+    asm("{\n .reg .b8 t;\n cvt.rn.satfinite.e2m1x2.f32 t, %1, %1;\n mov.b32 %0, {t, t, t, t};\n}"
+        : "=r"(byte)
+        : "f"(v));
+    uint32_t h2;
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %1;\n cvt.rn.f16x2.e2m1x2 %0, b0;\n}"
+        : "=r"(h2)
+        : "r"(byte));
+    back = __half2float(__ushort_as_half((uint16_t)(h2 & 0xFFFF)));
+    return byte & 0xF;
+}
+
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }  // -126..127
+
+// Warp-collective: the 32 lanes hold one block of 32 values (lane = column).
+// Writes the packed limb bytes of the block (lane pair 2i, 2i+1 -> byte i:
+// low nibble the even column) at dst[l * ld + i] from the even lanes, and from
+// lane 0 limb l's scale code at codes[4 l], for l < BS_LQ.  Limb 0's scale is
+// 2^(E - 1), E the exponent of the block maximum (so the scaled values lie
+// below 4, e2m1 max 6); limb l's is 4^-l times that (never below 2^-126).  An
+// all-zero or non-finite block gets code 127 throughout (NaN passes on).
+__device__ __forceinline__ void bs_limbs(float v, uint8_t *dst, int64_t ld, uint8_t *codes) {
+    const int lane = threadIdx.x & 31;
+    const float m = warp_max(fabsf(v));
+    int e = 0;
+    bool scaled = false;
+    if (m > 0.f && m <= 3.4e38f) {
+        e = (int)((__float_as_uint(m) >> 23) & 0xFF) - 128;  // E - 1
+        if (e < -126) e = -126;
+        scaled = true;
+    }
+    float r = v;
+#pragma unroll
+    for (int l = 0; l < BS_LQ; l++) {
+        float back;
+        const uint32_t q = e2m1_rn(r * pow2f(-e), back);
+        r = fmaf(-back, pow2f(e), r);
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, q, 1);
+        if (!(lane & 1)) dst[(int64_t)l * ld + (lane >> 1)] = (uint8_t)(q | (hi << 4));
+        if (lane == 0) codes[4 * l] = (uint8_t)(scaled ? e + 127 : 127);
+        if (scaled && e - 2 >= -126) e -= 2;
+    }
+}
+
+// rows x K floats -> packed limbs [row*16 + l][kpad/2] and scale words
+// [row][kpad/128][16] (byte kb % 4 of word (row, kb / 4, l) = limb l's code of
+// block kb).  Blocks past K encode zeros.  One warp per (row, block of 32).
+__global__ void k_bs_limbs(const float *x, int64_t ldx, int rows, int K, int kpad, uint8_t *limbs, uint8_t *sfw) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nb = kpad / 32;
+    if (warp >= rows * nb) return;
+    const int row = warp / nb, kb = warp - row * nb, k = kb * 32 + lane;
+    const float v = k < K ? x[(int64_t)row * ldx + k] : 0.f;
+    bs_limbs(v, limbs + (int64_t)row * BS_LIMBS * (kpad / 2) + kb * 16, kpad / 2,
+             sfw + (((int64_t)row * (kpad / 128) + kb / 4) * BS_LIMBS) * 4 + (kb & 3));
+}
+
+// ---------------------------------------------------------- routed experts
+struct BsPol : MoeCommon {
+    int mode;  // 0 gate/up, 1 down
+    int act_plain;
+    float alpha, limit;
+    const uint32_t *bsf;  // B scale words [src][g4][16] (src: token for gate/up, slot for down)
+    int g4;
+    uint8_t *hl;          // gate/up: h limbs out [slot*16 + l][hl_ld]
+    uint8_t *hsf;         // gate/up: their scale words (bytes) [slot][hg4][16][4]
+    int64_t hl_ld;        // bytes per limb row
+    int hg4;
+    float *y;             // down: [ks][n_tok*top_k][hidden]
+    int ks_count, kst;    // down: K splits and K stages per split
+    int nk;               // K stages of an A row
+    int G;                // scale groups per A row
+    int *err;
+    const int *vl;        // token groups: (list index) | (group << 16)
+
+    __device__ int tpe() const {
+        return mode == 0 ? (int)((L.ffn + 63) / 64) : (int)((L.hidden + 127) / 128) * ks_count;
+    }
+    __device__ void unit(int u, int &d, int &tg, int &tile, int &ks, int &k0, int &k1) const {
+        const int t = tpe();
+        const int v = u / t, r = u - v * t;
+        d = vl[v] & 0xFFFF;
+        tg = vl[v] >> 16;
+        if (mode == 0) {
+            tile = r; ks = 0; k0 = 0; k1 = nk;
+        } else {
+            tile = r / ks_count; ks = r - tile * ks_count;
+            k0 = ks * kst; k1 = min(nk, k0 + kst);
+        }
+    }
+    // routing slots of (expert d, group tg) and their B source rows
+    __device__ int ntok(int d, int tg) const { return min(BS_TOKG, min(ms->ecount[d], SW_MAX_TOK) - BS_TOKG * tg); }
+    __device__ int slot_of(int d, int tg, int j) const { return ms->eslot[d][BS_TOKG * tg + j]; }
+    __device__ int src_of(int d, int tg, int j) const {
+        const int s = slot_of(d, tg, j);
+        return mode == 0 ? s / top_k : s;
+    }
+    __device__ uint32_t scale_bytes(int tile) const {
+        if (mode == 0) return 2 * round16((uint32_t)(min((int64_t)64, L.ffn - tile * 64) * G));
+        return round16((uint32_t)(min((int64_t)128, L.hidden - tile * 128) * G));
+    }
+    // the slot: the 128 rows' scales [128][G], then the group's B scale words
+    // [token j][g4][16] (bwoff: 16-byte aligned)
+    __device__ uint32_t bwoff() const { return (uint32_t)((128 * G + 15) & ~15); }
+    __device__ uint32_t bw_bytes() const { return (uint32_t)g4 * BS_LIMBS * 4; }
+};
+
+__device__ __forceinline__ float bs_act(float gv, float uv, const BsPol &p) {
+    if (p.act_plain) return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+    if (gv > p.limit) gv = p.limit;
+    if (uv > p.limit) uv = p.limit;
+    if (uv < -p.limit) uv = -p.limit;
+    return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(__fmul_rn(-p.alpha, gv)))), __fadd_rn(uv, 1.0f));
+}
+
+__global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__ BsMapsK maps, BsPol pol, int nst,
+                                                         int ssb) {
+    extern __shared__ __align__(1024) uint8_t bs_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bs_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *stages = sm;
+    uint8_t *atoms = stages + (size_t)nst * BS_STAGE;
+    uint8_t *slots = atoms + (size_t)nst * BS_ATOMS;
+    float *ex = reinterpret_cast<float *>(slots + 2 * (size_t)ssb);  // 64 rows x 4 tokens (up values)
+    BsBars *bb = reinterpret_cast<BsBars *>(ex + 64 * BS_TOKG);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ int vlist[BS_MAX_V];
+    __shared__ int nv_sh;
+    {
+        __shared__ MoeShared s;
+        pol.ms = &s;
+        pol.build_list();  // all threads; ends with __syncthreads
+    }
+    if (tid == 0) {
+        int n = 0;
+        for (int d = 0; d < pol.ms->nd; d++) {
+            const int ng = (min(pol.ms->ecount[d], SW_MAX_TOK) + BS_TOKG - 1) / BS_TOKG;
+            for (int g = 0; g < ng && n < BS_MAX_V; g++) vlist[n++] = d | (g << 16);
+        }
+        nv_sh = n;
+        for (int i = 0; i < nst; i++) {
+            mbar_init(&bb->full[i], 1);
+            mbar_init(&bb->empty[i], 1);
+            mbar_init(&bb->sfready[i], 4);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&bb->sfull[i], 1);
+            mbar_init(&bb->sempty[i], 4);
+            mbar_init(&bb->accfull[i], 1);
+            mbar_init(&bb->accempty[i], 4);
+        }
+        mbar_init(&bb->done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(&bb->tmem, BS_TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    pol.vl = vlist;
+    const uint32_t tb = bb->tmem;
+    const int nunits = nv_sh * pol.tpe();
+    const int per = (nunits + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int u0 = (int)blockIdx.x * per, u1 = min(nunits, u0 + per);
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        if (lane == 0 && u0 < u1) {
+            bool ok = true;
+            int s = 0, q = 0, nsl = 0;
+            uint32_t ph = 0, it = 0;
+            for (int u = u0; u < u1 && ok; u++, q++) {
+                int d, tg, tile, ks, k0, k1;
+                pol.unit(u, d, tg, tile, ks, k0, k1);
+                const int e = pol.ms->list[d];
+                const uint8_t *eb = pol.expert(e);
+                const int slot = q & 1, nt = pol.ntok(d, tg);
+                if (q >= 2 && !mbar_wait(&bb->sempty[slot], (uint32_t)(((q >> 1) - 1) & 1))) { ok = false; break; }
+                uint8_t *ss = slots + (size_t)slot * ssb;
+                mbar_arrive_expect_tx(&bb->sfull[slot], pol.scale_bytes(tile) + (uint32_t)nt * pol.bw_bytes());
+                if (pol.mode == 0) {
+                    const uint32_t n = pol.scale_bytes(tile) / 2;
+                    const int64_t off = (int64_t)tile * 64 * pol.G;
+                    bulk_g2s(ss, eb + pol.L.off[0][1] + off, n, &bb->sfull[slot]);
+                    bulk_g2s(ss + 64 * pol.G, eb + pol.L.off[1][1] + off, n, &bb->sfull[slot]);
+                } else {
+                    bulk_g2s(ss, eb + pol.L.off[2][1] + (int64_t)tile * 128 * pol.G, pol.scale_bytes(tile),
+                             &bb->sfull[slot]);
+                }
+                for (int j = 0; j < nt; j++)
+                    bulk_g2s(ss + pol.bwoff() + j * pol.bw_bytes(),
+                             pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS, pol.bw_bytes(),
+                             &bb->sfull[slot]);
+                nsl = q + 1;
+                for (int k = k0; k < k1; k++) {
+                    if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { ok = false; break; }
+                    uint8_t *st = stages + (size_t)s * BS_STAGE;
+                    uint8_t *bs = st + BS_A_BYTES;
+                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES + nt * BS_B_TOK);
+                    if (pol.mode == 0) {
+                        tma_box_4d(st, &maps.a0, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
+                        tma_box_4d(st + BS_A_BYTES / 2, &maps.a1, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
+                    } else {
+                        tma_box_4d(st, &maps.a0, k * 128, tile * 128, e, pol.layer, &bb->full[s]);
+                    }
+                    for (int j = 0; j < nt; j++)
+                        tma_load_2d(bs + j * BS_B_TOK, &maps.b, k * 128, pol.src_of(d, tg, j) * BS_LIMBS, &bb->full[s]);
+                    it++;
+                    if (++s == nst) { s = 0; ph ^= 1u; }
+                }
+            }
+            if (!ok) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            // every copy issued has landed before the CTA may exit
+            for (int64_t k = (int64_t)it - 1; k >= 0 && k >= (int64_t)it - nst; k--)
+                if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            for (int j = nsl - 1; j >= 0 && j >= nsl - 2; j--)
+                if (!mbar_wait(&bb->sfull[j & 1], (uint32_t)((j >> 1) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------ MMA issuer
+        if (lane == 0 && u0 < u1) {
+            bool ok = true;
+            int s = 0, q = 0;
+            uint32_t ph = 0;
+            const uint64_t da0 = umma_desc_sw128(smem_u32(stages));
+            const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
+            for (int u = u0; u < u1 && ok; u++, q++) {
+                int d, tg, tile, ks, k0, k1;
+                pol.unit(u, d, tg, tile, ks, k0, k1);
+                const int N = BS_LIMBS * pol.ntok(d, tg);
+                const int b = q & 1;
+                if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t tacc = tb + (uint32_t)(b * 64);
+                const uint32_t id0 = bs_idesc(N, 0), id2 = bs_idesc(N, 2);
+                for (int k = k0; k < k1; k++) {
+                    if (!mbar_wait(&bb->full[s], ph) || !mbar_wait(&bb->sfready[s], ph)) { ok = false; break; }
+                    tc_fence_after();
+                    // descriptors: the start-address field is the low 14 bits (address >> 4)
+                    const uint64_t dat = dat0 + (uint64_t)((s * BS_ATOMS) >> 4);
+                    const uint64_t da = da0 + (uint64_t)((s * BS_STAGE) >> 4), db = da + (BS_A_BYTES >> 4);
+                    const uint32_t tsf = tb + BS_SF_COL0 + 16u * (uint32_t)s;  // A atoms +0, +4; B atoms +8, +12
+#pragma unroll
+                    for (int i = 0; i < 4; i++) bs_cp_atom(tsf + 4 * i, dat + 32 * i);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const uint32_t sid = 2u * (uint32_t)(j & 1), g = 4u * (uint32_t)(j >> 1);
+                        bs_mma(tacc, da + 2 * j, db + 2 * j, (j & 1) ? id2 : id0, (tsf + g) | (sid << 30),
+                               (tsf + 8 + g) | (sid << 30), (k > k0 || j > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&bb->empty[s]);
+                    if (++s == nst) { s = 0; ph ^= 1u; }
+                }
+                if (ok) tc_commit(&bb->accfull[b]);
+            }
+            if (!ok) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            tc_commit(&bb->done);
+            if (!mbar_wait(&bb->done, 0)) atomicExch(pol.err, BS_ERR_TIMEOUT);
+        }
+    } else if (warp < 6) {
+        // ------------------------------------------------------ scale-factor atoms
+        const int t2 = tid - 64;  // 0..127: A row t2, B row t2 (< 64)
+        bool ok = true;
+        int s = 0, q = 0;
+        uint32_t ph = 0, it = 0;
+        for (int u = u0; u < u1 && ok; u++, q++) {
+            int d, tg, tile, ks, k0, k1;
+            pol.unit(u, d, tg, tile, ks, k0, k1);
+            const int slot = q & 1;
+            if (!mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) { ok = false; break; }
+            const uint8_t *ss = slots + (size_t)slot * ssb;
+            const uint32_t *bw = reinterpret_cast<const uint32_t *>(ss + pol.bwoff());
+            const int nrows = BS_LIMBS * pol.ntok(d, tg);
+            const uint8_t *arow = ss + t2 * pol.G;
+            const int aoff = (t2 & 31) * 16 + (t2 >> 5) * 4;
+            for (int k = k0; k < k1; k++) {
+                if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { ok = false; break; }
+                uint8_t *at = atoms + (size_t)s * BS_ATOMS;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {  // A row t2: blocks 8k + 4h .. +3 -> atom h
+                    uint32_t w = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int kb = 8 * k + 4 * h + i;
+                        const uint32_t c = kb < pol.G ? arow[kb] : 127u;
+                        w |= c << (8 * i);
+                    }
+                    *reinterpret_cast<uint32_t *>(at + 512 * h + aoff) = w;
+                }
+                if (t2 < nrows) {  // B row t2 = limb t2 % 16 of token t2 / 16
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+                        *reinterpret_cast<uint32_t *>(at + 1024 + 512 * h + aoff) =
+                            bw[((t2 >> 4) * pol.g4 + 2 * k + h) * BS_LIMBS + (t2 & 15)];
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bb->sfready[s]);
+                it++;
+                if (++s == nst) { s = 0; ph ^= 1u; }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bb->sempty[slot]);
+        }
+        if (!ok && lane == 0) atomicExch(pol.err, BS_ERR_TIMEOUT);
+    } else {
+        // ------------------------------------------------------ epilogue
+        const int ew = warp & 3, r = 32 * ew + lane;  // TMEM lane quadrant = warp % 4
+        // after a timed-out wait a warp stops waiting and computing but keeps
+        // taking part in the named barriers, so no other warp is left waiting
+        bool failed = false;
+        int q = 0;
+        for (int u = u0; u < u1; u++, q++) {
+            int d, tg, tile, ks, k0, k1;
+            pol.unit(u, d, tg, tile, ks, k0, k1);
+            const int e = pol.ms->list[d];
+            const uint8_t *eb = pol.expert(e);
+            const int nt = pol.ntok(d, tg), b = q & 1;
+            float bias = 0.f;
+            if (pol.mode == 0) {
+                const int64_t f = (int64_t)tile * 64 + (r & 63);
+                if (f < pol.L.ffn) bias = reinterpret_cast<const float *>(eb + pol.L.off[r < 64 ? 0 : 1][2])[f];
+            } else {
+                const int64_t row = (int64_t)tile * 128 + r;
+                if (ks == 0 && row < pol.L.hidden) bias = reinterpret_cast<const float *>(eb + pol.L.off[2][2])[row];
+            }
+            if (!failed && !mbar_wait(&bb->accfull[b], (uint32_t)((q >> 1) & 1))) {
+                failed = true;
+                if (lane == 0) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            }
+            tc_fence_after();
+            float v[BS_TOKG];
+#pragma unroll
+            for (int j = 0; j < BS_TOKG; j++) {
+                v[j] = 0.f;
+                if (j < nt && !failed) {
+                    float t[16];
+                    tmem_ld16(tb + (uint32_t)(b * 64 + BS_LIMBS * j) + ((uint32_t)(32 * ew) << 16), t);
+                    float acc = t[0];
+#pragma unroll
+                    for (int i = 1; i < 16; i++) acc += t[i];
+                    v[j] = acc;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0 && !failed) mbar_arrive(&bb->accempty[b]);
+            if (pol.mode == 0) {
+                if (r >= 64)  // up values + up bias
+#pragma unroll
+                    for (int j = 0; j < BS_TOKG; j++) ex[(r - 64) * BS_TOKG + j] = __fadd_rn(v[j], bias);
+                named_bar_sync(1, 128);
+                if (r < 64 && !failed) {
+                    const int64_t f = (int64_t)tile * 64 + r;
+                    const bool valid = f < pol.L.ffn;
+                    const int64_t fb = (int64_t)tile * 64 + 32 * ew;  // this warp's block of 32 features
+#pragma unroll
+                    for (int j = 0; j < BS_TOKG; j++) {
+                        if (j >= nt) break;  // warp-uniform
+                        const int slot = pol.slot_of(d, tg, j);
+                        const float hv = valid ? bs_act(__fadd_rn(v[j], bias), ex[r * BS_TOKG + j], pol) : 0.f;
+                        bs_limbs(hv, pol.hl + (int64_t)slot * BS_LIMBS * pol.hl_ld + fb / 2, pol.hl_ld,
+                                 pol.hsf + (((int64_t)slot * pol.hg4 + fb / 128) * BS_LIMBS) * 4 + ((fb / 32) & 3));
+                    }
+                }
+                named_bar_sync(1, 128);  // ex is read before the next unit overwrites it
+            } else if (!failed) {
+                const int64_t row = (int64_t)tile * 128 + r;
+                if (row < pol.L.hidden)
+#pragma unroll
+                    for (int j = 0; j < BS_TOKG; j++)
+                        if (j < nt)
+                            pol.y[((int64_t)ks * pol.n_tok * pol.top_k + pol.slot_of(d, tg, j)) * pol.L.hidden + row] =
+                                __fadd_rn(v[j], bias);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tb, BS_TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------- host side
+static int bs_launch(const BsMapsK &maps, BsPol &pol, size_t ssb, cudaStream_t st) {
+    cudaFuncAttributes fa{};
+    MG_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(k_bsmoe)));
+    ssb = (ssb + 127) & ~(size_t)127;
+    const size_t fixed = 1024 + 2 * ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
+    const size_t budget = 227 * 1024 - fa.sharedSizeBytes;
+    MG_REQUIRE(budget > fixed + 2 * (BS_STAGE + BS_ATOMS), MG_ERR_ARG, "block-scaled MoE: no room for a ring");
+    int nst = (int)((budget - fixed) / (BS_STAGE + BS_ATOMS));
+    if (nst > BS_MAX_STAGES) nst = BS_MAX_STAGES;
+    const size_t smem = fixed + (size_t)nst * (BS_STAGE + BS_ATOMS);
+    BS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(k_bsmoe), smem));
+    k_bsmoe<<<num_sms(), BS_THREADS, smem, st>>>(maps, pol, nst, (int)ssb);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
+bool bsmoe_supported(const mg_expert_layout &L) {
+    return L.dt == MG_MXFP4 && L.scale_fmt == MG_SCALE_UE8M0 && L.hidden % 64 == 0 && L.ffn % 64 == 0;
+}
+
+int bs_kpad(int64_t k) { return (int)((k + BS_KE - 1) / BS_KE * BS_KE); }
+size_t bs_limb_bytes(int rows, int kpad) { return (size_t)rows * BS_LIMBS * (kpad / 2); }
+size_t bs_word_bytes(int rows, int kpad) { return (size_t)rows * (kpad / 128) * BS_LIMBS * 4; }
+
+int bs_map_limbs(CUtensorMap *map, const uint8_t *limbs, int kpad, int rows) {
+    BsEncodeFn fn = reinterpret_cast<BsEncodeFn>(encode_tiled_fn());
+    MG_REQUIRE(fn, MG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)(kpad / 2), (cuuint64_t)rows * BS_LIMBS};
+    cuuint64_t strides[1] = {(cuuint64_t)(kpad / 2)};
+    cuuint32_t box[2] = {128, (cuuint32_t)BS_LIMBS};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(limbs), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    MG_REQUIRE(r == CUDA_SUCCESS, MG_ERR_CUDA, "block-scaled MoE: limb tensor map failed (%d)", (int)r);
+    return MG_OK;
+}
+
+int bs_buffers_init(BsBuffers &b) {
+    // limbs zero everywhere and scale codes 127: the K pad and the unencoded
+    // rows BS_LQ..BS_LIMBS-1 of every token keep them
+    MG_CUDA(cudaMemset(b.xl, 0, bs_limb_bytes(8, b.kpad_h)));
+    MG_CUDA(cudaMemset(b.xsf, 0x7F, bs_word_bytes(8, b.kpad_h)));
+    MG_CUDA(cudaMemset(b.hl, 0, bs_limb_bytes(b.slots_max, b.kpad_f)));
+    MG_CUDA(cudaMemset(b.hsf, 0x7F, bs_word_bytes(b.slots_max, b.kpad_f)));
+    return MG_OK;
+}
+
+int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
+    const BsBuffers &B = *a.bs;
+    const mg_expert_layout &L = a.L;
+    MG_REQUIRE(bsmoe_supported(L) && a.maps && a.n_tok >= 1 && a.n_tok <= 8 && a.n_tok * a.top_k <= B.slots_max,
+               MG_ERR_ARG, "block-scaled MoE: unsupported call");
+    int *err = stream_error_word();
+    MG_REQUIRE(err, MG_ERR_OOM, "block-scaled MoE: no error word");
+    {  // activations -> limbs
+        const int warps = a.n_tok * (B.kpad_h / 32);
+        k_bs_limbs<<<(warps * 32 + 255) / 256, 256, 0, st>>>(a.xb, L.hidden, a.n_tok, (int)L.hidden, B.kpad_h, B.xl,
+                                                             reinterpret_cast<uint8_t *>(B.xsf));
+        MG_CHECK_LAUNCH();
+    }
+    BsPol p{};
+    p.L = L;
+    p.experts_layer = a.experts_layer;
+    p.layer = a.layer;
+    p.e0 = a.e0;
+    p.n_experts = a.n_experts;
+    p.n_tok = a.n_tok;
+    p.top_k = a.top_k;
+    p.sel = a.sel;
+    p.act_plain = a.act_plain;
+    p.alpha = a.alpha;
+    p.limit = a.limit;
+    p.err = err;
+    // gate/up: B = the expert's tokens' x limbs, output: their h limbs
+    BsMapsK mg{};
+    mg.a0 = a.maps[0];
+    mg.a1 = a.maps[1];
+    mg.b = B.map_x;
+    p.mode = 0;
+    p.bsf = B.xsf;
+    p.g4 = B.kpad_h / 128;
+    p.hl = B.hl;
+    p.hsf = reinterpret_cast<uint8_t *>(B.hsf);
+    p.hl_ld = B.kpad_f / 2;
+    p.hg4 = B.kpad_f / 128;
+    p.nk = B.kpad_h / BS_KE;
+    p.G = (int)(L.hidden / 32);
+    BS_TRY(bs_launch(mg, p, ((128 * (size_t)p.G + 15) & ~(size_t)15) + (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st));
+    // down: B = the expert's slots' h limbs
+    BsMapsK md{};
+    md.a0 = a.maps[2];
+    md.a1 = a.maps[2];
+    md.b = B.map_h;
+    p.mode = 1;
+    p.bsf = B.hsf;
+    p.g4 = B.kpad_f / 128;
+    p.nk = B.kpad_f / BS_KE;
+    p.G = (int)(L.ffn / 32);
+    p.y = a.y;
+    p.ks_count = a.down_ksplit_out;
+    p.kst = (p.nk + p.ks_count - 1) / p.ks_count;
+    return bs_launch(md, p, ((128 * (size_t)p.G + 15) & ~(size_t)15) + (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st);
+}
+
+}  // namespace mg

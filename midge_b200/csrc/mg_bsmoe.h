@@ -1,0 +1,33 @@
+// mg_bsmoe.h -- decode-time routed experts on block-scaled tcgen05 MMAs
+// (MXFP4 experts with ue8m0 scales); see mg_bsmoe.cu.
+#pragma once
+#include <cuda.h>
+#include <stdint.h>
+
+#include "mg_kernels.h"
+
+namespace mg {
+
+// Device buffers and TMA maps of the block-scaled decode MoE, owned by the
+// model.  Activation rows are held as 16 packed e2m1 limbs each
+// ([row*16 + limb][kpad/2] bytes) with one ue8m0 code per limb and block of
+// 32 values (scale words [row][kpad/128][16], byte kb % 4 = block kb).
+struct BsBuffers {
+    CUtensorMap map_x;     // x limbs, box 128 B x 16 rows
+    CUtensorMap map_h;     // h limbs, box 128 B x 16 rows
+    uint8_t *xl;           // [8 tokens * 16][kpad_h/2] packed e2m1 limbs
+    uint32_t *xsf;         // [8 tokens][kpad_h/128][16] scale words
+    uint8_t *hl;           // [slots_max * 16][kpad_f/2]
+    uint32_t *hsf;         // [slots_max][kpad_f/128][16]
+    int kpad_h, kpad_f, slots_max;
+};
+
+bool bsmoe_supported(const mg_expert_layout &L);
+int bs_kpad(int64_t k);  // K rounded up to the 256-value stage
+size_t bs_limb_bytes(int rows, int kpad);
+size_t bs_word_bytes(int rows, int kpad);
+int bs_map_limbs(CUtensorMap *map, const uint8_t *limbs, int kpad, int rows);
+int bs_buffers_init(BsBuffers &b);
+int moe_bs(const MoeStreamArgs &a, cudaStream_t st);
+
+}  // namespace mg

@@ -49,6 +49,7 @@ struct StreamGemvArgs {
 };
 int stream_gemv(const StreamGemvArgs &a, cudaStream_t st);
 
+struct BsBuffers;
 struct MoeStreamArgs {
     mg_expert_layout L;
     const CUtensorMap *maps;  // gate (box 64 rows), up (64), down (128): 4-D over all experts and layers
@@ -66,6 +67,7 @@ struct MoeStreamArgs {
     int down_ksplit_out;  // what moe_down_ksplit() returned for it
     const int *rebase;    // MXFP4: this layer's [n_experts x 3] f16 rebase exponents (null: none)
     int use_tc;           // run the tensor-core kernels when the format allows
+    const BsBuffers *bs;  // block-scaled tensor-core kernels (MXFP4, ue8m0), or null
 };
 int moe_stream(const MoeStreamArgs &a, cudaStream_t st);
 bool tmoe_supported(const mg_expert_layout &L, const int *rebase);

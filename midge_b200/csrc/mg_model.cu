@@ -265,6 +265,7 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     m->tc_attn = !(ak && !strcmp(ak, "scalar"));
     const char *mk = getenv("MIDGE_MOE_KERNELS");
     m->tc_moe = mk && !strcmp(mk, "tc");
+    m->bs_moe = !(mk && (!strcmp(mk, "tc") || !strcmp(mk, "mma")));  // where the format allows (set in ready)
     const char *pk = getenv("MIDGE_PREFILL_KERNELS");
     m->tc_prefill = !(pk && !strcmp(pk, "tile"));
     const char *pc = getenv("MIDGE_PREFILL_CHUNK");
@@ -628,6 +629,22 @@ extern "C" int mg_model_ready(mg_model *m) {
             m->maps_ok = true;
         }
     }
+    // block-scaled decode MoE: activation limb buffers and their maps
+    if (m->bs_moe && m->maps_ok && bsmoe_supported(m->el) && s.top_k <= 16) {
+        BsBuffers &b = m->bs;
+        b.kpad_h = bs_kpad(H);
+        b.kpad_f = bs_kpad(m->el.ffn);
+        b.slots_max = 8 * s.top_k;
+        TRY(dalloc(m, &b.xl, bs_limb_bytes(8, b.kpad_h)));
+        TRY(dalloc(m, &b.xsf, bs_word_bytes(8, b.kpad_h)));
+        TRY(dalloc(m, &b.hl, bs_limb_bytes(b.slots_max, b.kpad_f)));
+        TRY(dalloc(m, &b.hsf, bs_word_bytes(b.slots_max, b.kpad_f)));
+        TRY(bs_map_limbs(&b.map_x, b.xl, b.kpad_h, 8));
+        TRY(bs_map_limbs(&b.map_h, b.hl, b.kpad_f, b.slots_max));
+        TRY(bs_buffers_init(b));
+    } else {
+        m->bs_moe = false;
+    }
     m->attn_max_splits = (m->ctx + m->attn_split - 1) / m->attn_split;
     TRY(dalloc(m, &m->attn_part, (size_t)DEC_MAX * s.n_heads * m->attn_max_splits * (s.head_dim + 2) * 4));
     MG_CUDA(cudaHostAlloc(&m->h_toks, R * 4, cudaHostAllocDefault));
@@ -921,6 +938,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
     ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
     ma.use_tc = m->tc_moe;
+    ma.bs = m->bs_moe ? &m->bs : nullptr;
     const size_t ycount = (size_t)m->ks_down * n * s.top_k * H;
     if (m->ep.world > 1)  // slots of other ranks' experts stay zero, then the sum over ranks fills them exactly
         MG_CUDA(cudaMemsetAsync(m->moe_y, 0, ycount * 4, st));
@@ -1129,6 +1147,7 @@ extern "C" int mg_model_moe_stream(mg_model *m, int layer, int n_tok, const int3
     ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
     ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
     ma.use_tc = m->tc_moe;
+    ma.bs = m->bs_moe ? &m->bs : nullptr;
     return moe_stream(ma, m->st);
 }
 

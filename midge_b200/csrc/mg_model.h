@@ -8,6 +8,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "mg_bsmoe.h"
 #include "mg_ep.h"
 #include "midgecuda.h"
 
@@ -84,7 +85,10 @@ struct mg_model {
     bool tc_prefill = false;
     bool tc_dense = false;  // trunk q/k/v/o of prefill on the tensor cores
     bool tc_attn = true;    // prefill attention on the tensor cores (MIDGE_ATTN_KERNELS=scalar: fp32 kernel)
-    bool tc_moe = false;    // decode MoE on tcgen05 (MIDGE_MOE_KERNELS=tc); default: the mma.sync kernels
+    bool tc_moe = false;    // decode MoE on tcgen05 kind::f16 with converted weights (MIDGE_MOE_KERNELS=tc)
+    bool bs_moe = false;    // decode MoE on block-scaled tcgen05 MMAs (default for MXFP4 with ue8m0 scales;
+                            // MIDGE_MOE_KERNELS=mma or tc select the mma.sync or kind::f16 kernels)
+    mg::BsBuffers bs{};
     bool rebase_ok = false; // pf_rebase holds exact f16 rebase exponents of every expert matrix
     int *pf_counts = nullptr, *pf_offs = nullptr, *pf_cursor = nullptr, *pf_ntiles = nullptr;
     int *pf_pos = nullptr, *pf_slot = nullptr, *pf_rebase = nullptr;

@@ -2,6 +2,7 @@
 #include <cstring>
 
 #include "mg_kernels.h"
+#include "mg_bsmoe.h"
 #include "mg_stream.cuh"
 
 namespace mg {
@@ -216,6 +217,7 @@ int moe_stream(const MoeStreamArgs &a, cudaStream_t st) {
     MG_REQUIRE(a.n_tok >= 1 && a.n_tok <= 8 && a.n_tok * a.top_k <= SW_MAX_SLOTS && a.n_experts <= 2048 && a.maps,
                MG_ERR_ARG, "moe stream: n_tok %d top_k %d unsupported", a.n_tok, a.top_k);
     const mg_expert_layout &L = a.L;
+    if (a.bs && bsmoe_supported(L)) return moe_bs(a, st);
     if (a.use_tc && tmoe_supported(L, a.rebase)) return moe_tmoe(a, a.rebase, st);
     switch (L.dt) {
     case MG_MXFP4:
