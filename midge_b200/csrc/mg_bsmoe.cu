@@ -31,11 +31,15 @@
 //   warp 0     producer: per unit the 128 rows' scales and the group's B
 //              scale words by bulk copy into one of two slots; per stage the
 //              A box(es) and the group's B rows by TMA into a ring
-//   warp 1     MMA issuer (one thread): per stage tcgen05.cp of the four
-//              scale atoms, 4 MMAs of K = 64, commit -> the stage is free;
-//              per unit commit -> accumulator buffer ready (2 buffers)
+//   warp 1     MMA issuer (one thread): per stage 4 MMAs of K = 64, commit
+//              -> the stage is free; per unit commit -> accumulator buffer
+//              ready (2 buffers)
 //   warps 2-5  scale-factor atoms: per stage the A atoms (from the unit's
-//              slot; blocks past K get code 127) and the B atoms
+//              slot; blocks past K get code 127) and the B atoms, then one
+//              thread copies them into the stage's TMEM columns
+//              (tcgen05.cp) and commits that onto the stage's full barrier,
+//              which thus completes when both the TMA data and the scale
+//              factors are in place
 //   warps 6-9  epilogue (TMEM lane quadrant = warp % 4): limb sums; gate/up:
 //              bias, clamped SwiGLU (engine/midge.c:386-392) and the h values
 //              re-encoded as 12 limbs for the down pass; down: bias in split
@@ -62,23 +66,25 @@ typedef CUresult (*BsEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, v
 constexpr int BS_LIMBS = 16;                           // B rows (MMA columns) per token
 constexpr int BS_LQ = 12;                              // of which encoded limbs
 constexpr int BS_KE = 256;                             // K values per stage (128 packed bytes)
-constexpr int BS_TOKG = 4;                             // tokens per unit
+constexpr int BS_TOKG = 2;                             // tokens per unit
 constexpr int BS_A_BYTES = 128 * 128;                  // A stage: 128 rows x 128 B
-constexpr int BS_B_TOK = BS_LIMBS * 128;               // B rows of one token per stage: 16 x 128 B
-constexpr int BS_B_BYTES = BS_TOKG * BS_B_TOK;
-constexpr int BS_STAGE = BS_A_BYTES + BS_B_BYTES;      // 24 KB, 1024-aligned
+constexpr int BS_B_TOK = BS_LIMBS * 128;               // B rows of one token per K stage: 16 x 128 B
+constexpr int BS_B_STAGE = BS_TOKG * BS_B_TOK;         // resident B: per K stage, the group's tokens
+constexpr int BS_MAX_NK = 16;                          // K stages of a row (K <= 4096)
+constexpr int BS_STAGE = BS_A_BYTES;                   // ring stage: the A tile (16 KB, 1024-aligned)
 constexpr int BS_ATOMS = 2048;                         // 2 A atoms + 2 B atoms per stage
 constexpr int BS_MAX_STAGES = 8;
 constexpr int BS_THREADS = 320;
 constexpr int BS_TMEM_COLS = 256;                      // 2 accumulators x 64 columns + 8 stages x 16 scale columns
 constexpr int BS_SF_COL0 = 128;
-constexpr int BS_MAX_V = 2 * SW_MAX_SLOTS;             // token groups (experts x up to 2)
+constexpr int BS_MAX_V = 4 * SW_MAX_SLOTS;             // token groups (experts x up to 4)
 constexpr int BS_ERR_TIMEOUT = 1;
 
 struct BsBars {
-    uint64_t full[BS_MAX_STAGES], empty[BS_MAX_STAGES], sfready[BS_MAX_STAGES];
+    uint64_t full[BS_MAX_STAGES], empty[BS_MAX_STAGES];
     uint64_t sfull[2], sempty[2], accfull[2], accempty[2];
-    uint64_t done;  // the MMA issuer's last commit: no MMA is in flight when TMEM is released
+    uint64_t bfull;  // the resident B rows of the unit's token group have landed
+    uint64_t done;   // the MMA issuer's last commit: no MMA is in flight when TMEM is released
     uint32_t tmem;
 };
 
@@ -204,6 +210,18 @@ struct BsPol : MoeCommon {
             k0 = ks * kst; k1 = min(nk, k0 + kst);
         }
     }
+    // Stage order of a unit: its K stages [k0, k1) from a start that depends
+    // on the tile and split only, so that the CTAs working on one expert
+    // read different parts of the shared activation limb rows at any time
+    // (the same rows read in lockstep by many SMs contend in L2); the order
+    // is fixed per (tile, split), so results do not depend on the grid.
+    __device__ int stage_k(int k0, int k1, int i, int tile, int ks) const {
+        const int n = k1 - k0;
+        int r = (tile * 5 + ks * 3) % n;
+        r += i;
+        if (r >= n) r -= n;
+        return k0 + r;
+    }
     // routing slots of (expert d, group tg) and their B source rows
     __device__ int ntok(int d, int tg) const { return min(BS_TOKG, min(ms->ecount[d], SW_MAX_TOK) - BS_TOKG * tg); }
     __device__ int slot_of(int d, int tg, int j) const { return ms->eslot[d][BS_TOKG * tg + j]; }
@@ -235,7 +253,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bs_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *stages = sm;
     uint8_t *atoms = stages + (size_t)nst * BS_STAGE;
-    uint8_t *slots = atoms + (size_t)nst * BS_ATOMS;
+    uint8_t *bres = atoms + (size_t)nst * BS_ATOMS;  // [K stage][token j][16 rows x 128 B], 1024-aligned
+    uint8_t *slots = bres + (size_t)pol.nk * BS_B_STAGE;
     float *ex = reinterpret_cast<float *>(slots + 2 * (size_t)ssb);  // 64 rows x 4 tokens (up values)
     BsBars *bb = reinterpret_cast<BsBars *>(ex + 64 * BS_TOKG);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -254,9 +273,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         }
         nv_sh = n;
         for (int i = 0; i < nst; i++) {
-            mbar_init(&bb->full[i], 1);
+            mbar_init(&bb->full[i], 2);  // the producer's expect-tx arrival + the scale copies' commit
             mbar_init(&bb->empty[i], 1);
-            mbar_init(&bb->sfready[i], 4);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&bb->sfull[i], 1);
@@ -264,6 +282,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             mbar_init(&bb->accfull[i], 1);
             mbar_init(&bb->accempty[i], 4);
         }
+        mbar_init(&bb->bfull, 1);
         mbar_init(&bb->done, 1);
         fence_mbar_init();
     }
@@ -281,7 +300,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         // ------------------------------------------------------ producer
         if (lane == 0 && u0 < u1) {
             bool ok = true;
-            int s = 0, q = 0, nsl = 0;
+            int s = 0, q = 0, nsl = 0, key = -1, nbl = 0;
             uint32_t ph = 0, it = 0;
             for (int u = u0; u < u1 && ok; u++, q++) {
                 int d, tg, tile, ks, k0, k1;
@@ -289,6 +308,22 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 const int e = pol.ms->list[d];
                 const uint8_t *eb = pol.expert(e);
                 const int slot = q & 1, nt = pol.ntok(d, tg);
+                // a new token group: its B rows replace the resident ones once the
+                // previous unit's MMAs are done (polled while this unit's A stages
+                // stream, waited for at the end of them otherwise)
+                bool bpend = (d | (tg << 16)) != key;
+                key = d | (tg << 16);
+                auto load_b = [&]() {
+                    mbar_arrive_expect_tx(&bb->bfull, (uint32_t)(nt * pol.nk * BS_B_TOK));
+                    for (int kk = 0; kk < pol.nk; kk++)
+                        for (int j = 0; j < nt; j++)
+                            tma_load_2d(bres + kk * BS_B_STAGE + j * BS_B_TOK, &maps.b, kk * 128,
+                                        pol.src_of(d, tg, j) * BS_LIMBS, &bb->bfull);
+                    nbl++;
+                    bpend = false;
+                };
+                const uint32_t pprev = (uint32_t)(((q - 1) >> 1) & 1);
+                if (bpend && q == 0) load_b();
                 if (q >= 2 && !mbar_wait(&bb->sempty[slot], (uint32_t)(((q >> 1) - 1) & 1))) { ok = false; break; }
                 uint8_t *ss = slots + (size_t)slot * ssb;
                 mbar_arrive_expect_tx(&bb->sfull[slot], pol.scale_bytes(tile) + (uint32_t)nt * pol.bw_bytes());
@@ -306,21 +341,24 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                              pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS, pol.bw_bytes(),
                              &bb->sfull[slot]);
                 nsl = q + 1;
-                for (int k = k0; k < k1; k++) {
+                for (int i = 0; i < k1 - k0; i++) {
+                    const int k = pol.stage_k(k0, k1, i, tile, ks);
                     if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { ok = false; break; }
                     uint8_t *st = stages + (size_t)s * BS_STAGE;
-                    uint8_t *bs = st + BS_A_BYTES;
-                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES + nt * BS_B_TOK);
+                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES);
                     if (pol.mode == 0) {
                         tma_box_4d(st, &maps.a0, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
                         tma_box_4d(st + BS_A_BYTES / 2, &maps.a1, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
                     } else {
                         tma_box_4d(st, &maps.a0, k * 128, tile * 128, e, pol.layer, &bb->full[s]);
                     }
-                    for (int j = 0; j < nt; j++)
-                        tma_load_2d(bs + j * BS_B_TOK, &maps.b, k * 128, pol.src_of(d, tg, j) * BS_LIMBS, &bb->full[s]);
                     it++;
                     if (++s == nst) { s = 0; ph ^= 1u; }
+                    if (bpend && mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev)) load_b();
+                }
+                if (ok && bpend) {
+                    if (!mbar_wait(&bb->accfull[(q - 1) & 1], pprev)) { ok = false; break; }
+                    load_b();
                 }
             }
             if (!ok) atomicExch(pol.err, BS_ERR_TIMEOUT);
@@ -329,6 +367,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
             for (int j = nsl - 1; j >= 0 && j >= nsl - 2; j--)
                 if (!mbar_wait(&bb->sfull[j & 1], (uint32_t)((j >> 1) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            if (nbl > 0 && !mbar_wait(&bb->bfull, (uint32_t)((nbl - 1) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
@@ -336,31 +375,35 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             bool ok = true;
             int s = 0, q = 0;
             uint32_t ph = 0;
-            const uint64_t da0 = umma_desc_sw128(smem_u32(stages));
-            const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
+            const uint64_t da0 = umma_desc_sw128(smem_u32(stages)), db0 = umma_desc_sw128(smem_u32(bres));
+            int key = -1, nbl = 0;
             for (int u = u0; u < u1 && ok; u++, q++) {
                 int d, tg, tile, ks, k0, k1;
                 pol.unit(u, d, tg, tile, ks, k0, k1);
                 const int N = BS_LIMBS * pol.ntok(d, tg);
                 const int b = q & 1;
+                if ((d | (tg << 16)) != key) {  // the token group's resident B rows
+                    key = d | (tg << 16);
+                    if (!mbar_wait(&bb->bfull, (uint32_t)(nbl & 1))) { ok = false; break; }
+                    nbl++;
+                }
                 if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t tacc = tb + (uint32_t)(b * 64);
                 const uint32_t id0 = bs_idesc(N, 0), id2 = bs_idesc(N, 2);
-                for (int k = k0; k < k1; k++) {
-                    if (!mbar_wait(&bb->full[s], ph) || !mbar_wait(&bb->sfready[s], ph)) { ok = false; break; }
+                for (int i = 0; i < k1 - k0; i++) {
+                    const int k = pol.stage_k(k0, k1, i, tile, ks);
+                    if (!mbar_wait(&bb->full[s], ph)) { ok = false; break; }
                     tc_fence_after();
                     // descriptors: the start-address field is the low 14 bits (address >> 4)
-                    const uint64_t dat = dat0 + (uint64_t)((s * BS_ATOMS) >> 4);
-                    const uint64_t da = da0 + (uint64_t)((s * BS_STAGE) >> 4), db = da + (BS_A_BYTES >> 4);
+                    const uint64_t da = da0 + (uint64_t)((s * BS_STAGE) >> 4);
+                    const uint64_t db = db0 + (uint64_t)((k * BS_B_STAGE) >> 4);
                     const uint32_t tsf = tb + BS_SF_COL0 + 16u * (uint32_t)s;  // A atoms +0, +4; B atoms +8, +12
-#pragma unroll
-                    for (int i = 0; i < 4; i++) bs_cp_atom(tsf + 4 * i, dat + 32 * i);
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         const uint32_t sid = 2u * (uint32_t)(j & 1), g = 4u * (uint32_t)(j >> 1);
                         bs_mma(tacc, da + 2 * j, db + 2 * j, (j & 1) ? id2 : id0, (tsf + g) | (sid << 30),
-                               (tsf + 8 + g) | (sid << 30), (k > k0 || j > 0) ? 1u : 0u);
+                               (tsf + 8 + g) | (sid << 30), (i > 0 || j > 0) ? 1u : 0u);
                     }
                     tc_commit(&bb->empty[s]);
                     if (++s == nst) { s = 0; ph ^= 1u; }
@@ -373,50 +416,63 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         }
     } else if (warp < 6) {
         // ------------------------------------------------------ scale-factor atoms
+        // After a timed-out wait a warp stops waiting and building but keeps
+        // taking part in the named barrier, so no other warp is left waiting.
         const int t2 = tid - 64;  // 0..127: A row t2, B row t2 (< 64)
-        bool ok = true;
+        const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
+        bool failed = false;
         int s = 0, q = 0;
         uint32_t ph = 0, it = 0;
-        for (int u = u0; u < u1 && ok; u++, q++) {
+        for (int u = u0; u < u1; u++, q++) {
             int d, tg, tile, ks, k0, k1;
             pol.unit(u, d, tg, tile, ks, k0, k1);
             const int slot = q & 1;
-            if (!mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) { ok = false; break; }
+            if (!failed && !mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) failed = true;
             const uint8_t *ss = slots + (size_t)slot * ssb;
             const uint32_t *bw = reinterpret_cast<const uint32_t *>(ss + pol.bwoff());
             const int nrows = BS_LIMBS * pol.ntok(d, tg);
             const uint8_t *arow = ss + t2 * pol.G;
             const int aoff = (t2 & 31) * 16 + (t2 >> 5) * 4;
-            for (int k = k0; k < k1; k++) {
-                if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { ok = false; break; }
+            for (int i = 0; i < k1 - k0; i++) {
+                const int k = pol.stage_k(k0, k1, i, tile, ks);
+                if (!failed && it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) failed = true;
                 uint8_t *at = atoms + (size_t)s * BS_ATOMS;
+                if (!failed) {
 #pragma unroll
-                for (int h = 0; h < 2; h++) {  // A row t2: blocks 8k + 4h .. +3 -> atom h
-                    uint32_t w = 0;
+                    for (int h = 0; h < 2; h++) {  // A row t2: blocks 8k + 4h .. +3 -> atom h
+                        uint32_t w = 0;
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const int kb = 8 * k + 4 * h + i;
-                        const uint32_t c = kb < pol.G ? arow[kb] : 127u;
-                        w |= c << (8 * i);
+                        for (int i = 0; i < 4; i++) {
+                            const int kb = 8 * k + 4 * h + i;
+                            const uint32_t c = kb < pol.G ? arow[kb] : 127u;
+                            w |= c << (8 * i);
+                        }
+                        *reinterpret_cast<uint32_t *>(at + 512 * h + aoff) = w;
                     }
-                    *reinterpret_cast<uint32_t *>(at + 512 * h + aoff) = w;
-                }
-                if (t2 < nrows) {  // B row t2 = limb t2 % 16 of token t2 / 16
+                    if (t2 < nrows) {  // B row t2 = limb t2 % 16 of token t2 / 16
 #pragma unroll
-                    for (int h = 0; h < 2; h++)
-                        *reinterpret_cast<uint32_t *>(at + 1024 + 512 * h + aoff) =
-                            bw[((t2 >> 4) * pol.g4 + 2 * k + h) * BS_LIMBS + (t2 & 15)];
+                        for (int h = 0; h < 2; h++)
+                            *reinterpret_cast<uint32_t *>(at + 1024 + 512 * h + aoff) =
+                                bw[((t2 >> 4) * pol.g4 + 2 * k + h) * BS_LIMBS + (t2 & 15)];
+                    }
+                    fence_proxy_async_smem();
                 }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bb->sfready[s]);
+                named_bar_sync(2, 128);  // the four atoms are written
+                if (t2 == 0 && !failed) {
+                    tc_fence_after();
+                    const uint64_t dat = dat0 + (uint64_t)((s * BS_ATOMS) >> 4);
+                    const uint32_t tsf = tb + BS_SF_COL0 + 16u * (uint32_t)s;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) bs_cp_atom(tsf + 4 * i, dat + 32 * i);
+                    tc_commit(&bb->full[s]);
+                }
                 it++;
                 if (++s == nst) { s = 0; ph ^= 1u; }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bb->sempty[slot]);
+            if (lane == 0 && !failed) mbar_arrive(&bb->sempty[slot]);
         }
-        if (!ok && lane == 0) atomicExch(pol.err, BS_ERR_TIMEOUT);
+        if (failed && lane == 0) atomicExch(pol.err, BS_ERR_TIMEOUT);
     } else {
         // ------------------------------------------------------ epilogue
         const int ew = warp & 3, r = 32 * ew + lane;  // TMEM lane quadrant = warp % 4
@@ -502,7 +558,8 @@ static int bs_launch(const BsMapsK &maps, BsPol &pol, size_t ssb, cudaStream_t s
     cudaFuncAttributes fa{};
     MG_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(k_bsmoe)));
     ssb = (ssb + 127) & ~(size_t)127;
-    const size_t fixed = 1024 + 2 * ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
+    MG_REQUIRE(pol.nk >= 1 && pol.nk <= BS_MAX_NK, MG_ERR_ARG, "block-scaled MoE: K of %d stages unsupported", pol.nk);
+    const size_t fixed = 1024 + (size_t)pol.nk * BS_B_STAGE + 2 * ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
     const size_t budget = 227 * 1024 - fa.sharedSizeBytes;
     MG_REQUIRE(budget > fixed + 2 * (BS_STAGE + BS_ATOMS), MG_ERR_ARG, "block-scaled MoE: no room for a ring");
     int nst = (int)((budget - fixed) / (BS_STAGE + BS_ATOMS));
