@@ -167,7 +167,14 @@ def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40, rank=0, world=1):
     ms = e0.elapsed_time(e1) / reps
     by = float(np.mean(nbytes))
     ach = by / (ms * 1e-3) / 1e9
-    return {"kernel": "k_stream<PolMoeGateUp> + k_stream<PolMoeDown> (8 tokens, top-4 of 128 experts)", "ms": ms,
+    kind = os.environ.get("MIDGE_MOE_KERNELS", "")
+    if kind == "mma":
+        kname = "k_stream<PolMoeGateUp> + k_stream<PolMoeDown> (mma.sync)"
+    elif kind == "tc":
+        kname = "k_tmoe<GATEUP> + k_tmoe<DOWN> (tcgen05 kind::f16)"
+    else:
+        kname = "k_bs_limbs + k_bsmoe gate/up + k_bsmoe down (tcgen05 kind::mxf4 block-scaled)"
+    return {"kernel": kname + ", 8 tokens, top-4 of 128 experts", "ms": ms,
             "bytes": by, "experts": float(np.mean(nexp)), "achieved_gbs": ach, "frac": ach / hbm_peak}
 
 

@@ -47,6 +47,8 @@
 // Every wait is bounded: a timed-out wait sets the error word and the role
 // stops; the producer waits for its copies in flight and the MMA issuer for
 // its MMAs before the CTA exits.
+#include <cstdlib>
+
 #include "mg_bsmoe.h"
 #include "mg_stream.cuh"
 #include "mg_tc.cuh"
@@ -78,7 +80,11 @@ constexpr int BS_THREADS = 320;
 constexpr int BS_TMEM_COLS = 256;                      // 2 accumulators x 64 columns + 8 stages x 16 scale columns
 constexpr int BS_SF_COL0 = 128;
 constexpr int BS_MAX_V = 4 * SW_MAX_SLOTS;             // token groups (experts x up to 4)
-constexpr int BS_ERR_TIMEOUT = 1;
+// error word codes of a timed-out wait, by role (beside the streamed kernels' 1)
+constexpr int BS_ERR_PRODUCER = 11, BS_ERR_MMA = 12, BS_ERR_ATOMS = 13, BS_ERR_EPILOGUE = 14, BS_ERR_DRAIN = 15;
+// the first failure is kept (21.. name the wait that gave up: producer 21 slot, 22 ring stage, 23 accumulator
+// before a B reload; MMA 24 B rows, 25 accumulator buffer, 26 stage; atoms 27 slot, 28 stage)
+__device__ __forceinline__ void bs_fail(int *err, int code) { atomicCAS(err, 0, code); }
 
 struct BsBars {
     uint64_t full[BS_MAX_STAGES], empty[BS_MAX_STAGES];
@@ -168,6 +174,7 @@ __device__ __forceinline__ void bs_limbs(float v, uint8_t *dst, int64_t ld, uint
 // [row][kpad/128][16] (byte kb % 4 of word (row, kb / 4, l) = limb l's code of
 // block kb).  Blocks past K encode zeros.  One warp per (row, block of 32).
 __global__ void k_bs_limbs(const float *x, int64_t ldx, int rows, int K, int kpad, uint8_t *limbs, uint8_t *sfw) {
+    asm volatile("griddepcontrol.launch_dependents;");  // the gate/up grid may start its setup
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nb = kpad / 32;
     if (warp >= rows * nb) return;
@@ -260,36 +267,57 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ int vlist[BS_MAX_V];
     __shared__ int nv_sh;
+    // barriers and TMEM first: they overlap the routing-slot loads of build_list
+    if (warp == 2) {
+        if (lane < nst) {
+            mbar_init(&bb->full[lane], 2);  // the producer's expect-tx arrival + the scale copies' commit
+            mbar_init(&bb->empty[lane], 1);
+        } else if (lane >= 8 && lane < 10) {
+            mbar_init(&bb->sfull[lane - 8], 1);
+            mbar_init(&bb->sempty[lane - 8], 4);
+        } else if (lane >= 10 && lane < 12) {
+            mbar_init(&bb->accfull[lane - 10], 1);
+            mbar_init(&bb->accempty[lane - 10], 4);
+        } else if (lane == 12) {
+            mbar_init(&bb->bfull, 1);
+        } else if (lane == 13) {
+            mbar_init(&bb->done, 1);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(&bb->tmem, BS_TMEM_COLS);
     {
         __shared__ MoeShared s;
         pol.ms = &s;
         pol.build_list();  // all threads; ends with __syncthreads
     }
-    if (tid == 0) {
-        int n = 0;
-        for (int d = 0; d < pol.ms->nd; d++) {
-            const int ng = (min(pol.ms->ecount[d], SW_MAX_TOK) + BS_TOKG - 1) / BS_TOKG;
-            for (int g = 0; g < ng && n < BS_MAX_V; g++) vlist[n++] = d | (g << 16);
+    if (warp == 0) {  // token groups in expert order: up to 4 experts per lane, prefix over the warp
+        int c[4], sum = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int d = 4 * lane + i;
+            c[i] = d < pol.ms->nd ? (min(pol.ms->ecount[d], SW_MAX_TOK) + BS_TOKG - 1) / BS_TOKG : 0;
+            sum += c[i];
         }
-        nv_sh = n;
-        for (int i = 0; i < nst; i++) {
-            mbar_init(&bb->full[i], 2);  // the producer's expect-tx arrival + the scale copies' commit
-            mbar_init(&bb->empty[i], 1);
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
         }
-        for (int i = 0; i < 2; i++) {
-            mbar_init(&bb->sfull[i], 1);
-            mbar_init(&bb->sempty[i], 4);
-            mbar_init(&bb->accfull[i], 1);
-            mbar_init(&bb->accempty[i], 4);
-        }
-        mbar_init(&bb->bfull, 1);
-        mbar_init(&bb->done, 1);
-        fence_mbar_init();
+        int pos = incl - sum;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            for (int g = 0; g < c[i]; g++) vlist[pos++] = (4 * lane + i) | (g << 16);
+        if (lane == 31) nv_sh = incl;
     }
-    if (warp == 1) tmem_alloc(&bb->tmem, BS_TMEM_COLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // the next kernel (the down pass after gate/up) may start its setup and
+    // weight prefetch on SMs this grid leaves; it waits for this grid before
+    // it reads what this one writes
+    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;");
     pol.vl = vlist;
     const uint32_t tb = bb->tmem;
     const int nunits = nv_sh * pol.tpe();
@@ -299,7 +327,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     if (warp == 0) {
         // ------------------------------------------------------ producer
         if (lane == 0 && u0 < u1) {
-            bool ok = true;
+            bool ok = true, dep = false;  // dep: the previous grid has completed (griddepcontrol.wait)
             int s = 0, q = 0, nsl = 0, key = -1, nbl = 0;
             uint32_t ph = 0, it = 0;
             for (int u = u0; u < u1 && ok; u++, q++) {
@@ -323,9 +351,23 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     bpend = false;
                 };
                 const uint32_t pprev = (uint32_t)(((q - 1) >> 1) & 1);
-                if (bpend && q == 0) load_b();
-                if (q >= 2 && !mbar_wait(&bb->sempty[slot], (uint32_t)(((q >> 1) - 1) & 1))) { ok = false; break; }
+                if (q >= 2 && !mbar_wait(&bb->sempty[slot], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 21); ok = false; break; }
                 uint8_t *ss = slots + (size_t)slot * ssb;
+                // the B scale words and the B rows come from the previous grid (the
+                // limbs kernel, or gate/up for the down pass): the first unit issues
+                // its weight stages (up to a ring) before waiting for that grid
+                auto load_dep = [&]() {
+                    for (int j = 0; j < nt; j++)
+                        bulk_g2s(ss + pol.bwoff() + j * pol.bw_bytes(),
+                                 pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS, pol.bw_bytes(),
+                                 &bb->sfull[slot]);
+                    if (bpend && q == 0) load_b();
+                };
+                auto wait_dep = [&]() {
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    dep = true;
+                    load_dep();
+                };
                 mbar_arrive_expect_tx(&bb->sfull[slot], pol.scale_bytes(tile) + (uint32_t)nt * pol.bw_bytes());
                 if (pol.mode == 0) {
                     const uint32_t n = pol.scale_bytes(tile) / 2;
@@ -336,14 +378,12 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     bulk_g2s(ss, eb + pol.L.off[2][1] + (int64_t)tile * 128 * pol.G, pol.scale_bytes(tile),
                              &bb->sfull[slot]);
                 }
-                for (int j = 0; j < nt; j++)
-                    bulk_g2s(ss + pol.bwoff() + j * pol.bw_bytes(),
-                             pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS, pol.bw_bytes(),
-                             &bb->sfull[slot]);
+                if (dep) load_dep();
                 nsl = q + 1;
                 for (int i = 0; i < k1 - k0; i++) {
                     const int k = pol.stage_k(k0, k1, i, tile, ks);
-                    if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { ok = false; break; }
+                    if (!dep && it >= (uint32_t)nst) wait_dep();
+                    if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { bs_fail(pol.err, 22); ok = false; break; }
                     uint8_t *st = stages + (size_t)s * BS_STAGE;
                     mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES);
                     if (pol.mode == 0) {
@@ -354,20 +394,21 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     }
                     it++;
                     if (++s == nst) { s = 0; ph ^= 1u; }
-                    if (bpend && mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev)) load_b();
+                    if (bpend && dep && q > 0 && mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev)) load_b();
                 }
+                if (ok && !dep) wait_dep();
                 if (ok && bpend) {
-                    if (!mbar_wait(&bb->accfull[(q - 1) & 1], pprev)) { ok = false; break; }
+                    if (!mbar_wait(&bb->accfull[(q - 1) & 1], pprev)) { bs_fail(pol.err, 23); ok = false; break; }
                     load_b();
                 }
             }
-            if (!ok) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            if (!ok) bs_fail(pol.err, BS_ERR_PRODUCER);
             // every copy issued has landed before the CTA may exit
             for (int64_t k = (int64_t)it - 1; k >= 0 && k >= (int64_t)it - nst; k--)
-                if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
+                if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
             for (int j = nsl - 1; j >= 0 && j >= nsl - 2; j--)
-                if (!mbar_wait(&bb->sfull[j & 1], (uint32_t)((j >> 1) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
-            if (nbl > 0 && !mbar_wait(&bb->bfull, (uint32_t)((nbl - 1) & 1))) atomicExch(pol.err, BS_ERR_TIMEOUT);
+                if (!mbar_wait(&bb->sfull[j & 1], (uint32_t)((j >> 1) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
+            if (nbl > 0 && !mbar_wait(&bb->bfull, (uint32_t)((nbl - 1) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
@@ -384,16 +425,16 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 const int b = q & 1;
                 if ((d | (tg << 16)) != key) {  // the token group's resident B rows
                     key = d | (tg << 16);
-                    if (!mbar_wait(&bb->bfull, (uint32_t)(nbl & 1))) { ok = false; break; }
+                    if (!mbar_wait(&bb->bfull, (uint32_t)(nbl & 1))) { bs_fail(pol.err, 24); ok = false; break; }
                     nbl++;
                 }
-                if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { ok = false; break; }
+                if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 25); ok = false; break; }
                 tc_fence_after();
                 const uint32_t tacc = tb + (uint32_t)(b * 64);
                 const uint32_t id0 = bs_idesc(N, 0), id2 = bs_idesc(N, 2);
                 for (int i = 0; i < k1 - k0; i++) {
                     const int k = pol.stage_k(k0, k1, i, tile, ks);
-                    if (!mbar_wait(&bb->full[s], ph)) { ok = false; break; }
+                    if (!mbar_wait(&bb->full[s], ph)) { bs_fail(pol.err, 26); ok = false; break; }
                     tc_fence_after();
                     // descriptors: the start-address field is the low 14 bits (address >> 4)
                     const uint64_t da = da0 + (uint64_t)((s * BS_STAGE) >> 4);
@@ -410,9 +451,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 }
                 if (ok) tc_commit(&bb->accfull[b]);
             }
-            if (!ok) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            if (!ok) bs_fail(pol.err, BS_ERR_MMA);
             tc_commit(&bb->done);
-            if (!mbar_wait(&bb->done, 0)) atomicExch(pol.err, BS_ERR_TIMEOUT);
+            if (!mbar_wait(&bb->done, 0)) bs_fail(pol.err, BS_ERR_MMA);
         }
     } else if (warp < 6) {
         // ------------------------------------------------------ scale-factor atoms
@@ -427,7 +468,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             int d, tg, tile, ks, k0, k1;
             pol.unit(u, d, tg, tile, ks, k0, k1);
             const int slot = q & 1;
-            if (!failed && !mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) failed = true;
+            if (!failed && !mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 27); }
             const uint8_t *ss = slots + (size_t)slot * ssb;
             const uint32_t *bw = reinterpret_cast<const uint32_t *>(ss + pol.bwoff());
             const int nrows = BS_LIMBS * pol.ntok(d, tg);
@@ -435,7 +476,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             const int aoff = (t2 & 31) * 16 + (t2 >> 5) * 4;
             for (int i = 0; i < k1 - k0; i++) {
                 const int k = pol.stage_k(k0, k1, i, tile, ks);
-                if (!failed && it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) failed = true;
+                if (!failed && it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { failed = true; if (lane == 0) bs_fail(pol.err, 28); }
                 uint8_t *at = atoms + (size_t)s * BS_ATOMS;
                 if (!failed) {
 #pragma unroll
@@ -472,7 +513,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             __syncwarp();
             if (lane == 0 && !failed) mbar_arrive(&bb->sempty[slot]);
         }
-        if (failed && lane == 0) atomicExch(pol.err, BS_ERR_TIMEOUT);
+        if (failed && lane == 0) bs_fail(pol.err, BS_ERR_ATOMS);
     } else {
         // ------------------------------------------------------ epilogue
         const int ew = warp & 3, r = 32 * ew + lane;  // TMEM lane quadrant = warp % 4
@@ -496,7 +537,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             }
             if (!failed && !mbar_wait(&bb->accfull[b], (uint32_t)((q >> 1) & 1))) {
                 failed = true;
-                if (lane == 0) atomicExch(pol.err, BS_ERR_TIMEOUT);
+                if (lane == 0) bs_fail(pol.err, BS_ERR_EPILOGUE);
             }
             tc_fence_after();
             float v[BS_TOKG];
@@ -566,8 +607,24 @@ static int bs_launch(const BsMapsK &maps, BsPol &pol, size_t ssb, cudaStream_t s
     if (nst > BS_MAX_STAGES) nst = BS_MAX_STAGES;
     const size_t smem = fixed + (size_t)nst * (BS_STAGE + BS_ATOMS);
     BS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(k_bsmoe), smem));
-    k_bsmoe<<<num_sms(), BS_THREADS, smem, st>>>(maps, pol, nst, (int)ssb);
-    MG_CHECK_LAUNCH();
+    // programmatic dependent launch: this grid may start while the previous
+    // kernel on the stream finishes; its producer waits for that grid
+    // (griddepcontrol.wait) before reading its outputs
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)num_sms());
+    cfg.blockDim = dim3(BS_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    static const bool pdl = [] {
+        const char *v = getenv("MIDGE_BS_PDL");
+        return !(v && *v == '0');
+    }();
+    cfg.numAttrs = pdl ? 1 : 0;
+    MG_CUDA(cudaLaunchKernelEx(&cfg, k_bsmoe, maps, pol, nst, (int)ssb));
     return MG_OK;
 }
 

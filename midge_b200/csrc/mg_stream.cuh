@@ -631,36 +631,59 @@ struct MoeCommon {
     // Experts routed to (ascending local ids) and, per expert, its routing
     // slots; the order of an expert's slots is immaterial (each is an
     // independent MMA column and output row).
+    // All threads; needs blockDim.x >= SW_MAX_SLOTS and n_tok * top_k <= SW_MAX_SLOTS
+    // (one routing slot per thread, read once).
     __device__ void build_list() {
         __shared__ uint32_t bm[64];
         __shared__ int wpre[65];
-        const int n = n_tok * top_k;
-        for (int i = threadIdx.x; i < 64; i += blockDim.x) bm[i] = 0;
-        for (int i = threadIdx.x; i < SW_MAX_SLOTS; i += blockDim.x) ms->ecount[i] = 0;
-        __syncthreads();
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            const int e = sel[i] - e0;  // local index; other ranks' experts fall outside
-            if (e >= 0 && e < n_experts) atomicOr(&bm[e >> 5], 1u << (e & 31));
+        const int n = n_tok * top_k, t = threadIdx.x;
+        int e = -1;
+        if (t < n) {
+            e = sel[t] - e0;  // local index; other ranks' experts fall outside
+            if (e < 0 || e >= n_experts) e = -1;
         }
+        if (t < 64) bm[t] = 0;
+        if (t < SW_MAX_SLOTS) ms->ecount[t] = 0;
         __syncthreads();
-        if (threadIdx.x == 0) {
-            int c = 0;
-            for (int wd = 0; wd < 64; wd++) { wpre[wd] = c; c += __popc(bm[wd]); }
-            wpre[64] = c;
-            ms->nd = c;
-        }
+        if (e >= 0) atomicOr(&bm[e >> 5], 1u << (e & 31));
         __syncthreads();
-        for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
-            const uint32_t word = bm[e >> 5], bit = 1u << (e & 31);
-            if (word & bit) ms->list[wpre[e >> 5] + __popc(word & (bit - 1))] = (uint16_t)e;
-        }
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            const int e = sel[i] - e0;
-            if (e >= 0 && e < n_experts) {
-                const int d = wpre[e >> 5] + __popc(bm[e >> 5] & ((1u << (e & 31)) - 1u));
-                const int k = atomicAdd(&ms->ecount[d], 1);
-                if (k < SW_MAX_TOK) ms->eslot[d][k] = (uint8_t)i;
+        if (t < 32) {  // exclusive prefix of the words' popcounts, two words per lane
+            const int c0 = __popc(bm[2 * t]), c1 = __popc(bm[2 * t + 1]);
+            int incl = c0 + c1;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (t >= o) incl += v;
             }
+            wpre[2 * t] = incl - c0 - c1;
+            wpre[2 * t + 1] = incl - c1;
+            if (t == 31) {
+                wpre[64] = incl;
+                ms->nd = incl;
+            }
+        }
+        __syncthreads();
+        for (int x = t; x < n_experts; x += blockDim.x) {
+            const uint32_t word = bm[x >> 5], bit = 1u << (x & 31);
+            if (word & bit) ms->list[wpre[x >> 5] + __popc(word & (bit - 1))] = (uint16_t)x;
+        }
+        if (e >= 0) {
+            const int d = wpre[e >> 5] + __popc(bm[e >> 5] & ((1u << (e & 31)) - 1u));
+            const int k = atomicAdd(&ms->ecount[d], 1);
+            if (k < SW_MAX_TOK) ms->eslot[d][k] = (uint8_t)t;
+        }
+        __syncthreads();
+        // ascending slot order: every CTA sees the same per-expert lists (the
+        // token groups of the block-scaled kernels split them)
+        if (t < wpre[64]) {
+            const int c = min(ms->ecount[t], SW_MAX_TOK);
+            uint8_t *v = ms->eslot[t];
+            for (int i = 1; i < c; i++)
+                for (int j = i; j > 0 && v[j - 1] > v[j]; j--) {
+                    const uint8_t x = v[j];
+                    v[j] = v[j - 1];
+                    v[j - 1] = x;
+                }
         }
         __syncthreads();
     }
