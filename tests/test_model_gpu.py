@@ -174,12 +174,15 @@ def test_decode_greedy_matches_step_loop(torch_cuda, c1_dir, monkeypatch, kernel
     a.close()
 
 
-@pytest.mark.parametrize("moe", ["tc", "mma"])
+@pytest.mark.parametrize("moe", ["bs", "tc", "mma"])
 def test_decode_moe_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, moe):
-    """Both decode expert kernels (tcgen05 with the weights in tensor memory,
-    and the mma.sync streamed kernels) against the oracle, 8 concurrent
-    sequences, and bit-identical across the two greedy entry points."""
-    monkeypatch.setenv("MIDGE_MOE_KERNELS", moe)
+    """Every decode expert kernel (block-scaled tcgen05, the default for
+    MXFP4; tcgen05 with the weights in tensor memory; the mma.sync streamed
+    kernels) against the oracle, 8 concurrent sequences."""
+    if moe == "bs":
+        monkeypatch.delenv("MIDGE_MOE_KERNELS", raising=False)
+    else:
+        monkeypatch.setenv("MIDGE_MOE_KERNELS", moe)
     rng = np.random.default_rng(41)
     prompts = [rng.integers(0, 1024, 6 + i).astype(np.int32) for i in range(8)]
     m = abi.Model.from_dir(c1_dir, ctx=64, max_seqs=8)
@@ -192,4 +195,30 @@ def test_decode_moe_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, moe):
         want = om.forward(int(first[i]))
         om.close()
         assert max_rel(want, lg[i]) < LOGIT_TOL
+    m.close()
+
+
+def test_decode_block_scaled_token_groups_vs_oracle(torch_cuda, tmp_path, monkeypatch):
+    """Block-scaled decode experts when every expert takes all 8 tokens: each
+    expert's slots form four token groups of two, each group's tiles spread
+    over several CTAs (the groups must be the same in every CTA).  Two decode
+    steps of 8 sequences against the oracle."""
+    monkeypatch.delenv("MIDGE_MOE_KERNELS", raising=False)
+    spec, edt = ct.config_spec("c1_tiny")
+    spec["moe"]["experts"] = 4
+    spec["moe"]["top_k"] = 4
+    md = ct.write_synthetic_model(str(tmp_path / "m"), spec, edt, seed=5)
+    rng = np.random.default_rng(43)
+    prompts = [rng.integers(0, 1024, 5 + i).astype(np.int32) for i in range(8)]
+    m = abi.Model.from_dir(md, ctx=64, max_seqs=8)
+    first = np.array([int(np.argmax(m.forward_batch(i, p, logits_mode=1))) for i, p in enumerate(prompts)], np.int32)
+    seqs = np.arange(8, dtype=np.int32)
+    lg1, nxt = m.decode_step(seqs, first, want_logits=True)
+    lg2, _ = m.decode_step(seqs, nxt, want_logits=True)
+    for i, p in enumerate(prompts):
+        om = orc.OracleModel(md, 64)
+        om.prefill(list(p))
+        assert max_rel(om.forward(int(first[i])), lg1[i]) < LOGIT_TOL
+        assert max_rel(om.forward(int(nxt[i])), lg2[i]) < LOGIT_TOL
+        om.close()
     m.close()
