@@ -49,11 +49,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
-# DRAM bytes (read + write) per routed expert of one gate/up + down launch
-# pair, from the ncu capture summarised in
-# profiles/moe_stream_gateup_down_c4_decode8.md (per-launch traffic =
+# DRAM bytes (read + write) per routed expert of one limbs + gate/up + down
+# launch triple of the block-scaled decode MoE, from the ncu capture
+# summarised in profiles/moe_bsmoe_c4_decode8.md (per-launch traffic =
 # experts routed x this figure)
-TRAFFIC_PER_EXPERT = 13640000
+TRAFFIC_PER_EXPERT = 13540000
 DECODE_PER_STEP = 64
 N_SEQ = 8
 
