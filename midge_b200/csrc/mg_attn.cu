@@ -332,21 +332,40 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
 
 // Combine splits and the sink:
 //   out = sum_s acc_s e^(m_s-M) / (e^(sink-M) + sum_s l_s e^(m_s-M)),  M = max(sink, m_s)
+// One block (2 warps) per (head, sequence): the split maxima and the
+// denominator are reduced once, each split's weight e^(m_s-M) is kept in
+// shared memory (max_splits floats), and each thread accumulates its output
+// dimensions over the splits in ascending order.
 __global__ void k_attn_combine(AttnDecodeArgs a) {
-    const int h = blockIdx.x, si = blockIdx.y;
+    extern __shared__ float cw[];
+    __shared__ float red[2][2];
+    const int h = blockIdx.x, si = blockIdx.y, t = threadIdx.x, w = t >> 5, lane = t & 31;
     const int hd = a.head_dim;
     const int pos = a.pos[si];
     const int nctx = pos + 1 < a.cap ? pos + 1 : a.cap;
     const int nsplit = (nctx + a.split_len - 1) / a.split_len;
     const float *part = a.partial + ((int64_t)si * a.n_heads + h) * (int64_t)a.max_splits * (hd + 2);
-    float M = a.sinks ? a.sinks[h] : -1e30f;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, part[s * (hd + 2)]);
-    float L = a.sinks ? expf(a.sinks[h] - M) : 0.f;
-    for (int s = 0; s < nsplit; s++) L += part[s * (hd + 2) + 1] * expf(part[s * (hd + 2)] - M);
-    float inv = 1.0f / L;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    const float sink = a.sinks ? a.sinks[h] : -1e30f;
+    float mx = sink;
+    for (int s = t; s < nsplit; s += blockDim.x) mx = fmaxf(mx, part[s * (hd + 2)]);
+    mx = warp_max(mx);
+    if (lane == 0) red[0][w] = mx;
+    __syncthreads();
+    const float M = fmaxf(red[0][0], red[0][1]);
+    float ls = 0.f;
+    for (int s = t; s < nsplit; s += blockDim.x) {
+        const float e = expf(part[s * (hd + 2)] - M);
+        cw[s] = e;
+        ls += part[s * (hd + 2) + 1] * e;
+    }
+    ls = warp_sum(ls);
+    if (lane == 0) red[1][w] = ls;
+    __syncthreads();
+    const float L = (a.sinks ? expf(sink - M) : 0.f) + (red[1][0] + red[1][1]);
+    const float inv = 1.0f / L;
+    for (int i = t; i < hd; i += blockDim.x) {
         float o = 0.f;
-        for (int s = 0; s < nsplit; s++) o = fmaf(part[s * (hd + 2) + 2 + i], expf(part[s * (hd + 2)] - M), o);
+        for (int s = 0; s < nsplit; s++) o = fmaf(part[s * (hd + 2) + 2 + i], cw[s], o);
         a.out[(int64_t)si * a.ldo + (int64_t)h * hd + i] = o * inv;
     }
 }
@@ -364,7 +383,9 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
         k_attn_decode_tc<<<g1, 32, 0, st>>>(a);
         MG_CHECK_LAUNCH();
         dim3 g2(a.n_heads, n_seqs);
-        k_attn_combine<<<g2, 64, 0, st>>>(a);
+        const size_t cs = (size_t)a.max_splits * 4;
+        if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
+        k_attn_combine<<<g2, 64, cs, st>>>(a);
         MG_CHECK_LAUNCH();
         return MG_OK;
     }
@@ -375,7 +396,9 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     k_attn_decode<HD><<<g1, ATTN_THREADS, smem, st>>>(a);
     MG_CHECK_LAUNCH();
     dim3 g2(a.n_heads, n_seqs);
-    k_attn_combine<<<g2, 64, 0, st>>>(a);
+    const size_t cs = (size_t)a.max_splits * 4;
+    if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
+    k_attn_combine<<<g2, 64, cs, st>>>(a);
     MG_CHECK_LAUNCH();
     return MG_OK;
 }
