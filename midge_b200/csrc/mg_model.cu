@@ -642,6 +642,9 @@ extern "C" int mg_model_ready(mg_model *m) {
         TRY(bs_map_limbs(&b.map_x, b.xl, b.kpad_h, 8));
         TRY(bs_map_limbs(&b.map_h, b.hl, b.kpad_f, b.slots_max));
         TRY(bs_buffers_init(b));
+        // the block-scaled down pass runs whole rows per unit: one partial
+        // plane (moe_y was sized for the streamed kernels' two)
+        m->ks_down = 1;
     } else {
         m->bs_moe = false;
     }
