@@ -20,26 +20,29 @@
 //   * scale factors: per stage the 128 A rows x 8 blocks and the B rows x 8
 //     blocks are laid out as 32 x 16-byte atoms (4 blocks each) and copied
 //     into TMEM with tcgen05.cp.32x128b.warpx4; an MMA (K = 64) reads two
-//     blocks, selected by its scale-factor id (0 or 2).
+//     blocks, selected by its scale-factor id (0 or 2).  The A atoms are
+//     written once, when the model is made ready (k_bs_atoms: 1 KB per
+//     (expert, tile, stage)), and streamed beside the A tile.
 //   * D (fp32, TMEM): 128 output rows x 16 columns per token; the epilogue
 //     sums each token's 16 limb columns.
-// Each unit multiplies one expert's weight tile by up to 4 of its routed
-// tokens (the MMA cost does not depend on N up to 64 columns); an expert with
-// more routed tokens takes a second token group.
+// Each unit multiplies one expert's weight tile by up to 2 of its routed
+// tokens (the MMA cost does not depend on N at these widths); an expert
+// with more routed tokens takes further token groups.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over the units):
-//   warp 0     producer: per unit the 128 rows' scales and the group's B
-//              scale words by bulk copy into one of two slots; per stage the
-//              A box(es) and the group's B rows by TMA into a ring
-//   warp 1     MMA issuer (one thread): per stage 4 MMAs of K = 64, commit
-//              -> the stage is free; per unit commit -> accumulator buffer
-//              ready (2 buffers)
-//   warps 2-5  scale-factor atoms: per stage the A atoms (from the unit's
-//              slot; blocks past K get code 127) and the B atoms, then one
-//              thread copies them into the stage's TMEM columns
-//              (tcgen05.cp) and commits that onto the stage's full barrier,
-//              which thus completes when both the TMA data and the scale
-//              factors are in place
+//   warp 0     producer: per unit the group's B scale words by bulk copy
+//              into one of two slots; per stage the A box(es) by TMA and the
+//              stage's A atoms by bulk copy into a ring; per token group its
+//              B rows (resident for all K stages)
+//   warp 1     MMA issuer (one thread): per stage the 4 scale atoms into the
+//              stage's TMEM columns (tcgen05.cp, ordered before the MMAs
+//              that read them), 4 MMAs of K = 64, commit -> the stage is
+//              free; per unit commit -> accumulator buffer ready (2 buffers)
+//   warp 2     B atoms: per stage the group's B atoms from the slot's
+//              words (lane = B row), then an arrival on the stage's full
+//              barrier, which thus completes when the TMA data, the A atoms
+//              and the B atoms are in place
+//   warps 3-5  idle after setup
 //   warps 6-9  epilogue (TMEM lane quadrant = warp % 4): limb sums; gate/up:
 //              bias, clamped SwiGLU (engine/midge.c:386-392) and the h values
 //              re-encoded as 12 limbs for the down pass; down: bias in split
@@ -75,10 +78,12 @@ constexpr int BS_B_STAGE = BS_TOKG * BS_B_TOK;         // resident B: per K stag
 constexpr int BS_MAX_NK = 16;                          // K stages of a row (K <= 4096)
 constexpr int BS_STAGE = BS_A_BYTES;                   // ring stage: the A tile (16 KB, 1024-aligned)
 constexpr int BS_ATOMS = 2048;                         // 2 A atoms + 2 B atoms per stage
-constexpr int BS_MAX_STAGES = 8;
+constexpr int BS_MAX_STAGES = 12;
 constexpr int BS_THREADS = 320;
-constexpr int BS_TMEM_COLS = 256;                      // 2 accumulators x 64 columns + 8 stages x 16 scale columns
-constexpr int BS_SF_COL0 = 128;
+constexpr int BS_ACC_COLS = BS_TOKG * BS_LIMBS;        // accumulator columns of a unit (N)
+constexpr int BS_SF_COL0 = 2 * BS_ACC_COLS;            // scale columns: 16 per stage after the 2 accumulators
+constexpr int BS_TMEM_COLS = 256;                      // >= BS_SF_COL0 + 16 * BS_MAX_STAGES
+static_assert(BS_SF_COL0 + 16 * BS_MAX_STAGES <= BS_TMEM_COLS, "TMEM columns");
 constexpr int BS_MAX_V = 4 * SW_MAX_SLOTS;             // token groups (experts x up to 4)
 // error word codes of a timed-out wait, by role (beside the streamed kernels' 1)
 constexpr int BS_ERR_PRODUCER = 11, BS_ERR_MMA = 12, BS_ERR_ATOMS = 13, BS_ERR_EPILOGUE = 14, BS_ERR_DRAIN = 15;
@@ -184,6 +189,46 @@ __global__ void k_bs_limbs(const float *x, int64_t ldx, int rows, int K, int kpa
              sfw + (((int64_t)row * (kpad / 128) + kb / 4) * BS_LIMBS) * 4 + (kb & 3));
 }
 
+// Expert scales -> the A scale atoms of every unit stage (once per model).
+// Unit u of an expert: gate/up tile u / nk_h, stage u % nk_h for u < atoms_dn
+// (rows 0-63 the tile's gate rows, 64-127 the up rows of the same outputs),
+// else down tile (u - atoms_dn) / nk_f (128 rows).  Its 1024 bytes are two
+// atoms (blocks 8k..8k+3, 8k+4..8k+7): block kb of row r at byte
+// 512 (kb / 4 % 2) + (r % 32) 16 + (r / 32) 4 + kb % 4.  Rows past the matrix
+// and blocks past K get code 127 (their weights are zero-filled by the TMA).
+// Block (256 threads) = one unit; thread = (atom h, row r).
+__global__ void k_bs_atoms(const uint8_t *experts, mg_expert_layout L, int64_t n_le, int n_local, int nk_h, int nk_f,
+                           int atoms_dn, uint8_t *atoms, int64_t atoms_expert) {
+    const int u = blockIdx.x, h = threadIdx.x >> 7, r = threadIdx.x & 127;
+    for (int64_t le = blockIdx.y; le < n_le; le += gridDim.y) {
+        const uint8_t *eb = experts + (le / n_local) * L.layer_stride + (le % n_local) * L.expert_stride;
+        const uint8_t *src = nullptr;
+        int G, k;
+        if (u < atoms_dn) {
+            const int tile = u / nk_h;
+            k = u - tile * nk_h;
+            G = (int)(L.hidden / 32);
+            const int64_t row = (int64_t)tile * 64 + (r & 63);
+            if (row < L.ffn) src = eb + L.off[r < 64 ? 0 : 1][1] + row * G;
+        } else {
+            const int v = u - atoms_dn, tile = v / nk_f;
+            k = v - tile * nk_f;
+            G = (int)(L.ffn / 32);
+            const int64_t row = (int64_t)tile * 128 + r;
+            if (row < L.hidden) src = eb + L.off[2][1] + row * G;
+        }
+        uint32_t w = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int kb = 8 * k + 4 * h + i;
+            const uint32_t c = (src && kb < G) ? src[kb] : 127u;
+            w |= c << (8 * i);
+        }
+        *reinterpret_cast<uint32_t *>(atoms + le * atoms_expert + (int64_t)u * 1024 + 512 * h + (r & 31) * 16 +
+                                      (r >> 5) * 4) = w;
+    }
+}
+
 // ---------------------------------------------------------- routed experts
 struct BsPol : MoeCommon {
     int mode;  // 0 gate/up, 1 down
@@ -201,6 +246,9 @@ struct BsPol : MoeCommon {
     int G;                // scale groups per A row
     int *err;
     const int *vl;        // token groups: (list index) | (group << 16)
+    const uint8_t *atoms; // this layer's expert scale atoms
+    int64_t atoms_expert; // bytes per expert
+    int atoms_u0;         // first unit of this pass (0 gate/up, atoms_dn down)
 
     __device__ int tpe() const {
         return mode == 0 ? (int)((L.ffn + 63) / 64) : (int)((L.hidden + 127) / 128) * ks_count;
@@ -236,13 +284,11 @@ struct BsPol : MoeCommon {
         const int s = slot_of(d, tg, j);
         return mode == 0 ? s / top_k : s;
     }
-    __device__ uint32_t scale_bytes(int tile) const {
-        if (mode == 0) return 2 * round16((uint32_t)(min((int64_t)64, L.ffn - tile * 64) * G));
-        return round16((uint32_t)(min((int64_t)128, L.hidden - tile * 128) * G));
+    // the A atoms of local expert e, tile, K stage k (1024 bytes)
+    __device__ const uint8_t *atoms_of(int e, int tile, int k) const {
+        return atoms + e * atoms_expert + ((int64_t)atoms_u0 + (int64_t)tile * nk + k) * 1024;
     }
-    // the slot: the 128 rows' scales [128][G], then the group's B scale words
-    // [token j][g4][16] (bwoff: 16-byte aligned)
-    __device__ uint32_t bwoff() const { return (uint32_t)((128 * G + 15) & ~15); }
+    // the slot: the group's B scale words [token j][g4][16]
     __device__ uint32_t bw_bytes() const { return (uint32_t)g4 * BS_LIMBS * 4; }
 };
 
@@ -259,10 +305,10 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     extern __shared__ __align__(1024) uint8_t bs_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bs_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *stages = sm;
-    uint8_t *atoms = stages + (size_t)nst * BS_STAGE;
+    uint8_t *atoms = stages + (size_t)nst * BS_STAGE;  // per stage: A atoms (bulk copy) +0, +512; B atoms +1024, +1536
     uint8_t *bres = atoms + (size_t)nst * BS_ATOMS;  // [K stage][token j][16 rows x 128 B], 1024-aligned
     uint8_t *slots = bres + (size_t)pol.nk * BS_B_STAGE;
-    float *ex = reinterpret_cast<float *>(slots + 2 * (size_t)ssb);  // 64 rows x 4 tokens (up values)
+    float *ex = reinterpret_cast<float *>(slots + 2 * (size_t)ssb);  // 64 rows x 2 tokens (up values)
     BsBars *bb = reinterpret_cast<BsBars *>(ex + 64 * BS_TOKG);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ int vlist[BS_MAX_V];
@@ -270,17 +316,17 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     // barriers and TMEM first: they overlap the routing-slot loads of build_list
     if (warp == 2) {
         if (lane < nst) {
-            mbar_init(&bb->full[lane], 2);  // the producer's expect-tx arrival + the scale copies' commit
+            mbar_init(&bb->full[lane], 2);  // the producer's expect-tx arrival + the B atoms' arrival
             mbar_init(&bb->empty[lane], 1);
-        } else if (lane >= 8 && lane < 10) {
-            mbar_init(&bb->sfull[lane - 8], 1);
-            mbar_init(&bb->sempty[lane - 8], 4);
-        } else if (lane >= 10 && lane < 12) {
-            mbar_init(&bb->accfull[lane - 10], 1);
-            mbar_init(&bb->accempty[lane - 10], 4);
-        } else if (lane == 12) {
+        } else if (lane >= 16 && lane < 18) {
+            mbar_init(&bb->sfull[lane - 16], 1);
+            mbar_init(&bb->sempty[lane - 16], 1);
+        } else if (lane >= 18 && lane < 20) {
+            mbar_init(&bb->accfull[lane - 18], 1);
+            mbar_init(&bb->accempty[lane - 18], 4);
+        } else if (lane == 20) {
             mbar_init(&bb->bfull, 1);
-        } else if (lane == 13) {
+        } else if (lane == 21) {
             mbar_init(&bb->done, 1);
         }
         fence_mbar_init();
@@ -318,6 +364,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     // weight prefetch on SMs this grid leaves; it waits for this grid before
     // it reads what this one writes
     if (tid == 0) asm volatile("griddepcontrol.launch_dependents;");
+    // Every role but the producer needs the previous grid's outputs before its
+    // first wait can complete: it waits for that grid here, so that its
+    // bounded waits count from then on.  The producer streams its first
+    // weight stages first and waits later.
+    if (warp != 0) asm volatile("griddepcontrol.wait;" ::: "memory");
     pol.vl = vlist;
     const uint32_t tb = bb->tmem;
     const int nunits = nv_sh * pol.tpe();
@@ -334,7 +385,6 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 int d, tg, tile, ks, k0, k1;
                 pol.unit(u, d, tg, tile, ks, k0, k1);
                 const int e = pol.ms->list[d];
-                const uint8_t *eb = pol.expert(e);
                 const int slot = q & 1, nt = pol.ntok(d, tg);
                 // a new token group: its B rows replace the resident ones once the
                 // previous unit's MMAs are done (polled while this unit's A stages
@@ -358,9 +408,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 // its weight stages (up to a ring) before waiting for that grid
                 auto load_dep = [&]() {
                     for (int j = 0; j < nt; j++)
-                        bulk_g2s(ss + pol.bwoff() + j * pol.bw_bytes(),
-                                 pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS, pol.bw_bytes(),
-                                 &bb->sfull[slot]);
+                        bulk_g2s(ss + j * pol.bw_bytes(), pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS,
+                                 pol.bw_bytes(), &bb->sfull[slot]);
                     if (bpend && q == 0) load_b();
                 };
                 auto wait_dep = [&]() {
@@ -368,16 +417,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     dep = true;
                     load_dep();
                 };
-                mbar_arrive_expect_tx(&bb->sfull[slot], pol.scale_bytes(tile) + (uint32_t)nt * pol.bw_bytes());
-                if (pol.mode == 0) {
-                    const uint32_t n = pol.scale_bytes(tile) / 2;
-                    const int64_t off = (int64_t)tile * 64 * pol.G;
-                    bulk_g2s(ss, eb + pol.L.off[0][1] + off, n, &bb->sfull[slot]);
-                    bulk_g2s(ss + 64 * pol.G, eb + pol.L.off[1][1] + off, n, &bb->sfull[slot]);
-                } else {
-                    bulk_g2s(ss, eb + pol.L.off[2][1] + (int64_t)tile * 128 * pol.G, pol.scale_bytes(tile),
-                             &bb->sfull[slot]);
-                }
+                mbar_arrive_expect_tx(&bb->sfull[slot], (uint32_t)nt * pol.bw_bytes());
                 if (dep) load_dep();
                 nsl = q + 1;
                 for (int i = 0; i < k1 - k0; i++) {
@@ -385,13 +425,14 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     if (!dep && it >= (uint32_t)nst) wait_dep();
                     if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { bs_fail(pol.err, 22); ok = false; break; }
                     uint8_t *st = stages + (size_t)s * BS_STAGE;
-                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES);
+                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES + 1024);
                     if (pol.mode == 0) {
                         tma_box_4d(st, &maps.a0, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
                         tma_box_4d(st + BS_A_BYTES / 2, &maps.a1, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
                     } else {
                         tma_box_4d(st, &maps.a0, k * 128, tile * 128, e, pol.layer, &bb->full[s]);
                     }
+                    bulk_g2s(atoms + (size_t)s * BS_ATOMS, pol.atoms_of(e, tile, k), 1024, &bb->full[s]);
                     it++;
                     if (++s == nst) { s = 0; ph ^= 1u; }
                     if (bpend && dep && q > 0 && mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev)) load_b();
@@ -403,7 +444,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 }
             }
             if (!ok) bs_fail(pol.err, BS_ERR_PRODUCER);
-            // every copy issued has landed before the CTA may exit
+            if (!dep) asm volatile("griddepcontrol.wait;" ::: "memory");
+            // every copy issued has landed before the CTA may exit (a full
+            // barrier also needs the B atoms' arrival; a failed wait is recorded)
             for (int64_t k = (int64_t)it - 1; k >= 0 && k >= (int64_t)it - nst; k--)
                 if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
             for (int j = nsl - 1; j >= 0 && j >= nsl - 2; j--)
@@ -417,6 +460,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             int s = 0, q = 0;
             uint32_t ph = 0;
             const uint64_t da0 = umma_desc_sw128(smem_u32(stages)), db0 = umma_desc_sw128(smem_u32(bres));
+            const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
             int key = -1, nbl = 0;
             for (int u = u0; u < u1 && ok; u++, q++) {
                 int d, tg, tile, ks, k0, k1;
@@ -430,16 +474,21 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 }
                 if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 25); ok = false; break; }
                 tc_fence_after();
-                const uint32_t tacc = tb + (uint32_t)(b * 64);
+                const uint32_t tacc = tb + (uint32_t)(b * BS_ACC_COLS);
                 const uint32_t id0 = bs_idesc(N, 0), id2 = bs_idesc(N, 2);
                 for (int i = 0; i < k1 - k0; i++) {
                     const int k = pol.stage_k(k0, k1, i, tile, ks);
                     if (!mbar_wait(&bb->full[s], ph)) { bs_fail(pol.err, 26); ok = false; break; }
                     tc_fence_after();
+                    // the stage's scale atoms into its TMEM columns (A +0, +4; B +8, +12),
+                    // executed in order before the MMAs below
+                    const uint64_t dat = dat0 + (uint64_t)((s * BS_ATOMS) >> 4);
+                    const uint32_t tsf = tb + BS_SF_COL0 + 16u * (uint32_t)s;
+#pragma unroll
+                    for (int c = 0; c < 4; c++) bs_cp_atom(tsf + 4 * c, dat + 32 * c);
                     // descriptors: the start-address field is the low 14 bits (address >> 4)
                     const uint64_t da = da0 + (uint64_t)((s * BS_STAGE) >> 4);
                     const uint64_t db = db0 + (uint64_t)((k * BS_B_STAGE) >> 4);
-                    const uint32_t tsf = tb + BS_SF_COL0 + 16u * (uint32_t)s;  // A atoms +0, +4; B atoms +8, +12
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         const uint32_t sid = 2u * (uint32_t)(j & 1), g = 4u * (uint32_t)(j >> 1);
@@ -455,58 +504,34 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             tc_commit(&bb->done);
             if (!mbar_wait(&bb->done, 0)) bs_fail(pol.err, BS_ERR_MMA);
         }
-    } else if (warp < 6) {
-        // ------------------------------------------------------ scale-factor atoms
-        // After a timed-out wait a warp stops waiting and building but keeps
-        // taking part in the named barrier, so no other warp is left waiting.
-        const int t2 = tid - 64;  // 0..127: A row t2, B row t2 (< 64)
-        const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
+    } else if (warp == 2) {
+        // ------------------------------------------------------ B scale atoms
+        // lane = B row (limb lane % 16 of token lane / 16); after a timed-out
+        // wait the warp stops
         bool failed = false;
         int s = 0, q = 0;
         uint32_t ph = 0, it = 0;
-        for (int u = u0; u < u1; u++, q++) {
+        const int aoff = lane * 16;  // B rows < 32: byte (r % 32) * 16 + kb % 4
+        for (int u = u0; u < u1 && !failed; u++, q++) {
             int d, tg, tile, ks, k0, k1;
             pol.unit(u, d, tg, tile, ks, k0, k1);
             const int slot = q & 1;
-            if (!failed && !mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 27); }
-            const uint8_t *ss = slots + (size_t)slot * ssb;
-            const uint32_t *bw = reinterpret_cast<const uint32_t *>(ss + pol.bwoff());
+            if (!mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 27); break; }
+            const uint32_t *bw = reinterpret_cast<const uint32_t *>(slots + (size_t)slot * ssb);
             const int nrows = BS_LIMBS * pol.ntok(d, tg);
-            const uint8_t *arow = ss + t2 * pol.G;
-            const int aoff = (t2 & 31) * 16 + (t2 >> 5) * 4;
             for (int i = 0; i < k1 - k0; i++) {
                 const int k = pol.stage_k(k0, k1, i, tile, ks);
-                if (!failed && it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { failed = true; if (lane == 0) bs_fail(pol.err, 28); }
-                uint8_t *at = atoms + (size_t)s * BS_ATOMS;
-                if (!failed) {
+                if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { failed = true; if (lane == 0) bs_fail(pol.err, 28); break; }
+                uint8_t *at = atoms + (size_t)s * BS_ATOMS + 1024;
+                if (lane < nrows) {
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {  // A row t2: blocks 8k + 4h .. +3 -> atom h
-                        uint32_t w = 0;
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const int kb = 8 * k + 4 * h + i;
-                            const uint32_t c = kb < pol.G ? arow[kb] : 127u;
-                            w |= c << (8 * i);
-                        }
-                        *reinterpret_cast<uint32_t *>(at + 512 * h + aoff) = w;
-                    }
-                    if (t2 < nrows) {  // B row t2 = limb t2 % 16 of token t2 / 16
-#pragma unroll
-                        for (int h = 0; h < 2; h++)
-                            *reinterpret_cast<uint32_t *>(at + 1024 + 512 * h + aoff) =
-                                bw[((t2 >> 4) * pol.g4 + 2 * k + h) * BS_LIMBS + (t2 & 15)];
-                    }
-                    fence_proxy_async_smem();
+                    for (int h = 0; h < 2; h++)
+                        *reinterpret_cast<uint32_t *>(at + 512 * h + aoff) =
+                            bw[((lane >> 4) * pol.g4 + 2 * k + h) * BS_LIMBS + (lane & 15)];
                 }
-                named_bar_sync(2, 128);  // the four atoms are written
-                if (t2 == 0 && !failed) {
-                    tc_fence_after();
-                    const uint64_t dat = dat0 + (uint64_t)((s * BS_ATOMS) >> 4);
-                    const uint32_t tsf = tb + BS_SF_COL0 + 16u * (uint32_t)s;
-#pragma unroll
-                    for (int i = 0; i < 4; i++) bs_cp_atom(tsf + 4 * i, dat + 32 * i);
-                    tc_commit(&bb->full[s]);
-                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bb->full[s]);
                 it++;
                 if (++s == nst) { s = 0; ph ^= 1u; }
             }
@@ -514,6 +539,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             if (lane == 0 && !failed) mbar_arrive(&bb->sempty[slot]);
         }
         if (failed && lane == 0) bs_fail(pol.err, BS_ERR_ATOMS);
+    } else if (warp < 6) {
+        // warps 3-5: no role after setup
     } else {
         // ------------------------------------------------------ epilogue
         const int ew = warp & 3, r = 32 * ew + lane;  // TMEM lane quadrant = warp % 4
@@ -546,7 +573,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 v[j] = 0.f;
                 if (j < nt && !failed) {
                     float t[16];
-                    tmem_ld16(tb + (uint32_t)(b * 64 + BS_LIMBS * j) + ((uint32_t)(32 * ew) << 16), t);
+                    tmem_ld16(tb + (uint32_t)(b * BS_ACC_COLS + BS_LIMBS * j) + ((uint32_t)(32 * ew) << 16), t);
                     float acc = t[0];
 #pragma unroll
                     for (int i = 1; i < 16; i++) acc += t[i];
@@ -650,6 +677,26 @@ int bs_map_limbs(CUtensorMap *map, const uint8_t *limbs, int kpad, int rows) {
     return MG_OK;
 }
 
+size_t bs_atoms_bytes(const mg_expert_layout &L, int kpad_h, int kpad_f) {
+    const int64_t units = (L.ffn / 64) * (kpad_h / BS_KE) + ((L.hidden + 127) / 128) * (kpad_f / BS_KE);
+    return (size_t)units * 1024;
+}
+
+int bs_atoms_build(BsBuffers &b, const mg_expert_layout &L, const uint8_t *experts, int n_layers, int n_local,
+                   cudaStream_t st) {
+    MG_REQUIRE(bsmoe_supported(L) && b.atoms && n_layers > 0 && n_local > 0, MG_ERR_ARG,
+               "block-scaled MoE: scale atoms need MXFP4 experts with ue8m0 scales");
+    const int nk_h = b.kpad_h / BS_KE, nk_f = b.kpad_f / BS_KE;
+    b.atoms_dn = (int)(L.ffn / 64) * nk_h;
+    b.atoms_expert = (int64_t)bs_atoms_bytes(L, b.kpad_h, b.kpad_f);
+    const int units = (int)(b.atoms_expert / 1024);
+    const int64_t n_le = (int64_t)n_layers * n_local;
+    dim3 g((unsigned)units, (unsigned)(n_le < 65535 ? n_le : 65535));
+    k_bs_atoms<<<g, 256, 0, st>>>(experts, L, n_le, n_local, nk_h, nk_f, b.atoms_dn, b.atoms, b.atoms_expert);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
 int bs_buffers_init(BsBuffers &b) {
     // limbs zero everywhere and scale codes 127: the K pad and the unencoded
     // rows BS_LQ..BS_LIMBS-1 of every token keep them
@@ -665,6 +712,7 @@ int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     const mg_expert_layout &L = a.L;
     MG_REQUIRE(bsmoe_supported(L) && a.maps && a.n_tok >= 1 && a.n_tok <= 8 && a.n_tok * a.top_k <= B.slots_max,
                MG_ERR_ARG, "block-scaled MoE: unsupported call");
+    MG_REQUIRE(B.atoms && B.atoms_expert > 0, MG_ERR_STATE, "block-scaled MoE: expert scale atoms not built");
     int *err = stream_error_word();
     MG_REQUIRE(err, MG_ERR_OOM, "block-scaled MoE: no error word");
     {  // activations -> limbs
@@ -686,6 +734,8 @@ int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     p.alpha = a.alpha;
     p.limit = a.limit;
     p.err = err;
+    p.atoms = B.atoms + (int64_t)a.layer * a.n_experts * B.atoms_expert;
+    p.atoms_expert = B.atoms_expert;
     // gate/up: B = the expert's tokens' x limbs, output: their h limbs
     BsMapsK mg{};
     mg.a0 = a.maps[0];
@@ -700,7 +750,8 @@ int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     p.hg4 = B.kpad_f / 128;
     p.nk = B.kpad_h / BS_KE;
     p.G = (int)(L.hidden / 32);
-    BS_TRY(bs_launch(mg, p, ((128 * (size_t)p.G + 15) & ~(size_t)15) + (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st));
+    p.atoms_u0 = 0;
+    BS_TRY(bs_launch(mg, p, (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st));
     // down: B = the expert's slots' h limbs
     BsMapsK md{};
     md.a0 = a.maps[2];
@@ -714,7 +765,8 @@ int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     p.y = a.y;
     p.ks_count = a.down_ksplit_out;
     p.kst = (p.nk + p.ks_count - 1) / p.ks_count;
-    return bs_launch(md, p, ((128 * (size_t)p.G + 15) & ~(size_t)15) + (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st);
+    p.atoms_u0 = B.atoms_dn;
+    return bs_launch(md, p, (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st);
 }
 
 }  // namespace mg

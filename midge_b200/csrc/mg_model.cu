@@ -642,6 +642,9 @@ extern "C" int mg_model_ready(mg_model *m) {
         TRY(bs_map_limbs(&b.map_x, b.xl, b.kpad_h, 8));
         TRY(bs_map_limbs(&b.map_h, b.hl, b.kpad_f, b.slots_max));
         TRY(bs_buffers_init(b));
+        // the experts' scales as the tensor core reads them (one atom copy)
+        TRY(dalloc(m, &b.atoms, (size_t)s.n_layers * m->n_local * bs_atoms_bytes(m->el, b.kpad_h, b.kpad_f)));
+        TRY(bs_atoms_build(b, m->el, m->experts, s.n_layers, m->n_local, m->st));
         // the block-scaled down pass runs whole rows per unit: one partial
         // plane (moe_y was sized for the streamed kernels' two)
         m->ks_down = 1;
