@@ -64,6 +64,87 @@ __global__ void k_qkv_post(QkvPostArgs a) {
     }
 }
 
+// The same steps with the K-split sum in front (decode): warp = (token, head)
+// over the q, k and v heads.  The head's values are the planes' sum in plane
+// order from 0 (as k_sum_parts), written back to q / k / v_out after the
+// per-head RMSNorm and RoPE of k_qkv_post, then k and v into the cache.
+constexpr int QP_WARPS = 8;
+__global__ void __launch_bounds__(QP_WARPS * 32) k_qkv_post_parts(QkvPostArgs a) {
+    __shared__ float hv[QP_WARPS][128];
+    const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.y * QP_WARPS + w;
+    const int hd = a.head_dim, half = hd >> 1, nh = a.n_heads, nkv = a.n_kv_heads;
+    if (h >= nh + 2 * nkv) return;  // warp-uniform; no block barrier follows
+    const int kind = h < nh ? 0 : (h < nh + nkv ? 1 : 2);  // q, k, v
+    const int hh = kind == 0 ? h : (kind == 1 ? h - nh : h - nh - nkv);
+    const float *src = kind == 0 ? a.q : (kind == 1 ? a.k : a.v);
+    const int64_t ld = kind == 0 ? a.ldq : a.ldk;
+    const int64_t off = (int64_t)t * ld + (int64_t)hh * hd;
+    const float *ps = a.parts + (src - a.q) + off;  // parts rows are laid out as q / k / v
+    float *vec = hv[w];
+    float ss = 0.f;
+    for (int i = lane; i < hd; i += 32) {
+        float v = 0.f;
+        for (int k = 0; k < a.ks; k++) v += ps[(int64_t)k * a.plane + i];
+        vec[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    __syncwarp();
+    const int pos = a.tok_pos[t];
+    const int seq = a.tok_seq ? a.tok_seq[t] : 0;
+    const int kv_dim = nkv * hd;
+    const int slot = pos % a.cap;
+    if (kind < 2) {
+        if (a.qn) {
+            ss = warp_sum(ss);
+            const float inv = 1.0f / sqrtf(ss / (float)hd + a.eps);
+            const float *nw = kind == 0 ? a.qn : a.kn;
+            for (int i = lane; i < hd; i += 32) vec[i] = __fmul_rn(__fmul_rn(vec[i], inv), nw[i]);
+            __syncwarp();
+        }
+        const float *co = a.rope_cos + (int64_t)pos * half, *si = a.rope_sin + (int64_t)pos * half;
+        float *dst = (kind == 0 ? a.q : a.k) + off;
+        for (int i = lane; i < half; i += 32) {
+            const float x0 = vec[i], x1 = vec[i + half];
+            const float y0 = __fsub_rn(__fmul_rn(x0, co[i]), __fmul_rn(x1, si[i]));
+            const float y1 = __fadd_rn(__fmul_rn(x1, co[i]), __fmul_rn(x0, si[i]));
+            dst[i] = y0;
+            dst[i + half] = y1;
+            if (kind == 1) {
+                const int64_t c = (int64_t)hh * hd + i;
+                if (a.write_cache) {
+                    uint16_t *kc = a.kc + ((int64_t)seq * a.cap + slot) * kv_dim;
+                    kc[c] = f2h_ftz(y0);
+                    kc[c + half] = f2h_ftz(y1);
+                }
+                if (a.tmp_k) {
+                    a.tmp_k[(int64_t)t * kv_dim + c] = f2h_ftz(y0);
+                    a.tmp_k[(int64_t)t * kv_dim + c + half] = f2h_ftz(y1);
+                }
+            }
+        }
+    } else {
+        for (int i = lane; i < hd; i += 32) {
+            const float v = vec[i];
+            const int64_t c = (int64_t)hh * hd + i;
+            if (a.v_out) a.v_out[off + i] = v;
+            if (a.write_cache) a.vc[((int64_t)seq * a.cap + slot) * kv_dim + c] = f2h_ftz(v);
+            if (a.tmp_v) a.tmp_v[(int64_t)t * kv_dim + c] = f2h_ftz(v);
+        }
+    }
+}
+
+int qkv_post_parts(const QkvPostArgs &a, int n_tok, cudaStream_t st) {
+    if (n_tok <= 0) return MG_OK;
+    MG_REQUIRE(a.parts && a.ks >= 1 && a.head_dim <= 128 && a.ldq == a.ldk && a.k >= a.q && a.v >= a.k &&
+                   (a.v - a.q) + (int64_t)a.n_kv_heads * a.head_dim <= a.ldq,
+               MG_ERR_ARG, "qkv_post_parts: q, k, v must share one row of stride ldq");
+    dim3 g(n_tok, (a.n_heads + 2 * a.n_kv_heads + QP_WARPS - 1) / QP_WARPS);
+    k_qkv_post_parts<<<g, QP_WARPS * 32, 0, st>>>(a);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
 int qkv_post(const QkvPostArgs &a, int n_tok, cudaStream_t st) {
     if (n_tok <= 0) return MG_OK;
     k_qkv_post<<<n_tok, 256, 0, st>>>(a);
@@ -332,13 +413,16 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
 
 // Combine splits and the sink:
 //   out = sum_s acc_s e^(m_s-M) / (e^(sink-M) + sum_s l_s e^(m_s-M)),  M = max(sink, m_s)
-// One block (2 warps) per (head, sequence): the split maxima and the
-// denominator are reduced once, each split's weight e^(m_s-M) is kept in
-// shared memory (max_splits floats), and each thread accumulates its output
-// dimensions over the splits in ascending order.
-__global__ void k_attn_combine(AttnDecodeArgs a) {
+// One block (8 warps) per (head, sequence): the split maxima and the
+// denominator are reduced once and each split's weight e^(m_s-M) is kept in
+// shared memory (max_splits floats); warp w sums the splits w, w + 8, ... in
+// ascending order for every output dimension (lane + 32 r), and the eight
+// warp sums are added in warp order.
+constexpr int AC_WARPS = 8;
+__global__ void __launch_bounds__(AC_WARPS * 32) k_attn_combine(AttnDecodeArgs a) {
     extern __shared__ float cw[];
-    __shared__ float red[2][2];
+    __shared__ float red[2][AC_WARPS];
+    __shared__ float ws[AC_WARPS][128];
     const int h = blockIdx.x, si = blockIdx.y, t = threadIdx.x, w = t >> 5, lane = t & 31;
     const int hd = a.head_dim;
     const int pos = a.pos[si];
@@ -351,7 +435,9 @@ __global__ void k_attn_combine(AttnDecodeArgs a) {
     mx = warp_max(mx);
     if (lane == 0) red[0][w] = mx;
     __syncthreads();
-    const float M = fmaxf(red[0][0], red[0][1]);
+    float M = red[0][0];
+#pragma unroll
+    for (int i = 1; i < AC_WARPS; i++) M = fmaxf(M, red[0][i]);
     float ls = 0.f;
     for (int s = t; s < nsplit; s += blockDim.x) {
         const float e = expf(part[s * (hd + 2)] - M);
@@ -361,12 +447,28 @@ __global__ void k_attn_combine(AttnDecodeArgs a) {
     ls = warp_sum(ls);
     if (lane == 0) red[1][w] = ls;
     __syncthreads();
-    const float L = (a.sinks ? expf(sink - M) : 0.f) + (red[1][0] + red[1][1]);
+    float lsum = red[1][0];
+#pragma unroll
+    for (int i = 1; i < AC_WARPS; i++) lsum += red[1][i];
+    const float L = (a.sinks ? expf(sink - M) : 0.f) + lsum;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};  // dimensions lane + 32 r (head_dim <= 128)
+    for (int s = w; s < nsplit; s += AC_WARPS) {
+        const float c = cw[s];
+        const float *ps = part + s * (hd + 2) + 2;
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+            if (lane + 32 * r < hd) o[r] = fmaf(ps[lane + 32 * r], c, o[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+        if (lane + 32 * r < hd) ws[w][lane + 32 * r] = o[r];
+    __syncthreads();
     const float inv = 1.0f / L;
     for (int i = t; i < hd; i += blockDim.x) {
-        float o = 0.f;
-        for (int s = 0; s < nsplit; s++) o = fmaf(part[s * (hd + 2) + 2 + i], cw[s], o);
-        a.out[(int64_t)si * a.ldo + (int64_t)h * hd + i] = o * inv;
+        float v = ws[0][i];
+#pragma unroll
+        for (int k = 1; k < AC_WARPS; k++) v += ws[k][i];
+        a.out[(int64_t)si * a.ldo + (int64_t)h * hd + i] = v * inv;
     }
 }
 
@@ -385,7 +487,7 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
         dim3 g2(a.n_heads, n_seqs);
         const size_t cs = (size_t)a.max_splits * 4;
         if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
-        k_attn_combine<<<g2, 64, cs, st>>>(a);
+        k_attn_combine<<<g2, AC_WARPS * 32, cs, st>>>(a);
         MG_CHECK_LAUNCH();
         return MG_OK;
     }
@@ -398,7 +500,7 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     dim3 g2(a.n_heads, n_seqs);
     const size_t cs = (size_t)a.max_splits * 4;
     if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
-    k_attn_combine<<<g2, 64, cs, st>>>(a);
+    k_attn_combine<<<g2, AC_WARPS * 32, cs, st>>>(a);
     MG_CHECK_LAUNCH();
     return MG_OK;
 }

@@ -19,8 +19,15 @@ struct QkvPostArgs {
     uint16_t *kc, *vc;                 // layer cache [max_seqs x cap x kv_dim]
     int cap;
     uint16_t *tmp_k, *tmp_v;           // optional [n_tok x kv_dim] f16 copies
+    // optional: q, k, v are the sums of ks K-split planes (plane stride
+    // `plane`, rows as q/k/v) and written to q, k and v_out (qkv_post_parts)
+    const float *parts;
+    int ks;
+    int64_t plane;
+    float *v_out;
 };
 int qkv_post(const QkvPostArgs &a, int n_tok, cudaStream_t st);
+int qkv_post_parts(const QkvPostArgs &a, int n_tok, cudaStream_t st);
 
 struct AttnDecodeArgs {
     const float *q;  // [n_seqs x ldq]

@@ -901,7 +901,6 @@ static int layer_stream(mg_model *m, int layer, int n) {
         g.mat[i].rows = mats[i]->rows; g.mat[i].y = m->qkv_part + off[i]; g.mat[i].ldy = qkv_dim;
     }
     TRY(stream_gemv(g, st));
-    TRY(sum_parts(m->qkv_part, m->ks_qkv, (int64_t)n * qkv_dim, n, qkv_dim, qkv_dim, m->qkv, qkv_dim, 0, st));
     const int cap = m->cap[layer];
     QkvPostArgs qa{};
     qa.q = m->qkv; qa.k = m->qkv + q_dim; qa.v = m->qkv + q_dim + kv_dim; qa.ldq = qkv_dim; qa.ldk = qkv_dim;
@@ -910,7 +909,9 @@ static int layer_stream(mg_model *m, int layer, int n) {
     qa.eps = s.norm_eps; qa.rope_cos = m->rope_cos; qa.rope_sin = m->rope_sin;
     qa.tok_pos = m->tok_pos; qa.tok_seq = m->tok_seq; qa.write_cache = 1;
     qa.kc = m->kc[layer]; qa.vc = m->vc[layer]; qa.cap = cap;
-    TRY(qkv_post(qa, n, st));
+    // the K-split partial planes are summed inside (k_sum_parts order)
+    qa.parts = m->qkv_part; qa.ks = m->ks_qkv; qa.plane = (int64_t)n * qkv_dim; qa.v_out = m->qkv + q_dim + kv_dim;
+    TRY(qkv_post_parts(qa, n, st));
     AttnDecodeArgs da{};
     da.q = m->qkv; da.ldq = qkv_dim; da.seq_ids = m->tok_seq; da.pos = m->tok_pos;
     da.kc = m->kc[layer]; da.vc = m->vc[layer]; da.cap = cap;

@@ -137,13 +137,13 @@ __global__ void __launch_bounds__(ROUTER_THREADS) k_router(RouterArgs a) {
 //   k_router_prep (block per token): residual = x + the attention-output
 //   K-split partials (summed in plane order), written to x_out; its RMS norm
 //   -> xb_out.
-//   k_router_logits (block per 8 experts, all tokens): the 8 weight rows and
+//   k_router_logits (block per 4 experts, all tokens): the 4 weight rows and
 //   the tokens' normed rows are bulk-copied into shared memory (row stride
 //   padded so the 8-lane groups of a warp hit distinct banks) and every logit
 //   is reduced in the AVX2 lane order (engine/mkern.h:85-99); the last block
 //   to finish (atomic ticket) runs the top-k, routing weights and usage for
 //   all tokens.
-constexpr int RG = 8;  // experts per logits block
+constexpr int RG = 4;  // experts per logits block (32 blocks stream the 128 rows of the 120b router)
 
 __global__ void __launch_bounds__(1024) k_router_prep(RouterArgs a) {
     __shared__ float scratch[32];
@@ -153,6 +153,43 @@ __global__ void __launch_bounds__(1024) k_router_prep(RouterArgs a) {
     constexpr int PER = 4;  // elements per thread per pass (loads issued together)
     float v[PER];
     float ss = 0.f;
+    if (H <= (int64_t)blockDim.x * PER) {  // one pass: the row stays in registers through the norm
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+            v[j] = c < H ? xr[c] : 0.f;
+        }
+        if (a.x_parts) {
+            float p[PER] = {0.f, 0.f, 0.f, 0.f};
+            for (int k = 0; k < a.x_parts_ks; k++) {
+                const float *pp = a.x_parts + (int64_t)k * a.x_parts_stride + (int64_t)tok * H;
+#pragma unroll
+                for (int j = 0; j < PER; j++) {
+                    const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+                    if (c < H) p[j] += pp[c];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+                v[j] = __fadd_rn(v[j], p[j]);
+                if (c < H) a.x_out[(int64_t)tok * H + c] = v[j];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+            if (c < H) ss = fmaf(v[j], v[j], ss);
+        }
+        ss = block_sum(ss, scratch);
+        const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+            if (c < H) a.xb_out[(int64_t)tok * H + c] = __fmul_rn(__fmul_rn(v[j], inv), a.norm_w[c]);
+        }
+        return;
+    }
     for (int64_t c0 = threadIdx.x; c0 < H; c0 += (int64_t)blockDim.x * PER) {
 #pragma unroll
         for (int j = 0; j < PER; j++) {
@@ -263,7 +300,7 @@ __global__ void k_router_topk(RouterArgs a, const float *logits) {
     router_topk_warp(a, logits + (int64_t)blockIdx.x * a.n_experts, blockIdx.x, taken, s_sel, s_val);
 }
 
-constexpr int RL_THREADS = 512;  // 64 groups of 8 lanes: 8 experts x 8 tokens
+constexpr int RL_THREADS = RG * 8 * 8;  // groups of 8 lanes: RG experts x 8 tokens
 
 // blockIdx.y: group of 8 tokens; ticket null: no top-k here (a separate
 // per-token kernel runs it)
@@ -299,7 +336,7 @@ __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, floa
         return;
     }
     const int gi = threadIdx.x >> 3, lane8 = threadIdx.x & 7;
-    const int j = gi & 7, t = gi >> 3;
+    const int j = gi % RG, t = gi / RG;
     const int64_t H8 = H & ~(int64_t)7;
     float acc = 0.f;
     const bool live = j < ne && t < ntk;
