@@ -53,7 +53,7 @@ MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # launch triple of the block-scaled decode MoE, from the ncu capture
 # summarised in profiles/moe_bsmoe_c4_decode8.md (per-launch traffic =
 # experts routed x this figure)
-TRAFFIC_PER_EXPERT = 13540000
+TRAFFIC_PER_EXPERT = 13780000
 DECODE_PER_STEP = 64
 N_SEQ = 8
 

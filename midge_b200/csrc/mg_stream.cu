@@ -242,7 +242,43 @@ int moe_stream(const MoeStreamArgs &a, cudaStream_t st) {
 
 // ----------------------------------------------- MoE combine + RMSNorm
 // x[t] += sum_i w[t][i] * sum_ks y[ks][t*k+i]   (rank order, engine/midge.c:544-548)
-// then xb[t] = rmsnorm(x[t]) * nw.  One block per token.
+// then xb[t] = rmsnorm(x[t]) * nw.  One block per token; with one plane, rows
+// of up to 4 x 1024 values stay in registers (all of a thread's loads issue
+// before any store), otherwise a strided loop.
+template <int KS>
+__device__ __forceinline__ float cn_value(const CombineNormArgs &a, const float *xi, int64_t c, int64_t H,
+                                          int64_t plane, int nk, const int *s_slot, const float *s_w) {
+    float v = xi[c];
+    if (!a.y) return v;
+    // all of this element's plane values first (independent loads), then the
+    // reference's order: per slot the planes in order, slots in rank order
+    float moe = 0.f;
+    if (nk <= 8) {
+        float yv[8][KS];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float *yp = a.y + (int64_t)s_slot[i < nk ? i : 0] * H + c;
+#pragma unroll
+            for (int ks = 0; ks < KS; ks++) yv[i][ks] = i < nk ? yp[ks * plane] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float yy = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ks++) yy += yv[i][ks];
+            if (i < nk) moe = __fadd_rn(moe, __fmul_rn(s_w[i], yy));
+        }
+    } else {
+        for (int i = 0; i < nk; i++) {
+            const float *yp = a.y + (int64_t)s_slot[i] * H + c;
+            float yy = 0.f;
+            for (int ks = 0; ks < KS; ks++) yy += yp[ks * plane];
+            moe = __fadd_rn(moe, __fmul_rn(s_w[i], yy));
+        }
+    }
+    return __fadd_rn(v, moe);
+}
+
 template <int KS>  // K-split planes of the expert outputs (compile time so their loads issue together)
 __global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
     __shared__ float scratch[32];
@@ -252,54 +288,56 @@ __global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
     const int64_t H = a.hidden;
     float *x = a.x + (int64_t)t * H;
     const float *xi = (a.x_in ? a.x_in : a.x) + (int64_t)t * H;
-    if (threadIdx.x == 0) {  // this token's valid routing slots, rank order
-        int k = 0;
-        if (a.y)
-            for (int i = 0; i < a.top_k && i < 16; i++) {
-                const int e = a.sel[t * a.top_k + i];
-                if (e < 0 || e >= a.n_experts) continue;
-                s_slot[k] = t * a.top_k + i;
-                s_w[k] = a.w[t * a.top_k + i];
-                k++;
-            }
-        s_k = k;
+    if (threadIdx.x < 32) {  // this token's valid routing slots in rank order (ballot prefix)
+        const int i = threadIdx.x;
+        bool valid = false;
+        float wv = 0.f;
+        if (a.y && i < a.top_k && i < 16) {
+            const int e = a.sel[t * a.top_k + i];
+            valid = e >= 0 && e < a.n_experts;
+            if (valid) wv = a.w[t * a.top_k + i];
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, valid);
+        if (valid) {
+            const int r = __popc(m & ((1u << i) - 1u));
+            s_slot[r] = t * a.top_k + i;
+            s_w[r] = wv;
+        }
+        if (i == 0) s_k = __popc(m);
     }
     __syncthreads();
     const int nk = s_k;
     const int64_t plane = (int64_t)a.n_tok * a.top_k * H;
     float ss = 0.f;
-    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
-        float v = xi[c];
-        if (a.y) {
-            // all of this element's plane values first (independent loads), then the
-            // reference's order: per slot the planes in order, slots in rank order
-            float moe = 0.f;
-            if (nk <= 8) {
-                float yv[8][KS];
+    constexpr int PER = 4;
+    if (KS == 1 && H <= (int64_t)blockDim.x * PER) {  // (more planes would spill registers)
+        float v[PER];
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const float *yp = a.y + (int64_t)s_slot[i < nk ? i : 0] * H + c;
-#pragma unroll
-                    for (int ks = 0; ks < KS; ks++) yv[i][ks] = i < nk ? yp[ks * plane] : 0.f;
-                }
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    float yy = 0.f;
-#pragma unroll
-                    for (int ks = 0; ks < KS; ks++) yy += yv[i][ks];
-                    if (i < nk) moe = __fadd_rn(moe, __fmul_rn(s_w[i], yy));
-                }
-            } else {
-                for (int i = 0; i < nk; i++) {
-                    const float *yp = a.y + (int64_t)s_slot[i] * H + c;
-                    float yy = 0.f;
-                    for (int ks = 0; ks < KS; ks++) yy += yp[ks * plane];
-                    moe = __fadd_rn(moe, __fmul_rn(s_w[i], yy));
-                }
-            }
-            v = __fadd_rn(v, moe);
-            x[c] = v;
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+            v[j] = c < H ? cn_value<KS>(a, xi, c, H, plane, nk, s_slot, s_w) : 0.f;
         }
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+            if (c < H) {
+                if (a.y) x[c] = v[j];
+                ss = fmaf(v[j], v[j], ss);
+            }
+        }
+        ss = block_sum(ss, scratch);
+        const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+        if (a.xb)
+#pragma unroll
+            for (int j = 0; j < PER; j++) {
+                const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+                if (c < H) a.xb[(int64_t)t * H + c] = __fmul_rn(__fmul_rn(v[j], inv), a.nw[c]);
+            }
+        return;
+    }
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
+        const float v = cn_value<KS>(a, xi, c, H, plane, nk, s_slot, s_w);
+        if (a.y) x[c] = v;
         ss = fmaf(v, v, ss);
     }
     ss = block_sum(ss, scratch);
