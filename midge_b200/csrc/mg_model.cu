@@ -266,6 +266,8 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     const char *mk = getenv("MIDGE_MOE_KERNELS");
     m->tc_moe = mk && !strcmp(mk, "tc");
     m->bs_moe = !(mk && (!strcmp(mk, "tc") || !strcmp(mk, "mma")));  // where the format allows (set in ready)
+    const char *tk = getenv("MIDGE_TRUNK_KERNELS");
+    m->q8mma = tk && !strcmp(tk, "i8");  // where the trunk is q8r (checked in ready)
     const char *pk = getenv("MIDGE_PREFILL_KERNELS");
     m->tc_prefill = !(pk && !strcmp(pk, "tile"));
     const char *pc = getenv("MIDGE_PREFILL_CHUNK");
@@ -651,6 +653,8 @@ extern "C" int mg_model_ready(mg_model *m) {
     } else {
         m->bs_moe = false;
     }
+    // int8 tensor-core trunk GEMVs: the q8r trunk's TMA maps
+    if (!(m->maps_ok && H % 16 == 0 && q_dim % 16 == 0)) m->q8mma = false;
     m->attn_max_splits = (m->ctx + m->attn_split - 1) / m->attn_split;
     TRY(dalloc(m, &m->attn_part, (size_t)DEC_MAX * s.n_heads * m->attn_max_splits * (s.head_dim + 2) * 4));
     MG_CUDA(cudaHostAlloc(&m->h_toks, R * 4, cudaHostAllocDefault));
@@ -900,7 +904,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
         g.mat[i].w = mats[i]->data; g.mat[i].scales = mats[i]->scales; g.mat[i].bias = bias[i];
         g.mat[i].rows = mats[i]->rows; g.mat[i].y = m->qkv_part + off[i]; g.mat[i].ldy = qkv_dim;
     }
-    TRY(stream_gemv(g, st));
+    TRY(m->q8mma ? q8mma_gemv(g, st) : stream_gemv(g, st));
     const int cap = m->cap[layer];
     QkvPostArgs qa{};
     qa.q = m->qkv; qa.k = m->qkv + q_dim; qa.v = m->qkv + q_dim + kv_dim; qa.ldq = qkv_dim; qa.ldk = qkv_dim;
@@ -927,7 +931,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     go.mat[0].map = &m->map_o[layer];
     go.mat[0].w = m->wo[layer].data; go.mat[0].scales = m->wo[layer].scales; go.mat[0].bias = m->bo[layer];
     go.mat[0].rows = H; go.mat[0].y = m->o_part; go.mat[0].ldy = H;
-    TRY(stream_gemv(go, st));
+    TRY(m->q8mma ? q8mma_gemv(go, st) : stream_gemv(go, st));
     RouterArgs ra{};
     ra.x = m->x; ra.norm_w = m->mlp_norm[layer]; ra.eps = s.norm_eps; ra.xb_out = m->xb;
     ra.rw = (const float *)m->router_w[layer].data; ra.rb = m->router_b[layer];

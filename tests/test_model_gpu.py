@@ -198,6 +198,33 @@ def test_decode_moe_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, moe):
     m.close()
 
 
+@pytest.mark.parametrize("trunk", ["i8", "mma"])
+def test_decode_trunk_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, trunk):
+    """Both decode kernels of the int8 trunk (q, k, v, o): tcgen05 kind::i8
+    on exact int8 activation limbs (MIDGE_TRUNK_KERNELS=i8) and the mma.sync
+    streamed kernels (the default), 8 concurrent sequences against the
+    oracle, two steps."""
+    if trunk == "i8":
+        monkeypatch.setenv("MIDGE_TRUNK_KERNELS", trunk)
+    else:
+        monkeypatch.delenv("MIDGE_TRUNK_KERNELS", raising=False)
+    rng = np.random.default_rng(47)
+    prompts = [rng.integers(0, 1024, 4 + i).astype(np.int32) for i in range(8)]
+    m = abi.Model.from_dir(c1_dir, ctx=64, max_seqs=8)
+    first = np.array([int(np.argmax(m.forward_batch(i, p, logits_mode=1))) for i, p in enumerate(prompts)], np.int32)
+    seqs = np.arange(8, dtype=np.int32)
+    _, nxt = m.decode_step(seqs, first)
+    lg, _ = m.decode_step(seqs, nxt, want_logits=True)
+    for i, p in enumerate(prompts):
+        om = orc.OracleModel(c1_dir, 64)
+        om.prefill(list(p))
+        om.forward(int(first[i]))
+        want = om.forward(int(nxt[i]))
+        om.close()
+        assert max_rel(want, lg[i]) < LOGIT_TOL
+    m.close()
+
+
 def test_decode_block_scaled_token_groups_vs_oracle(torch_cuda, tmp_path, monkeypatch):
     """Block-scaled decode experts when every expert takes all 8 tokens: each
     expert's slots form four token groups of two, each group's tiles spread
