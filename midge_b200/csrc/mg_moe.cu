@@ -361,9 +361,18 @@ __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, floa
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // every token's logits into shared memory once (the weight and token rows
+    // are no longer needed), so the top-k rounds do not go back to L2
+    const int nl = a.n_tok * a.n_experts;
+    const bool stage = nl <= (RG + a.n_tok) * (int)ld;
+    if (stage) {
+        for (int i = threadIdx.x; i < nl; i += RL_THREADS) rs_[i] = logits[i];
+        __syncthreads();
+    }
+    const float *lsrc = stage ? rs_ : logits;
     const int w = threadIdx.x >> 5;
     for (int tok = w; tok < a.n_tok; tok += RL_THREADS / 32)
-        router_topk_warp(a, logits + (int64_t)tok * a.n_experts, tok, taken[w], s_sel[w], s_val[w]);
+        router_topk_warp(a, lsrc + (int64_t)tok * a.n_experts, tok, taken[w], s_sel[w], s_val[w]);
     if (threadIdx.x == 0) *ticket = 0;  // ready for the next launch
 }
 
