@@ -268,54 +268,66 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnDecodeArgs a) 
 }
 
 // Decode attention on the tensor cores (head_dim 64, up to 8 query heads per
-// KV head).  Block = one warp = (kv head, sequence, split of 64 positions).
-// The A operand of every MMA stacks the f16 hi halves of the group's query
-// rows (rows 0..7) over their lo halves (rows 8..15), so D rows g and g + 8
-// are the two halves of the same (head, position) and sum exactly in fp32:
-//   S = [q_hi; q_lo] K^T, softmax pieces in fp32, O = [P_hi; P_lo] V.
-// K and V tiles (64 positions x 64 dims of f16, as cached) come in by
-// cp.async into 128-byte-swizzled shared memory, read with ldmatrix.  Writes
-// the same per-split partials (max, sum, acc) as k_attn_decode.
+// KV head).  Block = one warp = (kv head, sequence, split of split_len
+// positions, a multiple of 64), walking the split in tiles of 64 positions
+// with an online softmax: the next tile's K and V (64 positions x 64 dims of
+// f16, as cached) come in by cp.async into 128-byte-swizzled shared memory
+// while the current one is multiplied.  The A operand of every MMA stacks
+// the f16 hi halves of the group's query rows (rows 0..7) over their lo
+// halves (rows 8..15), so D rows g and g + 8 are the two halves of the same
+// (head, position) and sum exactly in fp32:
+//   S = [q_hi; q_lo] K^T, softmax pieces in fp32 against the running maximum
+//   M (earlier tiles' sums and outputs rescaled by e^(M_old - M)),
+//   O += [P_hi; P_lo] V.
+// Writes per-split partials (max, sum, acc) for the combine.
 constexpr int TCD_POS = 64;
 
 __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
     constexpr int HD = 64;
-    __shared__ __align__(128) uint16_t kv[2][TCD_POS * HD];
+    // [buffer][K, V] tiles: two buffers when a split has more than one tile
+    extern __shared__ __align__(128) uint16_t kv[];
     const int kh = blockIdx.x, si = blockIdx.y, sp = blockIdx.z;
     const int seq = a.seq_ids[si];
     const int gq = a.n_heads / a.n_kv_heads, kv_dim = a.n_kv_heads * HD;
     const int pos = a.pos[si];
     const int nctx = pos + 1 < a.cap ? pos + 1 : a.cap;
-    const int t0 = sp * TCD_POS;
-    const int np = min(TCD_POS, nctx - t0);
+    const int t0 = sp * a.split_len;
+    const int npa = min(a.split_len, nctx - t0);  // positions of this split
     const int lane = threadIdx.x, g = lane >> 2, t = lane & 3;
     const int64_t pstride = (int64_t)a.max_splits * (HD + 2);
     float *part = a.partial + ((int64_t)si * a.n_heads + kh * gq) * pstride + (int64_t)sp * (HD + 2);
-    if (np <= 0) {
+    if (npa <= 0) {
         if (lane < gq) {
             part[lane * pstride + 0] = -INFINITY;
             part[lane * pstride + 1] = 0.f;
         }
         return;
     }
-    // positions [t0, t0 + np) of the ring, rows beyond np zero-filled
-    const uint32_t sb = (uint32_t)__cvta_generic_to_shared(&kv[0][0]);
+    const int ntile = (npa + TCD_POS - 1) / TCD_POS;
+    const uint32_t sb = (uint32_t)__cvta_generic_to_shared(kv);
     auto swz = [](int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); };
     const uint16_t *kc = a.kc + (int64_t)seq * a.cap * kv_dim + (int64_t)kh * HD;
     const uint16_t *vc = a.vc + (int64_t)seq * a.cap * kv_dim + (int64_t)kh * HD;
+    constexpr uint32_t MAT = TCD_POS * HD * 2;  // bytes of one 64 x 64 f16 tile
+    // positions [t0 + 64 i, + np) of the ring into buffer b, rows beyond np zero-filled
+    auto load_tile = [&](int i, int b) {
+        const int p0 = t0 + i * TCD_POS, np = min(TCD_POS, npa - i * TCD_POS);
+        const uint32_t kb = sb + (uint32_t)b * 2 * MAT, vb = kb + MAT;
 #pragma unroll
-    for (int i = 0; i < 16; i++) {  // 512 chunks of 16 bytes per matrix, 16 per lane
-        const int c = lane + 32 * i, r = c >> 3, part8 = c & 7;
-        const uint32_t dk = sb + swz(r, part8), dv = sb + (uint32_t)(TCD_POS * HD * 2) + swz(r, part8);
-        if (r < np) {
-            cp_async16(dk, kc + (int64_t)(t0 + r) * kv_dim + part8 * 8);
-            cp_async16(dv, vc + (int64_t)(t0 + r) * kv_dim + part8 * 8);
-        } else {
-            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dk), "r"(0) : "memory");
-            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dv), "r"(0) : "memory");
+        for (int j = 0; j < 16; j++) {  // 512 chunks of 16 bytes per matrix, 16 per lane
+            const int c = lane + 32 * j, r = c >> 3, part8 = c & 7;
+            const uint32_t dk = kb + swz(r, part8), dv = vb + swz(r, part8);
+            if (r < np) {
+                cp_async16(dk, kc + (int64_t)(p0 + r) * kv_dim + part8 * 8);
+                cp_async16(dv, vc + (int64_t)(p0 + r) * kv_dim + part8 * 8);
+            } else {
+                asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dk), "r"(0) : "memory");
+                asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dv), "r"(0) : "memory");
+            }
         }
-    }
-    cp_async_commit();
+        cp_async_commit();
+    };
+    load_tile(0, 0);
     // A fragments of [q_hi; q_lo] for the 4 k-steps (row g = head g)
     uint32_t qa[4][4];
     {
@@ -330,77 +342,95 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
             split2(x2, x3, qa[ks][2], qa[ks][3]);
         }
     }
-    cp_async_wait<0>();
-    __syncwarp();
-    const uint32_t kb = sb, vb = sb + (uint32_t)(TCD_POS * HD * 2);
-    float sc[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
-#pragma unroll
-    for (int np2 = 0; np2 < 4; np2++) {
-#pragma unroll
-        for (int ks = 0; ks < 4; ks++) {
-            const int mi = lane >> 3, rr = lane & 7;
-            const int r = np2 * 16 + (mi >> 1) * 8 + rr, chunk = ks * 2 + (mi & 1);
-            uint32_t b00, b01, b10, b11;
-            ldsm_x4(kb + swz(r, chunk), b00, b01, b10, b11);
-            mma_16816(sc[2 * np2], qa[ks], b00, b01);
-            mma_16816(sc[2 * np2 + 1], qa[ks], b10, b11);
-        }
-    }
-    // head g's scores at positions 8 nt + 2t (+1): hi part in c0/c1, lo part in c2/c3
-    float sv[8][2];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const int p = nt * 8 + 2 * t + e;
-            const float v = p < np ? __fadd_rn(sc[nt][e], sc[nt][2 + e]) * a.scale : -INFINITY;
-            sv[nt][e] = v;
-            mx = fmaxf(mx, v);
-        }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    float sum = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const float pv = sv[nt][e] == -INFINITY ? 0.f : expf(sv[nt][e] - mx);
-            sv[nt][e] = pv;
-            sum += pv;
-        }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    // O = [P_hi; P_lo] V
+    float M = -INFINITY, lsum = 0.f;
     float o[8][4];
 #pragma unroll
     for (int i = 0; i < 8; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) o[i][j] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 4; kk++) {  // positions 16 kk .. 16 kk + 15
-        uint32_t pa[4];
-        split2(sv[2 * kk][0], sv[2 * kk][1], pa[0], pa[1]);
-        split2(sv[2 * kk + 1][0], sv[2 * kk + 1][1], pa[2], pa[3]);
-#pragma unroll
-        for (int dp = 0; dp < 4; dp++) {
-            const int mi = lane >> 3, rr = lane & 7;
-            const int r = kk * 16 + (mi & 1) * 8 + rr, chunk = dp * 2 + (mi >> 1);
-            uint32_t b00, b01, b10, b11;
-            ldsm_x4_t(vb + swz(r, chunk), b00, b01, b10, b11);
-            mma_16816(o[2 * dp], pa, b00, b01);
-            mma_16816(o[2 * dp + 1], pa, b10, b11);
+    for (int it = 0; it < ntile; it++) {
+        if (it + 1 < ntile) {
+            load_tile(it + 1, (it + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
+        __syncwarp();
+        const int np = min(TCD_POS, npa - it * TCD_POS);
+        const uint32_t kb = sb + (uint32_t)(it & 1) * 2 * MAT, vb = kb + MAT;
+        float sc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll
+        for (int np2 = 0; np2 < 4; np2++) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int r = np2 * 16 + (mi >> 1) * 8 + rr, chunk = ks * 2 + (mi & 1);
+                uint32_t b00, b01, b10, b11;
+                ldsm_x4(kb + swz(r, chunk), b00, b01, b10, b11);
+                mma_16816(sc[2 * np2], qa[ks], b00, b01);
+                mma_16816(sc[2 * np2 + 1], qa[ks], b10, b11);
+            }
+        }
+        // head g's scores at positions 8 nt + 2t (+1): hi part in c0/c1, lo part in c2/c3
+        float sv[8][2];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int p = nt * 8 + 2 * t + e;
+                const float v = p < np ? __fadd_rn(sc[nt][e], sc[nt][2 + e]) * a.scale : -INFINITY;
+                sv[nt][e] = v;
+                mx = fmaxf(mx, v);
+            }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float Mn = fmaxf(M, mx);
+        const float alpha = M == -INFINITY ? 0.f : expf(M - Mn);  // rescales the earlier tiles
+        float sum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const float pv = sv[nt][e] == -INFINITY ? 0.f : expf(sv[nt][e] - Mn);
+                sv[nt][e] = pv;
+                sum += pv;
+            }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        lsum = lsum * alpha + sum;
+        M = Mn;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[i][j] *= alpha;
+        // O += [P_hi; P_lo] V
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {  // positions 16 kk .. 16 kk + 15
+            uint32_t pa[4];
+            split2(sv[2 * kk][0], sv[2 * kk][1], pa[0], pa[1]);
+            split2(sv[2 * kk + 1][0], sv[2 * kk + 1][1], pa[2], pa[3]);
+#pragma unroll
+            for (int dp = 0; dp < 4; dp++) {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int r = kk * 16 + (mi & 1) * 8 + rr, chunk = dp * 2 + (mi >> 1);
+                uint32_t b00, b01, b10, b11;
+                ldsm_x4_t(vb + swz(r, chunk), b00, b01, b10, b11);
+                mma_16816(o[2 * dp], pa, b00, b01);
+                mma_16816(o[2 * dp + 1], pa, b10, b11);
+            }
+        }
+        __syncwarp();  // every lane is done with this buffer before the next load refills it
     }
     if (g < gq) {
         float *ph = part + (int64_t)g * pstride;
         if (t == 0) {
-            ph[0] = mx;
-            ph[1] = sum;
+            ph[0] = M;
+            ph[1] = lsum;
         }
 #pragma unroll
         for (int dt = 0; dt < 8; dt++) {
@@ -480,9 +510,10 @@ static int attn_smem_cfg(K kfn, size_t smem) {
 template <int HD>
 static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     int gq = a.n_heads / a.n_kv_heads;
-    if (HD == 64 && a.use_tc && gq <= 8 && a.split_len == TCD_POS) {
+    if (HD == 64 && a.use_tc && gq <= 8 && a.split_len % TCD_POS == 0) {
         dim3 g1(a.n_kv_heads, n_seqs, a.max_splits);
-        k_attn_decode_tc<<<g1, 32, 0, st>>>(a);
+        const size_t ts = (size_t)(a.split_len > TCD_POS ? 2 : 1) * 2 * TCD_POS * 64 * 2;
+        k_attn_decode_tc<<<g1, 32, ts, st>>>(a);
         MG_CHECK_LAUNCH();
         dim3 g2(a.n_heads, n_seqs);
         const size_t cs = (size_t)a.max_splits * 4;

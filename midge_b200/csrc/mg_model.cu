@@ -268,6 +268,11 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     m->bs_moe = !(mk && (!strcmp(mk, "tc") || !strcmp(mk, "mma")));  // where the format allows (set in ready)
     const char *tk = getenv("MIDGE_TRUNK_KERNELS");
     m->q8mma = tk && !strcmp(tk, "i8");  // where the trunk is q8r (checked in ready)
+    const char *as = getenv("MIDGE_ATTN_SPLIT");
+    if (as && *as) {  // positions per decode-attention split: a multiple of 64, 64..1024
+        int v = atoi(as);
+        m->attn_split = v < 64 ? 64 : (v > 1024 ? 1024 : v / 64 * 64);
+    }
     const char *pk = getenv("MIDGE_PREFILL_KERNELS");
     m->tc_prefill = !(pk && !strcmp(pk, "tile"));
     const char *pc = getenv("MIDGE_PREFILL_CHUNK");

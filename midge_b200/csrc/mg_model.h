@@ -75,7 +75,7 @@ struct mg_model {
     CUtensorMap map_lm;
     CUtensorMap map_ex[3];
     bool maps_ok = false;
-    int attn_split = 64, attn_max_splits = 1;  // decode attention: positions per split
+    int attn_split = 64, attn_max_splits = 1;  // decode attention: positions per split (MIDGE_ATTN_SPLIT)
 
     // pinned host staging for per-step inputs/outputs
     int32_t *h_toks = nullptr, *h_pos = nullptr, *h_seq = nullptr, *h_amax = nullptr;
