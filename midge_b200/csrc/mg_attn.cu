@@ -282,6 +282,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnDecodeArgs a) 
 // Writes per-split partials (max, sum, acc) for the combine.
 constexpr int TCD_POS = 64;
 
+// MULTI = false: one tile per split (split_len 64), compiled without the
+// loop-carried rescaling so that it keeps the register count of a single tile.
+template <bool MULTI>
 __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
     constexpr int HD = 64;
     // [buffer][K, V] tiles: two buffers when a split has more than one tile
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
         }
         return;
     }
-    const int ntile = (npa + TCD_POS - 1) / TCD_POS;
+    const int ntile = MULTI ? (npa + TCD_POS - 1) / TCD_POS : 1;
     const uint32_t sb = (uint32_t)__cvta_generic_to_shared(kv);
     auto swz = [](int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); };
     const uint16_t *kc = a.kc + (int64_t)seq * a.cap * kv_dim + (int64_t)kh * HD;
@@ -348,8 +351,9 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
     for (int i = 0; i < 8; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) o[i][j] = 0.f;
+#pragma unroll 1
     for (int it = 0; it < ntile; it++) {
-        if (it + 1 < ntile) {
+        if (MULTI && it + 1 < ntile) {
             load_tile(it + 1, (it + 1) & 1);
             cp_async_wait<1>();
         } else {
@@ -389,8 +393,8 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
             }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float Mn = fmaxf(M, mx);
-        const float alpha = M == -INFINITY ? 0.f : expf(M - Mn);  // rescales the earlier tiles
+        const float Mn = MULTI ? fmaxf(M, mx) : mx;
+        const float alpha = (!MULTI || M == -INFINITY) ? 0.f : expf(M - Mn);  // rescales the earlier tiles
         float sum = 0.f;
 #pragma unroll
         for (int nt = 0; nt < 8; nt++)
@@ -402,12 +406,13 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
             }
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        lsum = lsum * alpha + sum;
+        lsum = MULTI ? lsum * alpha + sum : sum;
         M = Mn;
+        if (MULTI)
 #pragma unroll
-        for (int i = 0; i < 8; i++)
+            for (int i = 0; i < 8; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) o[i][j] *= alpha;
+                for (int j = 0; j < 4; j++) o[i][j] *= alpha;
         // O += [P_hi; P_lo] V
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {  // positions 16 kk .. 16 kk + 15
@@ -512,8 +517,10 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     int gq = a.n_heads / a.n_kv_heads;
     if (HD == 64 && a.use_tc && gq <= 8 && a.split_len % TCD_POS == 0) {
         dim3 g1(a.n_kv_heads, n_seqs, a.max_splits);
-        const size_t ts = (size_t)(a.split_len > TCD_POS ? 2 : 1) * 2 * TCD_POS * 64 * 2;
-        k_attn_decode_tc<<<g1, 32, ts, st>>>(a);
+        const bool multi = a.split_len > TCD_POS;
+        const size_t ts = (size_t)(multi ? 2 : 1) * 2 * TCD_POS * 64 * 2;
+        if (multi) k_attn_decode_tc<true><<<g1, 32, ts, st>>>(a);
+        else k_attn_decode_tc<false><<<g1, 32, ts, st>>>(a);
         MG_CHECK_LAUNCH();
         dim3 g2(a.n_heads, n_seqs);
         const size_t cs = (size_t)a.max_splits * 4;
