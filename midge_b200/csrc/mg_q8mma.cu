@@ -17,8 +17,9 @@
 // K splits of whole 128-byte segments; each K split writes its partial plane
 // (bias in split 0), summed downstream in plane order.  Roles (320 threads,
 // one CTA per SM, each CTA a contiguous, balanced range of units):
-//   warp 0    producer: per segment the A box (128 rows x 128 B) by TMA
-//             into a ring stage
+//   warp 0    producer: first every unit's f32 activation slice (all
+//             tokens) by bulk copy, then per segment the A box (128 rows x
+//             128 B) by TMA into a ring stage
 //   warp 1    MMA issuer: 4 MMAs (K = 32) per stage into one of eight TMEM
 //             accumulators (128 lanes x 32 columns: token t limb l = t*4+l),
 //             so the MMAs never wait for the epilogue of a CTA's few units
