@@ -50,12 +50,20 @@ sys.path.insert(0, ROOT)
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # DRAM bytes (read + write) per routed expert of one limbs + gate/up + down
-# launch triple of the block-scaled decode MoE, from the ncu capture
-# summarised in profiles/moe_bsmoe_c4_decode8.md (per-launch traffic =
-# experts routed x this figure)
+# launch triple of the block-scaled decode MoE, from an ncu capture of that
+# triple at 8 tokens (dram__bytes_read.sum + dram__bytes_write.sum divided by
+# the experts routed); per-launch traffic = experts routed x this figure
 TRAFFIC_PER_EXPERT = 13780000
 DECODE_PER_STEP = 64
 N_SEQ = 8
+
+
+def sustained_tflops():
+    try:
+        with open(MEASURED) as f:
+            return float(json.load(f)["bf16_tflops_sustained"])
+    except Exception:
+        return 1400.0
 
 
 def peaks():
@@ -176,6 +184,54 @@ def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40, rank=0, world=1):
         kname = "k_bs_limbs + k_bsmoe gate/up + k_bsmoe down (tcgen05 kind::mxf4 block-scaled)"
     return {"kernel": kname + ", 8 tokens, top-4 of 128 experts", "ms": ms,
             "bytes": by, "experts": float(np.mean(nexp)), "achieved_gbs": ach, "frac": ach / hbm_peak}
+
+
+def prefill_flops_per_token(spec, prompt_len):
+    """Algorithmic FLOPs per prompt token of the prefill (2 per multiply-add):
+    routed experts (top_k x 3 matrices of hidden x ffn), q/k/v/o, the router,
+    causal attention (QK^T and PV over min(position + 1, window) keys per head,
+    averaged over the prompt) and the last position's lm_head spread over the
+    prompt."""
+    H, F, k = spec["hidden"], spec["moe"]["ffn"], spec["moe"]["top_k"]
+    nh, nkv, hd, E = spec["n_heads"], spec["n_kv_heads"], spec["head_dim"], spec["moe"]["experts"]
+    win = spec["attn"].get("sliding_window", 0)
+    per_layer = 2 * 3 * H * F * k + 2 * (nh * hd * H * 2 + 2 * nkv * hd * H) + 2 * E * H
+    flops = 0.0
+    for lt in spec["attn"]["layer_types"]:
+        if "sliding" in lt and win:
+            ctx_avg = float(np.mean(np.minimum(np.arange(1, prompt_len + 1), win)))
+        else:
+            ctx_avg = (prompt_len + 1) / 2.0
+        flops += per_layer + 4.0 * nh * hd * ctx_avg
+    flops += 2.0 * spec["vocab"] * H / prompt_len
+    return flops
+
+
+def gemv_microbench(device, hbm_peak, seconds=0.25):
+    """BASELINE configs[1] (C2): the MXFP4 dequant-GEMV of the gpt-oss expert
+    shapes, gate_up [5760 x 2880] and down [2880 x 2880], at token batches 1,
+    4, 16, 64 and 256 (mg_bench_gemv: seeded weights, ue8m0 scales, enough
+    copies to exceed L2, CUDA-graph replays timed by events).  GB/s counts the
+    bytes the device reads per call once (nibbles + one ue8m0 byte per 32
+    values); ref_gib_s counts them as run_bench does (f16 scales, GiB)."""
+    import ctypes as C
+
+    from midge_b200 import abi
+
+    out = []
+    for name, rows, cols in (("gate_up", 5760, 2880), ("down", 2880, 2880)):
+        db = rows * cols // 2
+        dev_bytes, file_bytes = db + rows * cols // 32, db + rows * cols // 16
+        for t in (1, 4, 16, 64, 256):
+            gib = C.c_double(0.0)
+            abi.check(abi.lib.mg_bench_gemv(abi.MG_MXFP4, rows, cols, t, seconds, device, C.byref(gib)))
+            sec_per_call = file_bytes / (gib.value * 2 ** 30)
+            gbs = dev_bytes / sec_per_call / 1e9
+            out.append({"matrix": name, "rows": rows, "cols": cols, "tokens": t, "gb_s": round(gbs, 1),
+                        "frac": round(gbs / hbm_peak, 4), "us_per_call": round(sec_per_call * 1e6, 2),
+                        "tflop_s": round(2.0 * rows * cols * t / sec_per_call / 1e12, 2),
+                        "ref_gib_s": round(gib.value, 1)})
+    return out
 
 
 def cpu_reference(spec_name="c4_120b", seconds_budget=20.0, gen=8):
@@ -304,6 +360,10 @@ def run_ours(args):
     roof = moe_kernel_roofline(torch, m, spec, hbm_peak, rank=rank, world=world)
     cpu = cpu_reference(args.config) if (rank == 0 and world == 1 and not args.no_cpu) else None
     m.close()
+    gemv = gemv_microbench(local, hbm_peak) if (rank == 0 and not args.no_gemv) else None
+    tc_sustained = sustained_tflops()
+    pf_flops = prefill_flops_per_token(spec, prompt_len) * N_SEQ * prompt_len
+    pf_tflops = pf_flops / (pf_ms * 1e-3) / 1e12
     if rank != 0:
         if dist:
             dist.destroy_process_group()
@@ -319,6 +379,14 @@ def run_ours(args):
                    "parallelism": f"expert-parallel ep{world} (trunk replicated)" if world > 1 else "single GPU",
                    "l2": "working set (~15 GB/step) >> L2, no flush"},
         "prefill_tok_s": round(prefill_tok_s, 1), "prefill_wall_s": round(pf_wall, 3),
+        "prefill": {"tok_s": round(prefill_tok_s, 1), "ms": round(pf_ms, 2),
+                    "roofline": {"bound": "tensor", "achieved": round(pf_tflops, 1), "peak": tc_sustained,
+                                 "unit": "TFLOP/s", "frac": round(pf_tflops / tc_sustained, 4),
+                                 "flops_per_token": round(pf_flops / (N_SEQ * prompt_len), 0),
+                                 "peak_kind": peak_kind + " (bf16_tflops_sustained, cuBLAS)",
+                                 "note": "useful FLOPs (experts, q/k/v/o, router, causal attention, lm_head of "
+                                         "the last position); the kernels run fp32-exact products as f16 hi/lo "
+                                         "pairs, two tensor-core MMAs per useful one"}},
         "e2e": {"value": round(e2e, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": N_SEQ * 12 * DECODE_PER_STEP,
                 "d2h_bytes_per_step": (N_SEQ * 8 + 4) * DECODE_PER_STEP},
@@ -331,6 +399,10 @@ def run_ours(args):
         "clocks": clk.summary(),
         "load_s": round(load_s, 1),
     }
+    if gemv:
+        line["gemv"] = {"config": "C2: MXFP4 gate_up [5760x2880] and down [2880x2880], fp32 activations",
+                        "peak_gb_s": hbm_peak, "kernel": "k_gemv (mg_gemv: 16 tokens per weight pass)",
+                        "results": gemv}
     if cpu:
         line["cpu_baseline"] = {"value": round(cpu[0], 4), "unit": "tok/s", "cores": cpu[1], "kind": "reference",
                                 "sample": cpu[2]}
@@ -369,6 +441,7 @@ def main():
     ap.add_argument("--config", default="c4_120b")
     ap.add_argument("--prompt", type=int, default=4096)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the C2 GEMV microbench block")
     ap.add_argument("--layers", type=int, default=None,
                     help="depth-reduced slice of the config (profiling captures); default: the full depth")
     ap.add_argument("--decode-per-step", type=int, default=DECODE_PER_STEP,

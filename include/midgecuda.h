@@ -49,7 +49,8 @@ int mg_version(void);
 /* y[t][r] = sum_c W[r][c] * x[t][c] (+ bias[r]) for t < n_tok; y may also be
  * accumulated into (accumulate != 0: y += result).  fp32 accumulation.
  * Replaces wk_matvec (engine/mkern.h:180) followed by wk_addbias
- * (engine/mkern.h:245), batched over n_tok <= 16 input vectors.
+ * (engine/mkern.h:245), batched over n_tok <= 256 input vectors (one weight
+ * pass per group of up to 16 vectors).
  * q4g32/mxfp4 need cols % 32 == 0; q8r needs cols % 64 == 0 or falls back to
  * the generic path; x rows have stride ldx floats, y rows stride ldy. */
 int mg_gemv(int dt, int scale_fmt, const void *w, const void *scales, int64_t rows, int64_t cols,
@@ -112,13 +113,15 @@ int mg_moe_ffn(const mg_expert_layout *L, const uint8_t *experts, int layer, int
  * allocate device memory on the call path (a fixed start-up memory budget,
  * an allocator owned by another component, a plain C or cgo host without a
  * device allocator): the gate/up activations live in a fixed device array
- * inside this library instead of a caller's h_scratch.  Limit:
+ * inside this library instead of a caller's h_scratch.  Limits: n_tok <=
+ * MG_NOALLOC_MAX_TOK (16, as for mg_moe_ffn), else MG_ERR_ARG; and
  * n_tok * top_k * ffn <= MG_NOALLOC_MAX_H floats, else MG_ERR_RANGE.  The
  * first call on a device (with that device current) looks up the array and
  * should come before any stream capture.  Calls that overlap in time on one
  * device share the array and race; serialise them.  The array needs no
  * zeroing. */
 #define MG_NOALLOC_MAX_H (1 << 20)
+#define MG_NOALLOC_MAX_TOK 16
 int mg_moe_ffn_noalloc(const mg_expert_layout *L, const uint8_t *experts, int layer, int n_experts,
                        const float *xb, int n_tok, int top_k, const int32_t *sel, const float *weights,
                        int act_plain, float alpha, float limit, float *x, void *stream);

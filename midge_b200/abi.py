@@ -161,6 +161,22 @@ class Model:
         check(lib.mg_model_ready(m.h))
         return m
 
+    @classmethod
+    def from_arrays(cls, spec: dict, dense, expert_dt: str, blob, ctx: int, max_seqs: int = 1, device: int = 0,
+                    ep=None):
+        """A model from in-memory tensors: dense = [(name, dt, shape, data, scales)]
+        as container.dense_tensors yields them, blob = the experts.midge data
+        region (container.expert_blob)."""
+        m = cls(spec, ctx, max_seqs, device, ep=ep)
+        for name, dt, shape, d, s in dense:
+            rows = int(shape[0])
+            cols = int(shape[1]) if len(shape) > 1 else 0
+            m.set_dense(name, dt, rows, cols, d, s if s is not None and len(s) else None)
+        blob = np.ascontiguousarray(blob, dtype=np.uint8)
+        check(lib.mg_model_set_experts(m.h, DT_CODES[expert_dt], blob.ctypes.data, blob.nbytes))
+        check(lib.mg_model_ready(m.h))
+        return m
+
     def set_dense(self, name, dt, rows, cols, data, scales=None):
         data = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray)) else data)
         if scales is not None and not isinstance(scales, np.ndarray):

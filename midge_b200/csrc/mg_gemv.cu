@@ -147,7 +147,7 @@ static int launch_gemv_nt(const uint8_t *w, const uint8_t *s, int64_t rows, int 
 
 int gemv(int dt, int scale_fmt, const void *w, const void *scales, int64_t rows, int64_t cols, const float *x,
          int64_t ldx, int n_tok, const float *bias, int accumulate, float *y, int64_t ldy, cudaStream_t st) {
-    MG_REQUIRE(w && x && y && rows > 0 && cols > 0 && n_tok >= 1 && n_tok <= 16, MG_ERR_ARG,
+    MG_REQUIRE(w && x && y && rows > 0 && cols > 0 && n_tok >= 1 && n_tok <= 256, MG_ERR_ARG,
                "gemv: bad arguments (rows=%lld cols=%lld n_tok=%d)", (long long)rows, (long long)cols, n_tok);
     MG_REQUIRE(cols < (1 << 30), MG_ERR_ARG, "gemv: cols too large");
     const uint8_t *wb = reinterpret_cast<const uint8_t *>(w), *sb = reinterpret_cast<const uint8_t *>(scales);

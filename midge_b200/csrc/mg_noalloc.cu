@@ -6,8 +6,9 @@
 // component owns the device allocator, or a host binding with no device
 // allocator of its own (a plain C / cgo caller).  For them the gate/up
 // activations live in a fixed device array compiled into this library,
-// sized for MG_NOALLOC_MAX_H floats (4 MiB; n_tok * top_k * ffn up to
-// 1,048,576: 91 tokens at top-k 4 and ffn 2880).
+// sized for MG_NOALLOC_MAX_H floats (4 MiB).  Limits: n_tok <= 16, as for
+// mg_moe_ffn (MG_ERR_ARG beyond), and n_tok * top_k * ffn <= 1,048,576
+// (MG_ERR_RANGE beyond): 16 tokens fit at top-k 16 and ffn 4096.
 //
 // Set-up: the first call on a device, with that device current, looks up the
 // array's device address (cudaGetSymbolAddress) and keeps it for the
@@ -56,6 +57,8 @@ extern "C" int mg_moe_ffn_noalloc(const mg_expert_layout *L, const uint8_t *expe
                                   const float *xb, int n_tok, int top_k, const int32_t *sel, const float *weights,
                                   int act_plain, float alpha, float limit, float *x, void *stream) {
     MG_REQUIRE(L && experts && layer >= 0 && n_tok >= 0 && top_k >= 0, MG_ERR_ARG, "moe_ffn_noalloc: bad arguments");
+    MG_REQUIRE(n_tok <= MG_NOALLOC_MAX_TOK, MG_ERR_ARG, "moe_ffn_noalloc: n_tok = %d exceeds %d tokens per call", n_tok,
+               MG_NOALLOC_MAX_TOK);
     const int64_t need = (int64_t)n_tok * top_k * L->ffn;
     MG_REQUIRE(need <= MG_NOALLOC_MAX_H, MG_ERR_RANGE,
                "moe_ffn_noalloc: n_tok*top_k*ffn = %lld exceeds the fixed scratch of %d floats", (long long)need,

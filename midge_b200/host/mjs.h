@@ -1,5 +1,12 @@
 /* mjs.h -- a small JSON reader for container headers and model specs.
  *
+ * Derived from the reference engine's reader (engine/mjson.h of
+ * drmihirbrahme/midge), whose node shape (kind letters o/a/s/n/b/z, num, str,
+ * n, keys, kids), cursor and get / at / number-or-default / string-or-default
+ * / free interface it keeps so that the host reads specs exactly as midged
+ * does; object and array parsing share one loop here, nesting depth is
+ * limited and arrays grow by powers of two.
+ *
  * Parses a complete document into a tree of nodes (objects keep key order);
  * numbers are doubles; string escapes are decoded (\uXXXX becomes '?', which
  * is all the headers need).  Lookups return NULL for missing keys so callers

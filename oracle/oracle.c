@@ -9,10 +9,16 @@
  * The matvecs follow the AVX2+FMA code path (the one midged runs on any x86 host
  * with AVX2), including its 8-lane accumulation order and the hsum256 tree, so
  * that this file reproduces the reference bit for bit.  Build with
- * -std=c11 -ffp-contract=off and no -march flag: the reference is compiled with
- * -std=c11 (ISO mode, so GCC does not contract a*b+c into an FMA) and the only
- * fused multiply-adds it executes are the explicit _mm256_fmadd_ps calls, which
- * are restated here with fmaf().
+ * -std=c11 -ffp-contract=off: the reference is compiled with -std=c11 (ISO
+ * mode, so GCC does not contract a*b+c into an FMA) and the only fused
+ * multiply-adds it executes are the explicit _mm256_fmadd_ps calls, which are
+ * restated here with fmaf().
+ *
+ * Speed (so that full-width model slices check in seconds): the matvecs keep
+ * each output row's operation order exactly and only (1) let the compiler
+ * vectorise the eight independent lane chains (an AVX2+FMA clone is selected
+ * at load time where the CPU has it; fmaf is exact either way) and (2) split
+ * the rows over OpenMP threads.  Neither changes a single rounding.
  *
  * Parity pin: tests/test_oracle_cpu.py compares this file against the reference
  * itself (oracle/_ref, compiled from the reference sources by oracle/Makefile)
@@ -23,6 +29,17 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* rows x cols above which a matvec splits its rows over threads */
+#define OR_PAR_WORK (1 << 18)
+#if defined(__x86_64__) && defined(__GNUC__) && !defined(__clang__)
+#define OR_CLONES __attribute__((target_clones("arch=x86-64-v3", "default")))
+#else
+#define OR_CLONES
+#endif
 
 #define OR_F32 0
 #define OR_Q8R 1
@@ -126,7 +143,8 @@ static float or_hsum8(const float a[8]) {
 }
 
 /* f32 matvec, AVX2 order; engine/mkern.h:85-99 */
-static void or_mv_f32(const float *W, const float *x, float *y, int64_t rows, int64_t cols) {
+OR_CLONES static void or_mv_f32(const float *W, const float *x, float *y, int64_t rows, int64_t cols) {
+#pragma omp parallel for schedule(static) if (rows * cols >= OR_PAR_WORK)
     for (int64_t r = 0; r < rows; r++) {
         const float *w = W + r * cols;
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -141,7 +159,8 @@ static void or_mv_f32(const float *W, const float *x, float *y, int64_t rows, in
 
 /* int8 per-row-scale matvec, AVX2 order, scale applied after the sum;
  * engine/mkern.h:102-118 */
-static void or_mv_q8r(const int8_t *W, const float *S, const float *x, float *y, int64_t rows, int64_t cols) {
+OR_CLONES static void or_mv_q8r(const int8_t *W, const float *S, const float *x, float *y, int64_t rows, int64_t cols) {
+#pragma omp parallel for schedule(static) if (rows * cols >= OR_PAR_WORK)
     for (int64_t r = 0; r < rows; r++) {
         const int8_t *w = W + r * cols;
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -158,28 +177,35 @@ static void or_mv_q8r(const int8_t *W, const float *S, const float *x, float *y,
  * give low-nibble (even column) and high-nibble (odd column) codes, four
  * 8-lane products are chained, then the group scale (halved for FP4, whose
  * codes are doubled) is fused into the 8-lane accumulator; engine/mkern.h:121-166 */
-static void or_mv_g32(const uint8_t *W, const uint16_t *S, const float *x, float *y, int64_t rows,
-                      int64_t cols, int is_fp4) {
+OR_CLONES static void or_mv_g32(const uint8_t *W, const uint16_t *S, const float *x, float *y, int64_t rows,
+                                int64_t cols, int is_fp4) {
     int64_t gpr = cols / 32, half = cols / 2;
     float *xe = (float *)malloc((size_t)half * 4), *xo = (float *)malloc((size_t)half * 4);
     for (int64_t k = 0; k < half; k++) { xe[k] = x[2 * k]; xo[k] = x[2 * k + 1]; }
+    /* per byte: the low (even column) and high (odd column) code as the float
+     * the AVX2 kernel multiplies (doubled FP4 magnitude, or code - 8) */
+    float tlo[256], thi[256];
+    for (int b = 0; b < 256; b++) {
+        tlo[b] = is_fp4 ? (float)OR_FP4X2[b & 15] : (float)((b & 15) - 8);
+        thi[b] = is_fp4 ? (float)OR_FP4X2[b >> 4] : (float)((b >> 4) - 8);
+    }
+#pragma omp parallel for schedule(static) if (rows * cols >= OR_PAR_WORK)
     for (int64_t r = 0; r < rows; r++) {
         const uint8_t *w = W + r * half;
         const uint16_t *s = S + r * gpr;
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int64_t g = 0; g < gpr; g++) {
-            int lo[16], hi[16];
+            float lo[16], hi[16];
             for (int j = 0; j < 16; j++) {
-                uint8_t b = w[g * 16 + j];
-                if (is_fp4) { lo[j] = OR_FP4X2[b & 15]; hi[j] = OR_FP4X2[b >> 4]; }
-                else { lo[j] = (int)(b & 15) - 8; hi[j] = (int)(b >> 4) - 8; }
+                lo[j] = tlo[w[g * 16 + j]];
+                hi[j] = thi[w[g * 16 + j]];
             }
             const float *pe = xe + g * 16, *po = xo + g * 16;
             float g0[8];
-            for (int i = 0; i < 8; i++) g0[i] = (float)lo[i] * pe[i];
-            for (int i = 0; i < 8; i++) g0[i] = fmaf((float)lo[8 + i], pe[8 + i], g0[i]);
-            for (int i = 0; i < 8; i++) g0[i] = fmaf((float)hi[i], po[i], g0[i]);
-            for (int i = 0; i < 8; i++) g0[i] = fmaf((float)hi[8 + i], po[8 + i], g0[i]);
+            for (int i = 0; i < 8; i++) g0[i] = lo[i] * pe[i];
+            for (int i = 0; i < 8; i++) g0[i] = fmaf(lo[8 + i], pe[8 + i], g0[i]);
+            for (int i = 0; i < 8; i++) g0[i] = fmaf(hi[i], po[i], g0[i]);
+            for (int i = 0; i < 8; i++) g0[i] = fmaf(hi[8 + i], po[8 + i], g0[i]);
             float sc = or_f16_to_f32(s[g]) * (is_fp4 ? 0.5f : 1.0f);
             for (int i = 0; i < 8; i++) acc[i] = fmaf(sc, g0[i], acc[i]);
         }
@@ -204,14 +230,18 @@ void or_matvec(int dt, const void *data, const void *scales, int64_t rows, int64
  * accumulation-order difference of a matvec (not a reference function). */
 void or_matvec_abs(int dt, const void *data, const void *scales, int64_t rows, int64_t cols, const float *x,
                    double *y) {
-    float *row = (float *)malloc((size_t)cols * 4);
-    for (int64_t r = 0; r < rows; r++) {
-        or_dequant_row(dt, data, scales, cols, r, row);
-        double a = 0;
-        for (int64_t c = 0; c < cols; c++) a += fabs((double)row[c]) * fabs((double)x[c]);
-        y[r] = a;
+#pragma omp parallel if (rows * cols >= OR_PAR_WORK)
+    {
+        float *row = (float *)malloc((size_t)cols * 4);
+#pragma omp for schedule(static)
+        for (int64_t r = 0; r < rows; r++) {
+            or_dequant_row(dt, data, scales, cols, r, row);
+            double a = 0;
+            for (int64_t c = 0; c < cols; c++) a += fabs((double)row[c]) * fabs((double)x[c]);
+            y[r] = a;
+        }
+        free(row);
     }
-    free(row);
 }
 
 /* sequential-sum RMSNorm; engine/mkern.h:238-243 */

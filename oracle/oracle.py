@@ -20,10 +20,31 @@ REF_MIDGED = os.path.join(HERE, "_ref", "midged")
 i64, i32, f32, vp = C.c_int64, C.c_int, C.c_float, C.c_void_p
 
 
+def reference_dir():
+    """The reference source tree, read-only: $MIDGE_REFERENCE, else the
+    reference_path that BASELINE.json at the repository root names; None when
+    neither names an existing directory (e.g. on a GPU box, which only uses
+    the prebuilt oracle/_ref)."""
+    cand = os.environ.get("MIDGE_REFERENCE")
+    if not cand:
+        try:
+            import json
+
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                cand = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return cand if cand and os.path.isdir(cand) else None
+
+
 def build():
     """Compile liboracle.so (always) and the reference build (when the
     reference tree is present)."""
-    r = subprocess.run(["make", "-s", "-f", os.path.join(HERE, "Makefile")], capture_output=True, text=True)
+    cmd = ["make", "-s", "-f", os.path.join(HERE, "Makefile")]
+    ref = reference_dir()
+    if ref:
+        cmd.append(f"REF={ref}")
+    r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + r.stdout + r.stderr)
 
@@ -139,13 +160,23 @@ def sample(logits: np.ndarray, temp: float, topp: float, state: int):
 class OracleModel:
     """The whole reference forward on the CPU, over a converted model dir."""
 
-    def __init__(self, model_dir: str, ctx: int):
+    def __init__(self, model_dir: str | None, ctx: int, arrays=None):
+        """model_dir: a converted model directory; or arrays = (spec, dense,
+        expert_dt, blob) held in memory (see from_arrays)."""
         import sys
         sys.path.insert(0, os.path.dirname(HERE))
         from midge_b200.container import DT_CODES, ModelDir, spec_fields
 
-        self.md = ModelDir(model_dir)
-        f = spec_fields(self.md.spec)
+        if arrays is None:
+            self.md = ModelDir(model_dir)
+            spec, expert_dt, blob = self.md.spec, self.md.expert_dt, self.md.expert_blob()
+            tensors = list(self.md.tensors())
+        else:
+            self.md = None
+            spec, dense, expert_dt, blob = arrays
+            tensors = [(n, dt, int(sh[0]), int(sh[1]) if len(sh) > 1 else 0, np.frombuffer(d, np.uint8),
+                        None if s is None or not len(s) else np.frombuffer(s, np.uint8)) for n, dt, sh, d, s in dense]
+        f = spec_fields(spec)
         self._sl = (i32 * f["n_layers"])(*f.pop("layer_sliding"))
         self.spec = OrSpec(**f)
         self.spec.layer_sliding = C.cast(self._sl, C.POINTER(i32))
@@ -153,15 +184,22 @@ class OracleModel:
         self.top_k = f["top_k"]
         self.n_layers = f["n_layers"]
         self.n_experts = f["n_experts"]
-        self._blob = self.md.expert_blob()
-        self.h = lib.or_model_new(C.byref(self.spec), ctx, DT_CODES[self.md.expert_dt], self._blob.ctypes.data)
+        self._blob = np.ascontiguousarray(blob, dtype=np.uint8)
+        self.h = lib.or_model_new(C.byref(self.spec), ctx, DT_CODES[expert_dt], self._blob.ctypes.data)
         self._keep = []
-        for name, dt, rows, cols, d, s in self.md.tensors():
+        for name, dt, rows, cols, d, s in tensors:
             self._keep.append((d, s))
             rc = lib.or_model_set(self.h, name.encode(), DT_CODES[dt], rows, cols, d.ctypes.data,
                                   None if s is None else s.ctypes.data)
             if rc != 0:
                 pass  # tensors the engine does not use
+
+    @classmethod
+    def from_arrays(cls, spec: dict, dense, expert_dt: str, blob, ctx: int):
+        """The oracle over in-memory tensors (the same arrays a GPU model was
+        built from): dense = [(name, dt, shape, data, scales)], blob = the
+        experts.midge data region.  The arrays must outlive the model."""
+        return cls(None, ctx, arrays=(spec, dense, expert_dt, blob))
 
     def forward(self, tok: int, trace=False):
         lg = np.empty(self.vocab, np.float32)
@@ -203,7 +241,8 @@ class OracleModel:
             lib.or_model_free(self.h)
             self.h = None
         self._keep, self._blob = [], None
-        self.md.close()
+        if self.md is not None:
+            self.md.close()
 
 
 # ------------------------------------------------------- the reference itself

@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a container that has the reference tree (REF, default /root/reference)
-and the reference engine built by oracle/Makefile (oracle/_ref/midged):
+Run in a container that has the reference tree ($MIDGE_REFERENCE, or the
+reference_path of BASELINE.json) and the reference engine built by oracle/Makefile (oracle/_ref/midged):
 
     python tests/golden/make_golden.py
 
@@ -31,9 +31,11 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("REF", "/root/reference")
-MIDGED = os.path.join(ROOT, "oracle", "_ref", "midged")
 sys.path.insert(0, ROOT)
+from oracle.oracle import reference_dir  # noqa: E402
+
+REF = reference_dir()
+MIDGED = os.path.join(ROOT, "oracle", "_ref", "midged")
 
 IDS = [1, 17, 42, 5, 99, 3, 77, 12, 63, 8, 120, 31]  # tools/validate.py:39
 CASES = [  # tools/validate.py:30-44: (name, make_tiny args, convert flags)

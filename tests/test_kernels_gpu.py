@@ -81,6 +81,35 @@ def test_gemv_matches_oracle(torch_cuda, dt, shape, n_tok):
             prev = got.copy()
 
 
+@pytest.mark.parametrize("dt", ["mxfp4", "q8r"])
+@pytest.mark.parametrize("shape", [(5760, 2880), (2880, 2880)])
+@pytest.mark.parametrize("n_tok", [64, 256])
+def test_gemv_wide_batches_c2(torch_cuda, dt, shape, n_tok):
+    """The C2 microbench shapes (gpt-oss gate_up [5760 x 2880] and down
+    [2880 x 2880]) at token batches 64 and 256, every output row of every
+    token against the oracle (16-token groups, each a full weight pass)."""
+    torch = torch_cuda
+    rows, cols = shape
+    rng = np.random.default_rng(zlib.crc32(f"wide-{dt}-{rows}-{n_tok}".encode()))
+    d, s = _mat(rng, dt, rows, cols)
+    x = rng.standard_normal((n_tok, cols)).astype(np.float32)
+    dtc = ct.DT_CODES[dt]
+    fmt = abi.MG_SCALE_UE8M0 if dt == "mxfp4" else abi.MG_SCALE_F16
+    d_dev = torch.from_numpy(d).cuda()
+    s_dev = _to_ue8m0(torch, s) if dt == "mxfp4" else torch.from_numpy(s).cuda()
+    x_dev = torch.from_numpy(x).cuda()
+    y_dev = torch.empty((n_tok, rows), dtype=torch.float32, device="cuda")
+    abi.check(abi.lib.mg_gemv(dtc, fmt, d_dev.data_ptr(), s_dev.data_ptr(), rows, cols, x_dev.data_ptr(), cols, n_tok,
+                              None, 0, y_dev.data_ptr(), rows, None))
+    torch.cuda.synchronize()
+    got = y_dev.cpu().numpy()
+    for t in range(n_tok):
+        want = orc.matvec(dtc, d, s, rows, cols, x[t]).astype(np.float64)
+        mag = orc.matvec_abs(dtc, d, s, rows, cols, x[t])
+        err = np.abs(got[t].astype(np.float64) - want)
+        assert np.all(err <= TOL_DOT * mag + 1e-6 * (1 + np.abs(want))), (t, float((err / (mag + 1e-30)).max()))
+
+
 @pytest.mark.parametrize("dt", ["mxfp4", "q4g32", "q8r", "f32"])
 def test_dequant_rows_bit_exact(torch_cuda, dt):
     torch = torch_cuda

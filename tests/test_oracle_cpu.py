@@ -110,8 +110,9 @@ def test_oracle_matches_reference_golden_c1(tmp_path):
 def test_container_writer_matches_reference_writer(tmp_path):
     """midge_b200.container writes byte-identical files to the reference's
     tools/midgepack.py writers (checked only where the reference tree exists)."""
-    ref_tools = "/root/reference/tools"
-    if not os.path.exists(os.path.join(ref_tools, "midgepack.py")):
+    ref = orc.reference_dir()
+    ref_tools = os.path.join(ref, "tools") if ref else ""
+    if not ref or not os.path.exists(os.path.join(ref_tools, "midgepack.py")):
         pytest.skip("reference tools absent")
     import importlib.util
     spec_ = importlib.util.spec_from_file_location("midgepack", os.path.join(ref_tools, "midgepack.py"))

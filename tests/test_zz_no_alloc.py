@@ -50,9 +50,16 @@ def test_noalloc_matches_moe_ffn(torch_cuda, dt, n_tok, top_k, E):
 
 
 def test_noalloc_rejects_oversize(torch_cuda):
+    """Both limits are checked before any launch: more than 16 tokens is a
+    bad argument (as for mg_moe_ffn); 16 tokens whose gate/up activations
+    exceed the fixed array are a range error."""
     L = abi.MgExpertLayout()
     abi.check(abi.lib.mg_expert_layout_init(C.byref(L), ct.DT_CODES["mxfp4"], 2880, 2880, 128))
-    # 100 tokens x top-4 x 2880 > the fixed scratch: refused before any launch
-    rc = abi.lib.mg_moe_ffn_noalloc(C.byref(L), 16, 0, 128, 16, 100, 4, 16, 16, 0, 1.702, 7.0, 16, None)
+    rc = abi.lib.mg_moe_ffn_noalloc(C.byref(L), 16, 0, 128, 16, 17, 4, 16, 16, 0, 1.702, 7.0, 16, None)
+    assert rc == abi.MG_ERR_ARG
+    assert b"tokens per call" in abi.lib.mg_last_error()
+    abi.check(abi.lib.mg_expert_layout_init(C.byref(L), ct.DT_CODES["mxfp4"], 2880, 8192, 128))
+    # 16 tokens x top-16 x 8192 = 2,097,152 floats > the fixed scratch
+    rc = abi.lib.mg_moe_ffn_noalloc(C.byref(L), 16, 0, 128, 16, 16, 16, 16, 16, 0, 1.702, 7.0, 16, None)
     assert rc == abi.MG_ERR_RANGE
     assert b"fixed scratch" in abi.lib.mg_last_error()
