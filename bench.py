@@ -22,9 +22,11 @@ The decode working set (~15 GB of weights per step) is far larger than L2,
 so no flush is needed between steps.
 
 --gpus N (torchrun, one rank per GPU): expert parallel -- every rank holds
-1/N of the experts and serves the same 8 sequences (trunk, attention and KV
-replicated), so value is the 8 sequences' tokens/s over the max of the ranks'
-times ("scaling": "strong").
+1/N of the experts and owns 8/N of the sequences (their attention, KV cache,
+router and lm_head; trunk weights replicated); each MoE layer sends the
+routed tokens to the expert holders and the slot outputs back.  value is the
+8 sequences' tokens/s over the max of the ranks' times ("scaling": "strong":
+the total work is the same 8 sequences at every N).
 
 --impl reference times the reference engine (oracle/_ref/midged, built from
 the reference sources with AVX2 + OpenMP) on the host cores: its per-token
@@ -304,27 +306,41 @@ def run_ours(args):
         from midge_b200 import ep as mep
 
         ep_arg = (rank, world, mep.exchange_id(rank, world))
-    m = build_model(torch, spec, edt, ctx, N_SEQ, device=local, seed=0, ep=ep_arg)
+    from midge_b200 import ep as mep
+
+    own = mep.sequence_split(N_SEQ, world, rank)  # this rank's sequences (global ids)
+    rounds = -(-N_SEQ // world)
+    m = build_model(torch, spec, edt, ctx, max(1, len(own)), device=local, seed=0, ep=ep_arg)
     load_s = time.time() - t0
     stream = torch.cuda.ExternalStream(m.stream())
     rng = np.random.default_rng(100)
     prompts = [rng.integers(0, spec["vocab"], prompt_len).astype(np.int32) for _ in range(N_SEQ)]
 
-    # prefill of the 8 prompts (device-timed on the model stream)
+    # prefill of the 8 prompts (device-timed on the model stream); expert
+    # parallel: every rank prefills one of its own sequences per round
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     t_pf = time.time()
     last = []
-    for s in range(N_SEQ):
-        last.append(m.forward_batch(s, prompts[s], logits_mode=1))
+    for r in range(rounds):
+        if r < len(own):
+            last.append(m.forward_batch(r, prompts[own[r]], logits_mode=1))
+        else:
+            m.forward_batch(0, np.zeros(0, np.int32), logits_mode=0)
     e1.record(stream)
     e1.synchronize()
     pf_wall = time.time() - t_pf
     pf_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([pf_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pf_ms = float(t[0])
     prefill_tok_s = N_SEQ * prompt_len / (pf_ms / 1e3)
     toks = np.array([int(np.argmax(l)) for l in last], np.int32)
-    seqs = np.arange(N_SEQ, dtype=np.int32)
+    seqs = np.arange(len(own), dtype=np.int32)
 
     # value: greedy decode fed back on the device (mg_decode_greedy), inputs
     # resident, no host round trip inside the timed region
@@ -354,7 +370,7 @@ def run_ours(args):
         t = torch.tensor([dev_ms, wall * 1e3], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms, wall = float(t[0]), float(t[1]) / 1e3
-    ntok = N_SEQ * DECODE_PER_STEP * args.steps  # every rank serves the same 8 sequences
+    ntok = N_SEQ * DECODE_PER_STEP * args.steps  # the 8 sequences, over all ranks
     value = ntok / (dev_ms / 1e3)
     e2e = ntok / wall
     roof = moe_kernel_roofline(torch, m, spec, hbm_peak, rank=rank, world=world)
@@ -376,7 +392,8 @@ def run_ours(args):
         "data": "synthetic (seeded random-init weights and token ids)",
         "config": {"workload": f"{args.config}{'' if args.layers is None else f' ({args.layers} layers)'}: 8 sequences x {prompt_len}-token prompt, "
                                f"{DECODE_PER_STEP} decode steps per bench step",
-                   "parallelism": f"expert-parallel ep{world} (trunk replicated)" if world > 1 else "single GPU",
+                   "parallelism": (f"expert-parallel ep{world}: experts and sequences sharded, trunk weights "
+                                   f"replicated, NCCL dispatch/combine per MoE layer") if world > 1 else "single GPU",
                    "l2": "working set (~15 GB/step) >> L2, no flush"},
         "prefill_tok_s": round(prefill_tok_s, 1), "prefill_wall_s": round(pf_wall, 3),
         "prefill": {"tok_s": round(prefill_tok_s, 1), "ms": round(pf_ms, 2),
@@ -388,8 +405,10 @@ def run_ours(args):
                                          "the last position); the kernels run fp32-exact products as f16 hi/lo "
                                          "pairs, two tensor-core MMAs per useful one"}},
         "e2e": {"value": round(e2e, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": N_SEQ * 12 * DECODE_PER_STEP,
-                "d2h_bytes_per_step": (N_SEQ * 8 + 4) * DECODE_PER_STEP},
+                # token id, position and sequence id in; argmax key out (+ the
+                # error word, and expert parallel the 3-int step agreement per rank)
+                "h2d_bytes_per_step": (N_SEQ * 12 + (world * 12 if world > 1 else 0)) * DECODE_PER_STEP,
+                "d2h_bytes_per_step": (N_SEQ * 8 + world * 4 + (world * 12 if world > 1 else 0)) * DECODE_PER_STEP},
         "roofline": {"bound": "hbm", "achieved": round(roof["achieved_gbs"], 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(roof["frac"], 4),
                      "traffic": round(roof["experts"] * TRAFFIC_PER_EXPERT, 0) if TRAFFIC_PER_EXPERT else None,

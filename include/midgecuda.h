@@ -24,8 +24,14 @@
 extern "C" {
 #endif
 
-/* weight dtypes: same codes as engine/mten.h:42 */
-enum { MG_F32 = 0, MG_Q8R = 1, MG_Q4G32 = 2, MG_MXFP4 = 3 };
+/* weight dtypes: same codes as engine/mten.h:42, plus MG_MXFP4_E8, the
+ * opt-in "mxfp4e8" expert container dtype (no counterpart in the reference,
+ * whose converter writes f16 group scales, tools/convert.py:37-53): MXFP4
+ * nibbles with one ue8m0 byte (2^(u-127), 0 = zero) per 32 columns, written
+ * by midge_b200/convert_ue8m0.py and uploaded without re-expression.  An
+ * mg_expert_layout of that dtype reports dt MG_MXFP4, scale_fmt
+ * MG_SCALE_UE8M0. */
+enum { MG_F32 = 0, MG_Q8R = 1, MG_Q4G32 = 2, MG_MXFP4 = 3, MG_MXFP4_E8 = 4 };
 /* encoding of the per-32-column scales of q4g32/mxfp4 */
 enum { MG_SCALE_F16 = 0, MG_SCALE_UE8M0 = 1 };
 
@@ -126,6 +132,17 @@ int mg_moe_ffn_noalloc(const mg_expert_layout *L, const uint8_t *experts, int la
                        const float *xb, int n_tok, int top_k, const int32_t *sel, const float *weights,
                        int act_plain, float alpha, float limit, float *x, void *stream);
 
+/* Sampling of the next token from n_rows logits rows (row i at
+ * logits + i*ldl, V entries): sample (engine/midge.c:650-678).  temp <= 0:
+ * the first maximum (greedy).  Otherwise softmax with the temperature, the
+ * shortest descending-probability prefix whose mass reaches top_p, and a draw
+ * from it with the reference's xorshift64* generator, whose per-row state
+ * rng[i] (device) advances by one draw.  Entries of exactly equal
+ * probability are ordered by index.  probs: device scratch of n_rows*V
+ * floats (may be NULL when temp <= 0).  out: device int32 [n_rows]. */
+int mg_sample_topp(const float *logits, int64_t ldl, int64_t V, int n_rows, float temp, float top_p, uint64_t *rng,
+                   int32_t *out, float *probs, void *stream);
+
 /* ====================================================== model level ==== */
 
 /* The model spec (engine/midge.c:46-63, parsed from the container's embedded
@@ -153,18 +170,35 @@ typedef struct mg_model mg_model;
 int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int device, mg_model **out);
 
 /* Expert parallelism over the GPUs of one box (no counterpart in the
- * reference, which is one process; its expert-swarm proposal shards experts
- * the same way).  Rank r of `world` holds experts [r E/world, (r+1) E/world);
- * tokens, attention, KV cache, router and trunk are replicated, every rank
- * drives the same calls with the same inputs, and each layer's per-slot
- * expert outputs are summed over the ranks through NCCL (loaded at run time),
- * so results equal the one-GPU results bit for bit.  mg_ep_unique_id fills
- * MG_EP_ID_BYTES bytes on one rank, which the host hands to every rank;
- * mg_model_set_ep goes between mg_model_create and the experts upload (which
- * then takes the full blob and keeps this rank's shard). */
+ * reference, which is one process; its expert-swarm proposal,
+ * docs/SPEED.md:94-99, shards experts the same way).  Rank r of `world`
+ * (<= 8) holds experts [r E/world, (r+1) E/world) and owns its own sequences
+ * (their attention, KV cache, router and lm_head; the trunk weights are
+ * replicated).  Each MoE layer sends every routed token to the ranks that hold
+ * its experts and the per-slot outputs back to the token's owner, which adds
+ * them in the reference's order: results equal the one-GPU results bit for
+ * bit.  NCCL is loaded at run time.  mg_ep_unique_id fills MG_EP_ID_BYTES
+ * bytes on one rank, which the host hands to every rank; mg_model_set_ep goes
+ * between mg_model_create and the experts upload (which then takes the full
+ * blob and keeps this rank's shard).
+ * With world > 1, mg_forward_batch, mg_decode_step, mg_decode_greedy and
+ * mg_forward are collective: every rank calls them together, each with its
+ * own sequences (a rank with nothing to do passes n = 0 / n_seqs = 0 and
+ * still serves its experts); decode serves at most 8 tokens per step over all
+ * ranks.  Blocking waits are watched: when the other ranks do not answer
+ * within MIDGE_EP_TIMEOUT_S seconds (default 600) or the communicator reports
+ * an error, the communicator is aborted (ncclCommAbort) and the call returns
+ * MG_ERR_COMM; the model then only accepts mg_model_free. */
 #define MG_EP_ID_BYTES 128
 int mg_ep_unique_id(void *id);
 int mg_model_set_ep(mg_model *m, int rank, int world, const void *id);
+
+/* Self-test of the expert-parallel watchdog loop against fakes (no GPU, no
+ * NCCL): scenario 0 = the wait completes, 1 = it never completes (timeout),
+ * 2 = the communicator reports an asynchronous error, 3 = a device error.
+ * Returns what the watchdog returns (MG_OK, MG_ERR_COMM, MG_ERR_CUDA);
+ * *aborted = how many times it aborted the (fake) communicator. */
+int mg_ep_watchdog_selftest(int scenario, double timeout_s, int *aborted);
 
 /* Upload one dense tensor named as in dense.midge (embed, lm_head,
  * final_norm, L<i>.attn.q ...; docs/ADDING_MODELS.md naming); host pointers,
@@ -230,10 +264,22 @@ uint64_t mg_model_kernel_launches(const mg_model *m);
  * model-level calls, so that a caller can time it with stream events. */
 int mg_model_moe_stream(mg_model *m, int layer, int n_tok, const int32_t *sel);
 
+/* Sample the next token of the first n_rows rows of the model's last
+ * logits on the device (mg_sample_topp): the rows of the last decode step's
+ * sequences, or row 0 = the last prompt position after mg_forward_batch.
+ * rng: HOST array of n_rows generator states, advanced in place (midged's
+ * one state for one sequence); out: host int32 [n_rows]. */
+int mg_model_sample(mg_model *m, int n_rows, float temp, float top_p, uint64_t *rng, int32_t *out);
+
 /* Copy row `row` of the logits the last forward / decode step / prefill
  * computed (host, vocab floats); the device-resident copy of the reference's
  * m->logits (engine/midge.c:82). */
 int mg_model_logits(mg_model *m, int row, float *out);
+
+/* Put a host logits row (vocab floats) into row `row` (< 16) of the model's
+ * device logits, where mg_model_sample reads it: a host serving several
+ * sequences keeps a sequence's pending logits while another one runs. */
+int mg_model_put_logits(mg_model *m, int row, const float *logits);
 
 /* usage histogram u32[n_layers x n_experts] (engine/midge.c:283-303) */
 int mg_model_get_usage(mg_model *m, uint32_t *usage);
@@ -249,7 +295,7 @@ int mg_model_free(mg_model *m);
 
 /* Weight-streaming microbench of one dequant-GEMV on device `device`: a
  * [rows x cols] matrix of dtype dt (seeded data, f16 scales re-expressed as
- * ue8m0 for mxfp4) times n_tok vectors, repeated over enough copies to exceed
+ * ue8m0 for mxfp4) times n_tok <= 256 vectors, repeated over enough copies to exceed
  * L2, for at least `seconds`.  *gbps = (weight + scale bytes) per call / time,
  * in GiB/s like run_bench (engine/midge.c:687-720), the device replacement of
  * midged --bench. */

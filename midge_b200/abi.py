@@ -18,7 +18,7 @@ LIB_PATH = os.path.join(PKG, "libmidgecuda.so")
 MG_F32, MG_Q8R, MG_Q4G32, MG_MXFP4 = 0, 1, 2, 3
 MG_SCALE_F16, MG_SCALE_UE8M0 = 0, 1
 MG_OK, MG_ERR_ARG, MG_ERR_CUDA, MG_ERR_OOM, MG_ERR_STATE, MG_ERR_RANGE, MG_ERR_SPEC = 0, -1, -2, -3, -4, -5, -6
-MG_ERR_COMM = -9
+MG_ERR_TIMEOUT, MG_ERR_COMM = -8, -9
 EP_ID_BYTES = 128
 
 i64, i32, f32, vp = C.c_int64, C.c_int, C.c_float, C.c_void_p
@@ -89,11 +89,15 @@ def _load():
         "mg_model_moe_stream": (i32, [vp, i32, i32, vp]),
         "mg_ep_unique_id": (i32, [vp]),
         "mg_model_set_ep": (i32, [vp, i32, i32, vp]),
+        "mg_ep_watchdog_selftest": (i32, [i32, C.c_double, C.POINTER(i32)]),
         "mg_model_experts_device": (vp, [vp, C.POINTER(MgExpertLayout)]),
         "mg_model_stream": (vp, [vp]),
         "mg_model_free": (i32, [vp]),
         "mg_model_logits": (i32, [vp, i32, vp]),
         "mg_bench_gemv": (i32, [i32, i64, i64, i32, C.c_double, i32, C.POINTER(C.c_double)]),
+        "mg_sample_topp": (i32, [vp, i64, i64, i32, f32, f32, vp, vp, vp, vp]),
+        "mg_model_sample": (i32, [vp, i32, f32, f32, vp, vp]),
+        "mg_model_put_logits": (i32, [vp, i32, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -237,6 +241,16 @@ class Model:
         t = np.ascontiguousarray(toks, dtype=np.int32)
         out = np.zeros((n_steps, len(s)), np.int32)
         check(lib.mg_decode_greedy(self.h, len(s), ptr(s), ptr(t), n_steps, ptr(out)))
+        return out
+
+    def sample(self, n_rows, temp, topp, rng_states):
+        """Next tokens of the first n_rows rows of the last logits, sampled on
+        the device; rng_states (uint64 array, n_rows) advance in place."""
+        out = np.zeros(n_rows, np.int32)
+        rng = np.ascontiguousarray(rng_states, dtype=np.uint64)
+        check(lib.mg_model_sample(self.h, n_rows, float(temp), float(topp), ptr(rng), ptr(out)))
+        if rng is not rng_states:
+            rng_states[:] = rng
         return out
 
     def kernel_launches(self):

@@ -21,7 +21,9 @@ import struct
 import numpy as np
 
 ALIGN = 64
-DT_CODES = {"f32": 0, "q8r": 1, "q4g32": 2, "mxfp4": 3}  # engine/mten.h:42
+# engine/mten.h:42, plus "mxfp4e8": MXFP4 with one ue8m0 byte per 32 columns
+# (an opt-in expert dtype of this implementation, see convert_ue8m0.py)
+DT_CODES = {"f32": 0, "q8r": 1, "q4g32": 2, "mxfp4": 3, "mxfp4e8": 4}
 DT_NAMES = {v: k for k, v in DT_CODES.items()}
 
 
@@ -37,6 +39,8 @@ def blob_sizes(dt: str, rows: int, cols: int):
         return rows * cols, rows * 4
     if dt in ("q4g32", "mxfp4"):
         return rows * cols // 2, rows * (cols // 32) * 2
+    if dt == "mxfp4e8":
+        return rows * cols // 2, rows * (cols // 32)
     raise ValueError(dt)
 
 

@@ -147,11 +147,16 @@ extern "C" int mg_router_topk(const float *xb, int n_tok, const float *rw, const
     return router(a, (cudaStream_t)stream);
 }
 
+extern "C" int mg_sample_topp(const float *logits, int64_t ldl, int64_t V, int n_rows, float temp, float top_p,
+                              uint64_t *rng, int32_t *out, float *probs, void *stream) {
+    return sample_topp(logits, ldl, V, n_rows, temp, top_p, rng, out, probs, (cudaStream_t)stream);
+}
+
 // wt_expert_layout (engine/mten.h:136-150) with wt_sizes (engine/mten.h:101-109)
 extern "C" int mg_expert_layout_init(mg_expert_layout *L, int dt, int64_t hidden, int64_t ffn, int64_t n_experts) {
     MG_REQUIRE(L && hidden > 0 && ffn > 0 && n_experts > 0, MG_ERR_ARG, "expert_layout: bad arguments");
-    L->dt = dt;
-    L->scale_fmt = MG_SCALE_F16;
+    L->dt = dt == MG_MXFP4_E8 ? MG_MXFP4 : dt;
+    L->scale_fmt = dt == MG_MXFP4_E8 ? MG_SCALE_UE8M0 : MG_SCALE_F16;
     L->hidden = hidden;
     L->ffn = ffn;
     const int64_t rows[3] = {ffn, ffn, hidden}, cols[3] = {hidden, hidden, ffn};
@@ -164,9 +169,10 @@ extern "C" int mg_expert_layout_init(mg_expert_layout *L, int dt, int64_t hidden
         case MG_Q8R: db = rows[m] * cols[m]; sb = rows[m] * 4; break;
         case MG_Q4G32:
         case MG_MXFP4:
+        case MG_MXFP4_E8:
             MG_REQUIRE(cols[m] % 32 == 0, MG_ERR_SPEC, "expert_layout: 4-bit needs dims %% 32 == 0");
             db = rows[m] * cols[m] / 2;
-            sb = rows[m] * (cols[m] / 32) * 2;
+            sb = rows[m] * (cols[m] / 32) * (dt == MG_MXFP4_E8 ? 1 : 2);
             break;
         default: set_error("expert_layout: bad dtype %d", dt); return MG_ERR_SPEC;
         }
@@ -226,7 +232,7 @@ __global__ void k_bench_scales(uint8_t *buf, int64_t per, int64_t soff, int64_t 
 }  // namespace mg
 
 extern "C" int mg_bench_gemv(int dt, int64_t rows, int64_t cols, int n_tok, double seconds, int device, double *gbps) {
-    MG_REQUIRE(gbps && rows > 0 && cols > 0 && n_tok >= 1 && n_tok <= 16 &&
+    MG_REQUIRE(gbps && rows > 0 && cols > 0 && n_tok >= 1 && n_tok <= 256 &&
                    (dt == MG_MXFP4 || dt == MG_Q4G32 || dt == MG_Q8R),
                MG_ERR_ARG, "bench_gemv: bad arguments");
     MG_CUDA(cudaSetDevice(device));

@@ -20,6 +20,11 @@ void set_error(const char *fmt, ...);
         }                                                                                   \
     } while (0)
 #define MG_CHECK_LAUNCH() MG_CUDA(cudaGetLastError())
+#define TRY(expr)                     \
+    do {                              \
+        int _rc = (expr);             \
+        if (_rc != MG_OK) return _rc; \
+    } while (0)
 #define MG_REQUIRE(cond, code, ...)          \
     do {                                     \
         if (!(cond)) {                       \

@@ -1,19 +1,54 @@
-// mg_ep.h -- expert-parallel communicator (NCCL loaded at run time).
+// mg_ep.h -- expert-parallel communicator (NCCL loaded at run time) and the
+// host watchdog around its blocking waits.
 #pragma once
 #include <cuda_runtime.h>
 #include <stddef.h>
+#include <stdint.h>
 
 namespace mg {
 
+constexpr int EP_MAX_WORLD = 8;  // ranks of one box
+
 struct EpComm {
     int rank = 0, world = 1;
-    void *comm = nullptr;  // ncclComm_t
+    void *comm = nullptr;    // ncclComm_t
+    bool broken = false;     // a collective failed or a wait timed out: the communicator was aborted
+    double timeout_s = 600;  // host waits on a stream that holds collectives (MIDGE_EP_TIMEOUT_S)
+    int *d_ints = nullptr;   // small device scratch for host-level agreements (allreduce of a few ints)
+    int *h_ints = nullptr;   // pinned mirror
 };
 
 int ep_unique_id(void *out);  // 128 bytes
 int ep_init(EpComm *c, int rank, int world, const void *id);
-int ep_allreduce_sum(const EpComm &c, float *buf, size_t count, cudaStream_t st);
 void ep_destroy(EpComm *c);
+
+// Collectives on `st` (enqueued, asynchronous; graph-capturable).
+int ep_allgather(EpComm &c, const float *send, float *recv, size_t count, cudaStream_t st);
+int ep_reduce_scatter_sum(EpComm &c, const float *send, float *recv, size_t recvcount, cudaStream_t st);
+int ep_allgather_ints(EpComm &c, const int *send, int *recv, size_t count, cudaStream_t st);
+// Variable all-to-all of float rows: to rank d send_cnt[d] floats from
+// send + send_off[d], from rank s recv_cnt[s] floats into recv + recv_off[s]
+// (one NCCL group of point-to-point calls; the rank's own block is a device copy).
+int ep_alltoallv(EpComm &c, const float *send, const int64_t *send_off, const int64_t *send_cnt, float *recv,
+                 const int64_t *recv_off, const int64_t *recv_cnt, cudaStream_t st);
+
+// Host agreement: out[i] = max over ranks of v[i] (n <= 8 ints); synchronous.
+int ep_allreduce_max_ints(EpComm &c, const int *v, int *out, int n, cudaStream_t st);
+
+// Wait for `st` to drain.  With one rank: cudaStreamSynchronize.  With
+// several: poll the stream and the communicator's asynchronous error; on an
+// error or after c.timeout_s the communicator is aborted (ncclCommAbort, which
+// ends collectives that wait for a rank that will not come) and MG_ERR_COMM
+// is returned; the model is then unusable for further collectives.
+int ep_stream_wait(EpComm &c, cudaStream_t st);
+
+// The watchdog loop itself, over callbacks (so that its logic runs on the CPU
+// against fakes): query() returns 1 when the work is done, 0 while it runs,
+// < 0 on a device error; async_error() returns nonzero once the communicator
+// reports an error; abort_comm() is called once on error or timeout.
+// Returns MG_OK, MG_ERR_COMM (error or timeout) or MG_ERR_CUDA.
+int ep_watchdog(int (*query)(void *), int (*async_error)(void *), void (*abort_comm)(void *), void *ctx,
+                double timeout_s, int poll_us);
 
 // contiguous expert shard of `rank`
 inline void ep_range(int n_experts, int world, int rank, int *e0, int *n_local) {

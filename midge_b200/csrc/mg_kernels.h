@@ -86,10 +86,14 @@ struct CombineNormArgs {
     const float *nw;       // norm weight
     float eps;
     float *xb;             // normed output (may be null)
+    int64_t plane;         // floats between the K-split planes of y (0: n_tok*top_k*hidden)
 };
 int combine_norm(const CombineNormArgs &a, cudaStream_t st);
 int sum_parts(const float *part, int ks, int64_t plane, int n_tok, int64_t rows, int64_t ldp, float *out, int64_t ldo,
               int accumulate, cudaStream_t st);
+// temperature / top-p sampling of n_rows logits rows (mg_sample.cu)
+int sample_topp(const float *logits, int64_t ldl, int64_t V, int n_rows, float temp, float topp, uint64_t *rng,
+                int32_t *out, float *probs, cudaStream_t st);
 int stream_error_check();
 int stream_prepare();
 int *stream_error_word();

@@ -11,6 +11,7 @@
 #include "mg_common.cuh"
 #include "mg_kernels.h"
 #include "mg_model.h"
+#include "mg_ep_xchg.h"
 #include "mg_prefill.h"
 
 using mg::DevMat;
@@ -218,11 +219,7 @@ static int dalloc(mg_model *m, T **p, size_t bytes) {
     return MG_OK;
 }
 
-#define TRY(expr)                     \
-    do {                              \
-        int _rc = (expr);             \
-        if (_rc != MG_OK) return _rc; \
-    } while (0)
+
 
 extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int device, mg_model **out) {
     MG_REQUIRE(spec && out, MG_ERR_ARG, "model_create: null argument");
@@ -350,7 +347,7 @@ extern "C" int mg_model_set_dense(mg_model *m, const char *name, int dt, int64_t
 
 static int convert_expert_scales(mg_model *m) {
     mg_expert_layout &L = m->el;
-    L.scale_fmt = MG_SCALE_F16;
+    if (L.scale_fmt == MG_SCALE_UE8M0) return MG_OK;  // an "mxfp4e8" container: already ue8m0 bytes
     if (L.dt != MG_MXFP4 && L.dt != MG_Q4G32) return MG_OK;
     const char *keep = getenv("MIDGE_F16_SCALES");
     if (keep && *keep && *keep != '0') return MG_OK;
@@ -533,6 +530,7 @@ static void rope_tables(const mg_spec &s, int ctx, std::vector<float> &co, std::
 
 static int prefill_prepare(mg_model *m);
 static int rebase_prepare(mg_model *m);
+static int ep_prepare(mg_model *m);
 
 extern "C" int mg_model_ready(mg_model *m) {
     MG_REQUIRE(m, MG_ERR_ARG, "ready: null model");
@@ -670,13 +668,50 @@ extern "C" int mg_model_ready(mg_model *m) {
         MG_REQUIRE(m->maps_ok && m->use_stream, MG_ERR_SPEC,
                    "expert parallelism needs the streamed decode kernels (q8r trunk, 4-bit/int8 experts)");
     }
+    TRY(dalloc(m, &m->samp_probs, (size_t)DEC_MAX * s.vocab * 4));
+    TRY(dalloc(m, &m->samp_rng, (size_t)DEC_MAX * 8));
+    TRY(dalloc(m, &m->samp_out, (size_t)DEC_MAX * 4));
     TRY(dalloc(m, &m->greedy_out, (size_t)GREEDY_MAX * DEC_MAX * 4));
     TRY(dalloc(m, &m->greedy_step, 16));
     TRY(rebase_prepare(m));
     TRY(prefill_prepare(m));
     MG_REQUIRE(m->ep.world == 1 || m->tc_prefill, MG_ERR_SPEC,
                "expert parallelism needs the tensor-core prefill (MXFP4 with power-of-two scales or q8r experts)");
+    if (m->ep.world > 1) TRY(ep_prepare(m));
     m->ready = true;
+    return MG_OK;
+}
+
+// Expert-parallel exchange buffers.  Decode: at most EP_DEC_TOK tokens per
+// step over all ranks (the streamed MoE kernels' batch).  Prefill: a chunk of
+// R local tokens goes to at most min(world, top_k) ranks per token; a rank
+// receives at most every rank's chunk.
+static int ep_prepare(mg_model *m) {
+    const mg_spec &s = m->spec;
+    const int G = m->ep.world, k = s.top_k, R = m->rows_max;
+    const int64_t H = s.hidden;
+    m->ep_rowf = ep_rowf(H, k);
+    const int rowf = m->ep_rowf;
+    TRY(dalloc(m, &m->epd_send, (size_t)EP_DEC_TOK * rowf * 4));
+    TRY(dalloc(m, &m->epd_recv, (size_t)EP_DEC_TOK * rowf * 4));
+    TRY(dalloc(m, &m->epd_xb, (size_t)EP_DEC_TOK * H * 4));
+    TRY(dalloc(m, &m->epd_sel, (size_t)EP_DEC_TOK * k * 4));
+    TRY(dalloc(m, &m->epd_y, (size_t)m->ks_down * EP_DEC_TOK * k * H * 4));
+    const int per_tok = std::min(G, k);
+    m->epp_cap_recv = (int64_t)G * R;
+    TRY(dalloc(m, &m->epp_counts, (size_t)2 * G * 4));
+    TRY(dalloc(m, &m->epp_all, (size_t)2 * G * G * 4));
+    MG_CUDA(cudaHostAlloc(&m->epp_h_all, (size_t)2 * G * G * 4, cudaHostAllocDefault));
+    m->host_allocs.push_back(m->epp_h_all);
+    TRY(dalloc(m, &m->epp_send_row, (size_t)R * G * 4));
+    TRY(dalloc(m, &m->epp_ret_pos, (size_t)R * k * 4));
+    TRY(dalloc(m, &m->epp_send, (size_t)R * per_tok * rowf * 4));
+    TRY(dalloc(m, &m->epp_recv, (size_t)m->epp_cap_recv * rowf * 4));
+    TRY(dalloc(m, &m->epp_sel, (size_t)m->epp_cap_recv * k * 4));
+    TRY(dalloc(m, &m->epp_ret_row, (size_t)m->epp_cap_recv * k * 4));
+    TRY(dalloc(m, &m->epp_slot2, (size_t)m->epp_cap_recv * k * 4));
+    TRY(dalloc(m, &m->epp_ret_send, (size_t)m->epp_cap_recv * k * H * 4));
+    TRY(dalloc(m, &m->epp_ret_recv, (size_t)R * k * H * 4));
     return MG_OK;
 }
 
@@ -695,7 +730,8 @@ static int prefill_prepare(mg_model *m) {
     m->tc_dense = dense;
     if (!m->tc_prefill || !fmt || L.hidden % 64 || L.ffn % 64) m->tc_prefill = false;
     if (!m->tc_prefill && !m->tc_dense) return MG_OK;
-    const int64_t slots = (int64_t)R * s.top_k;
+    // expert parallel: the experts of this rank may receive every rank's slots
+    const int64_t slots = (int64_t)R * s.top_k * m->ep.world;
     const int64_t xrow = std::max((int64_t)slots * L.hidden, (int64_t)R * std::max<int64_t>(s.hidden, q_dim));
     TRY(dalloc(m, &m->pf_xhi, (size_t)xrow * 2));
     TRY(dalloc(m, &m->pf_xlo, (size_t)xrow * 2));
@@ -709,7 +745,7 @@ static int prefill_prepare(mg_model *m) {
     TRY(dalloc(m, (uint8_t **)&m->pf_tiles, (size_t)(slots / 128 + 1 + E) * sizeof(XgTile)));
     TRY(dalloc(m, &m->pf_hhi, (size_t)slots * L.ffn * 2));
     TRY(dalloc(m, &m->pf_hlo, (size_t)slots * L.ffn * 2));
-    TRY(dalloc(m, &m->pf_y, (size_t)slots * L.hidden * 4));
+    if (m->ep.world == 1) TRY(dalloc(m, &m->pf_y, (size_t)slots * L.hidden * 4));  // else the return buffer
     if (L.dt == MG_MXFP4 && !m->rebase_ok) {
         fprintf(stderr, "# expert matrices span more than 35 scale binades: tile prefill kernels\n");
         m->tc_prefill = false;
@@ -758,6 +794,68 @@ static int gemv_rows(mg_model *m, const DevMat &w, const float *x, int64_t ldx, 
                  y + (int64_t)r0 * ldy, ldy, m->st));
     }
     return MG_OK;
+}
+
+static MoePrefill prefill_args(mg_model *m, int layer) {
+    const mg_spec &s = m->spec;
+    MoePrefill pf{};
+    pf.L = m->el;
+    pf.experts_layer = m->experts + (int64_t)layer * m->el.layer_stride;
+    pf.rebase = m->pf_rebase ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
+    pf.top_k = s.top_k; pf.n_experts = s.n_experts; pf.e0 = m->e0; pf.n_local = m->n_local;
+    pf.act_plain = s.act_plain; pf.alpha = s.alpha; pf.limit = s.limit;
+    pf.counts = m->pf_counts; pf.offs = m->pf_offs; pf.cursor = m->pf_cursor; pf.ntiles = m->pf_ntiles;
+    pf.pos_of_slot = m->pf_pos; pf.slot_of_pos = m->pf_slot; pf.tiles = (XgTile *)m->pf_tiles;
+    pf.x_hi = m->pf_xhi; pf.x_lo = m->pf_xlo; pf.h_hi = m->pf_hhi; pf.h_lo = m->pf_hlo;
+    pf.err = stream_error_word();
+    return pf;
+}
+
+// Expert-parallel MoE block of a prefill chunk (engine/midge.c:595-611 with
+// the experts spread over the ranks).  The n local tokens (0: this rank only
+// serves its experts to the other ranks' tokens) are routed in m->sel / m->wts
+// with their normed rows in m->xb.  One host agreement (the per-destination
+// token and slot counts of every rank), then the dispatch of [row | ids] to
+// the ranks holding the experts, the grouped GEMMs over the received tokens,
+// the outputs back to the owners, and the combine in ascending expert order.
+static int moe_prefill_ep(mg_model *m, int layer, int n) {
+    const mg_spec &s = m->spec;
+    EpComm &c = m->ep;
+    const int G = c.world, me = c.rank, k = s.top_k, rowf = m->ep_rowf;
+    const int64_t H = s.hidden;
+    cudaStream_t st = m->st;
+    TRY(ep_pf_plan(m->sel, n, k, G, m->n_local, s.n_experts, m->epp_counts, m->epp_send_row, m->epp_ret_pos, st));
+    TRY(ep_allgather_ints(c, m->epp_counts, m->epp_all, (size_t)2 * G, st));
+    MG_CUDA(cudaMemcpyAsync(m->epp_h_all, m->epp_all, (size_t)2 * G * G * 4, cudaMemcpyDeviceToHost, st));
+    TRY(ep_stream_wait(c, st));
+    const int *A = m->epp_h_all;  // A[r*2G + d]: tokens r -> d; A[r*2G + G + d]: slots r -> d
+    int64_t so[EP_MAX_WORLD], sc[EP_MAX_WORLD], ro[EP_MAX_WORLD], rc[EP_MAX_WORLD];
+    int64_t bso[EP_MAX_WORLD], bsc[EP_MAX_WORLD], bro[EP_MAX_WORLD], brc[EP_MAX_WORLD];
+    int64_t a = 0, b = 0, a2 = 0, b2 = 0, n_recv = 0;
+    for (int d = 0; d < G; d++) {
+        sc[d] = (int64_t)A[me * 2 * G + d] * rowf; so[d] = a; a += sc[d];          // my tokens to d
+        rc[d] = (int64_t)A[d * 2 * G + me] * rowf; ro[d] = b; b += rc[d];          // d's tokens to me
+        n_recv += A[d * 2 * G + me];
+        bsc[d] = (int64_t)A[d * 2 * G + G + me] * H; bso[d] = a2; a2 += bsc[d];    // outputs of d's slots, back
+        brc[d] = (int64_t)A[me * 2 * G + G + d] * H; bro[d] = b2; b2 += brc[d];    // outputs of my slots on d
+    }
+    MG_REQUIRE(n_recv <= m->epp_cap_recv, MG_ERR_STATE, "expert parallel prefill: %lld tokens received (room for %lld)",
+               (long long)n_recv, (long long)m->epp_cap_recv);
+    TRY(ep_pf_pack(m->xb, m->sel, n, k, G, H, rowf, m->epp_send_row, m->epp_send, st));
+    TRY(ep_alltoallv(c, m->epp_send, so, sc, m->epp_recv, ro, rc, st));
+    TRY(ep_pf_unpack_sel(m->epp_recv, (int)n_recv, k, H, rowf, m->epp_sel, st));
+    TRY(ep_pf_retplan(m->epp_sel, (int)n_recv, k, m->e0, m->n_local, m->epp_ret_row, st));
+    MoePrefill pf = prefill_args(m, layer);
+    pf.n = (int)n_recv;
+    pf.sel = m->epp_sel;
+    pf.xb = m->epp_recv;
+    pf.ldx = rowf;
+    pf.out_row = m->epp_ret_row;
+    pf.slot2 = m->epp_slot2;
+    pf.y = m->epp_ret_send;
+    TRY(moe_prefill_experts(pf, st));
+    TRY(ep_alltoallv(c, m->epp_ret_send, bso, bsc, m->epp_ret_recv, bro, brc, st));
+    return pf_combine(m->x, H, m->sel, m->wts, n, k, s.n_experts, m->epp_ret_recv, m->epp_ret_pos, st);
 }
 
 // The per-layer body shared by decode (n rows = sequences, one token each)
@@ -836,18 +934,10 @@ static int layer_pass(mg_model *m, int layer, int n, bool prefill, int seq, int 
     else TRY(router(ra, st));
     const uint8_t *lb = m->experts + (int64_t)layer * m->el.layer_stride;
     if (prefill && m->tc_prefill) {
-        MoePrefill pf{};
-        pf.L = m->el;
-        pf.experts_layer = lb;
-        pf.rebase = m->pf_rebase + (int64_t)layer * m->n_local * 3;
-        pf.n = n; pf.top_k = s.top_k; pf.n_experts = s.n_experts; pf.e0 = m->e0; pf.n_local = m->n_local;
-        pf.ep = &m->ep;
-        pf.sel = m->sel; pf.w = m->wts; pf.xb = m->xb; pf.x = m->x;
-        pf.act_plain = s.act_plain; pf.alpha = s.alpha; pf.limit = s.limit;
-        pf.counts = m->pf_counts; pf.offs = m->pf_offs; pf.cursor = m->pf_cursor; pf.ntiles = m->pf_ntiles;
-        pf.pos_of_slot = m->pf_pos; pf.slot_of_pos = m->pf_slot; pf.tiles = (XgTile *)m->pf_tiles;
-        pf.x_hi = m->pf_xhi; pf.x_lo = m->pf_xlo; pf.h_hi = m->pf_hhi; pf.h_lo = m->pf_hlo; pf.y = m->pf_y;
-        pf.err = stream_error_word();
+        if (m->ep.world > 1) return moe_prefill_ep(m, layer, n);
+        MoePrefill pf = prefill_args(m, layer);
+        pf.n = n;
+        pf.sel = m->sel; pf.w = m->wts; pf.xb = m->xb; pf.x = m->x; pf.y = m->pf_y;
         return moe_prefill(pf, st);
     }
     for (int r0 = 0; r0 < n; r0 += DEC_MAX) {
@@ -883,6 +973,46 @@ static bool stream_ok(const mg_model *m, int n) {
     return m->maps_ok && trunk && ex && q8r_ok(m->lm_head) && n <= 8 && n * s.top_k <= 128 && m->el.dt != MG_F32;
 }
 
+static MoeStreamArgs stream_moe_args(mg_model *m, int layer) {
+    const mg_spec &s = m->spec;
+    MoeStreamArgs ma{};
+    ma.L = m->el; ma.experts_layer = m->experts + (int64_t)layer * m->el.layer_stride;
+    ma.maps = m->map_ex; ma.layer = layer;
+    ma.n_experts = m->n_local; ma.e0 = m->e0; ma.top_k = s.top_k;
+    ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit; ma.h = m->h;
+    ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
+    ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
+    ma.use_tc = m->tc_moe;
+    ma.bs = m->bs_moe ? &m->bs : nullptr;
+    return ma;
+}
+
+// Expert-parallel routed experts of one decode layer: every rank's n_max rows
+// [normed row | ids] are gathered (pads route nowhere), this rank's experts
+// run over all of them (their outputs in the slots of local experts, zero in
+// the others), and a sum reduce-scatter gives each owner its own tokens' slot
+// outputs -- exactly one rank holds a nonzero value per slot, so the sum is
+// exact and the owner's combine sees the one-GPU values.  n = 0: this rank has
+// no tokens this step and only serves its experts.
+static int ep_decode_moe(mg_model *m, int layer, int n) {
+    const mg_spec &s = m->spec;
+    EpComm &c = m->ep;
+    const int G = c.world, k = s.top_k, nm = m->dec_nmax, n_all = G * nm, rowf = m->ep_rowf;
+    const int64_t H = s.hidden;
+    cudaStream_t st = m->st;
+    TRY(ep_dec_pack(m->xb, m->sel, n, nm, H, k, rowf, m->epd_send, st));
+    TRY(ep_allgather(c, m->epd_send, m->epd_recv, (size_t)nm * rowf, st));
+    TRY(ep_dec_unpack(m->epd_recv, n_all, H, k, rowf, m->epd_xb, m->epd_sel, st));
+    const size_t plane_all = (size_t)n_all * k * H, plane_loc = (size_t)nm * k * H;
+    MG_CUDA(cudaMemsetAsync(m->epd_y, 0, (size_t)m->ks_down * plane_all * 4, st));
+    MoeStreamArgs ma = stream_moe_args(m, layer);
+    ma.n_tok = n_all; ma.sel = m->epd_sel; ma.xb = m->epd_xb; ma.y = m->epd_y;
+    TRY(moe_stream(ma, st));
+    for (int p = 0; p < m->ks_down; p++)
+        TRY(ep_reduce_scatter_sum(c, m->epd_y + p * plane_all, m->moe_y + p * plane_loc, plane_loc, st));
+    return MG_OK;
+}
+
 // One layer of the streamed decode: combine(previous MoE)+norm, QKV (K-split
 // partials), RoPE/QK-norm/KV store, attention, O (partials folded into the
 // residual by the router), router, streamed MoE.
@@ -896,6 +1026,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     cn.x = m->x; cn.y = layer > 0 ? m->moe_y : nullptr; cn.ksplit = m->ks_down;
     cn.sel = m->sel; cn.w = m->wts; cn.n_tok = n; cn.top_k = s.top_k; cn.n_experts = s.n_experts;
     cn.hidden = H; cn.nw = m->attn_norm[layer]; cn.eps = s.norm_eps; cn.xb = m->xb;
+    if (m->ep.world > 1) cn.plane = (int64_t)m->dec_nmax * s.top_k * H;
     TRY(combine_norm(cn, st));
     StreamGemvArgs g{};
     g.dt = MG_Q8R; g.scale_fmt = MG_SCALE_F16; g.nmat = 3; g.cols = H; g.x = m->xb; g.ldx = H; g.n_tok = n;
@@ -955,18 +1086,18 @@ static int layer_stream(mg_model *m, int layer, int n) {
     ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
     ma.use_tc = m->tc_moe;
     ma.bs = m->bs_moe ? &m->bs : nullptr;
-    const size_t ycount = (size_t)m->ks_down * n * s.top_k * H;
-    if (m->ep.world > 1)  // slots of other ranks' experts stay zero, then the sum over ranks fills them exactly
-        MG_CUDA(cudaMemsetAsync(m->moe_y, 0, ycount * 4, st));
-    TRY(moe_stream(ma, st));
-    TRY(ep_allreduce_sum(m->ep, m->moe_y, ycount, st));
-    return MG_OK;
+    if (m->ep.world > 1) return ep_decode_moe(m, layer, n);
+    return moe_stream(ma, st);
 }
 
 // embedding -> logits and argmax keys, device only (tokens/positions in m->toks / tok_pos)
 static int decode_core_stream(mg_model *m, int n) {
     const mg_spec &s = m->spec;
     cudaStream_t st = m->st;
+    if (n == 0) {  // expert parallel, no local sequence this step: serve the experts only
+        for (int l = 0; l < s.n_layers; l++) TRY(ep_decode_moe(m, l, 0));
+        return MG_OK;
+    }
     TRY(dequant_rows(m->embed.dt, MG_SCALE_F16, m->embed.data, m->embed.scales, m->embed.rows, m->embed.cols, m->toks, n,
                      m->x, st));
     for (int l = 0; l < s.n_layers; l++) TRY(layer_stream(m, l, n));
@@ -975,6 +1106,7 @@ static int decode_core_stream(mg_model *m, int n) {
     cn.x = m->x; cn.y = m->moe_y; cn.ksplit = m->ks_down; cn.sel = m->sel; cn.w = m->wts; cn.n_tok = n;
     cn.top_k = s.top_k; cn.n_experts = s.n_experts; cn.hidden = s.hidden; cn.nw = m->final_norm;
     cn.eps = s.norm_eps; cn.xb = m->xb;
+    if (m->ep.world > 1) cn.plane = (int64_t)m->dec_nmax * s.top_k * s.hidden;
     TRY(combine_norm(cn, st));
     StreamGemvArgs g{};
     g.dt = MG_Q8R; g.scale_fmt = MG_SCALE_F16; g.nmat = 1; g.cols = s.hidden; g.x = m->xb; g.ldx = s.hidden;
@@ -1004,7 +1136,7 @@ static int decode_core_tile(mg_model *m, int n) {
 // decode body for n sequences whose tokens/positions are already in the
 // pinned staging arrays; everything stream-ordered (graph-capturable)
 static int decode_body(mg_model *m, int n) {
-    m->last_streamed = m->use_stream && stream_ok(m, n);
+    m->last_streamed = m->ep.world > 1 || (m->use_stream && stream_ok(m, n));
     cudaStream_t st = m->st;
     MG_CUDA(cudaMemcpyAsync(m->toks, m->h_toks, n * 4, cudaMemcpyHostToDevice, st));
     MG_CUDA(cudaMemcpyAsync(m->tok_pos, m->h_pos, n * 4, cudaMemcpyHostToDevice, st));
@@ -1022,10 +1154,12 @@ static int decode_body(mg_model *m, int n) {
 
 // one greedy step fed from the previous step's argmax, device only
 static int decode_chain_body(mg_model *m, int n) {
-    const bool streamed = m->use_stream && stream_ok(m, n);
-    k_advance<<<1, 32, 0, m->st>>>(streamed ? m->amax_keys : nullptr, m->amax, n, m->toks, m->tok_pos, m->greedy_out,
-                                   m->greedy_step);
-    MG_CHECK_LAUNCH();
+    const bool streamed = m->ep.world > 1 || (m->use_stream && stream_ok(m, n));
+    if (n > 0) {
+        k_advance<<<1, 32, 0, m->st>>>(streamed ? m->amax_keys : nullptr, m->amax, n, m->toks, m->tok_pos,
+                                       m->greedy_out, m->greedy_step);
+        MG_CHECK_LAUNCH();
+    }
     return streamed ? decode_core_stream(m, n) : decode_core_tile(m, n);
 }
 
@@ -1048,7 +1182,8 @@ static int graph_kernels(cudaGraph_t g) {
 // (capture executes nothing).  Counts the kernels launched.
 static int graph_run(mg_model *m, std::unordered_map<int, Graph> &tab, int n, int (*body)(mg_model *, int)) {
     if (!m->use_graphs) return body(m, n);  // eager-only runs are not counted
-    auto it = tab.find(n);
+    const int key = n + 256 * (m->ep.world > 1 ? m->dec_nmax : 0);
+    auto it = tab.find(key);
     if (it != tab.end()) {
         MG_CUDA(cudaGraphLaunch(it->second.exec, m->st));
         m->kernel_launches += (uint64_t)it->second.kernels;
@@ -1070,18 +1205,39 @@ static int graph_run(mg_model *m, std::unordered_map<int, Graph> &tab, int n, in
     cudaError_t ie = cudaGraphInstantiate(&gr.exec, g, 0);
     cudaGraphDestroy(g);
     MG_REQUIRE(ie == cudaSuccess, MG_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(ie));
-    tab[n] = gr;
+    tab[key] = gr;
     m->kernel_launches += (uint64_t)gr.kernels;  // the eager run launched the same kernels
     return MG_OK;
 }
 
 static int run_decode(mg_model *m, int n) { return graph_run(m, m->dec_graphs, n, decode_body); }
 
+// Expert parallel: every rank takes part in each decode step (n_seqs may be
+// 0 on some ranks); the ranks agree on the tokens per rank of the step.
+static int ep_decode_agree(mg_model *m, int n_seqs, int n_steps) {
+    if (m->ep.world == 1) {
+        m->dec_nmax = n_seqs;
+        return MG_OK;
+    }
+    const int v[3] = {n_seqs, n_steps, -n_steps};
+    int mx[3];
+    TRY(ep_allreduce_max_ints(m->ep, v, mx, 3, m->st));
+    MG_REQUIRE(mx[1] == -mx[2], MG_ERR_ARG, "expert parallel decode: the ranks asked for different step counts");
+    MG_REQUIRE(mx[0] * m->ep.world <= EP_DEC_TOK, MG_ERR_ARG,
+               "expert parallel decode: %d tokens per rank x %d ranks exceed %d per step", mx[0], m->ep.world,
+               EP_DEC_TOK);
+    MG_REQUIRE(m->use_stream && stream_ok(m, mx[0] * m->ep.world), MG_ERR_SPEC,
+               "expert parallel decode needs the streamed kernels");
+    m->dec_nmax = mx[0];
+    return MG_OK;
+}
+
 extern "C" int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, float *logits,
                               int32_t *argmax) {
     MG_REQUIRE(m && m->ready, MG_ERR_STATE, "decode: model not ready");
-    MG_REQUIRE(n_seqs >= 1 && n_seqs <= DEC_MAX && n_seqs <= m->max_seqs && toks, MG_ERR_ARG, "decode: bad n_seqs %d",
-               n_seqs);
+    const int n_min = m->ep.world > 1 ? 0 : 1;
+    MG_REQUIRE(n_seqs >= n_min && n_seqs <= DEC_MAX && n_seqs <= m->max_seqs && (n_seqs == 0 || toks), MG_ERR_ARG,
+               "decode: bad n_seqs %d", n_seqs);
     MG_CUDA(cudaSetDevice(m->device));
     const mg_spec &s = m->spec;
     for (int i = 0; i < n_seqs; i++) {
@@ -1094,10 +1250,12 @@ extern "C" int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, c
         m->h_pos[i] = m->pos[sq];
         m->h_seq[i] = sq;
     }
+    TRY(ep_decode_agree(m, n_seqs, 1));
+    if (m->dec_nmax == 0) return MG_OK;  // no rank decodes
     TRY(run_decode(m, n_seqs));
-    if (logits)
+    if (logits && n_seqs)
         MG_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)n_seqs * s.vocab * 4, cudaMemcpyDeviceToHost, m->st));
-    MG_CUDA(cudaStreamSynchronize(m->st));
+    TRY(ep_stream_wait(m->ep, m->st));
     if (*m->h_err) {  // a bounded wait in a streamed kernel gave up
         *m->h_err = 0;
         return stream_error_check();
@@ -1114,8 +1272,9 @@ extern "C" int mg_decode_step(mg_model *m, int n_seqs, const int32_t *seq_ids, c
 extern "C" int mg_decode_greedy(mg_model *m, int n_seqs, const int32_t *seq_ids, const int32_t *toks, int n_steps,
                                 int32_t *out_toks) {
     MG_REQUIRE(m && m->ready, MG_ERR_STATE, "greedy: model not ready");
-    MG_REQUIRE(n_seqs >= 1 && n_seqs <= DEC_MAX && n_seqs <= m->max_seqs && toks && out_toks, MG_ERR_ARG,
-               "greedy: bad arguments");
+    const int n_min = m->ep.world > 1 ? 0 : 1;
+    MG_REQUIRE(n_seqs >= n_min && n_seqs <= DEC_MAX && n_seqs <= m->max_seqs && (n_seqs == 0 || (toks && out_toks)),
+               MG_ERR_ARG, "greedy: bad arguments");
     MG_REQUIRE(n_steps >= 1 && n_steps <= GREEDY_MAX, MG_ERR_ARG, "greedy: n_steps %d not in [1, %d]", n_steps,
                GREEDY_MAX);
     MG_CUDA(cudaSetDevice(m->device));
@@ -1131,16 +1290,20 @@ extern "C" int mg_decode_greedy(mg_model *m, int n_seqs, const int32_t *seq_ids,
         m->h_seq[i] = sq;
     }
     cudaStream_t st = m->st;
+    TRY(ep_decode_agree(m, n_seqs, n_steps));
+    if (m->dec_nmax == 0) return MG_OK;  // no rank decodes
     MG_CUDA(cudaMemsetAsync(m->greedy_step, 0, 4, st));
     TRY(run_decode(m, n_seqs));
     for (int k = 1; k < n_steps; k++) TRY(graph_run(m, m->chain_graphs, n_seqs, decode_chain_body));
-    const bool streamed = m->use_stream && stream_ok(m, n_seqs);
-    k_advance<<<1, 32, 0, st>>>(streamed ? m->amax_keys : nullptr, m->amax, n_seqs, m->toks, m->tok_pos, m->greedy_out,
-                                m->greedy_step);
-    MG_CHECK_LAUNCH();
-    m->kernel_launches += 1;
-    MG_CUDA(cudaMemcpyAsync(out_toks, m->greedy_out, (size_t)n_steps * n_seqs * 4, cudaMemcpyDeviceToHost, st));
-    MG_CUDA(cudaStreamSynchronize(st));
+    const bool streamed = m->ep.world > 1 || (m->use_stream && stream_ok(m, n_seqs));
+    if (n_seqs > 0) {
+        k_advance<<<1, 32, 0, st>>>(streamed ? m->amax_keys : nullptr, m->amax, n_seqs, m->toks, m->tok_pos,
+                                    m->greedy_out, m->greedy_step);
+        MG_CHECK_LAUNCH();
+        m->kernel_launches += 1;
+        MG_CUDA(cudaMemcpyAsync(out_toks, m->greedy_out, (size_t)n_steps * n_seqs * 4, cudaMemcpyDeviceToHost, st));
+    }
+    TRY(ep_stream_wait(m->ep, st));
     *m->h_err = 0;
     TRY(stream_error_check());
     for (int i = 0; i < n_seqs; i++) m->pos[m->h_seq[i]] += n_steps;
@@ -1175,7 +1338,7 @@ extern "C" int mg_forward(mg_model *m, int seq, int32_t token, float *logits, in
 extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n, int logits_mode, float *logits) {
     MG_REQUIRE(m && m->ready, MG_ERR_STATE, "forward_batch: model not ready");
     MG_REQUIRE(seq >= 0 && seq < m->max_seqs && n >= 0 && (n == 0 || toks), MG_ERR_ARG, "forward_batch: bad arguments");
-    MG_REQUIRE(logits_mode >= 0 && logits_mode <= 2 && (logits_mode == 0 || logits), MG_ERR_ARG,
+    MG_REQUIRE(logits_mode >= 0 && logits_mode <= 2 && (logits_mode == 0 || logits || n == 0), MG_ERR_ARG,
                "forward_batch: bad logits mode");
     MG_CUDA(cudaSetDevice(m->device));
     const mg_spec &s = m->spec;
@@ -1183,8 +1346,20 @@ extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n
         MG_REQUIRE(m->pos[seq] + t < m->ctx, MG_ERR_RANGE, "context full (%d)", m->ctx);
         MG_REQUIRE(toks[t] >= 0 && toks[t] < s.vocab, MG_ERR_RANGE, "token %d out of range", toks[t]);
     }
-    for (int c0 = 0; c0 < n; c0 += m->pf_chunk) {
+    int n_all = n;  // expert parallel: every rank runs as many chunks as the longest prompt needs
+    if (m->ep.world > 1) {
+        int mx = 0;
+        TRY(ep_allreduce_max_ints(m->ep, &n, &mx, 1, m->st));
+        n_all = mx;
+    }
+    for (int c0 = 0; c0 < n_all; c0 += m->pf_chunk) {
         int nc = n - c0 < m->pf_chunk ? n - c0 : m->pf_chunk;
+        if (nc <= 0) {  // expert parallel, no local tokens in this chunk: serve the experts only
+            for (int l = 0; l < s.n_layers; l++) TRY(moe_prefill_ep(m, l, 0));
+            TRY(ep_stream_wait(m->ep, m->st));
+            TRY(stream_error_check());
+            continue;
+        }
         int pos0 = m->pos[seq];
         for (int t = 0; t < nc; t++) {
             m->h_toks[t] = toks[c0 + t];
@@ -1205,16 +1380,42 @@ extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n
                 TRY(logits_rows(m, m->x + (int64_t)r0 * s.hidden, nn));
                 MG_CUDA(cudaMemcpyAsync(logits + (int64_t)(c0 + r0) * s.vocab, m->logits, (size_t)nn * s.vocab * 4,
                                         cudaMemcpyDeviceToHost, st));
+                if (last_chunk && r0 + nn == nc && nn > 1)  // the last position's logits stay in row 0
+                    MG_CUDA(cudaMemcpyAsync(m->logits, m->logits + (int64_t)(nn - 1) * s.vocab, (size_t)s.vocab * 4,
+                                            cudaMemcpyDeviceToDevice, st));
             }
         } else if (logits_mode == 1 && last_chunk) {
             TRY(logits_rows(m, m->x + (int64_t)(nc - 1) * s.hidden, 1));
             MG_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)s.vocab * 4, cudaMemcpyDeviceToHost, st));
         }
-        MG_CUDA(cudaStreamSynchronize(st));
+        TRY(ep_stream_wait(m->ep, st));
         if (m->tc_prefill || m->tc_dense) TRY(stream_error_check());
         m->pos[seq] += nc;
         m->expert_loads += (uint64_t)nc * s.top_k * s.n_layers;
     }
+    return MG_OK;
+}
+
+extern "C" int mg_model_sample(mg_model *m, int n_rows, float temp, float top_p, uint64_t *rng, int32_t *out) {
+    MG_REQUIRE(m && m->ready && out && n_rows >= 1 && n_rows <= DEC_MAX && (temp <= 0.f || rng), MG_ERR_ARG,
+               "sample: bad arguments");
+    MG_CUDA(cudaSetDevice(m->device));
+    cudaStream_t st = m->st;
+    const int64_t V = m->spec.vocab;
+    if (temp > 0.f) MG_CUDA(cudaMemcpyAsync(m->samp_rng, rng, (size_t)n_rows * 8, cudaMemcpyHostToDevice, st));
+    TRY(sample_topp(m->logits, V, V, n_rows, temp, top_p, m->samp_rng, m->samp_out, m->samp_probs, st));
+    MG_CUDA(cudaMemcpyAsync(m->h_amax, m->samp_out, (size_t)n_rows * 4, cudaMemcpyDeviceToHost, st));
+    if (temp > 0.f) MG_CUDA(cudaMemcpyAsync(rng, m->samp_rng, (size_t)n_rows * 8, cudaMemcpyDeviceToHost, st));
+    MG_CUDA(cudaStreamSynchronize(st));
+    memcpy(out, m->h_amax, (size_t)n_rows * 4);
+    return MG_OK;
+}
+
+extern "C" int mg_model_put_logits(mg_model *m, int row, const float *logits) {
+    MG_REQUIRE(m && m->ready && logits && row >= 0 && row < DEC_MAX, MG_ERR_ARG, "put_logits: bad arguments");
+    MG_CUDA(cudaSetDevice(m->device));
+    MG_CUDA(cudaMemcpy(m->logits + (int64_t)row * m->spec.vocab, logits, (size_t)m->spec.vocab * 4,
+                       cudaMemcpyHostToDevice));
     return MG_OK;
 }
 
@@ -1269,6 +1470,7 @@ extern "C" int mg_model_free(mg_model *m) {
             if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     ep_destroy(&m->ep);
     for (void *p : m->allocs) cudaFree(p);
+    for (void *p : m->host_allocs) cudaFreeHost(p);
     for (void *p : {(void *)m->h_toks, (void *)m->h_pos, (void *)m->h_seq, (void *)m->h_amax, (void *)m->h_err,
                     (void *)m->h_keys})
         if (p) cudaFreeHost(p);

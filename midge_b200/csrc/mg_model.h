@@ -26,6 +26,7 @@ constexpr int PF_CHUNK = 4096;  // default tokens per prefill pass through the l
 constexpr int DEC_MAX = 16;     // sequences per decode step
 
 constexpr int GREEDY_MAX = 4096;  // steps per mg_decode_greedy call
+constexpr int EP_DEC_TOK = 8;     // expert parallel: tokens per decode step over all ranks
 
 struct Graph {
     cudaGraphExec_t exec = nullptr;
@@ -40,6 +41,7 @@ struct mg_model {
     int ctx = 0, max_seqs = 0, device = 0;
     cudaStream_t st = nullptr;
     std::vector<void *> allocs;
+    std::vector<void *> host_allocs;  // pinned host buffers freed with the model
 
     mg::DevMat embed, lm_head;
     float *final_norm = nullptr;
@@ -99,7 +101,22 @@ struct mg_model {
     __half *pf_xhi = nullptr, *pf_xlo = nullptr, *pf_hhi = nullptr, *pf_hlo = nullptr;
     float *pf_y = nullptr;
 
-    std::unordered_map<int, mg::Graph> dec_graphs;    // keyed by n_seqs
+    // device sampling (mg_model_sample): probabilities, generator states, picks
+    float *samp_probs = nullptr;
+    uint64_t *samp_rng = nullptr;
+    int32_t *samp_out = nullptr;
+    // expert parallelism (world > 1): token exchange buffers
+    int ep_rowf = 0;       // floats per packed [normed row | top-k ids] row
+    int dec_nmax = 0;      // decode: tokens per rank of the current step (max over the ranks)
+    float *epd_send = nullptr, *epd_recv = nullptr, *epd_xb = nullptr, *epd_y = nullptr;
+    int32_t *epd_sel = nullptr;
+    int64_t epp_cap_recv = 0;  // prefill: received tokens per layer and chunk, at most
+    int *epp_counts = nullptr, *epp_all = nullptr, *epp_h_all = nullptr;
+    int *epp_send_row = nullptr, *epp_ret_pos = nullptr, *epp_ret_row = nullptr, *epp_slot2 = nullptr;
+    int32_t *epp_sel = nullptr;
+    float *epp_send = nullptr, *epp_recv = nullptr, *epp_ret_send = nullptr, *epp_ret_recv = nullptr;
+
+    std::unordered_map<int, mg::Graph> dec_graphs;    // keyed by n_seqs (and, expert-parallel, the step's n_max)
     std::unordered_map<int, mg::Graph> chain_graphs;  // device-fed greedy steps, keyed by n_seqs
     int32_t *greedy_out = nullptr, *greedy_step = nullptr;  // [GREEDY_MAX x DEC_MAX] tokens, step counter
     uint64_t kernel_launches = 0;  // kernels launched by the decode paths

@@ -8,6 +8,7 @@
 #include "mg_gemm.h"
 #include "mg_kernels.h"
 #include "mg_prefill.h"
+#include "mg_ep_xchg.h"
 
 namespace mg {
 
@@ -54,14 +55,14 @@ __global__ void k_pf_scatter(const int32_t *__restrict__ sel, int nslots, int e0
 }
 
 // X rows in expert-major order as f16 hi/lo
-__global__ void k_pf_gather(const float *__restrict__ xb, int64_t H, int top_k, const int *__restrict__ slot_of_pos,
-                            const int *offs_end, __half *hi, __half *lo) {
+__global__ void k_pf_gather(const float *__restrict__ xb, int64_t ldx, int64_t H, int top_k,
+                            const int *__restrict__ slot_of_pos, const int *offs_end, __half *hi, __half *lo) {
     const int64_t P = *offs_end;
     const int64_t n8 = H / 8;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < P * n8; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t p = i / n8, c = (i - p * n8) * 8;
         const int t = slot_of_pos[p] / top_k;
-        const float4 *src = reinterpret_cast<const float4 *>(xb + (int64_t)t * H + c);
+        const float4 *src = reinterpret_cast<const float4 *>(xb + (int64_t)t * ldx + c);
         const float4 a = src[0], b = src[1];
         const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         __half h[8], l[8];
@@ -92,7 +93,7 @@ __global__ void k_split_rows(const float *__restrict__ x, int64_t ldx, int n, in
 // x[t] += w * y per routed expert in ascending expert id (engine/midge.c:595-611, :466);
 // Y is slot-major (row t*top_k + i)
 __global__ void k_pf_combine(float *x, int64_t H, const int32_t *__restrict__ sel, const float *__restrict__ w,
-                             int top_k, int n_experts, const float *__restrict__ Y) {
+                             int top_k, int n_experts, const float *__restrict__ Y, const int *__restrict__ slot_row) {
     const int t = blockIdx.x;
     int ord[16];
     int k = 0;
@@ -108,7 +109,8 @@ __global__ void k_pf_combine(float *x, int64_t H, const int32_t *__restrict__ se
         float acc = xr[c];
         for (int j = 0; j < k; j++) {
             const int i = ord[j];
-            acc = __fadd_rn(acc, __fmul_rn(w[t * top_k + i], Y[(int64_t)(t * top_k + i) * H + c]));
+            const int64_t row = slot_row ? slot_row[t * top_k + i] : t * top_k + i;
+            acc = __fadd_rn(acc, __fmul_rn(w[t * top_k + i], Y[row * H + c]));
         }
         xr[c] = acc;
     }
@@ -179,10 +181,12 @@ int dense_gemm(const DenseGemm &d, cudaStream_t st) {
     return xgemm(XG_DENSE, MG_Q8R, l, st);
 }
 
-int moe_prefill(const MoePrefill &a, cudaStream_t st) {
+int moe_prefill_experts(const MoePrefill &a, cudaStream_t st) {
     const int nslots = a.n * a.top_k;
     const int E = a.n_local;
-    const bool ep = a.ep && a.ep->world > 1;
+    if (nslots <= 0) return MG_OK;
+    const int64_t ldx = a.ldx ? a.ldx : a.L.hidden;
+    MG_REQUIRE(ldx % 4 == 0, MG_ERR_ARG, "moe_prefill: activation stride %lld not a multiple of 4", (long long)ldx);
     MG_CUDA(cudaMemsetAsync(a.counts, 0, (size_t)E * sizeof(int), st));
     int g = ceil_div(nslots, 256);
     k_pf_count<<<g, 256, 0, st>>>(a.sel, nslots, a.e0, E, a.counts);
@@ -194,7 +198,7 @@ int moe_prefill(const MoePrefill &a, cudaStream_t st) {
     MG_CHECK_LAUNCH();
     int gg = ceil_div((int64_t)nslots * (a.L.hidden / 8), 256);
     if (gg > 148 * 16) gg = 148 * 16;
-    k_pf_gather<<<gg, 256, 0, st>>>(a.xb, a.L.hidden, a.top_k, a.slot_of_pos, a.offs + E, a.x_hi, a.x_lo);
+    k_pf_gather<<<gg, 256, 0, st>>>(a.xb, ldx, a.L.hidden, a.top_k, a.slot_of_pos, a.offs + E, a.x_hi, a.x_lo);
     MG_CHECK_LAUNCH();
     XgLaunch l{};
     l.args.L = a.L;
@@ -218,24 +222,36 @@ int moe_prefill(const MoePrefill &a, cudaStream_t st) {
     l.x_rows = nslots;
     int rc = xgemm(XG_GATEUP, a.L.dt, l, st);
     if (rc) return rc;
-    // down -> y (slot-major); slots of other ranks' experts stay zero
-    if (ep) MG_CUDA(cudaMemsetAsync(a.y, 0, (size_t)nslots * a.L.hidden * sizeof(float), st));
+    // down -> y: slot-major, or at out_row[slot] (expert parallel: the return rows)
+    const int *slot_rows = a.slot_of_pos;
+    if (a.out_row) {
+        MG_REQUIRE(a.slot2, MG_ERR_ARG, "moe_prefill: out_row needs slot2 scratch");
+        rc = ep_pf_remap(a.slot_of_pos, a.offs + E, a.out_row, nslots, a.slot2, st);
+        if (rc) return rc;
+        slot_rows = a.slot2;
+    }
     l.args.M = a.L.hidden;
     l.args.K = a.L.ffn;
-    l.args.slot_of_pos = a.slot_of_pos;
+    l.args.slot_of_pos = slot_rows;
     l.args.y = a.y;
     l.args.ldy = a.L.hidden;
     l.x_hi = a.h_hi;
     l.x_lo = a.h_lo;
-    rc = xgemm(XG_DOWN, a.L.dt, l, st);
-    if (rc) return rc;
-    if (ep) {  // every slot's output on every rank: exact, each slot is nonzero on one rank only
-        rc = ep_allreduce_sum(*a.ep, a.y, (size_t)nslots * a.L.hidden, st);
-        if (rc) return rc;
-    }
-    k_pf_combine<<<a.n, 256, 0, st>>>(a.x, a.L.hidden, a.sel, a.w, a.top_k, a.n_experts, a.y);
+    return xgemm(XG_DOWN, a.L.dt, l, st);
+}
+
+int pf_combine(float *x, int64_t H, const int32_t *sel, const float *w, int n, int top_k, int n_experts, const float *Y,
+               const int *slot_row, cudaStream_t st) {
+    if (n <= 0) return MG_OK;
+    k_pf_combine<<<n, 256, 0, st>>>(x, H, sel, w, top_k, n_experts, Y, slot_row);
     MG_CHECK_LAUNCH();
     return MG_OK;
+}
+
+int moe_prefill(const MoePrefill &a, cudaStream_t st) {
+    int rc = moe_prefill_experts(a, st);
+    if (rc) return rc;
+    return pf_combine(a.x, a.L.hidden, a.sel, a.w, a.n, a.top_k, a.n_experts, a.y, nullptr, st);
 }
 
 }  // namespace mg

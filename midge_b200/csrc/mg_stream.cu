@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
     }
     __syncthreads();
     const int nk = s_k;
-    const int64_t plane = (int64_t)a.n_tok * a.top_k * H;
+    const int64_t plane = a.plane ? a.plane : (int64_t)a.n_tok * a.top_k * H;
     float ss = 0.f;
     constexpr int PER = 4;
     if (KS == 1 && H <= (int64_t)blockDim.x * PER) {  // (more planes would spill registers)

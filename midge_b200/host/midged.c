@@ -10,6 +10,13 @@
  *   stdin:  ids: / tf: / tfall: / gen: N / set: T P [seed] / quit
  *   stdout: LOADING, READY, T <id>, L <v..> (%.7g), OK <pos>, OK set,
  *           DONE <prompt> <gen> <sec> <expert_loads>
+ * Extension (opt-in, --seqs N > 1: N concurrent contexts; absent from the
+ * reference, which serves one): "seq: i" selects the sequence that ids:,
+ * tf:, tfall:, gen: and set:'s seed act on (reply "OK seq i"); "genall: N
+ * [i j ...]" decodes the listed sequences (default: every one with a context)
+ * together, N steps, one "TS <seq> <id>" line per token, then DONE.  A
+ * sequence that draws a stop token or fills its context leaves the batch.
+ * Sequence s > 0 starts its generator at seed ^ (s * 0x9E3779B97F4A7C15) | 1.
  *   stderr: "# ..." diagnostics; exit 2 = cannot open, 3 = bad spec/tensor,
  *           4 = context full / token out of range (engine/midge.c:209-211,
  *           :136, :195-201, :554-555).
@@ -76,6 +83,7 @@ static int dt_code(const char *s) {
     if (!strcmp(s, "q8r")) return MG_Q8R;
     if (!strcmp(s, "q4g32")) return MG_Q4G32;
     if (!strcmp(s, "mxfp4")) return MG_MXFP4;
+    if (!strcmp(s, "mxfp4e8")) return MG_MXFP4_E8; /* opt-in ue8m0-scale experts (midge_b200/convert_ue8m0.py) */
     return -1;
 }
 
@@ -136,46 +144,62 @@ static int spec_load(mg_spec *s, int **sliding, const Js *j) {
     return 0;
 }
 
-/* ------------------------------------------------------------- sampling */
-/* xorshift64* and temperature / top-p sampling as engine/midge.c:642-678 */
-static uint64_t rng_state = 0x853c49e6748fea9bULL;
-static uint32_t rng_u32(void) {
-    rng_state ^= rng_state >> 12;
-    rng_state ^= rng_state << 25;
-    rng_state ^= rng_state >> 27;
-    return (uint32_t)((rng_state * 0x2545F4914F6CDD1DULL) >> 32);
+/* ---------------------------------------------------- sequences, sampling */
+/* Every next token is chosen on the GPU (mg_model_sample: the reference's
+ * greedy argmax or temperature / top-p draw with its xorshift64* generator,
+ * engine/midge.c:642-678) from the logits the last forward left in a device
+ * row.  The reference holds one context; --seqs N holds N (a protocol
+ * extension: seq: selects the sequence ids:/tf:/tfall:/gen: act on, genall:
+ * decodes several at once).  Each sequence remembers where its pending
+ * next-token logits are: a device row, or a host copy made when another
+ * sequence's forward pass was about to overwrite that row. */
+typedef struct {
+    int has;      /* next-token logits exist (after ids:/tf:/tfall:/gen:) */
+    int dev_row;  /* device logits row holding them, or -1 (host copy hl) */
+    float *hl;
+    uint64_t rng; /* generator state (sequence 0: the reference's rng_state) */
+    int prompt;   /* prompt tokens since the last gen (DONE's first field) */
+} Seq;
+
+static Seq *S;
+static int NS;
+static int64_t V;
+
+static void die_mg(int rc, const char *what);
+
+static void to_host(mg_model *m, int s) {
+    if (S[s].dev_row < 0) return;
+    if (!S[s].hl) S[s].hl = (float *)malloc((size_t)V * 4);
+    int rc = mg_model_logits(m, S[s].dev_row, S[s].hl);
+    if (rc) die_mg(rc, "logits");
+    S[s].dev_row = -1;
 }
 
-typedef struct { float p; int i; } Prob;
-static int prob_desc(const void *a, const void *b) {
-    float pa = ((const Prob *)a)->p, pb = ((const Prob *)b)->p;
-    return pa < pb ? 1 : pa > pb ? -1 : 0;
+/* before a forward pass of the sequences in keep[]: the other sequences'
+ * pending logits leave the device rows (the pass overwrites them) */
+static void park_others(mg_model *m, const int *keep, int nkeep) {
+    for (int s = 0; s < NS; s++) {
+        int kept = 0;
+        for (int j = 0; j < nkeep; j++) kept |= keep[j] == s;
+        if (!kept && S[s].has) to_host(m, s);
+    }
 }
 
-static int sample_topp(const float *logits, int64_t V, float temp, float topp) {
-    float mx = logits[0];
-    for (int64_t i = 1; i < V; i++) if (logits[i] > mx) mx = logits[i];
-    Prob *pr = (Prob *)malloc(V * sizeof(Prob));
-    double den = 0;
-    for (int64_t i = 0; i < V; i++) { pr[i].p = expf((logits[i] - mx) / temp); den += pr[i].p; }
-    for (int64_t i = 0; i < V; i++) { pr[i].p /= (float)den; pr[i].i = (int)i; }
-    qsort(pr, V, sizeof(Prob), prob_desc);
-    double cum = 0;
-    int64_t n = 0;
-    for (; n < V; n++) { cum += pr[n].p; if (cum >= topp) { n++; break; } }
-    float r = (rng_u32() >> 8) / 16777216.0f * (float)cum;
-    double acc = 0;
-    int pick = pr[n - 1].i;
-    for (int64_t i = 0; i < n; i++) { acc += pr[i].p; if (r <= acc) { pick = pr[i].i; break; } }
-    free(pr);
-    return pick;
-}
-
-static int argmax_host(const float *l, int64_t V) { /* engine/midge.c:657-660 */
-    int best = 0;
-    float bv = l[0];
-    for (int64_t i = 1; i < V; i++) if (l[i] > bv) { bv = l[i]; best = (int)i; }
-    return best;
+/* the pending logits of sequences list[i] into device rows i (zeros, the
+ * reference's fresh m->logits, for a sequence that has none) */
+static void place_rows(mg_model *m, const int *list, int n) {
+    park_others(m, list, n);
+    for (int i = 0; i < n; i++)
+        if (S[list[i]].dev_row >= 0 && S[list[i]].dev_row != i) to_host(m, list[i]);
+    for (int i = 0; i < n; i++) {
+        Seq *q = &S[list[i]];
+        if (q->dev_row == i) continue;
+        if (!q->hl) q->hl = (float *)calloc((size_t)V, 4);
+        int rc = mg_model_put_logits(m, i, q->hl);
+        if (rc) die_mg(rc, "logits");
+        q->dev_row = i;
+        q->has = 1;
+    }
 }
 
 /* ------------------------------------------------------------------ main */
@@ -224,7 +248,7 @@ int main(int argc, char **argv) {
     for (int i = 1; i + 1 < argc; i++) if (!strcmp(argv[i], "--gpu")) device = atoi(argv[i + 1]);
     if (argc > 1 && !strcmp(argv[1], "--bench")) return run_bench(device);
     const char *dir = NULL;
-    int ctx = 4096, ngen_default = 512, stats = 1;
+    int ctx = 4096, ngen_default = 512, stats = 1, n_seqs = 1;
     float temp = 0.0f, topp = 0.9f;
     uint64_t seed = 42;
     int stops[64], n_stops = 0;
@@ -237,6 +261,7 @@ int main(int argc, char **argv) {
         else if (!strcmp(argv[i], "--preload-gb") && i + 1 < argc) ++i; /* experts are HBM-resident */
         else if (!strcmp(argv[i], "--gpu") && i + 1 < argc) ++i;
         else if (!strcmp(argv[i], "--no-stats")) stats = 0;
+        else if (!strcmp(argv[i], "--seqs") && i + 1 < argc) n_seqs = atoi(argv[++i]);
         else if (!strcmp(argv[i], "--stop") && i + 1 < argc) {
             char *tok = strtok(argv[++i], ",");
             while (tok && n_stops < 64) { stops[n_stops++] = atoi(tok); tok = strtok(NULL, ","); }
@@ -245,10 +270,10 @@ int main(int argc, char **argv) {
     }
     if (!dir) {
         fprintf(stderr, "usage: midged <model_dir> [--ctx N] [--temp F] [--topp F] [--seed N] [--ngen N] "
-                        "[--stop id,id] [--preload-gb F] [--gpu N]\n");
+                        "[--stop id,id] [--preload-gb F] [--gpu N] [--seqs N]\n");
         return 2;
     }
-    rng_state = seed ? seed : 1;
+    if (n_seqs < 1 || n_seqs > 16) { fprintf(stderr, "# --seqs %d: 1..16\n", n_seqs); return 2; }
     double t0 = now_s();
     setvbuf(stdout, NULL, _IOLBF, 0);
     printf("LOADING\n");
@@ -271,7 +296,7 @@ int main(int argc, char **argv) {
     if (edt < 0) { fprintf(stderr, "# bad experts dtype %s\n", edt_name); return 3; }
 
     mg_model *m = NULL;
-    int rc = mg_model_create(&spec, ctx, 1, device, &m);
+    int rc = mg_model_create(&spec, ctx, n_seqs, device, &m);
     if (rc) die_mg(rc, "model create");
     const Js *tens = js_get(dense.hdr, "tensors");
     for (int i = 0; tens && i < tens->n; i++) {
@@ -309,14 +334,19 @@ int main(int argc, char **argv) {
     printf("READY\n");
     fflush(stdout);
 
-    const int64_t V = spec.vocab;
+    V = spec.vocab;
+    NS = n_seqs;
+    S = (Seq *)calloc(NS, sizeof(Seq));
+    for (int i = 0; i < NS; i++) {
+        S[i].dev_row = -1;
+        S[i].rng = i == 0 ? (seed ? seed : 1) : ((seed ^ (0x9E3779B97F4A7C15ull * (uint64_t)i)) | 1ull);
+    }
     float *logits = (float *)calloc(V, 4);
-    int have_logits = 1, next_greedy = 0;  /* logits (host) or the device argmax describe the position */
     const char *nb = getenv("MIDGE_NO_BATCH");
     int no_batch = nb != NULL;
     char *line = NULL;
     size_t cap = 0;
-    int prompt_toks = 0;
+    int cur = 0;  /* the selected sequence */
     while (getline(&line, &cap, stdin) > 0) {
         char *nl = strchr(line, '\n');
         if (nl) *nl = 0;
@@ -326,8 +356,16 @@ int main(int argc, char **argv) {
             temp = (float)t;
             topp = (float)tp;
             while (*q == ' ') q++;
-            if (*q) rng_state = strtoull(q, NULL, 10) | 1ull;
+            if (*q) S[cur].rng = strtoull(q, NULL, 10) | 1ull;
             printf("OK set\n");
+            fflush(stdout);
+            continue;
+        }
+        if (!strncmp(line, "seq:", 4)) {
+            int i = atoi(line + 4);
+            if (i < 0 || i >= NS) { fprintf(stderr, "# sequence %d out of range (--seqs %d)\n", i, NS); exit(4); }
+            cur = i;
+            printf("OK seq %d\n", cur);
             fflush(stdout);
             continue;
         }
@@ -343,28 +381,32 @@ int main(int argc, char **argv) {
                 if (count == capn) toks = (int32_t *)realloc(toks, (capn *= 2) * sizeof(int32_t));
                 toks[count++] = (int32_t)strtol(q, &q, 10);
             }
-            prompt_toks += count;
+            S[cur].prompt += count;
+            park_others(m, &cur, 1);
             if (no_batch) {
                 for (int i = 0; i < count; i++) {
                     int32_t am = 0;
-                    rc = mg_forward(m, 0, toks[i], logits, &am);
+                    rc = mg_forward(m, cur, toks[i], logits, &am);
                     if (rc) die_mg(rc, "forward");
                     if (tfall) print_logits(logits, V);
                 }
             } else if (count > 0) {
                 if (tfall) {
                     float *all = (float *)malloc((size_t)count * V * 4);
-                    rc = mg_forward_batch(m, 0, toks, count, 2, all);
+                    rc = mg_forward_batch(m, cur, toks, count, 2, all);
                     if (rc) die_mg(rc, "forward_batch");
                     for (int i = 0; i < count; i++) print_logits(all + (size_t)i * V, V);
                     memcpy(logits, all + (size_t)(count - 1) * V, V * 4);
                     free(all);
                 } else {
-                    rc = mg_forward_batch(m, 0, toks, count, 1, logits);
+                    rc = mg_forward_batch(m, cur, toks, count, 1, logits);
                     if (rc) die_mg(rc, "forward_batch");
                 }
             }
-            have_logits = 1;
+            if (count > 0) {  /* the last position's logits: host copy here, device row 0 */
+                S[cur].has = 1;
+                S[cur].dev_row = 0;
+            }
             free(toks);
             if (tf && !tfall) print_logits(logits, V);
             if (tf) {
@@ -374,7 +416,7 @@ int main(int argc, char **argv) {
             }
             fprintf(stderr, "# prefill %d toks in %.2fs (%.2f tok/s)\n", count, now_s() - ts,
                     count / (now_s() - ts + 1e-9));
-            printf("OK %d\n", mg_model_pos(m, 0));
+            printf("OK %d\n", mg_model_pos(m, cur));
             fflush(stdout);
         } else if (!strncmp(line, "gen:", 4)) { /* engine/midge.c:808-832 */
             int ngen = atoi(line + 4);
@@ -382,38 +424,87 @@ int main(int argc, char **argv) {
             double ts = now_s();
             uint64_t loads0 = mg_model_expert_loads(m);
             int produced = 0;
-            for (int i = 0; i < ngen && mg_model_pos(m, 0) < ctx; i++) {
-                int tok;
-                if (temp <= 0.f) tok = have_logits ? argmax_host(logits, V) : next_greedy;
-                else {
-                    if (!have_logits) {
-                        rc = mg_model_logits(m, 0, logits);
-                        if (rc) die_mg(rc, "logits");
-                    }
-                    tok = sample_topp(logits, V, temp, topp);
-                }
+            place_rows(m, &cur, 1);
+            for (int i = 0; i < ngen && mg_model_pos(m, cur) < ctx; i++) {
+                int32_t tok = 0;
+                rc = mg_model_sample(m, 1, temp, topp, &S[cur].rng, &tok);
+                if (rc) die_mg(rc, "sample");
                 printf("T %d\n", tok);
                 fflush(stdout);
                 produced++;
                 int is_stop = 0;
                 for (int j = 0; j < n_stops; j++) if (stops[j] == tok) is_stop = 1;
                 if (is_stop) break;
-                int32_t am = 0;
-                rc = mg_forward(m, 0, tok, temp <= 0.f ? NULL : logits, &am);
+                rc = mg_forward(m, cur, tok, NULL, NULL);
                 if (rc) die_mg(rc, "forward");
-                have_logits = temp > 0.f;
-                next_greedy = am;
+                S[cur].dev_row = 0;
             }
             double dt = now_s() - ts;
             if (stats)
                 fprintf(stderr, "# gen %d toks in %.2fs (%.2f tok/s) · %llu expert loads · pos=%d\n", produced, dt,
                         produced / (dt + 1e-9), (unsigned long long)(mg_model_expert_loads(m) - loads0),
-                        mg_model_pos(m, 0));
-            printf("DONE %d %d %.3f %llu\n", prompt_toks, produced, dt,
+                        mg_model_pos(m, cur));
+            printf("DONE %d %d %.3f %llu\n", S[cur].prompt, produced, dt,
                    (unsigned long long)(mg_model_expert_loads(m) - loads0));
             fflush(stdout);
             usage_io(m, dir, &spec, 1);
-            prompt_toks = 0;
+            S[cur].prompt = 0;
+        } else if (!strncmp(line, "genall:", 7)) { /* extension: concurrent decode of several sequences */
+            char *q = line + 7;
+            int ngen = (int)strtol(q, &q, 10);
+            if (ngen <= 0) ngen = ngen_default;
+            int list[16], n = 0;
+            while (*q && n < NS) {
+                while (*q == ' ') q++;
+                if (!*q) break;
+                int i = (int)strtol(q, &q, 10);
+                if (i < 0 || i >= NS) { fprintf(stderr, "# sequence %d out of range (--seqs %d)\n", i, NS); exit(4); }
+                list[n++] = i;
+            }
+            if (n == 0)
+                for (int i = 0; i < NS; i++) if (S[i].has) list[n++] = i;
+            double ts = now_s();
+            uint64_t loads0 = mg_model_expert_loads(m);
+            int produced = 0, prompt = 0;
+            for (int i = 0; i < n; i++) { prompt += S[list[i]].prompt; S[list[i]].prompt = 0; }
+            if (n > 0) place_rows(m, list, n);
+            int32_t toks[16], seqs[16];
+            uint64_t rngs[16];
+            for (int step = 0; step < ngen && n > 0; step++) {
+                for (int i = 0; i < n; i++) rngs[i] = S[list[i]].rng;
+                rc = mg_model_sample(m, n, temp, topp, rngs, toks);
+                if (rc) die_mg(rc, "sample");
+                int a = 0;
+                for (int i = 0; i < n; i++) {
+                    Seq *sq = &S[list[i]];
+                    sq->rng = rngs[i];
+                    printf("TS %d %d\n", list[i], toks[i]);
+                    produced++;
+                    int leave = mg_model_pos(m, list[i]) + 1 > ctx;
+                    for (int j = 0; j < n_stops; j++) leave |= stops[j] == toks[i];
+                    if (leave) {  /* not forwarded (engine/midge.c:818-820): its logits stay pending */
+                        to_host(m, list[i]);
+                        continue;
+                    }
+                    seqs[a] = list[i];
+                    toks[a] = toks[i];
+                    a++;
+                }
+                fflush(stdout);
+                n = a;
+                for (int i = 0; i < n; i++) list[i] = seqs[i];
+                if (n == 0) break;
+                rc = mg_decode_step(m, n, seqs, toks, NULL, NULL);
+                if (rc) die_mg(rc, "decode");
+                for (int i = 0; i < n; i++) S[list[i]].dev_row = i;
+            }
+            double dt = now_s() - ts;
+            if (stats)
+                fprintf(stderr, "# genall %d toks in %.2fs (%.2f tok/s)\n", produced, dt, produced / (dt + 1e-9));
+            printf("DONE %d %d %.3f %llu\n", prompt, produced, dt,
+                   (unsigned long long)(mg_model_expert_loads(m) - loads0));
+            fflush(stdout);
+            usage_io(m, dir, &spec, 1);
         } else if (!strcmp(line, "quit")) {
             break;
         }
@@ -421,6 +512,8 @@ int main(int argc, char **argv) {
     usage_io(m, dir, &spec, 1);
     free(line);
     free(logits);
+    for (int i = 0; i < NS; i++) free(S[i].hl);
+    free(S);
     mg_model_free(m);
     cont_close(&dense);
     free(sliding);

@@ -249,3 +249,22 @@ def test_decode_block_scaled_token_groups_vs_oracle(torch_cuda, tmp_path, monkey
         assert max_rel(om.forward(int(nxt[i])), lg2[i]) < LOGIT_TOL
         om.close()
     m.close()
+
+
+def test_ue8m0_container_bit_identical(torch_cuda, c1_dir, tmp_path):
+    """An experts.midge rewritten as dtype mxfp4e8 (ue8m0 scales on disk,
+    midge_b200.convert_ue8m0) loads without re-expression and gives the same
+    logits and greedy tokens, bit for bit, as the original f16-scale file."""
+    from midge_b200 import convert_ue8m0 as cv
+
+    e8 = cv.convert(c1_dir, str(tmp_path / "e8"))
+    prompt = np.random.default_rng(8).integers(0, 1024, 40)
+    out = []
+    for md in (c1_dir, e8):
+        m = abi.Model.from_dir(md, ctx=96)
+        lg = m.forward_batch(0, prompt, logits_mode=2)
+        toks = m.decode_greedy(np.zeros(1, np.int32), np.array([int(np.argmax(lg[-1]))], np.int32), 12)
+        m.close()
+        out.append((lg, toks))
+    assert np.array_equal(out[0][0].view(np.uint32), out[1][0].view(np.uint32))
+    assert np.array_equal(out[0][1], out[1][1])
