@@ -143,6 +143,15 @@ int mg_moe_ffn_noalloc(const mg_expert_layout *L, const uint8_t *experts, int la
 int mg_sample_topp(const float *logits, int64_t ldl, int64_t V, int n_rows, float temp, float top_p, uint64_t *rng,
                    int32_t *out, float *probs, void *stream);
 
+/* Failure-path self-test of a bounded device wait (no counterpart in the
+ * reference): a one-CTA kernel waits `polls` times (1..2^20) on an mbarrier
+ * that nothing arrives on, records the timeout in the library's error word,
+ * waits for the bulk copy it issued to land (*drained = 43 when it did),
+ * frees its tensor memory and exits -- the sequence every pipelined kernel of
+ * the library follows when a wait runs out.  Returns MG_ERR_TIMEOUT; the
+ * context stays usable. */
+int mg_wait_selftest(int polls, int *drained);
+
 /* ====================================================== model level ==== */
 
 /* The model spec (engine/midge.c:46-63, parsed from the container's embedded

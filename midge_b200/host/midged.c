@@ -291,7 +291,8 @@ int main(int argc, char **argv) {
     mg_spec spec;
     int *sliding = NULL;
     if (spec_load(&spec, &sliding, jspec) != 0) { fprintf(stderr, "# invalid spec\n"); return 3; }
-    const char *edt_name = js_str(experts.hdr, "dt", "?");
+    char edt_name[16];  /* copied: the header is freed once the experts are in HBM */
+    snprintf(edt_name, sizeof(edt_name), "%s", js_str(experts.hdr, "dt", "?"));
     int edt = dt_code(edt_name);
     if (edt < 0) { fprintf(stderr, "# bad experts dtype %s\n", edt_name); return 3; }
 

@@ -112,7 +112,8 @@ def _c1(tmp_path, seed=0):
 
 def test_midged_exit_codes(torch_cuda, tmp_path):
     def run(args, stdin=""):
-        r = subprocess.run([MIDGED, *args], input=stdin, capture_output=True, text=True, timeout=120)
+        r = subprocess.run([MIDGED, *args], input=stdin, capture_output=True, text=True, errors="replace",
+                           timeout=120)
         return r.returncode, r.stderr
 
     rc, err = run([str(tmp_path / "missing")])

@@ -268,3 +268,23 @@ def test_ue8m0_container_bit_identical(torch_cuda, c1_dir, tmp_path):
         out.append((lg, toks))
     assert np.array_equal(out[0][0].view(np.uint32), out[1][0].view(np.uint32))
     assert np.array_equal(out[0][1], out[1][1])
+
+
+def test_bounded_wait_runs_out_and_context_survives(torch_cuda, c1_dir):
+    """A device wait that nothing satisfies runs out after its poll budget:
+    the kernel records the timeout, drains its own copy, frees its tensor
+    memory and exits; the host gets MG_ERR_TIMEOUT (not a hang, not a fault)
+    and the next model call on the same context is exact."""
+    import ctypes as C
+
+    m = abi.Model.from_dir(c1_dir, ctx=64)
+    prompt = np.random.default_rng(2).integers(0, 1024, 12)
+    want = m.forward_batch(0, prompt, logits_mode=2)
+    m.reset(0)
+    for polls in (1, 1000):
+        d = C.c_int(0)
+        assert abi.lib.mg_wait_selftest(polls, C.byref(d)) == abi.MG_ERR_TIMEOUT
+        assert d.value == 43  # the copy issued before the wait landed before the CTA exited
+    got = m.forward_batch(0, prompt, logits_mode=2)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    m.close()
