@@ -285,7 +285,7 @@ def cpu_reference(spec_name="c4_120b", seconds_budget=20.0, gen=8):
 def run_ours(args):
     import torch
 
-    from midge_b200 import abi  # noqa: F401  (fails loudly without the CUDA library)
+    from midge_b200 import abi  # fails loudly without the CUDA library
     from midge_b200 import container as ct
 
     rank = int(os.environ.get("RANK", "0"))
@@ -308,6 +308,8 @@ def run_ours(args):
         ep_arg = (rank, world, mep.exchange_id(rank, world))
     from midge_b200 import ep as mep
 
+    if world > 1:
+        os.environ.setdefault("MIDGE_EP_STATS", "1")  # per-phase timing of the expert-parallel prefill
     own = mep.sequence_split(N_SEQ, world, rank)  # this rank's sequences (global ids)
     rounds = -(-N_SEQ // world)
     m = build_model(torch, spec, edt, ctx, max(1, len(own)), device=local, seed=0, ep=ep_arg)
@@ -339,6 +341,14 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pf_ms = float(t[0])
     prefill_tok_s = N_SEQ * prompt_len / (pf_ms / 1e3)
+    ep_phases = None
+    if world > 1:
+        import ctypes as C
+
+        ph = (C.c_double * 4)()
+        abi.check(abi.lib.mg_model_ep_stats(m.h, ph))
+        ep_phases = {"plan_agree_ms": round(ph[0], 2), "dispatch_ms": round(ph[1], 2),
+                     "experts_ms": round(ph[2], 2), "return_combine_ms": round(ph[3], 2)}
     toks = np.array([int(np.argmax(l)) for l in last], np.int32)
     seqs = np.arange(len(own), dtype=np.int32)
 
@@ -418,6 +428,8 @@ def run_ours(args):
         "clocks": clk.summary(),
         "load_s": round(load_s, 1),
     }
+    if ep_phases:
+        line["prefill"]["ep_moe_phases_rank0"] = ep_phases
     if gemv:
         line["gemv"] = {"config": "C2: MXFP4 gate_up [5760x2880] and down [2880x2880], fp32 activations",
                         "peak_gb_s": hbm_peak, "kernel": "k_gemv (mg_gemv: 16 tokens per weight pass)",

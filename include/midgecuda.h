@@ -202,6 +202,12 @@ int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int device, mg_m
 int mg_ep_unique_id(void *id);
 int mg_model_set_ep(mg_model *m, int rank, int world, const void *id);
 
+/* Expert-parallel prefill timing, with MIDGE_EP_STATS=1 at model creation:
+ * milliseconds summed over every MoE layer of every prefill chunk so far,
+ * per phase [plan + count agreement, dispatch, expert GEMMs, return +
+ * combine] (CUDA events on the model's stream); zeros otherwise. */
+int mg_model_ep_stats(mg_model *m, double *ms4);
+
 /* Self-test of the expert-parallel watchdog loop against fakes (no GPU, no
  * NCCL): scenario 0 = the wait completes, 1 = it never completes (timeout),
  * 2 = the communicator reports an asynchronous error, 3 = a device error.

@@ -99,6 +99,7 @@ def _load():
         "mg_model_sample": (i32, [vp, i32, f32, f32, vp, vp]),
         "mg_model_put_logits": (i32, [vp, i32, vp]),
         "mg_wait_selftest": (i32, [i32, C.POINTER(i32)]),
+        "mg_model_ep_stats": (i32, [vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -16,6 +16,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "mg_common.cuh"
 #include "mg_ep.h"
@@ -208,6 +209,75 @@ int ep_allreduce_max_ints(EpComm &c, const int *v, int *out, int n, cudaStream_t
     MG_CUDA(cudaMemcpyAsync(c.h_ints, c.d_ints, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost, st));
     TRY(ep_stream_wait(c, st));
     memcpy(out, c.h_ints, (size_t)n * sizeof(int));
+    return MG_OK;
+}
+
+// ------------------------------------------------------ peer buffers
+int ep_peer_alloc(EpComm &c, EpPeer &b, size_t bytes, cudaStream_t st) {
+    MG_REQUIRE(bytes > 0, MG_ERR_ARG, "ep_peer_alloc: empty buffer");
+    b.bytes = bytes;
+    void *local = nullptr;
+    MG_CUDA(cudaMalloc(&local, bytes));
+    MG_CUDA(cudaMemset(local, 0, bytes));
+    b.peer[c.rank] = local;
+    if (c.world <= 1) return MG_OK;
+    TRY(ep_ready(c));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    const int G = c.world;
+    cudaIpcMemHandle_t h;
+    MG_CUDA(cudaIpcGetMemHandle(&h, local));
+    int *dh = nullptr;
+    MG_CUDA(cudaMalloc(&dh, (size_t)(G + 1) * 64));
+    std::vector<cudaIpcMemHandle_t> all(G);
+    int rc = MG_OK;
+    if (cudaMemcpy(reinterpret_cast<uint8_t *>(dh) + (size_t)G * 64, &h, 64, cudaMemcpyHostToDevice) != cudaSuccess) {
+        set_error("ep_peer_alloc: handle upload failed");
+        rc = MG_ERR_CUDA;
+    }
+    if (rc == MG_OK) rc = ep_allgather_ints(c, dh + G * 16, dh, 16, st);
+    if (rc == MG_OK) rc = ep_stream_wait(c, st);
+    if (rc == MG_OK && cudaMemcpy(all.data(), dh, (size_t)G * 64, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        set_error("ep_peer_alloc: handle download failed");
+        rc = MG_ERR_CUDA;
+    }
+    cudaFree(dh);
+    for (int d = 0; d < G && rc == MG_OK; d++) {
+        if (d == c.rank) continue;
+        cudaError_t e = cudaIpcOpenMemHandle(&b.peer[d], all[d], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            set_error("ep_peer_alloc: cudaIpcOpenMemHandle of rank %d: %s", d, cudaGetErrorString(e));
+            rc = MG_ERR_CUDA;
+        }
+    }
+    return rc;
+}
+
+void ep_peer_free(EpComm &c, EpPeer &b) {
+    for (int d = 0; d < c.world && d < EP_MAX_WORLD; d++) {
+        if (!b.peer[d]) continue;
+        if (d == c.rank) cudaFree(b.peer[d]);
+        else cudaIpcCloseMemHandle(b.peer[d]);
+        b.peer[d] = nullptr;
+    }
+}
+
+int ep_barrier(EpComm &c, cudaStream_t st) {
+    if (c.world <= 1) return MG_OK;
+    TRY(ep_ready(c));
+    MG_NCCL(c, g_nccl.all_reduce(c.d_ints + 32, c.d_ints + 32, 1, ncclInt32, ncclSum, nc(c), st));
+    return MG_OK;
+}
+
+int ep_put(EpComm &c, const float *src, const int64_t *src_off, const int64_t *cnt, EpPeer &dst,
+           const int64_t *dst_off, cudaStream_t st) {
+    for (int d = 0; d < c.world; d++) {
+        if (!cnt[d]) continue;
+        float *to = static_cast<float *>(dst.peer[d]) + dst_off[d];
+        MG_REQUIRE(dst.peer[d] && (size_t)(dst_off[d] + cnt[d]) * 4 <= dst.bytes, MG_ERR_ARG,
+                   "ep_put: block of %lld floats at %lld exceeds rank %d's buffer", (long long)cnt[d],
+                   (long long)dst_off[d], d);
+        MG_CUDA(cudaMemcpyAsync(to, src + src_off[d], (size_t)cnt[d] * 4, cudaMemcpyDeviceToDevice, st));
+    }
     return MG_OK;
 }
 

@@ -50,6 +50,22 @@ int ep_stream_wait(EpComm &c, cudaStream_t st);
 int ep_watchdog(int (*query)(void *), int (*async_error)(void *), void (*abort_comm)(void *), void *ctx,
                 double timeout_s, int poll_us);
 
+// A buffer every rank allocates and maps into every other rank's process
+// (CUDA IPC over NVLink): peer[d] is rank d's copy, peer[rank] the local one.
+struct EpPeer {
+    void *peer[EP_MAX_WORLD] = {};
+    size_t bytes = 0;
+};
+int ep_peer_alloc(EpComm &c, EpPeer &b, size_t bytes, cudaStream_t st);
+void ep_peer_free(EpComm &c, EpPeer &b);
+// every rank's stream reaches this point before any passes it (a 1-int
+// NCCL all-reduce): orders peer writes before the reads they feed
+int ep_barrier(EpComm &c, cudaStream_t st);
+// copy engine puts: to rank d, cnt[d] floats from src + src_off[d] into rank
+// d's copy of dst at dst_off[d] (the own block is a local copy)
+int ep_put(EpComm &c, const float *src, const int64_t *src_off, const int64_t *cnt, EpPeer &dst,
+           const int64_t *dst_off, cudaStream_t st);
+
 // contiguous expert shard of `rank`
 inline void ep_range(int n_experts, int world, int rank, int *e0, int *n_local) {
     *n_local = n_experts / world;

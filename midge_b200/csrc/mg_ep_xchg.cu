@@ -66,6 +66,103 @@ int ep_dec_unpack(const float *recv, int n_all, int64_t H, int k, int rowf, floa
     return MG_OK;
 }
 
+// ------------------------------------------------- decode over peer memory
+// A rank's data reaches a peer by plain stores to the peer's mapped buffer;
+// the hand-over is a flag the writer stores with release semantics at system
+// scope after a system fence, and the reader polls with acquire semantics.
+// The flag value is an epoch: a per-site counter in device memory that every
+// rank advances identically (the last CTA of each exchange kernel), so the
+// kernels replay correctly inside CUDA graphs.  Every poll is bounded (about a
+// second); a wait that runs out sets the error word and the CTA moves on.
+constexpr uint32_t EP_SPIN = 1u << 23;
+constexpr int EP_ERR_SPIN = 41;
+
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// thread 0: publish to rank d, wait for source d, and (last CTA) advance the epoch
+__device__ void ep_handover(const EpDecPeers &p, int site, uint32_t ep, int me, int d, int G) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        st_release_sys(p.flag[d] + site * EP_MAX_WORLD + me, ep);
+        bool ok = false;
+        for (uint32_t i = 0; i < EP_SPIN; i++) {
+            if (ld_acquire_sys(p.flag[me] + site * EP_MAX_WORLD + d) == ep) { ok = true; break; }
+            __nanosleep(64);
+        }
+        if (!ok) atomicCAS(p.err, 0, EP_ERR_SPIN);
+        __threadfence();
+        if (atomicAdd(p.seq + 2 + site, 1u) == (unsigned)G - 1) {
+            p.seq[2 + site] = 0;
+            p.seq[site] = ep;
+        }
+    }
+    __syncthreads();
+}
+
+// CTA d: this rank's n_max rows [normed row | ids | pad] into rank d's buffer
+__global__ void k_ep_dec_dispatch(EpDecPeers p, const float *__restrict__ xb, const int32_t *__restrict__ sel, int n,
+                                  int nmax, int64_t H, int k, int rowf, int me, int G) {
+    const int d = blockIdx.x;
+    const uint32_t ep = *reinterpret_cast<volatile uint32_t *>(p.seq) + 1;
+    float *dst = p.recv[d] + (int64_t)me * nmax * rowf;
+    for (int r = 0; r < nmax; r++) {
+        const bool real = r < n;
+        for (int64_t c = threadIdx.x; c < rowf; c += blockDim.x) {
+            float v;
+            if (c < H) v = real ? xb[(int64_t)r * H + c] : 0.f;
+            else if (c < H + k) v = __int_as_float(real ? sel[(int64_t)r * k + (c - H)] : -1);
+            else v = 0.f;
+            dst[(int64_t)r * rowf + c] = v;
+        }
+    }
+    ep_handover(p, 0, ep, me, d, G);
+}
+
+// CTA d: the outputs of this rank's experts for owner d's tokens into d's moe_y
+__global__ void k_ep_dec_return(EpDecPeers p, const float *__restrict__ y_all, const int32_t *__restrict__ sel_all,
+                                int nmax, int64_t H, int k, int ks, int64_t plane_all, int64_t plane_loc, int e0,
+                                int n_local, int me, int G) {
+    const int d = blockIdx.x;
+    const uint32_t ep = *reinterpret_cast<volatile uint32_t *>(p.seq + 1) + 1;
+    for (int j = 0; j < nmax; j++) {
+        const int r = d * nmax + j;
+        for (int i = 0; i < k; i++) {
+            const int e = sel_all[(int64_t)r * k + i] - e0;
+            if (e < 0 || e >= n_local) continue;  // uniform over the block
+            for (int q = 0; q < ks; q++) {
+                const float4 *src = reinterpret_cast<const float4 *>(y_all + q * plane_all + ((int64_t)r * k + i) * H);
+                float4 *dst = reinterpret_cast<float4 *>(p.y[d] + q * plane_loc + ((int64_t)j * k + i) * H);
+                for (int64_t c = threadIdx.x; c < H / 4; c += blockDim.x) dst[c] = src[c];
+            }
+        }
+    }
+    ep_handover(p, 1, ep, me, d, G);
+}
+
+int ep_dec_dispatch(const EpDecPeers &p, const float *xb, const int32_t *sel, int n, int n_max, int64_t H, int k,
+                    int rowf, int me, int G, cudaStream_t st) {
+    MG_REQUIRE(G >= 2 && G <= EP_MAX_WORLD && n_max >= 1, MG_ERR_ARG, "ep_dec_dispatch: bad arguments");
+    k_ep_dec_dispatch<<<G, 256, 0, st>>>(p, xb, sel, n, n_max, H, k, rowf, me, G);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
+int ep_dec_return(const EpDecPeers &p, const float *y_all, const int32_t *sel_all, int n_max, int64_t H, int k, int ks,
+                  int64_t plane_all, int64_t plane_loc, int e0, int n_local, int me, int G, cudaStream_t st) {
+    MG_REQUIRE(G >= 2 && G <= EP_MAX_WORLD && n_max >= 1 && H % 4 == 0, MG_ERR_ARG, "ep_dec_return: bad arguments");
+    k_ep_dec_return<<<G, 256, 0, st>>>(p, y_all, sel_all, n_max, H, k, ks, plane_all, plane_loc, e0, n_local, me, G);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
 // --------------------------------------------------------------- prefill
 constexpr int XG_PLAN_THREADS = 1024;
 

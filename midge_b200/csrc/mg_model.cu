@@ -692,8 +692,23 @@ static int ep_prepare(mg_model *m) {
     const int64_t H = s.hidden;
     m->ep_rowf = ep_rowf(H, k);
     const int rowf = m->ep_rowf;
-    TRY(dalloc(m, &m->epd_send, (size_t)EP_DEC_TOK * rowf * 4));
-    TRY(dalloc(m, &m->epd_recv, (size_t)EP_DEC_TOK * rowf * 4));
+    EpComm &c = m->ep;
+    cudaStream_t st = m->st;
+    // buffers the other ranks write into (CUDA IPC over NVLink)
+    TRY(ep_peer_alloc(c, m->epd_recv_p, (size_t)EP_DEC_TOK * rowf * 4, st));
+    TRY(ep_peer_alloc(c, m->epd_y_p, (size_t)2 * DEC_MAX * k * H * 4, st));
+    TRY(ep_peer_alloc(c, m->ep_flags_p, 256, st));
+    m->epd_recv = static_cast<float *>(m->epd_recv_p.peer[c.rank]);
+    m->moe_y = static_cast<float *>(m->epd_y_p.peer[c.rank]);  // the owner's slot outputs arrive here
+    TRY(dalloc(m, &m->ep_seq, 16));
+    MG_CUDA(cudaMemset(m->ep_seq, 0, 16));
+    for (int d = 0; d < G; d++) {
+        m->epd_peers.recv[d] = static_cast<float *>(m->epd_recv_p.peer[d]);
+        m->epd_peers.y[d] = static_cast<float *>(m->epd_y_p.peer[d]);
+        m->epd_peers.flag[d] = static_cast<uint32_t *>(m->ep_flags_p.peer[d]);
+    }
+    m->epd_peers.seq = m->ep_seq;
+    m->epd_peers.err = stream_error_word();
     TRY(dalloc(m, &m->epd_xb, (size_t)EP_DEC_TOK * H * 4));
     TRY(dalloc(m, &m->epd_sel, (size_t)EP_DEC_TOK * k * 4));
     TRY(dalloc(m, &m->epd_y, (size_t)m->ks_down * EP_DEC_TOK * k * H * 4));
@@ -706,12 +721,20 @@ static int ep_prepare(mg_model *m) {
     TRY(dalloc(m, &m->epp_send_row, (size_t)R * G * 4));
     TRY(dalloc(m, &m->epp_ret_pos, (size_t)R * k * 4));
     TRY(dalloc(m, &m->epp_send, (size_t)R * per_tok * rowf * 4));
-    TRY(dalloc(m, &m->epp_recv, (size_t)m->epp_cap_recv * rowf * 4));
+    TRY(ep_peer_alloc(c, m->epp_recv_p, (size_t)m->epp_cap_recv * rowf * 4, st));
+    m->epp_recv = static_cast<float *>(m->epp_recv_p.peer[c.rank]);
     TRY(dalloc(m, &m->epp_sel, (size_t)m->epp_cap_recv * k * 4));
     TRY(dalloc(m, &m->epp_ret_row, (size_t)m->epp_cap_recv * k * 4));
     TRY(dalloc(m, &m->epp_slot2, (size_t)m->epp_cap_recv * k * 4));
     TRY(dalloc(m, &m->epp_ret_send, (size_t)m->epp_cap_recv * k * H * 4));
-    TRY(dalloc(m, &m->epp_ret_recv, (size_t)R * k * H * 4));
+    TRY(ep_peer_alloc(c, m->epp_ret_recv_p, (size_t)R * k * H * 4, st));
+    m->epp_ret_recv = static_cast<float *>(m->epp_ret_recv_p.peer[c.rank]);
+    const char *es = getenv("MIDGE_EP_STATS");
+    m->ep_stats = es && *es == '1';
+    if (m->ep_stats) {
+        m->ep_ev.resize((size_t)s.n_layers * 5);
+        for (auto &e : m->ep_ev) MG_CUDA(cudaEventCreate(&e));
+    }
     return MG_OK;
 }
 
@@ -824,25 +847,38 @@ static int moe_prefill_ep(mg_model *m, int layer, int n) {
     const int G = c.world, me = c.rank, k = s.top_k, rowf = m->ep_rowf;
     const int64_t H = s.hidden;
     cudaStream_t st = m->st;
+    cudaEvent_t *ev = m->ep_stats ? &m->ep_ev[(size_t)layer * 5] : nullptr;
+    if (ev) MG_CUDA(cudaEventRecord(ev[0], st));
     TRY(ep_pf_plan(m->sel, n, k, G, m->n_local, s.n_experts, m->epp_counts, m->epp_send_row, m->epp_ret_pos, st));
     TRY(ep_allgather_ints(c, m->epp_counts, m->epp_all, (size_t)2 * G, st));
     MG_CUDA(cudaMemcpyAsync(m->epp_h_all, m->epp_all, (size_t)2 * G * G * 4, cudaMemcpyDeviceToHost, st));
     TRY(ep_stream_wait(c, st));
     const int *A = m->epp_h_all;  // A[r*2G + d]: tokens r -> d; A[r*2G + G + d]: slots r -> d
-    int64_t so[EP_MAX_WORLD], sc[EP_MAX_WORLD], ro[EP_MAX_WORLD], rc[EP_MAX_WORLD];
-    int64_t bso[EP_MAX_WORLD], bsc[EP_MAX_WORLD], bro[EP_MAX_WORLD], brc[EP_MAX_WORLD];
-    int64_t a = 0, b = 0, a2 = 0, b2 = 0, n_recv = 0;
+    // my blocks (offsets in my buffers) and where they land in the receiver's
+    // buffers: rank d's receive buffer is source-major, its return buffer
+    // expert-rank-major
+    int64_t so[EP_MAX_WORLD], sc[EP_MAX_WORLD], dsto[EP_MAX_WORLD];
+    int64_t bso[EP_MAX_WORLD], bsc[EP_MAX_WORLD], bdsto[EP_MAX_WORLD];
+    int64_t a = 0, a2 = 0, n_recv = 0;
     for (int d = 0; d < G; d++) {
         sc[d] = (int64_t)A[me * 2 * G + d] * rowf; so[d] = a; a += sc[d];          // my tokens to d
-        rc[d] = (int64_t)A[d * 2 * G + me] * rowf; ro[d] = b; b += rc[d];          // d's tokens to me
-        n_recv += A[d * 2 * G + me];
         bsc[d] = (int64_t)A[d * 2 * G + G + me] * H; bso[d] = a2; a2 += bsc[d];    // outputs of d's slots, back
-        brc[d] = (int64_t)A[me * 2 * G + G + d] * H; bro[d] = b2; b2 += brc[d];    // outputs of my slots on d
+        n_recv += A[d * 2 * G + me];
+        int64_t t = 0, u = 0;
+        for (int q = 0; q < me; q++) {
+            t += A[q * 2 * G + d];      // tokens ranks < me send to d
+            u += A[d * 2 * G + G + q];  // d's slots on ranks < me
+        }
+        dsto[d] = t * rowf;
+        bdsto[d] = u * H;
     }
     MG_REQUIRE(n_recv <= m->epp_cap_recv, MG_ERR_STATE, "expert parallel prefill: %lld tokens received (room for %lld)",
                (long long)n_recv, (long long)m->epp_cap_recv);
+    if (ev) MG_CUDA(cudaEventRecord(ev[1], st));
     TRY(ep_pf_pack(m->xb, m->sel, n, k, G, H, rowf, m->epp_send_row, m->epp_send, st));
-    TRY(ep_alltoallv(c, m->epp_send, so, sc, m->epp_recv, ro, rc, st));
+    TRY(ep_put(c, m->epp_send, so, sc, m->epp_recv_p, dsto, st));  // copy engines, NVLink
+    TRY(ep_barrier(c, st));                                          // every rank's rows have landed
+    if (ev) MG_CUDA(cudaEventRecord(ev[2], st));
     TRY(ep_pf_unpack_sel(m->epp_recv, (int)n_recv, k, H, rowf, m->epp_sel, st));
     TRY(ep_pf_retplan(m->epp_sel, (int)n_recv, k, m->e0, m->n_local, m->epp_ret_row, st));
     MoePrefill pf = prefill_args(m, layer);
@@ -854,8 +890,31 @@ static int moe_prefill_ep(mg_model *m, int layer, int n) {
     pf.slot2 = m->epp_slot2;
     pf.y = m->epp_ret_send;
     TRY(moe_prefill_experts(pf, st));
-    TRY(ep_alltoallv(c, m->epp_ret_send, bso, bsc, m->epp_ret_recv, bro, brc, st));
-    return pf_combine(m->x, H, m->sel, m->wts, n, k, s.n_experts, m->epp_ret_recv, m->epp_ret_pos, st);
+    if (ev) MG_CUDA(cudaEventRecord(ev[3], st));
+    TRY(ep_put(c, m->epp_ret_send, bso, bsc, m->epp_ret_recv_p, bdsto, st));
+    TRY(ep_barrier(c, st));
+    TRY(pf_combine(m->x, H, m->sel, m->wts, n, k, s.n_experts, m->epp_ret_recv, m->epp_ret_pos, st));
+    if (ev) MG_CUDA(cudaEventRecord(ev[4], st));
+    return MG_OK;
+}
+
+// after a synchronised prefill chunk: add the phase times of every layer
+static void ep_stats_collect(mg_model *m) {
+    if (!m->ep_stats) return;
+    for (int l = 0; l < m->spec.n_layers; l++) {
+        cudaEvent_t *ev = &m->ep_ev[(size_t)l * 5];
+        for (int p = 0; p < 4; p++) {
+            float ms = 0.f;
+            if (cudaEventElapsedTime(&ms, ev[p], ev[p + 1]) == cudaSuccess) m->ep_ms[p] += ms;
+        }
+    }
+    cudaGetLastError();
+}
+
+extern "C" int mg_model_ep_stats(mg_model *m, double *ms4) {
+    MG_REQUIRE(m && ms4, MG_ERR_ARG, "ep_stats: bad arguments");
+    for (int p = 0; p < 4; p++) ms4[p] = m->ep_ms[p];
+    return MG_OK;
 }
 
 // The per-layer body shared by decode (n rows = sequences, one token each)
@@ -1000,17 +1059,14 @@ static int ep_decode_moe(mg_model *m, int layer, int n) {
     const int G = c.world, k = s.top_k, nm = m->dec_nmax, n_all = G * nm, rowf = m->ep_rowf;
     const int64_t H = s.hidden;
     cudaStream_t st = m->st;
-    TRY(ep_dec_pack(m->xb, m->sel, n, nm, H, k, rowf, m->epd_send, st));
-    TRY(ep_allgather(c, m->epd_send, m->epd_recv, (size_t)nm * rowf, st));
+    TRY(ep_dec_dispatch(m->epd_peers, m->xb, m->sel, n, nm, H, k, rowf, c.rank, G, st));
     TRY(ep_dec_unpack(m->epd_recv, n_all, H, k, rowf, m->epd_xb, m->epd_sel, st));
-    const size_t plane_all = (size_t)n_all * k * H, plane_loc = (size_t)nm * k * H;
-    MG_CUDA(cudaMemsetAsync(m->epd_y, 0, (size_t)m->ks_down * plane_all * 4, st));
+    const int64_t plane_all = (int64_t)n_all * k * H, plane_loc = (int64_t)nm * k * H;
     MoeStreamArgs ma = stream_moe_args(m, layer);
     ma.n_tok = n_all; ma.sel = m->epd_sel; ma.xb = m->epd_xb; ma.y = m->epd_y;
     TRY(moe_stream(ma, st));
-    for (int p = 0; p < m->ks_down; p++)
-        TRY(ep_reduce_scatter_sum(c, m->epd_y + p * plane_all, m->moe_y + p * plane_loc, plane_loc, st));
-    return MG_OK;
+    return ep_dec_return(m->epd_peers, m->epd_y, m->epd_sel, nm, H, k, m->ks_down, plane_all, plane_loc, m->e0,
+                         m->n_local, c.rank, G, st);
 }
 
 // One layer of the streamed decode: combine(previous MoE)+norm, QKV (K-split
@@ -1358,6 +1414,7 @@ extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n
             for (int l = 0; l < s.n_layers; l++) TRY(moe_prefill_ep(m, l, 0));
             TRY(ep_stream_wait(m->ep, m->st));
             TRY(stream_error_check());
+            ep_stats_collect(m);
             continue;
         }
         int pos0 = m->pos[seq];
@@ -1390,6 +1447,7 @@ extern "C" int mg_forward_batch(mg_model *m, int seq, const int32_t *toks, int n
         }
         TRY(ep_stream_wait(m->ep, st));
         if (m->tc_prefill || m->tc_dense) TRY(stream_error_check());
+        if (m->ep.world > 1) ep_stats_collect(m);
         m->pos[seq] += nc;
         m->expert_loads += (uint64_t)nc * s.top_k * s.n_layers;
     }
@@ -1468,9 +1526,12 @@ extern "C" int mg_model_free(mg_model *m) {
     for (auto *tab : {&m->dec_graphs, &m->chain_graphs})  // graphs holding collectives go before the communicator
         for (auto &kv : *tab)
             if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (mg::EpPeer *b : {&m->epd_recv_p, &m->epd_y_p, &m->ep_flags_p, &m->epp_recv_p, &m->epp_ret_recv_p})
+        ep_peer_free(m->ep, *b);
     ep_destroy(&m->ep);
     for (void *p : m->allocs) cudaFree(p);
     for (void *p : m->host_allocs) cudaFreeHost(p);
+    for (cudaEvent_t e : m->ep_ev) cudaEventDestroy(e);
     for (void *p : {(void *)m->h_toks, (void *)m->h_pos, (void *)m->h_seq, (void *)m->h_amax, (void *)m->h_err,
                     (void *)m->h_keys})
         if (p) cudaFreeHost(p);

@@ -11,6 +11,7 @@
 #include "mg_bsmoe.h"
 #include "mg_q8mma.h"
 #include "mg_ep.h"
+#include "mg_ep_xchg.h"
 #include "midgecuda.h"
 
 namespace mg {
@@ -110,11 +111,19 @@ struct mg_model {
     int dec_nmax = 0;      // decode: tokens per rank of the current step (max over the ranks)
     float *epd_send = nullptr, *epd_recv = nullptr, *epd_xb = nullptr, *epd_y = nullptr;
     int32_t *epd_sel = nullptr;
+    mg::EpPeer epd_recv_p, epd_y_p, ep_flags_p, epp_recv_p, epp_ret_recv_p;  // peer-mapped buffers
+    mg::EpDecPeers epd_peers{};
+    uint32_t *ep_seq = nullptr;  // decode hand-over epochs and tickets
     int64_t epp_cap_recv = 0;  // prefill: received tokens per layer and chunk, at most
     int *epp_counts = nullptr, *epp_all = nullptr, *epp_h_all = nullptr;
     int *epp_send_row = nullptr, *epp_ret_pos = nullptr, *epp_ret_row = nullptr, *epp_slot2 = nullptr;
     int32_t *epp_sel = nullptr;
     float *epp_send = nullptr, *epp_recv = nullptr, *epp_ret_send = nullptr, *epp_ret_recv = nullptr;
+
+    // expert-parallel prefill phase timing (MIDGE_EP_STATS=1): per layer 5 events, summed per call
+    bool ep_stats = false;
+    std::vector<cudaEvent_t> ep_ev;
+    double ep_ms[4] = {0, 0, 0, 0};  // plan + agreement, dispatch, expert GEMMs, return + combine
 
     std::unordered_map<int, mg::Graph> dec_graphs;    // keyed by n_seqs (and, expert-parallel, the step's n_max)
     std::unordered_map<int, mg::Graph> chain_graphs;  // device-fed greedy steps, keyed by n_seqs
