@@ -5,7 +5,11 @@
 // cache, router and lm_head of its own tokens; the trunk weights are
 // replicated).  Each MoE layer exchanges routed tokens with the ranks that hold
 // their experts and sends the per-slot expert outputs back to the token's
-// owner, which combines them in the reference's order (mg_ep_xchg.cu).
+// owner, which combines them in the reference's order (mg_ep_xchg.cu).  The
+// data moves through buffers every rank maps into every other (CUDA IPC over
+// NVLink): copy-engine puts in prefill, store-and-flag kernels in decode.
+// NCCL carries only control: the communicator-id bootstrap, the all-gather
+// of prefill counts and IPC handles, small all-reduces (agreements, barriers).
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2, the copy already in the
 // process when there is one), so a single-GPU process never needs it.
@@ -30,12 +34,6 @@ struct NcclApi {
     ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                                cudaStream_t) = nullptr;
     ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
-    ncclResult_t (*reduce_scatter)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
-                                   cudaStream_t) = nullptr;
-    ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-    ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
-    ncclResult_t (*group_start)() = nullptr;
-    ncclResult_t (*group_end)() = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
     ncclResult_t (*async_error)(ncclComm_t, ncclResult_t *) = nullptr;
@@ -64,9 +62,7 @@ static int nccl_load() {
     a.lib = h;
     bool ok = sym(h, a.get_unique_id, "ncclGetUniqueId") && sym(h, a.comm_init_rank, "ncclCommInitRank") &&
               sym(h, a.all_reduce, "ncclAllReduce") && sym(h, a.all_gather, "ncclAllGather") &&
-              sym(h, a.reduce_scatter, "ncclReduceScatter") && sym(h, a.send, "ncclSend") &&
-              sym(h, a.recv, "ncclRecv") && sym(h, a.group_start, "ncclGroupStart") &&
-              sym(h, a.group_end, "ncclGroupEnd") && sym(h, a.comm_destroy, "ncclCommDestroy") &&
+              sym(h, a.comm_destroy, "ncclCommDestroy") &&
               sym(h, a.comm_abort, "ncclCommAbort") && sym(h, a.async_error, "ncclCommGetAsyncError") &&
               sym(h, a.error_string, "ncclGetErrorString");
     if (!ok) {
@@ -144,16 +140,6 @@ void ep_destroy(EpComm *c) {
     c->h_ints = nullptr;
 }
 
-int ep_allgather(EpComm &c, const float *send, float *recv, size_t count, cudaStream_t st) {
-    if (c.world <= 1) {
-        if (count && send != recv) MG_CUDA(cudaMemcpyAsync(recv, send, count * 4, cudaMemcpyDeviceToDevice, st));
-        return MG_OK;
-    }
-    TRY(ep_ready(c));
-    MG_NCCL(c, g_nccl.all_gather(send, recv, count, ncclFloat32, nc(c), st));
-    return MG_OK;
-}
-
 int ep_allgather_ints(EpComm &c, const int *send, int *recv, size_t count, cudaStream_t st) {
     if (c.world <= 1) {
         if (count && send != recv) MG_CUDA(cudaMemcpyAsync(recv, send, count * 4, cudaMemcpyDeviceToDevice, st));
@@ -161,38 +147,6 @@ int ep_allgather_ints(EpComm &c, const int *send, int *recv, size_t count, cudaS
     }
     TRY(ep_ready(c));
     MG_NCCL(c, g_nccl.all_gather(send, recv, count, ncclInt32, nc(c), st));
-    return MG_OK;
-}
-
-int ep_reduce_scatter_sum(EpComm &c, const float *send, float *recv, size_t recvcount, cudaStream_t st) {
-    if (c.world <= 1) {
-        if (recvcount && send != recv)
-            MG_CUDA(cudaMemcpyAsync(recv, send, recvcount * 4, cudaMemcpyDeviceToDevice, st));
-        return MG_OK;
-    }
-    TRY(ep_ready(c));
-    MG_NCCL(c, g_nccl.reduce_scatter(send, recv, recvcount, ncclFloat32, ncclSum, nc(c), st));
-    return MG_OK;
-}
-
-int ep_alltoallv(EpComm &c, const float *send, const int64_t *send_off, const int64_t *send_cnt, float *recv,
-                 const int64_t *recv_off, const int64_t *recv_cnt, cudaStream_t st) {
-    const int me = c.rank;
-    if (send_cnt[me]) {
-        MG_REQUIRE(send_cnt[me] == recv_cnt[me], MG_ERR_ARG, "alltoallv: own block %lld != %lld",
-                   (long long)send_cnt[me], (long long)recv_cnt[me]);
-        MG_CUDA(cudaMemcpyAsync(recv + recv_off[me], send + send_off[me], (size_t)send_cnt[me] * 4,
-                                cudaMemcpyDeviceToDevice, st));
-    }
-    if (c.world <= 1) return MG_OK;
-    TRY(ep_ready(c));
-    MG_NCCL(c, g_nccl.group_start());
-    for (int d = 0; d < c.world; d++) {
-        if (d == me) continue;
-        if (send_cnt[d]) MG_NCCL(c, g_nccl.send(send + send_off[d], (size_t)send_cnt[d], ncclFloat32, d, nc(c), st));
-        if (recv_cnt[d]) MG_NCCL(c, g_nccl.recv(recv + recv_off[d], (size_t)recv_cnt[d], ncclFloat32, d, nc(c), st));
-    }
-    MG_NCCL(c, g_nccl.group_end());
     return MG_OK;
 }
 

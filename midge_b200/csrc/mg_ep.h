@@ -23,14 +23,7 @@ int ep_init(EpComm *c, int rank, int world, const void *id);
 void ep_destroy(EpComm *c);
 
 // Collectives on `st` (enqueued, asynchronous; graph-capturable).
-int ep_allgather(EpComm &c, const float *send, float *recv, size_t count, cudaStream_t st);
-int ep_reduce_scatter_sum(EpComm &c, const float *send, float *recv, size_t recvcount, cudaStream_t st);
 int ep_allgather_ints(EpComm &c, const int *send, int *recv, size_t count, cudaStream_t st);
-// Variable all-to-all of float rows: to rank d send_cnt[d] floats from
-// send + send_off[d], from rank s recv_cnt[s] floats into recv + recv_off[s]
-// (one NCCL group of point-to-point calls; the rank's own block is a device copy).
-int ep_alltoallv(EpComm &c, const float *send, const int64_t *send_off, const int64_t *send_cnt, float *recv,
-                 const int64_t *recv_off, const int64_t *recv_cnt, cudaStream_t st);
 
 // Host agreement: out[i] = max over ranks of v[i] (n <= 8 ints); synchronous.
 int ep_allreduce_max_ints(EpComm &c, const int *v, int *out, int n, cudaStream_t st);

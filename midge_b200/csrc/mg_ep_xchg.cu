@@ -1,6 +1,7 @@
 // mg_ep_xchg.cu -- expert-parallel token exchange: the device side of the
 // dispatch (tokens to the ranks that hold their routed experts) and of the
-// combine (per-slot expert outputs back to the token's owner).
+// combine (per-slot expert outputs back to the token's owner).  Data moves
+// through buffers every rank maps into every other (CUDA IPC over NVLink).
 //
 // Prefill (variable sizes, one host agreement per layer and chunk):
 //   plan     per destination rank d: the owner's tokens routed to any expert of
@@ -8,17 +9,18 @@
 //            routed to d (in token order, then top-k rank order); counts,
 //            send rows and the return row of every slot
 //   pack     [normed row | top-k expert ids] per (token, destination)
-//   -- NCCL grouped send/recv of the packed rows --
+//   -- copy-engine puts into each destination's receive buffer, a barrier --
 //   retplan  on the expert side: the received tokens' local slots numbered in
 //            received order (= per source, the source's own slot order), which
 //            is where the DOWN GEMM writes each slot's output
-//   -- NCCL grouped send/recv of the outputs back; the owner adds them to the
-//      residual in ascending expert order (k_pf_combine through ret_pos) --
-// Decode (<= 8 tokens per step over all ranks; graph-capturable): every rank
-// gathers all ranks' [row | ids] (fixed size per rank, pads carry id -1), runs
-// its experts over all of them, and a reduce-scatter returns each owner the
-// sum over ranks of its tokens' slot outputs -- exactly one rank holds a
-// nonzero value per slot, so the sum is exact.
+//   -- puts of the outputs into each owner's return buffer, a barrier; the
+//      owner adds them to the residual in ascending expert order
+//      (k_pf_combine through ret_pos) --
+// Decode (<= 8 tokens per step over all ranks; graph-captured): every rank
+// stores its [row | ids] rows (fixed count per rank, pads carry id -1) into
+// every rank's gather buffer, runs its experts over all gathered tokens, and
+// stores each slot output of its experts into the owner's slot buffer; flags
+// hand the data over (k_ep_dec_dispatch, k_ep_dec_return).
 #include "mg_common.cuh"
 #include "mg_ep.h"
 #include "mg_ep_xchg.h"
@@ -26,20 +28,6 @@
 namespace mg {
 
 // ---------------------------------------------------------------- decode
-__global__ void k_ep_dec_pack(const float *__restrict__ xb, const int32_t *__restrict__ sel, int n, int64_t H, int k,
-                              int rowf, float *__restrict__ send) {
-    const int r = blockIdx.x;
-    float *dst = send + (int64_t)r * rowf;
-    const bool real = r < n;
-    for (int64_t c = threadIdx.x; c < rowf; c += blockDim.x) {
-        float v;
-        if (c < H) v = real ? xb[(int64_t)r * H + c] : 0.f;
-        else if (c < H + k) v = __int_as_float(real ? sel[(int64_t)r * k + (c - H)] : -1);
-        else v = 0.f;
-        dst[c] = v;
-    }
-}
-
 __global__ void k_ep_dec_unpack(const float *__restrict__ recv, int64_t H, int k, int rowf, float *__restrict__ xb_all,
                                 int32_t *__restrict__ sel_all) {
     const int r = blockIdx.x;
@@ -48,14 +36,6 @@ __global__ void k_ep_dec_unpack(const float *__restrict__ recv, int64_t H, int k
         if (c < H) xb_all[(int64_t)r * H + c] = src[c];
         else sel_all[(int64_t)r * k + (c - H)] = __float_as_int(src[c]);
     }
-}
-
-int ep_dec_pack(const float *xb, const int32_t *sel, int n, int n_max, int64_t H, int k, int rowf, float *send,
-                cudaStream_t st) {
-    if (n_max <= 0) return MG_OK;
-    k_ep_dec_pack<<<n_max, 256, 0, st>>>(xb, sel, n, H, k, rowf, send);
-    MG_CHECK_LAUNCH();
-    return MG_OK;
 }
 
 int ep_dec_unpack(const float *recv, int n_all, int64_t H, int k, int rowf, float *xb_all, int32_t *sel_all,

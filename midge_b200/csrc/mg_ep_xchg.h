@@ -5,9 +5,7 @@
 
 namespace mg {
 
-// decode: fixed-size rows [normed row (H) | top-k ids (k, as int bits) | pad] per token
-int ep_dec_pack(const float *xb, const int32_t *sel, int n, int n_max, int64_t H, int k, int rowf, float *send,
-                cudaStream_t st);
+// decode: gathered rows [normed row (H) | top-k ids (k, as int bits) | pad] -> rows and ids
 int ep_dec_unpack(const float *recv, int n_all, int64_t H, int k, int rowf, float *xb_all, int32_t *sel_all,
                   cudaStream_t st);
 

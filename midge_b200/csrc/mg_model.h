@@ -109,7 +109,7 @@ struct mg_model {
     // expert parallelism (world > 1): token exchange buffers
     int ep_rowf = 0;       // floats per packed [normed row | top-k ids] row
     int dec_nmax = 0;      // decode: tokens per rank of the current step (max over the ranks)
-    float *epd_send = nullptr, *epd_recv = nullptr, *epd_xb = nullptr, *epd_y = nullptr;
+    float *epd_recv = nullptr, *epd_xb = nullptr, *epd_y = nullptr;
     int32_t *epd_sel = nullptr;
     mg::EpPeer epd_recv_p, epd_y_p, ep_flags_p, epp_recv_p, epp_ret_recv_p;  // peer-mapped buffers
     mg::EpDecPeers epd_peers{};
