@@ -22,7 +22,11 @@
 //     into TMEM with tcgen05.cp.32x128b.warpx4; an MMA (K = 64) reads two
 //     blocks, selected by its scale-factor id (0 or 2).  The A atoms are
 //     written once, when the model is made ready (k_bs_atoms: 1 KB per
-//     (expert, tile, stage)), and streamed beside the A tile.
+//     (expert, tile, stage)), and streamed beside the A tile; the B atoms of
+//     a token group stay in TMEM for all its units, so a stage costs two
+//     atom copies and four MMAs (the MMA issuer's loop sets the kernel's
+//     pace: measured per-stage marks showed the data ready ~3 us after issue
+//     and the issuer never waiting for it).
 //   * D (fp32, TMEM): 128 output rows x 16 columns per token; the epilogue
 //     sums each token's 16 limb columns.
 // Each unit multiplies one expert's weight tile by up to 2 of its routed
@@ -30,18 +34,17 @@
 // with more routed tokens takes further token groups.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over the units):
-//   warp 0     producer: per unit the group's B scale words by bulk copy
-//              into one of two slots; per stage the A box(es) by TMA and the
-//              stage's A atoms by bulk copy into a ring; per token group its
-//              B rows (resident for all K stages)
-//   warp 1     MMA issuer (one thread): per stage the 4 scale atoms into the
-//              stage's TMEM columns (tcgen05.cp, ordered before the MMAs
-//              that read them), 4 MMAs of K = 64, commit -> the stage is
-//              free; per unit commit -> accumulator buffer ready (2 buffers)
-//   warp 2     B atoms: per stage the group's B atoms from the slot's
-//              words (lane = B row), then an arrival on the stage's full
-//              barrier, which thus completes when the TMA data, the A atoms
-//              and the B atoms are in place
+//   warp 0     producer: per stage the A box(es) by TMA and the stage's A
+//              atoms by bulk copy into a ring; per token group its B rows
+//              (resident for all K stages) and its B scale words
+//   warp 1     MMA issuer (one thread): per token group the B scale atoms of
+//              every K stage into one of two resident TMEM buffers; per stage
+//              the 2 A scale atoms into the stage's TMEM columns (tcgen05.cp,
+//              ordered before the MMAs that read them), 4 MMAs of K = 64,
+//              commit -> the stage is free; per unit commit -> accumulator
+//              buffer ready (2 buffers)
+//   warp 2     B atoms: per token group, the B atoms of every K stage from
+//              the group's words (lane = B row) into shared memory
 //   warps 3-5  idle after setup
 //   warps 6-9  epilogue (TMEM lane quadrant = warp % 4): limb sums; gate/up:
 //              bias, clamped SwiGLU (engine/midge.c:386-392) and the h values
@@ -77,24 +80,30 @@ constexpr int BS_B_TOK = BS_LIMBS * 128;               // B rows of one token pe
 constexpr int BS_B_STAGE = BS_TOKG * BS_B_TOK;         // resident B: per K stage, the group's tokens
 constexpr int BS_MAX_NK = 16;                          // K stages of a row (K <= 4096)
 constexpr int BS_STAGE = BS_A_BYTES;                   // ring stage: the A tile (16 KB, 1024-aligned)
-constexpr int BS_ATOMS = 2048;                         // 2 A atoms + 2 B atoms per stage
+constexpr int BS_ATOMS = 1024;                         // the 2 A scale atoms of a ring stage
+constexpr int BS_BATOMS = 1024;                        // the 2 B scale atoms of a K stage (resident per token group)
 constexpr int BS_MAX_STAGES = 12;
 constexpr int BS_THREADS = 320;
 constexpr int BS_ACC_COLS = BS_TOKG * BS_LIMBS;        // accumulator columns of a unit (N)
-constexpr int BS_SF_COL0 = 2 * BS_ACC_COLS;            // scale columns: 16 per stage after the 2 accumulators
-constexpr int BS_TMEM_COLS = 256;                      // >= BS_SF_COL0 + 16 * BS_MAX_STAGES
-static_assert(BS_SF_COL0 + 16 * BS_MAX_STAGES <= BS_TMEM_COLS, "TMEM columns");
+constexpr int BS_SFA_COL0 = 2 * BS_ACC_COLS;           // A scale columns: 8 per ring stage after the 2 accumulators
+constexpr int BS_SFB_COL0 = BS_SFA_COL0 + 8 * BS_MAX_STAGES;  // B scale columns: 2 buffers x 8 per K stage
+constexpr int BS_TMEM_COLS = 512;
+static_assert(BS_SFB_COL0 + 2 * 8 * BS_MAX_NK <= BS_TMEM_COLS, "TMEM columns");
 constexpr int BS_MAX_V = 4 * SW_MAX_SLOTS;             // token groups (experts x up to 4)
 // error word codes of a timed-out wait, by role (beside the streamed kernels' 1)
 constexpr int BS_ERR_PRODUCER = 11, BS_ERR_MMA = 12, BS_ERR_ATOMS = 13, BS_ERR_EPILOGUE = 14, BS_ERR_DRAIN = 15;
-// the first failure is kept (21.. name the wait that gave up: producer 21 slot, 22 ring stage, 23 accumulator
-// before a B reload; MMA 24 B rows, 25 accumulator buffer, 26 stage; atoms 27 slot, 28 stage)
+// the first failure is kept (21.. name the wait that gave up: producer 21 B words consumed, 22 ring stage,
+// 23 accumulator before a B reload; MMA 24 B rows, 25 accumulator buffer, 26 stage, 29 B atoms built;
+// atoms 27 B rows + words, 28 previous B atoms copied)
 __device__ __forceinline__ void bs_fail(int *err, int code) { atomicCAS(err, 0, code); }
 
 struct BsBars {
     uint64_t full[BS_MAX_STAGES], empty[BS_MAX_STAGES];
-    uint64_t sfull[2], sempty[2], accfull[2], accempty[2];
-    uint64_t bfull;  // the resident B rows of the unit's token group have landed
+    uint64_t accfull[2], accempty[2];
+    uint64_t bfull;     // the token group's resident B rows and B scale words have landed
+    uint64_t bwempty;   // the B-atom warp has read the group's scale words
+    uint64_t batfull;   // the group's B atoms (all K stages) are built in shared memory
+    uint64_t batempty;  // the MMA issuer's copies of them into TMEM have completed
     uint64_t done;   // the MMA issuer's last commit: no MMA is in flight when TMEM is released
     uint32_t tmem;
 };
@@ -305,10 +314,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     extern __shared__ __align__(1024) uint8_t bs_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bs_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *stages = sm;
-    uint8_t *atoms = stages + (size_t)nst * BS_STAGE;  // per stage: A atoms (bulk copy) +0, +512; B atoms +1024, +1536
+    uint8_t *atoms = stages + (size_t)nst * BS_STAGE;  // per ring stage: its 2 A atoms (bulk copy) +0, +512
     uint8_t *bres = atoms + (size_t)nst * BS_ATOMS;  // [K stage][token j][16 rows x 128 B], 1024-aligned
-    uint8_t *slots = bres + (size_t)pol.nk * BS_B_STAGE;
-    float *ex = reinterpret_cast<float *>(slots + 2 * (size_t)ssb);  // 64 rows x 2 tokens (up values)
+    uint8_t *batoms = bres + (size_t)pol.nk * BS_B_STAGE;  // [K stage][2 B atoms of 512 B] of the token group
+    uint8_t *bwreg = batoms + (size_t)pol.nk * BS_BATOMS;  // the token group's B scale words [token j][g4][16]
+    float *ex = reinterpret_cast<float *>(bwreg + (size_t)ssb);  // 64 rows x 2 tokens (up values)
     BsBars *bb = reinterpret_cast<BsBars *>(ex + 64 * BS_TOKG);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ int vlist[BS_MAX_V];
@@ -316,11 +326,10 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     // barriers and TMEM first: they overlap the routing-slot loads of build_list
     if (warp == 2) {
         if (lane < nst) {
-            mbar_init(&bb->full[lane], 2);  // the producer's expect-tx arrival + the B atoms' arrival
+            mbar_init(&bb->full[lane], 1);  // the producer's expect-tx arrival: A tile + A atoms
             mbar_init(&bb->empty[lane], 1);
         } else if (lane >= 16 && lane < 18) {
-            mbar_init(&bb->sfull[lane - 16], 1);
-            mbar_init(&bb->sempty[lane - 16], 1);
+            mbar_init(lane == 16 ? &bb->batfull : &bb->batempty, 1);
         } else if (lane >= 18 && lane < 20) {
             mbar_init(&bb->accfull[lane - 18], 1);
             mbar_init(&bb->accempty[lane - 18], 4);
@@ -379,60 +388,54 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         // ------------------------------------------------------ producer
         if (lane == 0 && u0 < u1) {
             bool ok = true, dep = false;  // dep: the previous grid has completed (griddepcontrol.wait)
-            int s = 0, q = 0, nsl = 0, key = -1, nbl = 0;
+            int s = 0, q = 0, key = -1, nbl = 0;
             uint32_t ph = 0, it = 0;
             for (int u = u0; u < u1 && ok; u++, q++) {
                 int d, tg, tile, ks, k0, k1;
                 pol.unit(u, d, tg, tile, ks, k0, k1);
                 const int e = pol.ms->list[d];
-                const int slot = q & 1, nt = pol.ntok(d, tg);
-                // a new token group: its B rows replace the resident ones once the
-                // previous unit's MMAs are done (polled while this unit's A stages
-                // stream, waited for at the end of them otherwise)
+                const int nt = pol.ntok(d, tg);
+                // a new token group: its B rows and B scale words replace the resident ones
+                // once the previous unit's MMAs are done (polled while this unit's A stages
+                // stream, waited for at the end of them otherwise).  Those MMAs read the
+                // group's B atoms, which the B-atom warp built from the old words before
+                // it released them, so the words are free as well.
                 bool bpend = (d | (tg << 16)) != key;
                 key = d | (tg << 16);
                 auto load_b = [&]() {
-                    mbar_arrive_expect_tx(&bb->bfull, (uint32_t)(nt * pol.nk * BS_B_TOK));
+                    mbar_arrive_expect_tx(&bb->bfull, (uint32_t)(nt * pol.nk * BS_B_TOK) + (uint32_t)nt * pol.bw_bytes());
                     for (int kk = 0; kk < pol.nk; kk++)
                         for (int j = 0; j < nt; j++)
                             tma_load_2d(bres + kk * BS_B_STAGE + j * BS_B_TOK, &maps.b, kk * 128,
                                         pol.src_of(d, tg, j) * BS_LIMBS, &bb->bfull);
+                    for (int j = 0; j < nt; j++)
+                        bulk_g2s(bwreg + j * pol.bw_bytes(), pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS,
+                                 pol.bw_bytes(), &bb->bfull);
                     nbl++;
                     bpend = false;
                 };
                 const uint32_t pprev = (uint32_t)(((q - 1) >> 1) & 1);
-                if (q >= 2 && !mbar_wait(&bb->sempty[slot], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 21); ok = false; break; }
-                uint8_t *ss = slots + (size_t)slot * ssb;
-                // the B scale words and the B rows come from the previous grid (the
-                // limbs kernel, or gate/up for the down pass): the first unit issues
-                // its weight stages (up to a ring) before waiting for that grid
-                auto load_dep = [&]() {
-                    for (int j = 0; j < nt; j++)
-                        bulk_g2s(ss + j * pol.bw_bytes(), pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS,
-                                 pol.bw_bytes(), &bb->sfull[slot]);
-                    if (bpend && q == 0) load_b();
-                };
+                // the B rows and words come from the previous grid (the limbs kernel,
+                // or gate/up for the down pass): the first unit issues its weight
+                // stages (up to a ring) before waiting for that grid
                 auto wait_dep = [&]() {
                     asm volatile("griddepcontrol.wait;" ::: "memory");
                     dep = true;
-                    load_dep();
+                    if (bpend && q == 0) load_b();
                 };
-                mbar_arrive_expect_tx(&bb->sfull[slot], (uint32_t)nt * pol.bw_bytes());
-                if (dep) load_dep();
-                nsl = q + 1;
                 for (int i = 0; i < k1 - k0; i++) {
                     const int k = pol.stage_k(k0, k1, i, tile, ks);
                     if (!dep && it >= (uint32_t)nst) wait_dep();
                     if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { bs_fail(pol.err, 22); ok = false; break; }
                     uint8_t *st = stages + (size_t)s * BS_STAGE;
-                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES + 1024);
+                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES + BS_ATOMS);
                     if (pol.mode == 0) {
                         tma_box_4d(st, &maps.a0, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
                         tma_box_4d(st + BS_A_BYTES / 2, &maps.a1, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
                     } else {
                         tma_box_4d(st, &maps.a0, k * 128, tile * 128, e, pol.layer, &bb->full[s]);
                     }
-                    bulk_g2s(atoms + (size_t)s * BS_ATOMS, pol.atoms_of(e, tile, k), 1024, &bb->full[s]);
+                    bulk_g2s(atoms + (size_t)s * BS_ATOMS, pol.atoms_of(e, tile, k), BS_ATOMS, &bb->full[s]);
                     it++;
                     if (++s == nst) { s = 0; ph ^= 1u; }
                     if (bpend && dep && q > 0 && mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev)) load_b();
@@ -445,12 +448,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             }
             if (!ok) bs_fail(pol.err, BS_ERR_PRODUCER);
             if (!dep) asm volatile("griddepcontrol.wait;" ::: "memory");
-            // every copy issued has landed before the CTA may exit (a full
-            // barrier also needs the B atoms' arrival; a failed wait is recorded)
+            // every copy issued has landed before the CTA may exit (a failed wait is recorded)
             for (int64_t k = (int64_t)it - 1; k >= 0 && k >= (int64_t)it - nst; k--)
                 if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
-            for (int j = nsl - 1; j >= 0 && j >= nsl - 2; j--)
-                if (!mbar_wait(&bb->sfull[j & 1], (uint32_t)((j >> 1) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
             if (nbl > 0 && !mbar_wait(&bb->bfull, (uint32_t)((nbl - 1) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
         }
     } else if (warp == 1) {
@@ -461,18 +461,34 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             uint32_t ph = 0;
             const uint64_t da0 = umma_desc_sw128(smem_u32(stages)), db0 = umma_desc_sw128(smem_u32(bres));
             const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
-            int key = -1, nbl = 0;
+            const uint64_t dbt0 = umma_desc_plain(smem_u32(batoms), 512, 128);
+            int key = -1, ng = 0;
+            uint32_t tbb = tb + BS_SFB_COL0;  // the current token group's B scale columns
             for (int u = u0; u < u1 && ok; u++, q++) {
                 int d, tg, tile, ks, k0, k1;
                 pol.unit(u, d, tg, tile, ks, k0, k1);
                 const int N = BS_LIMBS * pol.ntok(d, tg);
                 const int b = q & 1;
-                if ((d | (tg << 16)) != key) {  // the token group's resident B rows
-                    key = d | (tg << 16);
-                    if (!mbar_wait(&bb->bfull, (uint32_t)(nbl & 1))) { bs_fail(pol.err, 24); ok = false; break; }
-                    nbl++;
-                }
+                // unit q - 2's accumulator handed back: its MMAs, and all before, are done
                 if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 25); ok = false; break; }
+                if ((d | (tg << 16)) != key) {
+                    // a new token group: its resident B rows, and its B scale atoms of every K
+                    // stage into one of two TMEM buffers; the other may still feed the MMAs of
+                    // the group before, this one was last read two groups ago, by MMAs of unit
+                    // q - 2 or earlier, which the wait above has seen completed
+                    key = d | (tg << 16);
+                    if (!mbar_wait(&bb->bfull, (uint32_t)(ng & 1))) { bs_fail(pol.err, 24); ok = false; break; }
+                    if (!mbar_wait(&bb->batfull, (uint32_t)(ng & 1))) { bs_fail(pol.err, 29); ok = false; break; }
+                    tc_fence_after();
+                    tbb = tb + BS_SFB_COL0 + (uint32_t)((ng & 1) * 8 * pol.nk);
+                    for (int kk = 0; kk < pol.nk; kk++) {
+                        const uint64_t dk = dbt0 + (uint64_t)((kk * BS_BATOMS) >> 4);
+                        bs_cp_atom(tbb + 8u * (uint32_t)kk, dk);
+                        bs_cp_atom(tbb + 8u * (uint32_t)kk + 4u, dk + 32);
+                    }
+                    tc_commit(&bb->batempty);  // the shared-memory atoms may be rebuilt once these copies are done
+                    ng++;
+                }
                 tc_fence_after();
                 const uint32_t tacc = tb + (uint32_t)(b * BS_ACC_COLS);
                 const uint32_t id0 = bs_idesc(N, 0), id2 = bs_idesc(N, 2);
@@ -480,20 +496,20 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     const int k = pol.stage_k(k0, k1, i, tile, ks);
                     if (!mbar_wait(&bb->full[s], ph)) { bs_fail(pol.err, 26); ok = false; break; }
                     tc_fence_after();
-                    // the stage's scale atoms into its TMEM columns (A +0, +4; B +8, +12),
-                    // executed in order before the MMAs below
+                    // the stage's A scale atoms into its TMEM columns (+0, +4), executed in
+                    // order before the MMAs below; the B atoms of K stage k are resident
                     const uint64_t dat = dat0 + (uint64_t)((s * BS_ATOMS) >> 4);
-                    const uint32_t tsf = tb + BS_SF_COL0 + 16u * (uint32_t)s;
-#pragma unroll
-                    for (int c = 0; c < 4; c++) bs_cp_atom(tsf + 4 * c, dat + 32 * c);
+                    const uint32_t tsa = tb + BS_SFA_COL0 + 8u * (uint32_t)s, tsb = tbb + 8u * (uint32_t)k;
+                    bs_cp_atom(tsa, dat);
+                    bs_cp_atom(tsa + 4u, dat + 32);
                     // descriptors: the start-address field is the low 14 bits (address >> 4)
                     const uint64_t da = da0 + (uint64_t)((s * BS_STAGE) >> 4);
                     const uint64_t db = db0 + (uint64_t)((k * BS_B_STAGE) >> 4);
 #pragma unroll
                     for (int j = 0; j < 4; j++) {
                         const uint32_t sid = 2u * (uint32_t)(j & 1), g = 4u * (uint32_t)(j >> 1);
-                        bs_mma(tacc, da + 2 * j, db + 2 * j, (j & 1) ? id2 : id0, (tsf + g) | (sid << 30),
-                               (tsf + 8 + g) | (sid << 30), (i > 0 || j > 0) ? 1u : 0u);
+                        bs_mma(tacc, da + 2 * j, db + 2 * j, (j & 1) ? id2 : id0, (tsa + g) | (sid << 30),
+                               (tsb + g) | (sid << 30), (i > 0 || j > 0) ? 1u : 0u);
                     }
                     tc_commit(&bb->empty[s]);
                     if (++s == nst) { s = 0; ph ^= 1u; }
@@ -506,37 +522,31 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         }
     } else if (warp == 2) {
         // ------------------------------------------------------ B scale atoms
-        // lane = B row (limb lane % 16 of token lane / 16); after a timed-out
-        // wait the warp stops
+        // once per token group, for every K stage: lane = B row (limb lane % 16 of
+        // token lane / 16); after a timed-out wait the warp stops
         bool failed = false;
-        int s = 0, q = 0;
-        uint32_t ph = 0, it = 0;
+        int key = -1, ng = 0;
         const int aoff = lane * 16;  // B rows < 32: byte (r % 32) * 16 + kb % 4
-        for (int u = u0; u < u1 && !failed; u++, q++) {
+        for (int u = u0; u < u1 && !failed; u++) {
             int d, tg, tile, ks, k0, k1;
             pol.unit(u, d, tg, tile, ks, k0, k1);
-            const int slot = q & 1;
-            if (!mbar_wait(&bb->sfull[slot], (uint32_t)((q >> 1) & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 27); break; }
-            const uint32_t *bw = reinterpret_cast<const uint32_t *>(slots + (size_t)slot * ssb);
+            if ((d | (tg << 16)) == key) continue;
+            key = d | (tg << 16);
+            if (!mbar_wait(&bb->bfull, (uint32_t)(ng & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 27); break; }
+            if (ng >= 1 && !mbar_wait(&bb->batempty, (uint32_t)((ng - 1) & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 28); break; }
+            const uint32_t *bw = reinterpret_cast<const uint32_t *>(bwreg);
             const int nrows = BS_LIMBS * pol.ntok(d, tg);
-            for (int i = 0; i < k1 - k0; i++) {
-                const int k = pol.stage_k(k0, k1, i, tile, ks);
-                if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { failed = true; if (lane == 0) bs_fail(pol.err, 28); break; }
-                uint8_t *at = atoms + (size_t)s * BS_ATOMS + 1024;
-                if (lane < nrows) {
+            if (lane < nrows) {
+                for (int kk = 0; kk < pol.nk; kk++)
 #pragma unroll
                     for (int h = 0; h < 2; h++)
-                        *reinterpret_cast<uint32_t *>(at + 512 * h + aoff) =
-                            bw[((lane >> 4) * pol.g4 + 2 * k + h) * BS_LIMBS + (lane & 15)];
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bb->full[s]);
-                it++;
-                if (++s == nst) { s = 0; ph ^= 1u; }
+                        *reinterpret_cast<uint32_t *>(batoms + (size_t)kk * BS_BATOMS + 512 * h + aoff) =
+                            bw[((lane >> 4) * pol.g4 + 2 * kk + h) * BS_LIMBS + (lane & 15)];
             }
+            fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0 && !failed) mbar_arrive(&bb->sempty[slot]);
+            if (lane == 0) mbar_arrive(&bb->batfull);
+            ng++;
         }
         if (failed && lane == 0) bs_fail(pol.err, BS_ERR_ATOMS);
     } else if (warp < 6) {
@@ -627,7 +637,7 @@ static int bs_launch(const BsMapsK &maps, BsPol &pol, size_t ssb, cudaStream_t s
     MG_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(k_bsmoe)));
     ssb = (ssb + 127) & ~(size_t)127;
     MG_REQUIRE(pol.nk >= 1 && pol.nk <= BS_MAX_NK, MG_ERR_ARG, "block-scaled MoE: K of %d stages unsupported", pol.nk);
-    const size_t fixed = 1024 + (size_t)pol.nk * BS_B_STAGE + 2 * ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
+    const size_t fixed = 1024 + (size_t)pol.nk * (BS_B_STAGE + BS_BATOMS) + ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
     const size_t budget = 227 * 1024 - fa.sharedSizeBytes;
     MG_REQUIRE(budget > fixed + 2 * (BS_STAGE + BS_ATOMS), MG_ERR_ARG, "block-scaled MoE: no room for a ring");
     int nst = (int)((budget - fixed) / (BS_STAGE + BS_ATOMS));
