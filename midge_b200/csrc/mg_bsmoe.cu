@@ -79,14 +79,17 @@ constexpr int BS_A_BYTES = 128 * 128;                  // A stage: 128 rows x 12
 constexpr int BS_B_TOK = BS_LIMBS * 128;               // B rows of one token per K stage: 16 x 128 B
 constexpr int BS_B_STAGE = BS_TOKG * BS_B_TOK;         // resident B: per K stage, the group's tokens
 constexpr int BS_MAX_NK = 16;                          // K stages of a row (K <= 4096)
-constexpr int BS_STAGE = BS_A_BYTES;                   // ring stage: the A tile (16 KB, 1024-aligned)
-constexpr int BS_ATOMS = 1024;                         // the 2 A scale atoms of a ring stage
+constexpr int BS_CH = 2;                               // K chunks (of 256 values) per ring stage
+constexpr int BS_STAGE = BS_CH * BS_A_BYTES;           // ring stage: the A tiles of its chunks (1024-aligned)
+constexpr int BS_ATOMS = 1024;                         // the 2 A scale atoms of a chunk
 constexpr int BS_BATOMS = 1024;                        // the 2 B scale atoms of a K stage (resident per token group)
-constexpr int BS_MAX_STAGES = 12;
+constexpr int BS_MAX_STAGES = 6;
 constexpr int BS_THREADS = 320;
 constexpr int BS_ACC_COLS = BS_TOKG * BS_LIMBS;        // accumulator columns of a unit (N)
-constexpr int BS_SFA_COL0 = 2 * BS_ACC_COLS;           // A scale columns: 8 per ring stage after the 2 accumulators
-constexpr int BS_SFB_COL0 = BS_SFA_COL0 + 8 * BS_MAX_STAGES;  // B scale columns: 2 buffers x 8 per K stage
+// accumulators: 2 units in flight x 2 independent halves (the MMAs of a stage
+// alternate between them, so consecutive MMAs do not wait for each other)
+constexpr int BS_SFA_COL0 = 4 * BS_ACC_COLS;           // A scale columns: 8 per ring stage after the accumulators
+constexpr int BS_SFB_COL0 = BS_SFA_COL0 + 8 * BS_CH * BS_MAX_STAGES;  // B scale columns: 2 buffers x 8 per K chunk
 constexpr int BS_TMEM_COLS = 512;
 static_assert(BS_SFB_COL0 + 2 * 8 * BS_MAX_NK <= BS_TMEM_COLS, "TMEM columns");
 constexpr int BS_MAX_V = 4 * SW_MAX_SLOTS;             // token groups (experts x up to 4)
@@ -314,8 +317,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     extern __shared__ __align__(1024) uint8_t bs_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bs_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *stages = sm;
-    uint8_t *atoms = stages + (size_t)nst * BS_STAGE;  // per ring stage: its 2 A atoms (bulk copy) +0, +512
-    uint8_t *bres = atoms + (size_t)nst * BS_ATOMS;  // [K stage][token j][16 rows x 128 B], 1024-aligned
+    uint8_t *atoms = stages + (size_t)nst * BS_STAGE;  // per ring stage and chunk: its 2 A atoms (bulk copy) +0, +512
+    uint8_t *bres = atoms + (size_t)nst * BS_CH * BS_ATOMS;  // [K chunk][token j][16 rows x 128 B], 1024-aligned
     uint8_t *batoms = bres + (size_t)pol.nk * BS_B_STAGE;  // [K stage][2 B atoms of 512 B] of the token group
     uint8_t *bwreg = batoms + (size_t)pol.nk * BS_BATOMS;  // the token group's B scale words [token j][g4][16]
     float *ex = reinterpret_cast<float *>(bwreg + (size_t)ssb);  // 64 rows x 2 tokens (up values)
@@ -423,19 +426,23 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     dep = true;
                     if (bpend && q == 0) load_b();
                 };
-                for (int i = 0; i < k1 - k0; i++) {
-                    const int k = pol.stage_k(k0, k1, i, tile, ks);
+                const int nchk = k1 - k0;
+                for (int i = 0; i < nchk; i += BS_CH) {
+                    const int nch = min(BS_CH, nchk - i);
                     if (!dep && it >= (uint32_t)nst) wait_dep();
                     if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { bs_fail(pol.err, 22); ok = false; break; }
-                    uint8_t *st = stages + (size_t)s * BS_STAGE;
-                    mbar_arrive_expect_tx(&bb->full[s], BS_A_BYTES + BS_ATOMS);
-                    if (pol.mode == 0) {
-                        tma_box_4d(st, &maps.a0, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
-                        tma_box_4d(st + BS_A_BYTES / 2, &maps.a1, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
-                    } else {
-                        tma_box_4d(st, &maps.a0, k * 128, tile * 128, e, pol.layer, &bb->full[s]);
+                    mbar_arrive_expect_tx(&bb->full[s], (uint32_t)nch * (BS_A_BYTES + BS_ATOMS));
+                    for (int h = 0; h < nch; h++) {
+                        const int k = pol.stage_k(k0, k1, i + h, tile, ks);
+                        uint8_t *st = stages + (size_t)s * BS_STAGE + (size_t)h * BS_A_BYTES;
+                        if (pol.mode == 0) {
+                            tma_box_4d(st, &maps.a0, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
+                            tma_box_4d(st + BS_A_BYTES / 2, &maps.a1, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
+                        } else {
+                            tma_box_4d(st, &maps.a0, k * 128, tile * 128, e, pol.layer, &bb->full[s]);
+                        }
+                        bulk_g2s(atoms + ((size_t)s * BS_CH + h) * BS_ATOMS, pol.atoms_of(e, tile, k), BS_ATOMS, &bb->full[s]);
                     }
-                    bulk_g2s(atoms + (size_t)s * BS_ATOMS, pol.atoms_of(e, tile, k), BS_ATOMS, &bb->full[s]);
                     it++;
                     if (++s == nst) { s = 0; ph ^= 1u; }
                     if (bpend && dep && q > 0 && mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev)) load_b();
@@ -490,26 +497,35 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     ng++;
                 }
                 tc_fence_after();
-                const uint32_t tacc = tb + (uint32_t)(b * BS_ACC_COLS);
+                const uint32_t tacc = tb + (uint32_t)(b * BS_ACC_COLS);  // half 1 at + 2 * BS_ACC_COLS
                 const uint32_t id0 = bs_idesc(N, 0), id2 = bs_idesc(N, 2);
-                for (int i = 0; i < k1 - k0; i++) {
-                    const int k = pol.stage_k(k0, k1, i, tile, ks);
+                const int nchk = k1 - k0;
+                for (int i = 0; i < nchk; i += BS_CH) {
+                    const int nch = min(BS_CH, nchk - i);
                     if (!mbar_wait(&bb->full[s], ph)) { bs_fail(pol.err, 26); ok = false; break; }
                     tc_fence_after();
-                    // the stage's A scale atoms into its TMEM columns (+0, +4), executed in
-                    // order before the MMAs below; the B atoms of K stage k are resident
-                    const uint64_t dat = dat0 + (uint64_t)((s * BS_ATOMS) >> 4);
-                    const uint32_t tsa = tb + BS_SFA_COL0 + 8u * (uint32_t)s, tsb = tbb + 8u * (uint32_t)k;
-                    bs_cp_atom(tsa, dat);
-                    bs_cp_atom(tsa + 4u, dat + 32);
-                    // descriptors: the start-address field is the low 14 bits (address >> 4)
-                    const uint64_t da = da0 + (uint64_t)((s * BS_STAGE) >> 4);
-                    const uint64_t db = db0 + (uint64_t)((k * BS_B_STAGE) >> 4);
+                    // the stage's A scale atoms into its TMEM columns (+0, +4 per chunk),
+                    // executed in order before the MMAs below; the B atoms of every K chunk
+                    // are resident
+                    for (int h = 0; h < nch; h++) {
+                        const uint64_t dat = dat0 + (uint64_t)((((size_t)s * BS_CH + h) * BS_ATOMS) >> 4);
+                        const uint32_t tsa = tb + BS_SFA_COL0 + 8u * (uint32_t)(s * BS_CH + h);
+                        bs_cp_atom(tsa, dat);
+                        bs_cp_atom(tsa + 4u, dat + 32);
+                    }
+                    for (int h = 0; h < nch; h++) {
+                        const int k = pol.stage_k(k0, k1, i + h, tile, ks);
+                        const uint32_t tsa = tb + BS_SFA_COL0 + 8u * (uint32_t)(s * BS_CH + h), tsb = tbb + 8u * (uint32_t)k;
+                        // descriptors: the start-address field is the low 14 bits (address >> 4)
+                        const uint64_t da = da0 + (uint64_t)(((size_t)s * BS_STAGE + (size_t)h * BS_A_BYTES) >> 4);
+                        const uint64_t db = db0 + (uint64_t)((k * BS_B_STAGE) >> 4);
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const uint32_t sid = 2u * (uint32_t)(j & 1), g = 4u * (uint32_t)(j >> 1);
-                        bs_mma(tacc, da + 2 * j, db + 2 * j, (j & 1) ? id2 : id0, (tsa + g) | (sid << 30),
-                               (tsb + g) | (sid << 30), (i > 0 || j > 0) ? 1u : 0u);
+                        for (int j = 0; j < 4; j++) {
+                            const uint32_t sid = 2u * (uint32_t)(j & 1), g = 4u * (uint32_t)(j >> 1);
+                            bs_mma(tacc + (uint32_t)((j & 1) * 2 * BS_ACC_COLS), da + 2 * j, db + 2 * j,
+                                   (j & 1) ? id2 : id0, (tsa + g) | (sid << 30), (tsb + g) | (sid << 30),
+                                   (i > 0 || h > 0 || j > 1) ? 1u : 0u);
+                        }
                     }
                     tc_commit(&bb->empty[s]);
                     if (++s == nst) { s = 0; ph ^= 1u; }
@@ -582,11 +598,15 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             for (int j = 0; j < BS_TOKG; j++) {
                 v[j] = 0.f;
                 if (j < nt && !failed) {
-                    float t[16];
-                    tmem_ld16(tb + (uint32_t)(b * BS_ACC_COLS + BS_LIMBS * j) + ((uint32_t)(32 * ew) << 16), t);
+                    float t[16], t2[16];
+                    const uint32_t ta = tb + (uint32_t)(b * BS_ACC_COLS + BS_LIMBS * j) + ((uint32_t)(32 * ew) << 16);
+                    tmem_ld16(ta, t);
+                    tmem_ld16(ta + 2 * BS_ACC_COLS, t2);
                     float acc = t[0];
 #pragma unroll
                     for (int i = 1; i < 16; i++) acc += t[i];
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc += t2[i];
                     v[j] = acc;
                 }
             }
@@ -639,10 +659,10 @@ static int bs_launch(const BsMapsK &maps, BsPol &pol, size_t ssb, cudaStream_t s
     MG_REQUIRE(pol.nk >= 1 && pol.nk <= BS_MAX_NK, MG_ERR_ARG, "block-scaled MoE: K of %d stages unsupported", pol.nk);
     const size_t fixed = 1024 + (size_t)pol.nk * (BS_B_STAGE + BS_BATOMS) + ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
     const size_t budget = 227 * 1024 - fa.sharedSizeBytes;
-    MG_REQUIRE(budget > fixed + 2 * (BS_STAGE + BS_ATOMS), MG_ERR_ARG, "block-scaled MoE: no room for a ring");
-    int nst = (int)((budget - fixed) / (BS_STAGE + BS_ATOMS));
+    MG_REQUIRE(budget > fixed + 2 * (BS_STAGE + BS_CH * BS_ATOMS), MG_ERR_ARG, "block-scaled MoE: no room for a ring");
+    int nst = (int)((budget - fixed) / (BS_STAGE + BS_CH * BS_ATOMS));
     if (nst > BS_MAX_STAGES) nst = BS_MAX_STAGES;
-    const size_t smem = fixed + (size_t)nst * (BS_STAGE + BS_ATOMS);
+    const size_t smem = fixed + (size_t)nst * (BS_STAGE + BS_CH * BS_ATOMS);
     BS_TRY(ensure_smem_attr(reinterpret_cast<const void *>(k_bsmoe), smem));
     // programmatic dependent launch: this grid may start while the previous
     // kernel on the stream finishes; its producer waits for that grid
