@@ -112,7 +112,8 @@ struct BsBars {
 };
 
 struct BsMapsK {
-    CUtensorMap a0, a1, b;  // gate/up: gate, up, x limbs; down: down, (unused), h limbs
+    CUtensorMap a[3];  // A boxes: gate, up (64 rows each), down (128 rows)
+    CUtensorMap b[2];  // B rows: x limbs (gate/up), h limbs (down)
 };
 
 // shared-memory matrix descriptor, no swizzle (the scale atoms: 8-row core
@@ -242,42 +243,65 @@ __global__ void k_bs_atoms(const uint8_t *experts, mg_expert_layout L, int64_t n
 }
 
 // ---------------------------------------------------------- routed experts
+// the parameters of one pass (0 gate/up, 1 down)
+struct BsPass {
+    const uint32_t *bsf;  // B scale words [src][g4][16] (src: token for gate/up, slot for down)
+    int g4;               // scale words per B row and limb
+    int nk;               // K chunks of an A row
+    int atoms_u0;         // first atom of the pass within an expert (0 gate/up, atoms_dn down)
+};
+// one unit of a CTA's sequence: 128 A rows of expert list[d] times token group tg
+struct BsUnit {
+    int mode, v, d, tg, tile, ks, k0, k1;
+};
 struct BsPol : MoeCommon {
-    int mode;  // 0 gate/up, 1 down
+    BsPass ps[2];
     int act_plain;
     float alpha, limit;
-    const uint32_t *bsf;  // B scale words [src][g4][16] (src: token for gate/up, slot for down)
-    int g4;
     uint8_t *hl;          // gate/up: h limbs out [slot*16 + l][hl_ld]
     uint8_t *hsf;         // gate/up: their scale words (bytes) [slot][hg4][16][4]
     int64_t hl_ld;        // bytes per limb row
     int hg4;
     float *y;             // down: [ks][n_tok*top_k][hidden]
-    int ks_count, kst;    // down: K splits and K stages per split
-    int nk;               // K stages of an A row
-    int G;                // scale groups per A row
+    int ks_count, kst;    // down: K splits and K chunks per split
     int *err;
+    uint32_t *sync;       // [0] CTAs finished, [1 + v] gate/up tiles done of token group v
     const int *vl;        // token groups: (list index) | (group << 16)
     const uint8_t *atoms; // this layer's expert scale atoms
     int64_t atoms_expert; // bytes per expert
-    int atoms_u0;         // first unit of this pass (0 gate/up, atoms_dn down)
+    int g_all, g_per, d_all, d_per;  // units of each pass, and per CTA (set in the kernel)
 
-    __device__ int tpe() const {
+    // (selected, not indexed: a run-time index into the parameter array would
+    // copy it to local memory)
+    __device__ BsPass pass(int mode) const { return mode ? ps[1] : ps[0]; }
+    __device__ int tpe(int mode) const {
         return mode == 0 ? (int)((L.ffn + 63) / 64) : (int)((L.hidden + 127) / 128) * ks_count;
     }
-    __device__ void unit(int u, int &d, int &tg, int &tile, int &ks, int &k0, int &k1) const {
-        const int t = tpe();
-        const int v = u / t, r = u - v * t;
-        d = vl[v] & 0xFFFF;
-        tg = vl[v] >> 16;
-        if (mode == 0) {
-            tile = r; ks = 0; k0 = 0; k1 = nk;
+    // CTA c runs gate/up units [c g_per, (c+1) g_per), then down units [c d_per, (c+1) d_per)
+    __device__ int seq_gate(int c) const { return max(0, min(g_all, (c + 1) * g_per) - c * g_per); }
+    __device__ int seq_len(int c) const { return seq_gate(c) + max(0, min(d_all, (c + 1) * d_per) - c * d_per); }
+    __device__ void seq_unit(int c, int j, BsUnit &x) const {
+        const int gn = seq_gate(c);
+        int u;
+        if (j < gn) {
+            x.mode = 0;
+            u = c * g_per + j;
         } else {
-            tile = r / ks_count; ks = r - tile * ks_count;
-            k0 = ks * kst; k1 = min(nk, k0 + kst);
+            x.mode = 1;
+            u = c * d_per + (j - gn);
+        }
+        const int t = tpe(x.mode), v = u / t, r = u - v * t;
+        x.v = v;
+        x.d = vl[v] & 0xFFFF;
+        x.tg = vl[v] >> 16;
+        if (x.mode == 0) {
+            x.tile = r; x.ks = 0; x.k0 = 0; x.k1 = ps[0].nk;
+        } else {
+            x.tile = r / ks_count; x.ks = r - x.tile * ks_count;
+            x.k0 = x.ks * kst; x.k1 = min(ps[1].nk, x.k0 + kst);
         }
     }
-    // Stage order of a unit: its K stages [k0, k1) from a start that depends
+    // Chunk order of a unit: its K chunks [k0, k1) from a start that depends
     // on the tile and split only, so that the CTAs working on one expert
     // read different parts of the shared activation limb rows at any time
     // (the same rows read in lockstep by many SMs contend in L2); the order
@@ -292,17 +316,33 @@ struct BsPol : MoeCommon {
     // routing slots of (expert d, group tg) and their B source rows
     __device__ int ntok(int d, int tg) const { return min(BS_TOKG, min(ms->ecount[d], SW_MAX_TOK) - BS_TOKG * tg); }
     __device__ int slot_of(int d, int tg, int j) const { return ms->eslot[d][BS_TOKG * tg + j]; }
-    __device__ int src_of(int d, int tg, int j) const {
+    __device__ int src_of(int mode, int d, int tg, int j) const {
         const int s = slot_of(d, tg, j);
         return mode == 0 ? s / top_k : s;
     }
-    // the A atoms of local expert e, tile, K stage k (1024 bytes)
-    __device__ const uint8_t *atoms_of(int e, int tile, int k) const {
-        return atoms + e * atoms_expert + ((int64_t)atoms_u0 + (int64_t)tile * nk + k) * 1024;
+    // the A atoms of local expert e, tile, K chunk k (1024 bytes)
+    __device__ const uint8_t *atoms_of(int mode, int e, int tile, int k) const {
+        return atoms + e * atoms_expert + ((int64_t)pass(mode).atoms_u0 + (int64_t)tile * pass(mode).nk + k) * 1024;
     }
-    // the slot: the group's B scale words [token j][g4][16]
-    __device__ uint32_t bw_bytes() const { return (uint32_t)g4 * BS_LIMBS * 4; }
+    // the group's B scale words [token j][g4][16]
+    __device__ uint32_t bw_bytes(int mode) const { return (uint32_t)pass(mode).g4 * BS_LIMBS * 4; }
 };
+
+// a down group's gate/up tiles: the count the epilogues raise (release) reaches
+// need; generic-proxy writes then feed async-proxy (TMA, bulk) reads
+constexpr uint32_t BS_TILE_POLLS = 1u << 22;
+__device__ __forceinline__ bool bs_tiles_done(const uint32_t *cnt, uint32_t need, bool block) {
+    for (uint32_t i = 0;; i++) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+        if (v >= need) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            return true;
+        }
+        if (!block || i >= BS_TILE_POLLS) return false;
+        __nanosleep(64);
+    }
+}
 
 __device__ __forceinline__ float bs_act(float gv, float uv, const BsPol &p) {
     if (p.act_plain) return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
@@ -316,20 +356,21 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                                                          int ssb) {
     extern __shared__ __align__(1024) uint8_t bs_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(bs_raw) + 1023) & ~(uintptr_t)1023);
+    const int nk_max = max(pol.ps[0].nk, pol.ps[1].nk);
     uint8_t *stages = sm;
     uint8_t *atoms = stages + (size_t)nst * BS_STAGE;  // per ring stage and chunk: its 2 A atoms (bulk copy) +0, +512
     uint8_t *bres = atoms + (size_t)nst * BS_CH * BS_ATOMS;  // [K chunk][token j][16 rows x 128 B], 1024-aligned
-    uint8_t *batoms = bres + (size_t)pol.nk * BS_B_STAGE;  // [K stage][2 B atoms of 512 B] of the token group
-    uint8_t *bwreg = batoms + (size_t)pol.nk * BS_BATOMS;  // the token group's B scale words [token j][g4][16]
+    uint8_t *batoms = bres + (size_t)nk_max * BS_B_STAGE;  // [K chunk][2 B atoms of 512 B] of the token group
+    uint8_t *bwreg = batoms + (size_t)nk_max * BS_BATOMS;  // the token group's B scale words [token j][g4][16]
     float *ex = reinterpret_cast<float *>(bwreg + (size_t)ssb);  // 64 rows x 2 tokens (up values)
     BsBars *bb = reinterpret_cast<BsBars *>(ex + 64 * BS_TOKG);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ int vlist[BS_MAX_V];
-    __shared__ int nv_sh;
+    __shared__ int nv_sh, last_cta;
     // barriers and TMEM first: they overlap the routing-slot loads of build_list
     if (warp == 2) {
         if (lane < nst) {
-            mbar_init(&bb->full[lane], 1);  // the producer's expect-tx arrival: A tile + A atoms
+            mbar_init(&bb->full[lane], 1);  // the producer's expect-tx arrival: A tiles + A atoms
             mbar_init(&bb->empty[lane], 1);
         } else if (lane >= 16 && lane < 18) {
             mbar_init(lane == 16 ? &bb->batfull : &bb->batempty, 1);
@@ -372,89 +413,107 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    // the next kernel (the down pass after gate/up) may start its setup and
-    // weight prefetch on SMs this grid leaves; it waits for this grid before
-    // it reads what this one writes
+    // the next kernel may start its setup on SMs this grid leaves; it waits
+    // for this grid before it reads what this one writes
     if (tid == 0) asm volatile("griddepcontrol.launch_dependents;");
-    // Every role but the producer needs the previous grid's outputs before its
-    // first wait can complete: it waits for that grid here, so that its
-    // bounded waits count from then on.  The producer streams its first
-    // weight stages first and waits later.
+    // Every role but the producer needs the previous grid's outputs (the x
+    // limbs) before its first wait can complete: it waits for that grid here,
+    // so that its bounded waits count from then on.
     if (warp != 0) asm volatile("griddepcontrol.wait;" ::: "memory");
     pol.vl = vlist;
     const uint32_t tb = bb->tmem;
-    const int nunits = nv_sh * pol.tpe();
-    const int per = (nunits + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int u0 = (int)blockIdx.x * per, u1 = min(nunits, u0 + per);
+    const int nv = nv_sh, c = (int)blockIdx.x;
+    pol.g_all = nv * pol.tpe(0);
+    pol.d_all = nv * pol.tpe(1);
+    pol.g_per = (pol.g_all + (int)gridDim.x - 1) / (int)gridDim.x;
+    pol.d_per = (pol.d_all + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int nseq = pol.seq_len(c);
+    const uint32_t tiles_need = (uint32_t)pol.tpe(0);
 
     if (warp == 0) {
         // ------------------------------------------------------ producer
-        if (lane == 0 && u0 < u1) {
-            bool ok = true, dep = false;  // dep: the previous grid has completed (griddepcontrol.wait)
-            int s = 0, q = 0, key = -1, nbl = 0;
+        if (lane == 0 && nseq > 0) {
+            bool ok = true;
+            int s = 0, key = -1, nbl = 0;
             uint32_t ph = 0, it = 0;
-            for (int u = u0; u < u1 && ok; u++, q++) {
-                int d, tg, tile, ks, k0, k1;
-                pol.unit(u, d, tg, tile, ks, k0, k1);
-                const int e = pol.ms->list[d];
-                const int nt = pol.ntok(d, tg);
-                // a new token group: its B rows and B scale words replace the resident ones
-                // once the previous unit's MMAs are done (polled while this unit's A stages
-                // stream, waited for at the end of them otherwise).  Those MMAs read the
+            // the x limbs come from the previous grid, which has finished by
+            // the time the setup above is done: the first B rows go out first
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int q = 0; q < nseq && ok; q++) {
+                BsUnit x;
+                pol.seq_unit(c, q, x);
+                const int e = pol.ms->list[x.d];
+                const int nt = pol.ntok(x.d, x.tg);
+                // a new token group (or pass): its B rows and B scale words replace the
+                // resident ones once the previous unit's MMAs are done (polled while this
+                // unit's A stages stream, waited for otherwise).  Those MMAs read the
                 // group's B atoms, which the B-atom warp built from the old words before
-                // it released them, so the words are free as well.
-                bool bpend = (d | (tg << 16)) != key;
-                key = d | (tg << 16);
+                // it released them, so the words are free as well.  A down group's B rows
+                // are the h limbs of its slots, written by the group's gate/up tiles on
+                // any SM: each tile counts itself done in sync[1 + v].
+                const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
+                bool bpend = gkey != key;
+                key = gkey;
+                auto b_inputs = [&](bool block) {
+                    return x.mode == 0 || bs_tiles_done(pol.sync + 1 + x.v, tiles_need, block);
+                };
                 auto load_b = [&]() {
-                    mbar_arrive_expect_tx(&bb->bfull, (uint32_t)(nt * pol.nk * BS_B_TOK) + (uint32_t)nt * pol.bw_bytes());
-                    for (int kk = 0; kk < pol.nk; kk++)
+                    const BsPass P = pol.pass(x.mode);
+                    const uint32_t bwb = pol.bw_bytes(x.mode);
+                    mbar_arrive_expect_tx(&bb->bfull, (uint32_t)(nt * P.nk * BS_B_TOK) + (uint32_t)nt * bwb);
+                    for (int kk = 0; kk < P.nk; kk++)
                         for (int j = 0; j < nt; j++)
-                            tma_load_2d(bres + kk * BS_B_STAGE + j * BS_B_TOK, &maps.b, kk * 128,
-                                        pol.src_of(d, tg, j) * BS_LIMBS, &bb->bfull);
+                            tma_load_2d(bres + kk * BS_B_STAGE + j * BS_B_TOK, &maps.b[x.mode], kk * 128,
+                                        pol.src_of(x.mode, x.d, x.tg, j) * BS_LIMBS, &bb->bfull);
                     for (int j = 0; j < nt; j++)
-                        bulk_g2s(bwreg + j * pol.bw_bytes(), pol.bsf + (int64_t)pol.src_of(d, tg, j) * pol.g4 * BS_LIMBS,
-                                 pol.bw_bytes(), &bb->bfull);
+                        bulk_g2s(bwreg + j * bwb, P.bsf + (int64_t)pol.src_of(x.mode, x.d, x.tg, j) * P.g4 * BS_LIMBS,
+                                 bwb, &bb->bfull);
                     nbl++;
                     bpend = false;
                 };
+                // the previous unit's MMAs are done (there is none before the first)
                 const uint32_t pprev = (uint32_t)(((q - 1) >> 1) & 1);
-                // the B rows and words come from the previous grid (the limbs kernel,
-                // or gate/up for the down pass): the first unit issues its weight
-                // stages (up to a ring) before waiting for that grid
-                auto wait_dep = [&]() {
-                    asm volatile("griddepcontrol.wait;" ::: "memory");
-                    dep = true;
-                    if (bpend && q == 0) load_b();
+                auto prev_done = [&](bool block) {
+                    return q == 0 || (block ? mbar_wait(&bb->accfull[(q - 1) & 1], pprev)
+                                            : mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev));
                 };
-                const int nchk = k1 - k0;
-                for (int i = 0; i < nchk; i += BS_CH) {
+                // at once where possible: the first unit's B goes out before its A stages
+                if (bpend && prev_done(false) && b_inputs(false)) load_b();
+                const int nchk = x.k1 - x.k0;
+                for (int i = 0, si = 0; i < nchk; i += BS_CH, si++) {
                     const int nch = min(BS_CH, nchk - i);
-                    if (!dep && it >= (uint32_t)nst) wait_dep();
+                    if (bpend && si >= nst) {
+                        // the slot to refill holds a stage of this unit, which the MMAs take
+                        // only after the unit's B: that goes first
+                        if (!prev_done(true)) { bs_fail(pol.err, 23); ok = false; break; }
+                        if (!b_inputs(true)) { bs_fail(pol.err, 30); ok = false; break; }
+                        load_b();
+                    }
                     if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { bs_fail(pol.err, 22); ok = false; break; }
                     mbar_arrive_expect_tx(&bb->full[s], (uint32_t)nch * (BS_A_BYTES + BS_ATOMS));
                     for (int h = 0; h < nch; h++) {
-                        const int k = pol.stage_k(k0, k1, i + h, tile, ks);
+                        const int k = pol.stage_k(x.k0, x.k1, i + h, x.tile, x.ks);
                         uint8_t *st = stages + (size_t)s * BS_STAGE + (size_t)h * BS_A_BYTES;
-                        if (pol.mode == 0) {
-                            tma_box_4d(st, &maps.a0, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
-                            tma_box_4d(st + BS_A_BYTES / 2, &maps.a1, k * 128, tile * 64, e, pol.layer, &bb->full[s]);
+                        if (x.mode == 0) {
+                            tma_box_4d(st, &maps.a[0], k * 128, x.tile * 64, e, pol.layer, &bb->full[s]);
+                            tma_box_4d(st + BS_A_BYTES / 2, &maps.a[1], k * 128, x.tile * 64, e, pol.layer, &bb->full[s]);
                         } else {
-                            tma_box_4d(st, &maps.a0, k * 128, tile * 128, e, pol.layer, &bb->full[s]);
+                            tma_box_4d(st, &maps.a[2], k * 128, x.tile * 128, e, pol.layer, &bb->full[s]);
                         }
-                        bulk_g2s(atoms + ((size_t)s * BS_CH + h) * BS_ATOMS, pol.atoms_of(e, tile, k), BS_ATOMS, &bb->full[s]);
+                        bulk_g2s(atoms + ((size_t)s * BS_CH + h) * BS_ATOMS, pol.atoms_of(x.mode, e, x.tile, k), BS_ATOMS,
+                                 &bb->full[s]);
                     }
                     it++;
                     if (++s == nst) { s = 0; ph ^= 1u; }
-                    if (bpend && dep && q > 0 && mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev)) load_b();
+                    if (bpend && prev_done(false) && b_inputs(false)) load_b();
                 }
-                if (ok && !dep) wait_dep();
                 if (ok && bpend) {
-                    if (!mbar_wait(&bb->accfull[(q - 1) & 1], pprev)) { bs_fail(pol.err, 23); ok = false; break; }
+                    if (!prev_done(true)) { bs_fail(pol.err, 23); ok = false; break; }
+                    if (!b_inputs(true)) { bs_fail(pol.err, 30); ok = false; break; }
                     load_b();
                 }
             }
             if (!ok) bs_fail(pol.err, BS_ERR_PRODUCER);
-            if (!dep) asm volatile("griddepcontrol.wait;" ::: "memory");
             // every copy issued has landed before the CTA may exit (a failed wait is recorded)
             for (int64_t k = (int64_t)it - 1; k >= 0 && k >= (int64_t)it - nst; k--)
                 if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
@@ -462,33 +521,34 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
-        if (lane == 0 && u0 < u1) {
+        if (lane == 0 && nseq > 0) {
             bool ok = true;
-            int s = 0, q = 0;
+            int s = 0;
             uint32_t ph = 0;
             const uint64_t da0 = umma_desc_sw128(smem_u32(stages)), db0 = umma_desc_sw128(smem_u32(bres));
             const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
             const uint64_t dbt0 = umma_desc_plain(smem_u32(batoms), 512, 128);
             int key = -1, ng = 0;
             uint32_t tbb = tb + BS_SFB_COL0;  // the current token group's B scale columns
-            for (int u = u0; u < u1 && ok; u++, q++) {
-                int d, tg, tile, ks, k0, k1;
-                pol.unit(u, d, tg, tile, ks, k0, k1);
-                const int N = BS_LIMBS * pol.ntok(d, tg);
+            for (int q = 0; q < nseq && ok; q++) {
+                BsUnit x;
+                pol.seq_unit(c, q, x);
+                const int N = BS_LIMBS * pol.ntok(x.d, x.tg);
                 const int b = q & 1;
                 // unit q - 2's accumulator handed back: its MMAs, and all before, are done
                 if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 25); ok = false; break; }
-                if ((d | (tg << 16)) != key) {
+                const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
+                if (gkey != key) {
                     // a new token group: its resident B rows, and its B scale atoms of every K
-                    // stage into one of two TMEM buffers; the other may still feed the MMAs of
+                    // chunk into one of two TMEM buffers; the other may still feed the MMAs of
                     // the group before, this one was last read two groups ago, by MMAs of unit
                     // q - 2 or earlier, which the wait above has seen completed
-                    key = d | (tg << 16);
+                    key = gkey;
                     if (!mbar_wait(&bb->bfull, (uint32_t)(ng & 1))) { bs_fail(pol.err, 24); ok = false; break; }
                     if (!mbar_wait(&bb->batfull, (uint32_t)(ng & 1))) { bs_fail(pol.err, 29); ok = false; break; }
                     tc_fence_after();
-                    tbb = tb + BS_SFB_COL0 + (uint32_t)((ng & 1) * 8 * pol.nk);
-                    for (int kk = 0; kk < pol.nk; kk++) {
+                    tbb = tb + BS_SFB_COL0 + (uint32_t)((ng & 1) * 8 * BS_MAX_NK);
+                    for (int kk = 0, nk = pol.pass(x.mode).nk; kk < nk; kk++) {
                         const uint64_t dk = dbt0 + (uint64_t)((kk * BS_BATOMS) >> 4);
                         bs_cp_atom(tbb + 8u * (uint32_t)kk, dk);
                         bs_cp_atom(tbb + 8u * (uint32_t)kk + 4u, dk + 32);
@@ -499,7 +559,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 tc_fence_after();
                 const uint32_t tacc = tb + (uint32_t)(b * BS_ACC_COLS);  // half 1 at + 2 * BS_ACC_COLS
                 const uint32_t id0 = bs_idesc(N, 0), id2 = bs_idesc(N, 2);
-                const int nchk = k1 - k0;
+                const int nchk = x.k1 - x.k0;
                 for (int i = 0; i < nchk; i += BS_CH) {
                     const int nch = min(BS_CH, nchk - i);
                     if (!mbar_wait(&bb->full[s], ph)) { bs_fail(pol.err, 26); ok = false; break; }
@@ -514,7 +574,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                         bs_cp_atom(tsa + 4u, dat + 32);
                     }
                     for (int h = 0; h < nch; h++) {
-                        const int k = pol.stage_k(k0, k1, i + h, tile, ks);
+                        const int k = pol.stage_k(x.k0, x.k1, i + h, x.tile, x.ks);
                         const uint32_t tsa = tb + BS_SFA_COL0 + 8u * (uint32_t)(s * BS_CH + h), tsb = tbb + 8u * (uint32_t)k;
                         // descriptors: the start-address field is the low 14 bits (address >> 4)
                         const uint64_t da = da0 + (uint64_t)(((size_t)s * BS_STAGE + (size_t)h * BS_A_BYTES) >> 4);
@@ -538,26 +598,28 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         }
     } else if (warp == 2) {
         // ------------------------------------------------------ B scale atoms
-        // once per token group, for every K stage: lane = B row (limb lane % 16 of
+        // once per token group, for every K chunk: lane = B row (limb lane % 16 of
         // token lane / 16); after a timed-out wait the warp stops
         bool failed = false;
         int key = -1, ng = 0;
         const int aoff = lane * 16;  // B rows < 32: byte (r % 32) * 16 + kb % 4
-        for (int u = u0; u < u1 && !failed; u++) {
-            int d, tg, tile, ks, k0, k1;
-            pol.unit(u, d, tg, tile, ks, k0, k1);
-            if ((d | (tg << 16)) == key) continue;
-            key = d | (tg << 16);
+        for (int q = 0; q < nseq && !failed; q++) {
+            BsUnit x;
+            pol.seq_unit(c, q, x);
+            const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
+            if (gkey == key) continue;
+            key = gkey;
             if (!mbar_wait(&bb->bfull, (uint32_t)(ng & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 27); break; }
             if (ng >= 1 && !mbar_wait(&bb->batempty, (uint32_t)((ng - 1) & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 28); break; }
             const uint32_t *bw = reinterpret_cast<const uint32_t *>(bwreg);
-            const int nrows = BS_LIMBS * pol.ntok(d, tg);
+            const BsPass P = pol.pass(x.mode);
+            const int nrows = BS_LIMBS * pol.ntok(x.d, x.tg);
             if (lane < nrows) {
-                for (int kk = 0; kk < pol.nk; kk++)
+                for (int kk = 0; kk < P.nk; kk++)
 #pragma unroll
                     for (int h = 0; h < 2; h++)
                         *reinterpret_cast<uint32_t *>(batoms + (size_t)kk * BS_BATOMS + 512 * h + aoff) =
-                            bw[((lane >> 4) * pol.g4 + 2 * kk + h) * BS_LIMBS + (lane & 15)];
+                            bw[((lane >> 4) * P.g4 + 2 * kk + h) * BS_LIMBS + (lane & 15)];
             }
             fence_proxy_async_smem();
             __syncwarp();
@@ -573,20 +635,19 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         // after a timed-out wait a warp stops waiting and computing but keeps
         // taking part in the named barriers, so no other warp is left waiting
         bool failed = false;
-        int q = 0;
-        for (int u = u0; u < u1; u++, q++) {
-            int d, tg, tile, ks, k0, k1;
-            pol.unit(u, d, tg, tile, ks, k0, k1);
-            const int e = pol.ms->list[d];
+        for (int q = 0; q < nseq; q++) {
+            BsUnit x;
+            pol.seq_unit(c, q, x);
+            const int e = pol.ms->list[x.d];
             const uint8_t *eb = pol.expert(e);
-            const int nt = pol.ntok(d, tg), b = q & 1;
+            const int nt = pol.ntok(x.d, x.tg), b = q & 1;
             float bias = 0.f;
-            if (pol.mode == 0) {
-                const int64_t f = (int64_t)tile * 64 + (r & 63);
+            if (x.mode == 0) {
+                const int64_t f = (int64_t)x.tile * 64 + (r & 63);
                 if (f < pol.L.ffn) bias = reinterpret_cast<const float *>(eb + pol.L.off[r < 64 ? 0 : 1][2])[f];
             } else {
-                const int64_t row = (int64_t)tile * 128 + r;
-                if (ks == 0 && row < pol.L.hidden) bias = reinterpret_cast<const float *>(eb + pol.L.off[2][2])[row];
+                const int64_t row = (int64_t)x.tile * 128 + r;
+                if (x.ks == 0 && row < pol.L.hidden) bias = reinterpret_cast<const float *>(eb + pol.L.off[2][2])[row];
             }
             if (!failed && !mbar_wait(&bb->accfull[b], (uint32_t)((q >> 1) & 1))) {
                 failed = true;
@@ -613,32 +674,38 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             tc_fence_before();
             __syncwarp();
             if (lane == 0 && !failed) mbar_arrive(&bb->accempty[b]);
-            if (pol.mode == 0) {
+            if (x.mode == 0) {
                 if (r >= 64)  // up values + up bias
 #pragma unroll
                     for (int j = 0; j < BS_TOKG; j++) ex[(r - 64) * BS_TOKG + j] = __fadd_rn(v[j], bias);
                 named_bar_sync(1, 128);
                 if (r < 64 && !failed) {
-                    const int64_t f = (int64_t)tile * 64 + r;
+                    const int64_t f = (int64_t)x.tile * 64 + r;
                     const bool valid = f < pol.L.ffn;
-                    const int64_t fb = (int64_t)tile * 64 + 32 * ew;  // this warp's block of 32 features
+                    const int64_t fb = (int64_t)x.tile * 64 + 32 * ew;  // this warp's block of 32 features
 #pragma unroll
                     for (int j = 0; j < BS_TOKG; j++) {
                         if (j >= nt) break;  // warp-uniform
-                        const int slot = pol.slot_of(d, tg, j);
+                        const int slot = pol.slot_of(x.d, x.tg, j);
                         const float hv = valid ? bs_act(__fadd_rn(v[j], bias), ex[r * BS_TOKG + j], pol) : 0.f;
                         bs_limbs(hv, pol.hl + (int64_t)slot * BS_LIMBS * pol.hl_ld + fb / 2, pol.hl_ld,
                                  pol.hsf + (((int64_t)slot * pol.hg4 + fb / 128) * BS_LIMBS) * 4 + ((fb / 32) & 3));
                     }
                 }
-                named_bar_sync(1, 128);  // ex is read before the next unit overwrites it
+                named_bar_sync(1, 128);  // ex is read, and this tile's h limbs written, before what follows
+                // the tile is done (also after a failed wait: the error word is set,
+                // and the down units waiting for it end at once)
+                if (r == 0) {
+                    __threadfence();
+                    atomicAdd(pol.sync + 1 + x.v, 1u);
+                }
             } else if (!failed) {
-                const int64_t row = (int64_t)tile * 128 + r;
+                const int64_t row = (int64_t)x.tile * 128 + r;
                 if (row < pol.L.hidden)
 #pragma unroll
                     for (int j = 0; j < BS_TOKG; j++)
                         if (j < nt)
-                            pol.y[((int64_t)ks * pol.n_tok * pol.top_k + pol.slot_of(d, tg, j)) * pol.L.hidden + row] =
+                            pol.y[((int64_t)x.ks * pol.n_tok * pol.top_k + pol.slot_of(x.d, x.tg, j)) * pol.L.hidden + row] =
                                 __fadd_rn(v[j], bias);
             }
         }
@@ -649,6 +716,18 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         tc_fence_after();
         tmem_dealloc(tb, BS_TMEM_COLS);
     }
+    // the last CTA to finish clears the tile counters for the next launch
+    // (which starts after this grid has completed)
+    if (tid == 0) {
+        __threadfence();
+        last_cta = atomicAdd(pol.sync, 1u) == gridDim.x - 1;
+        __threadfence();
+    }
+    __syncthreads();
+    if (last_cta) {
+        for (int i = tid; i < nv; i += BS_THREADS) pol.sync[1 + i] = 0;
+        if (tid == 0) pol.sync[0] = 0;
+    }
 }
 
 // ---------------------------------------------------------- host side
@@ -656,8 +735,11 @@ static int bs_launch(const BsMapsK &maps, BsPol &pol, size_t ssb, cudaStream_t s
     cudaFuncAttributes fa{};
     MG_CUDA(cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(k_bsmoe)));
     ssb = (ssb + 127) & ~(size_t)127;
-    MG_REQUIRE(pol.nk >= 1 && pol.nk <= BS_MAX_NK, MG_ERR_ARG, "block-scaled MoE: K of %d stages unsupported", pol.nk);
-    const size_t fixed = 1024 + (size_t)pol.nk * (BS_B_STAGE + BS_BATOMS) + ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
+    const int nk_max = pol.ps[0].nk > pol.ps[1].nk ? pol.ps[0].nk : pol.ps[1].nk;
+    for (int m = 0; m < 2; m++)
+        MG_REQUIRE(pol.ps[m].nk >= 1 && pol.ps[m].nk <= BS_MAX_NK, MG_ERR_ARG,
+                   "block-scaled MoE: K of %d chunks unsupported", pol.ps[m].nk);
+    const size_t fixed = 1024 + (size_t)nk_max * (BS_B_STAGE + BS_BATOMS) + ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
     const size_t budget = 227 * 1024 - fa.sharedSizeBytes;
     MG_REQUIRE(budget > fixed + 2 * (BS_STAGE + BS_CH * BS_ATOMS), MG_ERR_ARG, "block-scaled MoE: no room for a ring");
     int nst = (int)((budget - fixed) / (BS_STAGE + BS_CH * BS_ATOMS));
@@ -734,8 +816,11 @@ int bs_buffers_init(BsBuffers &b) {
     MG_CUDA(cudaMemset(b.xsf, 0x7F, bs_word_bytes(8, b.kpad_h)));
     MG_CUDA(cudaMemset(b.hl, 0, bs_limb_bytes(b.slots_max, b.kpad_f)));
     MG_CUDA(cudaMemset(b.hsf, 0x7F, bs_word_bytes(b.slots_max, b.kpad_f)));
+    MG_CUDA(cudaMemset(b.sync, 0, bs_sync_bytes()));
     return MG_OK;
 }
+
+size_t bs_sync_bytes() { return (size_t)(1 + BS_MAX_V) * 4; }
 
 int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     const BsBuffers &B = *a.bs;
@@ -743,6 +828,7 @@ int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     MG_REQUIRE(bsmoe_supported(L) && a.maps && a.n_tok >= 1 && a.n_tok <= 8 && a.n_tok * a.top_k <= B.slots_max,
                MG_ERR_ARG, "block-scaled MoE: unsupported call");
     MG_REQUIRE(B.atoms && B.atoms_expert > 0, MG_ERR_STATE, "block-scaled MoE: expert scale atoms not built");
+    MG_REQUIRE(B.sync, MG_ERR_STATE, "block-scaled MoE: no tile counters");
     int *err = stream_error_word();
     MG_REQUIRE(err, MG_ERR_OOM, "block-scaled MoE: no error word");
     {  // activations -> limbs
@@ -766,37 +852,30 @@ int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     p.err = err;
     p.atoms = B.atoms + (int64_t)a.layer * a.n_experts * B.atoms_expert;
     p.atoms_expert = B.atoms_expert;
-    // gate/up: B = the expert's tokens' x limbs, output: their h limbs
-    BsMapsK mg{};
-    mg.a0 = a.maps[0];
-    mg.a1 = a.maps[1];
-    mg.b = B.map_x;
-    p.mode = 0;
-    p.bsf = B.xsf;
-    p.g4 = B.kpad_h / 128;
+    p.sync = B.sync;
+    // one launch, both passes.  gate/up: B = the expert's tokens' x limbs,
+    // output: their h limbs; down: B = the expert's slots' h limbs
+    BsMapsK mk{};
+    for (int i = 0; i < 3; i++) mk.a[i] = a.maps[i];
+    mk.b[0] = B.map_x;
+    mk.b[1] = B.map_h;
+    p.ps[0].bsf = B.xsf;
+    p.ps[0].g4 = B.kpad_h / 128;
+    p.ps[0].nk = B.kpad_h / BS_KE;
+    p.ps[0].atoms_u0 = 0;
+    p.ps[1].bsf = B.hsf;
+    p.ps[1].g4 = B.kpad_f / 128;
+    p.ps[1].nk = B.kpad_f / BS_KE;
+    p.ps[1].atoms_u0 = B.atoms_dn;
     p.hl = B.hl;
     p.hsf = reinterpret_cast<uint8_t *>(B.hsf);
     p.hl_ld = B.kpad_f / 2;
     p.hg4 = B.kpad_f / 128;
-    p.nk = B.kpad_h / BS_KE;
-    p.G = (int)(L.hidden / 32);
-    p.atoms_u0 = 0;
-    BS_TRY(bs_launch(mg, p, (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st));
-    // down: B = the expert's slots' h limbs
-    BsMapsK md{};
-    md.a0 = a.maps[2];
-    md.a1 = a.maps[2];
-    md.b = B.map_h;
-    p.mode = 1;
-    p.bsf = B.hsf;
-    p.g4 = B.kpad_f / 128;
-    p.nk = B.kpad_f / BS_KE;
-    p.G = (int)(L.ffn / 32);
     p.y = a.y;
     p.ks_count = a.down_ksplit_out;
-    p.kst = (p.nk + p.ks_count - 1) / p.ks_count;
-    p.atoms_u0 = B.atoms_dn;
-    return bs_launch(md, p, (size_t)BS_TOKG * p.g4 * BS_LIMBS * 4, st);
+    p.kst = (p.ps[1].nk + p.ks_count - 1) / p.ks_count;
+    const int g4_max = p.ps[0].g4 > p.ps[1].g4 ? p.ps[0].g4 : p.ps[1].g4;
+    return bs_launch(mk, p, (size_t)BS_TOKG * g4_max * BS_LIMBS * 4, st);
 }
 
 }  // namespace mg

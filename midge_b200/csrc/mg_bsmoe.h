@@ -27,6 +27,7 @@ struct BsBuffers {
     uint8_t *atoms;        // expert scale atoms, atoms_expert bytes per (layer, local expert)
     int64_t atoms_expert;  // bytes per expert
     int atoms_dn;          // first down unit of an expert (the gate/up units come first)
+    uint32_t *sync;        // bs_sync_bytes(), zero between launches: per token group, its gate/up tiles done
 };
 
 bool bsmoe_supported(const mg_expert_layout &L);
@@ -35,6 +36,7 @@ size_t bs_limb_bytes(int rows, int kpad);
 size_t bs_word_bytes(int rows, int kpad);
 int bs_map_limbs(CUtensorMap *map, const uint8_t *limbs, int kpad, int rows);
 int bs_buffers_init(BsBuffers &b);
+size_t bs_sync_bytes();
 size_t bs_atoms_bytes(const mg_expert_layout &L, int kpad_h, int kpad_f);  // per expert
 int bs_atoms_build(BsBuffers &b, const mg_expert_layout &L, const uint8_t *experts, int n_layers, int n_local,
                    cudaStream_t st);

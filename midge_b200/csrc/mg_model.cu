@@ -644,6 +644,7 @@ extern "C" int mg_model_ready(mg_model *m) {
         TRY(dalloc(m, &b.xsf, bs_word_bytes(8, b.kpad_h)));
         TRY(dalloc(m, &b.hl, bs_limb_bytes(b.slots_max, b.kpad_f)));
         TRY(dalloc(m, &b.hsf, bs_word_bytes(b.slots_max, b.kpad_f)));
+        TRY(dalloc(m, &b.sync, bs_sync_bytes()));
         TRY(bs_map_limbs(&b.map_x, b.xl, b.kpad_h, 8));
         TRY(bs_map_limbs(&b.map_h, b.hl, b.kpad_f, b.slots_max));
         TRY(bs_buffers_init(b));
