@@ -67,10 +67,6 @@ namespace mg {
         if (_rc != MG_OK) return _rc; \
     } while (0)
 
-typedef CUresult (*BsEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                               const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
 constexpr int BS_LIMBS = 16;                           // B rows (MMA columns) per token
 constexpr int BS_LQ = 12;                              // of which encoded limbs
 constexpr int BS_KE = 256;                             // K values per stage (128 packed bytes)
@@ -95,26 +91,28 @@ static_assert(BS_SFB_COL0 + 2 * 8 * BS_MAX_NK <= BS_TMEM_COLS, "TMEM columns");
 constexpr int BS_MAX_V = 4 * SW_MAX_SLOTS;             // token groups (experts x up to 4)
 // error word codes of a timed-out wait, by role (beside the streamed kernels' 1)
 constexpr int BS_ERR_PRODUCER = 11, BS_ERR_MMA = 12, BS_ERR_ATOMS = 13, BS_ERR_EPILOGUE = 14, BS_ERR_DRAIN = 15;
-// the first failure is kept (21.. name the wait that gave up: producer 21 B words consumed, 22 ring stage,
-// 23 accumulator before a B reload; MMA 24 B rows, 25 accumulator buffer, 26 stage, 29 B atoms built;
-// atoms 27 B rows + words, 28 previous B atoms copied)
+// the first failure is kept (21.. name the wait that gave up: producer 22 ring stage; MMA 24 B ready,
+// 25 accumulator buffer, 26 stage; stager 27 previous group's MMAs, 30 a down group's gate/up tiles)
 __device__ __forceinline__ void bs_fail(int *err, int code) { atomicCAS(err, 0, code); }
 
 struct BsBars {
     uint64_t full[BS_MAX_STAGES], empty[BS_MAX_STAGES];
     uint64_t accfull[2], accempty[2];
-    uint64_t bfull;     // the token group's resident B rows and B scale words have landed
-    uint64_t bwempty;   // the B-atom warp has read the group's scale words
-    uint64_t batfull;   // the group's B atoms (all K stages) are built in shared memory
-    uint64_t batempty;  // the MMA issuer's copies of them into TMEM have completed
-    uint64_t done;   // the MMA issuer's last commit: no MMA is in flight when TMEM is released
+    uint64_t bready;  // the token group's B rows and B atoms (all K chunks) are in shared memory
+    uint64_t bfree;   // the MMAs of the token group's last unit are done: its B may be replaced
+    uint64_t done;    // the MMA issuer's last commit: no MMA is in flight when TMEM is released
     uint32_t tmem;
 };
 
 struct BsMapsK {
     CUtensorMap a[3];  // A boxes: gate, up (64 rows each), down (128 rows)
-    CUtensorMap b[2];  // B rows: x limbs (gate/up), h limbs (down)
 };
+
+// 16-byte global -> shared copy (L2 only), completed by cp.async.wait_all
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // shared-memory matrix descriptor, no swizzle (the scale atoms: 8-row core
 // matrices of 16-byte rows, 128 B apart; one core matrix along K)
@@ -245,7 +243,9 @@ __global__ void k_bs_atoms(const uint8_t *experts, mg_expert_layout L, int64_t n
 // ---------------------------------------------------------- routed experts
 // the parameters of one pass (0 gate/up, 1 down)
 struct BsPass {
-    const uint32_t *bsf;  // B scale words [src][g4][16] (src: token for gate/up, slot for down)
+    const uint8_t *limbs; // B limb rows [src * 16 + l][ld] (src: token for gate/up, slot for down)
+    int64_t ld;           // bytes per limb row
+    const uint32_t *bsf;  // B scale words [src][g4][16]
     int g4;               // scale words per B row and limb
     int nk;               // K chunks of an A row
     int atoms_u0;         // first atom of the pass within an expert (0 gate/up, atoms_dn down)
@@ -366,19 +366,22 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     BsBars *bb = reinterpret_cast<BsBars *>(ex + 64 * BS_TOKG);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ int vlist[BS_MAX_V];
-    __shared__ int nv_sh, last_cta;
+    __shared__ int nv_sh, last_cta, stage_ok;
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < 3; i++) tma_prefetch_map(&maps.a[i]);
+    }
     // barriers and TMEM first: they overlap the routing-slot loads of build_list
     if (warp == 2) {
         if (lane < nst) {
             mbar_init(&bb->full[lane], 1);  // the producer's expect-tx arrival: A tiles + A atoms
             mbar_init(&bb->empty[lane], 1);
-        } else if (lane >= 16 && lane < 18) {
-            mbar_init(lane == 16 ? &bb->batfull : &bb->batempty, 1);
         } else if (lane >= 18 && lane < 20) {
             mbar_init(&bb->accfull[lane - 18], 1);
             mbar_init(&bb->accempty[lane - 18], 4);
         } else if (lane == 20) {
-            mbar_init(&bb->bfull, 1);
+            mbar_init(&bb->bready, 1);
+            mbar_init(&bb->bfree, 1);
         } else if (lane == 21) {
             mbar_init(&bb->done, 1);
         }
@@ -432,63 +435,18 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
 
     if (warp == 0) {
         // ------------------------------------------------------ producer
+        // the A stages of the CTA's units, back to back through the ring
         if (lane == 0 && nseq > 0) {
             bool ok = true;
-            int s = 0, key = -1, nbl = 0;
+            int s = 0;
             uint32_t ph = 0, it = 0;
-            // the x limbs come from the previous grid, which has finished by
-            // the time the setup above is done: the first B rows go out first
-            asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int q = 0; q < nseq && ok; q++) {
                 BsUnit x;
                 pol.seq_unit(c, q, x);
                 const int e = pol.ms->list[x.d];
-                const int nt = pol.ntok(x.d, x.tg);
-                // a new token group (or pass): its B rows and B scale words replace the
-                // resident ones once the previous unit's MMAs are done (polled while this
-                // unit's A stages stream, waited for otherwise).  Those MMAs read the
-                // group's B atoms, which the B-atom warp built from the old words before
-                // it released them, so the words are free as well.  A down group's B rows
-                // are the h limbs of its slots, written by the group's gate/up tiles on
-                // any SM: each tile counts itself done in sync[1 + v].
-                const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
-                bool bpend = gkey != key;
-                key = gkey;
-                auto b_inputs = [&](bool block) {
-                    return x.mode == 0 || bs_tiles_done(pol.sync + 1 + x.v, tiles_need, block);
-                };
-                auto load_b = [&]() {
-                    const BsPass P = pol.pass(x.mode);
-                    const uint32_t bwb = pol.bw_bytes(x.mode);
-                    mbar_arrive_expect_tx(&bb->bfull, (uint32_t)(nt * P.nk * BS_B_TOK) + (uint32_t)nt * bwb);
-                    for (int kk = 0; kk < P.nk; kk++)
-                        for (int j = 0; j < nt; j++)
-                            tma_load_2d(bres + kk * BS_B_STAGE + j * BS_B_TOK, &maps.b[x.mode], kk * 128,
-                                        pol.src_of(x.mode, x.d, x.tg, j) * BS_LIMBS, &bb->bfull);
-                    for (int j = 0; j < nt; j++)
-                        bulk_g2s(bwreg + j * bwb, P.bsf + (int64_t)pol.src_of(x.mode, x.d, x.tg, j) * P.g4 * BS_LIMBS,
-                                 bwb, &bb->bfull);
-                    nbl++;
-                    bpend = false;
-                };
-                // the previous unit's MMAs are done (there is none before the first)
-                const uint32_t pprev = (uint32_t)(((q - 1) >> 1) & 1);
-                auto prev_done = [&](bool block) {
-                    return q == 0 || (block ? mbar_wait(&bb->accfull[(q - 1) & 1], pprev)
-                                            : mbar_try_wait(&bb->accfull[(q - 1) & 1], pprev));
-                };
-                // at once where possible: the first unit's B goes out before its A stages
-                if (bpend && prev_done(false) && b_inputs(false)) load_b();
                 const int nchk = x.k1 - x.k0;
-                for (int i = 0, si = 0; i < nchk; i += BS_CH, si++) {
+                for (int i = 0; i < nchk; i += BS_CH) {
                     const int nch = min(BS_CH, nchk - i);
-                    if (bpend && si >= nst) {
-                        // the slot to refill holds a stage of this unit, which the MMAs take
-                        // only after the unit's B: that goes first
-                        if (!prev_done(true)) { bs_fail(pol.err, 23); ok = false; break; }
-                        if (!b_inputs(true)) { bs_fail(pol.err, 30); ok = false; break; }
-                        load_b();
-                    }
                     if (it >= (uint32_t)nst && !mbar_wait(&bb->empty[s], ph ^ 1u)) { bs_fail(pol.err, 22); ok = false; break; }
                     mbar_arrive_expect_tx(&bb->full[s], (uint32_t)nch * (BS_A_BYTES + BS_ATOMS));
                     for (int h = 0; h < nch; h++) {
@@ -505,19 +463,12 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     }
                     it++;
                     if (++s == nst) { s = 0; ph ^= 1u; }
-                    if (bpend && prev_done(false) && b_inputs(false)) load_b();
-                }
-                if (ok && bpend) {
-                    if (!prev_done(true)) { bs_fail(pol.err, 23); ok = false; break; }
-                    if (!b_inputs(true)) { bs_fail(pol.err, 30); ok = false; break; }
-                    load_b();
                 }
             }
             if (!ok) bs_fail(pol.err, BS_ERR_PRODUCER);
             // every copy issued has landed before the CTA may exit (a failed wait is recorded)
             for (int64_t k = (int64_t)it - 1; k >= 0 && k >= (int64_t)it - nst; k--)
                 if (!mbar_wait(&bb->full[k % nst], (uint32_t)((k / nst) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
-            if (nbl > 0 && !mbar_wait(&bb->bfull, (uint32_t)((nbl - 1) & 1))) bs_fail(pol.err, BS_ERR_DRAIN);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
@@ -539,13 +490,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 25); ok = false; break; }
                 const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
                 if (gkey != key) {
-                    // a new token group: its resident B rows, and its B scale atoms of every K
-                    // chunk into one of two TMEM buffers; the other may still feed the MMAs of
-                    // the group before, this one was last read two groups ago, by MMAs of unit
-                    // q - 2 or earlier, which the wait above has seen completed
+                    // a new token group: its B rows, and its B scale atoms of every K chunk into
+                    // one of two TMEM buffers (the stager has seen the previous group's MMAs
+                    // complete before it rebuilt them)
                     key = gkey;
-                    if (!mbar_wait(&bb->bfull, (uint32_t)(ng & 1))) { bs_fail(pol.err, 24); ok = false; break; }
-                    if (!mbar_wait(&bb->batfull, (uint32_t)(ng & 1))) { bs_fail(pol.err, 29); ok = false; break; }
+                    if (!mbar_wait(&bb->bready, (uint32_t)(ng & 1))) { bs_fail(pol.err, 24); ok = false; break; }
                     tc_fence_after();
                     tbb = tb + BS_SFB_COL0 + (uint32_t)((ng & 1) * 8 * BS_MAX_NK);
                     for (int kk = 0, nk = pol.pass(x.mode).nk; kk < nk; kk++) {
@@ -553,7 +502,6 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                         bs_cp_atom(tbb + 8u * (uint32_t)kk, dk);
                         bs_cp_atom(tbb + 8u * (uint32_t)kk + 4u, dk + 32);
                     }
-                    tc_commit(&bb->batempty);  // the shared-memory atoms may be rebuilt once these copies are done
                     ng++;
                 }
                 tc_fence_after();
@@ -590,45 +538,91 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                     tc_commit(&bb->empty[s]);
                     if (++s == nst) { s = 0; ph ^= 1u; }
                 }
-                if (ok) tc_commit(&bb->accfull[b]);
+                if (!ok) break;
+                tc_commit(&bb->accfull[b]);
+                // the group's last unit: its B rows and atoms are free once these MMAs are
+                // done (one phase per group, so the stager's parity waits cannot alias)
+                bool last = q + 1 == nseq;
+                if (!last) {
+                    BsUnit y;
+                    pol.seq_unit(c, q + 1, y);
+                    last = (y.d | (y.tg << 16) | (y.mode << 30)) != gkey;
+                }
+                if (last) tc_commit(&bb->bfree);
             }
             if (!ok) bs_fail(pol.err, BS_ERR_MMA);
             tc_commit(&bb->done);
             if (!mbar_wait(&bb->done, 0)) bs_fail(pol.err, BS_ERR_MMA);
         }
-    } else if (warp == 2) {
-        // ------------------------------------------------------ B scale atoms
-        // once per token group, for every K chunk: lane = B row (limb lane % 16 of
-        // token lane / 16); after a timed-out wait the warp stops
+    } else if (warp < 6) {
+        // ------------------------------------------------------ B stager
+        // warps 2-5, once per token group: after the previous group's MMAs (and, for
+        // a down group, its gate/up tiles) are done, the group's B rows (12 limbs per
+        // token and K chunk, 16-byte async copies into the 128-byte-swizzled layout)
+        // and B scale words from L2, then the B atoms of every K chunk from the
+        // words (lane = B row); after a timed-out wait all four warps stop
+        const int t = tid - 64;
+        const uint32_t *bw = reinterpret_cast<const uint32_t *>(bwreg);
+        // limb rows 12..15 of both token slots stay zero (never copied)
+        for (int i = t; i < nk_max * BS_TOKG * (BS_LIMBS - BS_LQ) * 8; i += 128) {
+            const int r = BS_LQ + (i >> 3) % (BS_LIMBS - BS_LQ), jk = (i >> 3) / (BS_LIMBS - BS_LQ);
+            *reinterpret_cast<uint4 *>(bres + (size_t)(jk >> 1) * BS_B_STAGE + (jk & 1) * BS_B_TOK + r * 128 +
+                                       (i & 7) * 16) = make_uint4(0, 0, 0, 0);
+        }
         bool failed = false;
         int key = -1, ng = 0;
-        const int aoff = lane * 16;  // B rows < 32: byte (r % 32) * 16 + kb % 4
         for (int q = 0; q < nseq && !failed; q++) {
             BsUnit x;
             pol.seq_unit(c, q, x);
             const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
             if (gkey == key) continue;
             key = gkey;
-            if (!mbar_wait(&bb->bfull, (uint32_t)(ng & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 27); break; }
-            if (ng >= 1 && !mbar_wait(&bb->batempty, (uint32_t)((ng - 1) & 1))) { failed = true; if (lane == 0) bs_fail(pol.err, 28); break; }
-            const uint32_t *bw = reinterpret_cast<const uint32_t *>(bwreg);
+            if (t == 0) {
+                bool okw = true;
+                if (ng > 0 && !mbar_wait(&bb->bfree, (uint32_t)((ng - 1) & 1))) {
+                    okw = false;
+                    bs_fail(pol.err, 27);
+                }
+                if (okw && x.mode == 1 && !bs_tiles_done(pol.sync + 1 + x.v, tiles_need, true)) {
+                    okw = false;
+                    bs_fail(pol.err, 30);
+                }
+                stage_ok = okw;
+            }
+            named_bar_sync(2, 128);
+            if (!stage_ok) {
+                failed = true;
+                break;
+            }
             const BsPass P = pol.pass(x.mode);
-            const int nrows = BS_LIMBS * pol.ntok(x.d, x.tg);
-            if (lane < nrows) {
-                for (int kk = 0; kk < P.nk; kk++)
+            const int nt = pol.ntok(x.d, x.tg);
+            const int src0 = pol.src_of(x.mode, x.d, x.tg, 0), src1 = nt > 1 ? pol.src_of(x.mode, x.d, x.tg, 1) : src0;
+            for (int i = t, n = P.nk * nt * BS_LQ * 8; i < n; i += 128) {
+                const int c16 = i & 7, l = (i >> 3) % BS_LQ, r = (i >> 3) / BS_LQ, j = r % nt, kk = r / nt;
+                const int row = BS_LIMBS * (j ? src1 : src0) + l;
+                cp_async16(bres + (size_t)kk * BS_B_STAGE + (j * BS_LIMBS + l) * 128 + ((c16 ^ (l & 7)) << 4),
+                           P.limbs + row * P.ld + kk * 128 + c16 * 16);
+            }
+            const int wv = P.g4 * BS_LIMBS / 4;  // 16-byte vectors of a token's words
+            for (int i = t; i < nt * wv; i += 128) {
+                const int j = i / wv, o = i - j * wv;
+                cp_async16(bwreg + (size_t)i * 16, P.bsf + ((int64_t)(j ? src1 : src0) * P.g4 * BS_LIMBS + o * 4));
+            }
+            cp_async_wait_all();
+            named_bar_sync(2, 128);  // every thread's words have landed
+            const int nrows = BS_LIMBS * nt;
+            if (lane < nrows)
+                for (int kk = warp - 2; kk < P.nk; kk += 4)
 #pragma unroll
                     for (int h = 0; h < 2; h++)
-                        *reinterpret_cast<uint32_t *>(batoms + (size_t)kk * BS_BATOMS + 512 * h + aoff) =
+                        *reinterpret_cast<uint32_t *>(batoms + (size_t)kk * BS_BATOMS + 512 * h + lane * 16) =
                             bw[((lane >> 4) * P.g4 + 2 * kk + h) * BS_LIMBS + (lane & 15)];
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bb->batfull);
+            fence_proxy_async_smem();  // the rows and atoms, for the tensor core's reads
+            named_bar_sync(2, 128);
+            if (t == 0) mbar_arrive(&bb->bready);
             ng++;
         }
-        if (failed && lane == 0) bs_fail(pol.err, BS_ERR_ATOMS);
-    } else if (warp < 6) {
-        // warps 3-5: no role after setup
+        if (failed && t == 0) bs_fail(pol.err, BS_ERR_ATOMS);
     } else {
         // ------------------------------------------------------ epilogue
         const int ew = warp & 3, r = 32 * ew + lane;  // TMEM lane quadrant = warp % 4
@@ -775,20 +769,6 @@ int bs_kpad(int64_t k) { return (int)((k + BS_KE - 1) / BS_KE * BS_KE); }
 size_t bs_limb_bytes(int rows, int kpad) { return (size_t)rows * BS_LIMBS * (kpad / 2); }
 size_t bs_word_bytes(int rows, int kpad) { return (size_t)rows * (kpad / 128) * BS_LIMBS * 4; }
 
-int bs_map_limbs(CUtensorMap *map, const uint8_t *limbs, int kpad, int rows) {
-    BsEncodeFn fn = reinterpret_cast<BsEncodeFn>(encode_tiled_fn());
-    MG_REQUIRE(fn, MG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)(kpad / 2), (cuuint64_t)rows * BS_LIMBS};
-    cuuint64_t strides[1] = {(cuuint64_t)(kpad / 2)};
-    cuuint32_t box[2] = {128, (cuuint32_t)BS_LIMBS};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(limbs), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    MG_REQUIRE(r == CUDA_SUCCESS, MG_ERR_CUDA, "block-scaled MoE: limb tensor map failed (%d)", (int)r);
-    return MG_OK;
-}
-
 size_t bs_atoms_bytes(const mg_expert_layout &L, int kpad_h, int kpad_f) {
     const int64_t units = (L.ffn / 64) * (kpad_h / BS_KE) + ((L.hidden + 127) / 128) * (kpad_f / BS_KE);
     return (size_t)units * 1024;
@@ -857,12 +837,14 @@ int moe_bs(const MoeStreamArgs &a, cudaStream_t st) {
     // output: their h limbs; down: B = the expert's slots' h limbs
     BsMapsK mk{};
     for (int i = 0; i < 3; i++) mk.a[i] = a.maps[i];
-    mk.b[0] = B.map_x;
-    mk.b[1] = B.map_h;
+    p.ps[0].limbs = B.xl;
+    p.ps[0].ld = B.kpad_h / 2;
     p.ps[0].bsf = B.xsf;
     p.ps[0].g4 = B.kpad_h / 128;
     p.ps[0].nk = B.kpad_h / BS_KE;
     p.ps[0].atoms_u0 = 0;
+    p.ps[1].limbs = B.hl;
+    p.ps[1].ld = B.kpad_f / 2;
     p.ps[1].bsf = B.hsf;
     p.ps[1].g4 = B.kpad_f / 128;
     p.ps[1].nk = B.kpad_f / BS_KE;

@@ -17,8 +17,6 @@ namespace mg {
 // stages][1024 B], then the down units' [ceil(hidden/128)][kpad_f/256][1024 B]
 // (bs_atoms_build, once the experts are loaded).
 struct BsBuffers {
-    CUtensorMap map_x;     // x limbs, box 128 B x 16 rows
-    CUtensorMap map_h;     // h limbs, box 128 B x 16 rows
     uint8_t *xl;           // [8 tokens * 16][kpad_h/2] packed e2m1 limbs
     uint32_t *xsf;         // [8 tokens][kpad_h/128][16] scale words
     uint8_t *hl;           // [slots_max * 16][kpad_f/2]
@@ -34,7 +32,6 @@ bool bsmoe_supported(const mg_expert_layout &L);
 int bs_kpad(int64_t k);  // K rounded up to the 256-value stage
 size_t bs_limb_bytes(int rows, int kpad);
 size_t bs_word_bytes(int rows, int kpad);
-int bs_map_limbs(CUtensorMap *map, const uint8_t *limbs, int kpad, int rows);
 int bs_buffers_init(BsBuffers &b);
 size_t bs_sync_bytes();
 size_t bs_atoms_bytes(const mg_expert_layout &L, int kpad_h, int kpad_f);  // per expert

@@ -645,8 +645,6 @@ extern "C" int mg_model_ready(mg_model *m) {
         TRY(dalloc(m, &b.hl, bs_limb_bytes(b.slots_max, b.kpad_f)));
         TRY(dalloc(m, &b.hsf, bs_word_bytes(b.slots_max, b.kpad_f)));
         TRY(dalloc(m, &b.sync, bs_sync_bytes()));
-        TRY(bs_map_limbs(&b.map_x, b.xl, b.kpad_h, 8));
-        TRY(bs_map_limbs(&b.map_h, b.hl, b.kpad_f, b.slots_max));
         TRY(bs_buffers_init(b));
         // the experts' scales as the tensor core reads them (one atom copy)
         TRY(dalloc(m, &b.atoms, (size_t)s.n_layers * m->n_local * bs_atoms_bytes(m->el, b.kpad_h, b.kpad_f)));

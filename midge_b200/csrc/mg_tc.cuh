@@ -119,18 +119,10 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// L2 prefetch of a 4-D tensor tile (no shared memory, no completion to wait
-// for): raises the bytes in flight beyond a shared-memory ring.  The innermost
-// coordinate obeys the same 16-byte rule as the loads.
-__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap *map, int x, int y, int z, int w) {
-    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(map), "r"(x), "r"(y),
-                 "r"(z), "r"(w)
-                 : "memory");
-}
-
-// L2 prefetch of a contiguous range (16-byte aligned address, size a multiple of 16)
-__device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// the TMA unit's copy of a tensor map (a __grid_constant__ parameter) fetched
+// ahead of its first use, so the first copies do not wait for it
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 }  // namespace mg
