@@ -588,10 +588,14 @@ extern "C" int mg_model_ready(mg_model *m) {
     TRY(dalloc(m, &m->tmp_v, (size_t)R * kv_dim * 2));
     TRY(dalloc(m, &m->usage, (size_t)s.n_layers * s.n_experts * 4));
     MG_CUDA(cudaMemset(m->usage, 0, (size_t)s.n_layers * s.n_experts * 4));
-    // streamed decode buffers (K splits sized for ~3 units per SM)
+    // streamed decode buffers.  K splits: about one unit (row tile x split)
+    // per SM; a unit's fixed cost (the two warps' hand-over, epilogue and the
+    // next unit's first wait, ~2 us measured at 8 tokens) outweighs its share
+    // of the weight stream when a CTA takes several short units.
     const int qkv_dim = q_dim + 2 * kv_dim;
-    m->ks_qkv = stream_ksplit(MG_Q8R, H, 12);
-    m->ks_o = stream_ksplit(MG_Q8R, q_dim, 6);
+    const int tiles_qkv = (int)((q_dim + 127) / 128 + 2 * ((kv_dim + 127) / 128)), tiles_o = (int)((H + 127) / 128);
+    m->ks_qkv = stream_ksplit(MG_Q8R, H, std::max(1, num_sms() / tiles_qkv));
+    m->ks_o = stream_ksplit(MG_Q8R, q_dim, std::max(1, num_sms() / tiles_o));
     m->ks_down = moe_down_ksplit(m->el, 2);
     MG_CUDA(cudaHostAlloc(&m->h_err, sizeof(int), cudaHostAllocDefault));
     *m->h_err = 0;

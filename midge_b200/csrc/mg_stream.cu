@@ -46,7 +46,7 @@ int stream_ksplit(int dt, int64_t cols, int want) {
     return (int)((nseg + sps - 1) / sps);
 }
 
-// Shared memory: [alignment slack][barriers][ring of nstages][2 scale slots of
+// Shared memory: [alignment slack][barriers][ring of nstages][sw_nslot scale slots of
 // ssb bytes][partial-sum hand-over][activations].  Scale slots are dropped (ssb = 0: per-lane scale
 // loads) when they would leave fewer than 4 ring stages.
 template <int DT, class P>
@@ -57,12 +57,13 @@ static int launch_policy(void (*kfn)(SwMaps, P, int, int, int *), const SwMaps &
     const size_t budget = 227 * 1024 - fa.sharedSizeBytes - 1024;  // static shared memory and the alignment slack
     ssb = (ssb + 127) & ~(size_t)127;
     xs_bytes += SW_RED_BYTES;  // the partial-sum hand-over sits just before the activations
-    if (ssb && budget < 1024 + xs_bytes + 2 * ssb + 4 * (size_t)SW_STAGE_BYTES) ssb = 0;
-    MG_REQUIRE(budget > 1024 + xs_bytes + 2 * ssb, MG_ERR_ARG, "streamed kernel: activations leave no room for a ring");
-    int nstages = (int)((budget - 1024 - xs_bytes - 2 * ssb) / SW_STAGE_BYTES);
+    constexpr size_t NS = sw_nslot(DT);
+    if (ssb && budget < 1024 + xs_bytes + NS * ssb + 4 * (size_t)SW_STAGE_BYTES) ssb = 0;
+    MG_REQUIRE(budget > 1024 + xs_bytes + NS * ssb, MG_ERR_ARG, "streamed kernel: activations leave no room for a ring");
+    int nstages = (int)((budget - 1024 - xs_bytes - NS * ssb) / SW_STAGE_BYTES);
     if (nstages > SW_MAX_STAGES) nstages = SW_MAX_STAGES;
     MG_REQUIRE(nstages >= 2, MG_ERR_ARG, "streamed kernel: activations leave no room for a ring");
-    const size_t smem = 1024 + 1024 + (size_t)nstages * SW_STAGE_BYTES + 2 * ssb + xs_bytes;
+    const size_t smem = 1024 + 1024 + (size_t)nstages * SW_STAGE_BYTES + NS * ssb + xs_bytes;
     int rc = ensure_smem_attr(reinterpret_cast<const void *>(kfn), smem);
     if (rc) return rc;
     int *err = sw_err_ptr();
@@ -113,7 +114,13 @@ static int launch_stream_gemv(const StreamGemvArgs &a, cudaStream_t st) {
     // scale slots need every matrix's scale blob 16-byte aligned and a whole
     // number of 16-byte pieces long (the last tile's copy ends at the blob's end)
     size_t ssb = 0;
-    if (DT != MG_Q8R) {
+    if (DT == MG_Q8R) {  // row scales (+ biases) through the scale slots: 16-byte aligned, rows % 4 == 0
+        bool fits = true;
+        for (int i = 0; i < a.nmat; i++)
+            fits = fits && (reinterpret_cast<uintptr_t>(a.mat[i].scales) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.mat[i].bias) & 15) == 0 && a.mat[i].rows % 4 == 0;
+        if (fits) ssb = (size_t)SW_ROWS * 4 * 2;
+    } else {
         const int64_t sb = SC == MG_SCALE_UE8M0 ? 1 : 2;
         bool fits = true;
         for (int i = 0; i < a.nmat; i++)

@@ -34,6 +34,11 @@ constexpr int SW_BAR_PAIR0 = 4;               // named barriers 4..11: the two w
 constexpr int SW_RED_BYTES = SW_RG * 32 * 8 * 4;  // hand-over of partial sums (NT <= 2)
 constexpr int SW_MAX_STAGES = 12;
 constexpr int SW_ERR_TIMEOUT = 1;
+constexpr int SW_SCALE_SLOTS = 8;
+// per-unit scale slots: 4-bit weights carry the tile's group scales (tens of
+// KB: two slots); int8 only its row scales and biases (1 KB: eight, so that
+// the producer runs as far ahead as the ring allows)
+__host__ __device__ constexpr int sw_nslot(int dt) { return dt == MG_Q8R ? SW_SCALE_SLOTS : 2; }
 constexpr int SW_SEGB = 128;                  // bytes of each row per stage: one 128-byte swizzle row
 constexpr int SW_STAGE_BYTES = SW_ROWS * SW_SEGB;  // 16 KB: one TMA box of 128 rows x 128 B
 
@@ -57,7 +62,7 @@ struct SwMaps {
 struct SwShared {
     uint64_t full[SW_MAX_STAGES];
     uint64_t empty[SW_MAX_STAGES];
-    uint64_t sfull[2], sempty[2];  // the two per-unit scale slots
+    uint64_t sfull[SW_SCALE_SLOTS], sempty[SW_SCALE_SLOTS];  // the per-unit scale slots (sw_nslot of them)
 };
 
 // Group scales of 4-bit weights: when the launch gives scale slots (ssb > 0),
@@ -98,8 +103,9 @@ __device__ void sw_producer(const P &pol, const SwMaps &maps, int64_t u0, int64_
         pol.unit(u, ui);
         if (ssb) {
             const int64_t j = u - u0;
-            const int slot = (int)(j & 1);
-            if (j >= 2 && !mbar_wait(&sh->sempty[slot], (uint32_t)(((j >> 1) - 1) & 1))) {
+            constexpr int NS = sw_nslot(DT);
+            const int slot = (int)(j % NS);
+            if (j >= NS && !mbar_wait(&sh->sempty[slot], (uint32_t)(((j / NS) - 1) & 1))) {
                 ok = false;
                 break;
             }
@@ -122,8 +128,9 @@ __device__ void sw_producer(const P &pol, const SwMaps &maps, int64_t u0, int64_
     // success: the consumers waited for all of them)
     for (int64_t k = it - 1; k >= 0 && k >= it - nstages; k--)
         if (!mbar_wait(&sh->full[k % nstages], (uint32_t)((k / nstages) & 1))) atomicExch(err, SW_ERR_TIMEOUT);
-    for (int64_t j = nu - 1; j >= 0 && j >= nu - 2; j--)
-        if (!mbar_wait(&sh->sfull[j & 1], (uint32_t)((j >> 1) & 1))) atomicExch(err, SW_ERR_TIMEOUT);
+    constexpr int NS = sw_nslot(DT);
+    for (int64_t j = nu - 1; j >= 0 && j >= nu - NS; j--)
+        if (!mbar_wait(&sh->sfull[j % NS], (uint32_t)((j / NS) & 1))) atomicExch(err, SW_ERR_TIMEOUT);
 }
 
 // -------------------------------------------------------------- consumer
@@ -317,10 +324,11 @@ __device__ __forceinline__ void sw_consumers(P &pol, int64_t u0, int64_t u1, uin
             for (int i = 0; i < 4; i++) acc[nt][i] = 0.f;
         const bool live = pol.warp_live(ui, w);
         const uint8_t *pa = nullptr, *pb = nullptr;
-        const int slot = (int)((u - u0) & 1);
+        constexpr int NS = sw_nslot(DT);
+        const int slot = (int)((u - u0) % NS);
         if (ssb && !failed) {
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(&sh->sfull[slot], (uint32_t)(((u - u0) >> 1) & 1));
+            if (lane == 0) ok = mbar_wait(&sh->sfull[slot], (uint32_t)(((u - u0) / NS) & 1));
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
                 if (lane == 0) atomicExch(err, SW_ERR_TIMEOUT);
@@ -389,8 +397,8 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant_
     uint8_t *sw_smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sw_smem_raw) + 1023) & ~(uintptr_t)1023);
     SwShared *sh = reinterpret_cast<SwShared *>(sw_smem);
     uint8_t *ring = sw_smem + 1024;  // stages 1024-aligned for the 128-byte swizzle
-    uint8_t *ss = ring + (size_t)nstages * SW_STAGE_BYTES;  // 2 scale slots of ssb bytes (ssb % 128 == 0)
-    float *red = reinterpret_cast<float *>(ss + 2 * (size_t)ssb);  // SW_RG x 32 lanes x NT*4 partial sums
+    uint8_t *ss = ring + (size_t)nstages * SW_STAGE_BYTES;  // sw_nslot scale slots of ssb bytes (ssb % 128 == 0)
+    float *red = reinterpret_cast<float *>(ss + sw_nslot(DT) * (size_t)ssb);  // SW_RG x 32 lanes x NT*4 partial sums
     __half *xs = reinterpret_cast<__half *>(reinterpret_cast<uint8_t *>(red) + SW_RED_BYTES);
     const int xs_stride = pol.xs_stride();
     pol.init_shared();  // all threads; ends with __syncthreads
@@ -402,7 +410,7 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant_
             mbar_init(&sh->full[s], 1);
             mbar_init(&sh->empty[s], SW_RG);  // the row-group warps that took the stage
         }
-        for (int s = 0; s < 2; s++) {
+        for (int s = 0; s < sw_nslot(DT); s++) {
             mbar_init(&sh->sfull[s], 1);
             mbar_init(&sh->sempty[s], SW_CONS);
         }
@@ -414,7 +422,7 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant_
     if (w == SW_CONS) {
         sw_producer<DT>(pol, maps, u0, u1, ring, nstages, ss, ssb, sh, err);
     } else {
-        pol.stage_x(u0, xs, xs_stride);
+        pol.stage_x_units(u0, u1, xs, xs_stride);
         named_bar_sync(1, SW_CONS * 32);
         sw_consumers<DT, SC, NT>(pol, u0, u1, ring, nstages, ss, ssb, red, sh, xs, xs_stride, err);
     }
@@ -517,8 +525,10 @@ struct PolGemv {
         return k;
     }
     __device__ void unit(int64_t u, UnitInfo &ui) const {
-        ui.tile = u / ks_count;
-        ui.ks = (int)(u % ks_count);
+        // K-split-major: a CTA's consecutive units share a K split (and so the
+        // activation columns it stages)
+        ui.ks = (int)(u / ntiles);
+        ui.tile = u - (int64_t)ui.ks * ntiles;
         ui.b0 = (int64_t)ui.ks * kbytes_per_split;
         ui.b1 = min(rowbytes(), ui.b0 + kbytes_per_split);
         ui.aux = mat_of(ui.tile);
@@ -541,13 +551,25 @@ struct PolGemv {
         if (SC == MG_SCALE_UE8M0) return ue8m0_to_f32(__ldg(sc + row * gpr + grp));
         return h2f(__ldg(reinterpret_cast<const uint16_t *>(sc) + row * gpr + grp));
     }
-    // unit scales: the tile's rows, whole rows (every K split reads all of them)
+    // Unit scales.  4-bit: the tile's rows' group scales, whole rows (every K
+    // split reads all of them).  int8: the rows' f32 scales at +0 and, in K
+    // split 0 of a matrix with a bias, the rows' biases at +SW_ROWS*4, read by
+    // the epilogue from shared memory (the launch gives int8 slots only when
+    // both arrays are 16-byte aligned and every matrix has rows % 4 == 0).
     static constexpr int SB = SC == MG_SCALE_UE8M0 ? 1 : 2;
+    __device__ bool slot_bias(const UnitInfo &ui) const { return MG_SEL(ui.aux, bias) != nullptr && ui.ks == 0; }
     __device__ uint32_t scale_bytes(const UnitInfo &ui) const {
         const int64_t nr = min((int64_t)SW_ROWS, MG_SEL(ui.aux, rows) - row0(ui));
+        if (DT == MG_Q8R) return (uint32_t)(nr * 4) * (slot_bias(ui) ? 2u : 1u);
         return round16((uint32_t)(nr * (cols / 32) * SB));
     }
     __device__ void issue_scales(const UnitInfo &ui, uint8_t *dst, uint64_t *bar) const {
+        if (DT == MG_Q8R) {
+            const int64_t nr = min((int64_t)SW_ROWS, MG_SEL(ui.aux, rows) - row0(ui));
+            bulk_g2s(dst, reinterpret_cast<const float *>(MG_SEL(ui.aux, sc)) + row0(ui), (uint32_t)(nr * 4), bar);
+            if (slot_bias(ui)) bulk_g2s(dst + SW_ROWS * 4, MG_SEL(ui.aux, bias) + row0(ui), (uint32_t)(nr * 4), bar);
+            return;
+        }
         bulk_g2s(dst, MG_SEL(ui.aux, sc) + row0(ui) * (cols / 32) * SB, scale_bytes(ui), bar);
     }
     __device__ const uint8_t *scale_sm(const UnitInfo &, const uint8_t *ss, int r16) const {
@@ -563,8 +585,16 @@ struct PolGemv {
     __device__ void stage_x(int64_t, __half *xs, int xs_stride) const {
         stage_x_n<DT>(x, ldx, n_tok, cols, xs, xs_stride, threadIdx.x, SW_CONS * 32);
     }
+    // only the columns of the K splits of units [u0, u1) (consecutive splits:
+    // the units are K-split-major); split starts are multiples of 128 bytes
+    __device__ void stage_x_units(int64_t u0, int64_t u1, __half *xs, int xs_stride) const {
+        const int64_t b0 = (u0 / ntiles) * kbytes_per_split;
+        const int64_t b1 = min(rowbytes(), ((u1 - 1) / ntiles + 1) * kbytes_per_split);
+        const int c0 = (int)(DT == MG_Q8R ? b0 : 2 * b0), c1 = (int)(DT == MG_Q8R ? b1 : 2 * b1);
+        stage_x_n<DT>(x + c0, ldx, n_tok, c1 - c0, xs + c0, xs_stride, threadIdx.x, SW_CONS * 32);
+    }
     template <int NT>
-    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4], const uint8_t *) {
+    __device__ void epilogue(const UnitInfo &ui, int w, const float acc[NT][4], const uint8_t *ss) {
         const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
         const int64_t mrows = MG_SEL(ui.aux, rows), mldy = MG_SEL(ui.aux, ldy);
         const uint8_t *msc = MG_SEL(ui.aux, sc);
@@ -574,9 +604,15 @@ struct PolGemv {
         for (int half = 0; half < 2; half++) {
             const int64_t row = row0(ui) + 16 * w + g + 8 * half;
             if (row >= mrows) continue;
-            float rs = 1.f;
-            if (DT == MG_Q8R) rs = reinterpret_cast<const float *>(msc)[row];
-            const float bias = (mbias && ui.ks == 0) ? mbias[row] : 0.f;
+            const int r = 16 * w + g + 8 * half;  // row within the tile
+            float rs = 1.f, bias;
+            if (DT == MG_Q8R && ss) {
+                rs = reinterpret_cast<const float *>(ss)[r];
+                bias = slot_bias(ui) ? reinterpret_cast<const float *>(ss + SW_ROWS * 4)[r] : 0.f;
+            } else {
+                if (DT == MG_Q8R) rs = reinterpret_cast<const float *>(msc)[row];
+                bias = (mbias && ui.ks == 0) ? mbias[row] : 0.f;
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 const int tok = nt * 4 + t;
@@ -781,6 +817,7 @@ struct PolMoeGateUp : MoeCommon {
         return (ne + 3) >> 2;
     }
     __device__ bool restage(int64_t, int64_t) const { return false; }
+    __device__ void stage_x_units(int64_t u0, int64_t, __half *xs, int xs_stride) const { stage_x(u0, xs, xs_stride); }
     __device__ void stage_x(int64_t, __half *xs, int xs_stride) const {
         stage_x_n<DT>(xb, L.hidden, n_tok, (int)L.hidden, xs, xs_stride, threadIdx.x, SW_CONS * 32);
     }
@@ -897,6 +934,7 @@ struct PolMoeDown : MoeCommon {
         return (min(ms->ecount[ui.aux], SW_MAX_TOK) + 3) >> 2;
     }
     __device__ bool restage(int64_t u, int64_t u0) const { return u != u0 && unit_expert(u) != unit_expert(u - 1); }
+    __device__ void stage_x_units(int64_t u0, int64_t, __half *xs, int xs_stride) const { stage_x(u0, xs, xs_stride); }
     __device__ int unit_expert(int64_t u) const { return (int)u / (int)tpe(); }
     // the expert's slots' h rows: slot j at activation rows 2j, 2j + 1
     __device__ void stage_x(int64_t u, __half *xs, int xs_stride) const {
