@@ -222,13 +222,19 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
     } else {
         // ------------------------------------------- converters + epilogue
         const int tid = threadIdx.x - 64;  // 0..127: the weight row this thread converts
-        XgRaw<DT> cur[C::NA], nxt[C::NA];
+        // the row's raw bytes of k-tiles kt, kt + 1 and kt + 2: each load is
+        // issued two k-tiles before its conversion (one ahead left the
+        // converters waiting on HBM, not the tensor core)
+        XgRaw<DT> cur[C::NA], nxt[C::NA], nx2[C::NA];
 #pragma unroll
-        for (int na = 0; na < C::NA; na++) xg_load<DT>(cur[na], wmat[na], smat[na], a.M, a.K, m0 + tid, 0);
+        for (int na = 0; na < C::NA; na++) {
+            xg_load<DT>(cur[na], wmat[na], smat[na], a.M, a.K, m0 + tid, 0);
+            if (KT > 1) xg_load<DT>(nxt[na], wmat[na], smat[na], a.M, a.K, m0 + tid, 1);
+        }
         for (int kt = 0; kt < KT && ok; kt++) {
-            if (kt + 1 < KT) {
+            if (kt + 2 < KT) {
 #pragma unroll
-                for (int na = 0; na < C::NA; na++) xg_load<DT>(nxt[na], wmat[na], smat[na], a.M, a.K, m0 + tid, kt + 1);
+                for (int na = 0; na < C::NA; na++) xg_load<DT>(nx2[na], wmat[na], smat[na], a.M, a.K, m0 + tid, kt + 2);
             }
             const int s = kt % C::STAGES;
             if (kt >= C::STAGES) ok = mbar_wait(&empty[s], ((kt / C::STAGES) - 1) & 1);
@@ -239,7 +245,10 @@ __global__ void __launch_bounds__(XG_THREADS, 1)
             fence_proxy_async_smem();
             mbar_arrive(&full_a[s]);
 #pragma unroll
-            for (int na = 0; na < C::NA; na++) cur[na] = nxt[na];
+            for (int na = 0; na < C::NA; na++) {
+                cur[na] = nxt[na];
+                nxt[na] = nx2[na];
+            }
         }
         const bool acc_ok = mbar_wait(&acc_full, 0);  // always: TMEM is freed only after the MMAs
         ok = ok && acc_ok;
