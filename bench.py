@@ -51,11 +51,13 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 MEASURED = os.path.join(ROOT, "MEASURED_PEAKS.json")
-# DRAM bytes (read + write) per routed expert of one limbs + gate/up + down
-# launch triple of the block-scaled decode MoE, from an ncu capture of that
-# triple at 8 tokens (dram__bytes_read.sum + dram__bytes_write.sum divided by
-# the experts routed); per-launch traffic = experts routed x this figure
-TRAFFIC_PER_EXPERT = 13780000
+# DRAM bytes (read + write) per routed expert of one launch of the
+# block-scaled decode MoE (gate/up and down in one kernel), from an ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum) of the 45 launches of
+# moe_kernel_roofline at 8 tokens, divided by the experts each launch routes
+# (its seeded routing replayed on the host): 1.012 x the algorithmic
+# 13,253,760 B; per-launch traffic = experts routed x this figure
+TRAFFIC_PER_EXPERT = 13418000
 DECODE_PER_STEP = 64
 N_SEQ = 8
 
