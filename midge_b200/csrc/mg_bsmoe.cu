@@ -92,14 +92,16 @@ constexpr int BS_MAX_V = 4 * SW_MAX_SLOTS;             // token groups (experts 
 // error word codes of a timed-out wait, by role (beside the streamed kernels' 1)
 constexpr int BS_ERR_PRODUCER = 11, BS_ERR_MMA = 12, BS_ERR_ATOMS = 13, BS_ERR_EPILOGUE = 14, BS_ERR_DRAIN = 15;
 // the first failure is kept (21.. name the wait that gave up: producer 22 ring stage; MMA 24 B ready,
-// 25 accumulator buffer, 26 stage; stager 27 previous group's MMAs, 30 a down group's gate/up tiles)
+// 25 accumulator buffer, 26 stage; stager 27 the buffer's previous group's MMAs, 28 the previous
+// group's atom copies, 30 a down group's gate/up tiles)
 __device__ __forceinline__ void bs_fail(int *err, int code) { atomicCAS(err, 0, code); }
 
 struct BsBars {
     uint64_t full[BS_MAX_STAGES], empty[BS_MAX_STAGES];
     uint64_t accfull[2], accempty[2];
-    uint64_t bready;  // the token group's B rows and B atoms (all K chunks) are in shared memory
-    uint64_t bfree;   // the MMAs of the token group's last unit are done: its B may be replaced
+    uint64_t bready[2];  // B buffer b holds a token group's rows, and the shared B atoms its atoms
+    uint64_t bfree[2];   // the MMAs of buffer b's group are done: its rows may be replaced
+    uint64_t batfree;    // the MMA issuer's copies of the shared B atoms into TMEM have completed
     uint64_t done;    // the MMA issuer's last commit: no MMA is in flight when TMEM is released
     uint32_t tmem;
 };
@@ -359,14 +361,18 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
     const int nk_max = max(pol.ps[0].nk, pol.ps[1].nk);
     uint8_t *stages = sm;
     uint8_t *atoms = stages + (size_t)nst * BS_STAGE;  // per ring stage and chunk: its 2 A atoms (bulk copy) +0, +512
-    uint8_t *bres = atoms + (size_t)nst * BS_CH * BS_ATOMS;  // [K chunk][token j][16 rows x 128 B], 1024-aligned
-    uint8_t *batoms = bres + (size_t)nk_max * BS_B_STAGE;  // [K chunk][2 B atoms of 512 B] of the token group
+    // two B row buffers [K chunk][token j][16 rows x 128 B] (1024-aligned), one
+    // per token group in flight; the group's B atoms pass through one shared
+    // buffer on their way to TMEM (whose two buffers hold them for the MMAs)
+    uint8_t *bres = atoms + (size_t)nst * BS_CH * BS_ATOMS;
+    const size_t bbuf = (size_t)nk_max * BS_B_STAGE;
+    uint8_t *batoms = bres + 2 * bbuf;  // [K chunk][2 B atoms of 512 B]
     uint8_t *bwreg = batoms + (size_t)nk_max * BS_BATOMS;  // the token group's B scale words [token j][g4][16]
     float *ex = reinterpret_cast<float *>(bwreg + (size_t)ssb);  // 64 rows x 2 tokens (up values)
     BsBars *bb = reinterpret_cast<BsBars *>(ex + 64 * BS_TOKG);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ int vlist[BS_MAX_V];
-    __shared__ int nv_sh, last_cta, stage_ok;
+    __shared__ int nv_sh, last_cta, stage_ok, atoms_ok;
     if (tid == 0) {
 #pragma unroll
         for (int i = 0; i < 3; i++) tma_prefetch_map(&maps.a[i]);
@@ -380,8 +386,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             mbar_init(&bb->accfull[lane - 18], 1);
             mbar_init(&bb->accempty[lane - 18], 4);
         } else if (lane == 20) {
-            mbar_init(&bb->bready, 1);
-            mbar_init(&bb->bfree, 1);
+            mbar_init(&bb->bready[0], 1);
+            mbar_init(&bb->bready[1], 1);
+            mbar_init(&bb->bfree[0], 1);
+            mbar_init(&bb->bfree[1], 1);
+            mbar_init(&bb->batfree, 1);
         } else if (lane == 21) {
             mbar_init(&bb->done, 1);
         }
@@ -479,8 +488,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             const uint64_t da0 = umma_desc_sw128(smem_u32(stages)), db0 = umma_desc_sw128(smem_u32(bres));
             const uint64_t dat0 = umma_desc_plain(smem_u32(atoms), 512, 128);
             const uint64_t dbt0 = umma_desc_plain(smem_u32(batoms), 512, 128);
-            int key = -1, ng = 0;
+            int key = -1, ng = 0, gb = 0;
             uint32_t tbb = tb + BS_SFB_COL0;  // the current token group's B scale columns
+            uint64_t dbg = db0;               // and its B row buffer
             for (int q = 0; q < nseq && ok; q++) {
                 BsUnit x;
                 pol.seq_unit(c, q, x);
@@ -490,18 +500,21 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 if (q >= 2 && !mbar_wait(&bb->accempty[b], (uint32_t)(((q >> 1) - 1) & 1))) { bs_fail(pol.err, 25); ok = false; break; }
                 const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
                 if (gkey != key) {
-                    // a new token group: its B rows, and its B scale atoms of every K chunk into
-                    // one of two TMEM buffers (the stager has seen the previous group's MMAs
-                    // complete before it rebuilt them)
+                    // a new token group: its B rows are in buffer ng % 2; its B scale atoms of
+                    // every K chunk go into TMEM buffer ng % 2 (the MMAs of group ng - 2, the
+                    // last to read it, have completed: the stager saw bfree before staging)
                     key = gkey;
-                    if (!mbar_wait(&bb->bready, (uint32_t)(ng & 1))) { bs_fail(pol.err, 24); ok = false; break; }
+                    gb = ng & 1;
+                    if (!mbar_wait(&bb->bready[gb], (uint32_t)((ng >> 1) & 1))) { bs_fail(pol.err, 24); ok = false; break; }
                     tc_fence_after();
-                    tbb = tb + BS_SFB_COL0 + (uint32_t)((ng & 1) * 8 * BS_MAX_NK);
+                    tbb = tb + BS_SFB_COL0 + (uint32_t)(gb * 8 * BS_MAX_NK);
+                    dbg = db0 + (uint64_t)((gb * bbuf) >> 4);
                     for (int kk = 0, nk = pol.pass(x.mode).nk; kk < nk; kk++) {
                         const uint64_t dk = dbt0 + (uint64_t)((kk * BS_BATOMS) >> 4);
                         bs_cp_atom(tbb + 8u * (uint32_t)kk, dk);
                         bs_cp_atom(tbb + 8u * (uint32_t)kk + 4u, dk + 32);
                     }
+                    tc_commit(&bb->batfree);  // the shared atoms may be rebuilt once these copies are done
                     ng++;
                 }
                 tc_fence_after();
@@ -526,7 +539,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                         const uint32_t tsa = tb + BS_SFA_COL0 + 8u * (uint32_t)(s * BS_CH + h), tsb = tbb + 8u * (uint32_t)k;
                         // descriptors: the start-address field is the low 14 bits (address >> 4)
                         const uint64_t da = da0 + (uint64_t)(((size_t)s * BS_STAGE + (size_t)h * BS_A_BYTES) >> 4);
-                        const uint64_t db = db0 + (uint64_t)((k * BS_B_STAGE) >> 4);
+                        const uint64_t db = dbg + (uint64_t)((k * BS_B_STAGE) >> 4);
 #pragma unroll
                         for (int j = 0; j < 4; j++) {
                             const uint32_t sid = 2u * (uint32_t)(j & 1), g = 4u * (uint32_t)(j >> 1);
@@ -540,15 +553,15 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 }
                 if (!ok) break;
                 tc_commit(&bb->accfull[b]);
-                // the group's last unit: its B rows and atoms are free once these MMAs are
-                // done (one phase per group, so the stager's parity waits cannot alias)
+                // the group's last unit: its B rows are free once these MMAs are done (one
+                // phase per group and buffer, so the stager's parity waits cannot alias)
                 bool last = q + 1 == nseq;
                 if (!last) {
                     BsUnit y;
                     pol.seq_unit(c, q + 1, y);
                     last = (y.d | (y.tg << 16) | (y.mode << 30)) != gkey;
                 }
-                if (last) tc_commit(&bb->bfree);
+                if (last) tc_commit(&bb->bfree[gb]);
             }
             if (!ok) bs_fail(pol.err, BS_ERR_MMA);
             tc_commit(&bb->done);
@@ -556,15 +569,17 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
         }
     } else if (warp < 6) {
         // ------------------------------------------------------ B stager
-        // warps 2-5, once per token group: after the previous group's MMAs (and, for
-        // a down group, its gate/up tiles) are done, the group's B rows (12 limbs per
-        // token and K chunk, 16-byte async copies into the 128-byte-swizzled layout)
-        // and B scale words from L2, then the B atoms of every K chunk from the
-        // words (lane = B row); after a timed-out wait all four warps stop
+        // warps 2-5, once per token group g, into B buffer g % 2: after the MMAs of
+        // group g - 2 (the buffer's last user) and, for a down group, its gate/up
+        // tiles are done, the group's B rows (12 limbs per token and K chunk, 16-byte
+        // async copies from L2 into the 128-byte-swizzled layout) and B scale words;
+        // then, once the MMA issuer has copied group g - 1's atoms into TMEM, the B
+        // atoms of every K chunk from the words (lane = B row).  After a timed-out
+        // wait all four warps stop.
         const int t = tid - 64;
         const uint32_t *bw = reinterpret_cast<const uint32_t *>(bwreg);
-        // limb rows 12..15 of both token slots stay zero (never copied)
-        for (int i = t; i < nk_max * BS_TOKG * (BS_LIMBS - BS_LQ) * 8; i += 128) {
+        // limb rows 12..15 of both token slots of both buffers stay zero (never copied)
+        for (int i = t; i < 2 * nk_max * BS_TOKG * (BS_LIMBS - BS_LQ) * 8; i += 128) {
             const int r = BS_LQ + (i >> 3) % (BS_LIMBS - BS_LQ), jk = (i >> 3) / (BS_LIMBS - BS_LQ);
             *reinterpret_cast<uint4 *>(bres + (size_t)(jk >> 1) * BS_B_STAGE + (jk & 1) * BS_B_TOK + r * 128 +
                                        (i & 7) * 16) = make_uint4(0, 0, 0, 0);
@@ -577,9 +592,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             const int gkey = x.d | (x.tg << 16) | (x.mode << 30);
             if (gkey == key) continue;
             key = gkey;
+            const int gb = ng & 1;
+            uint8_t *bdst = bres + gb * bbuf;
             if (t == 0) {
                 bool okw = true;
-                if (ng > 0 && !mbar_wait(&bb->bfree, (uint32_t)((ng - 1) & 1))) {
+                if (ng >= 2 && !mbar_wait(&bb->bfree[gb], (uint32_t)(((ng - 2) >> 1) & 1))) {
                     okw = false;
                     bs_fail(pol.err, 27);
                 }
@@ -600,7 +617,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
             for (int i = t, n = P.nk * nt * BS_LQ * 8; i < n; i += 128) {
                 const int c16 = i & 7, l = (i >> 3) % BS_LQ, r = (i >> 3) / BS_LQ, j = r % nt, kk = r / nt;
                 const int row = BS_LIMBS * (j ? src1 : src0) + l;
-                cp_async16(bres + (size_t)kk * BS_B_STAGE + (j * BS_LIMBS + l) * 128 + ((c16 ^ (l & 7)) << 4),
+                cp_async16(bdst + (size_t)kk * BS_B_STAGE + (j * BS_LIMBS + l) * 128 + ((c16 ^ (l & 7)) << 4),
                            P.limbs + row * P.ld + kk * 128 + c16 * 16);
             }
             const int wv = P.g4 * BS_LIMBS / 4;  // 16-byte vectors of a token's words
@@ -609,7 +626,15 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                 cp_async16(bwreg + (size_t)i * 16, P.bsf + ((int64_t)(j ? src1 : src0) * P.g4 * BS_LIMBS + o * 4));
             }
             cp_async_wait_all();
+            if (t == 0) {  // the shared atoms of group ng - 1 are in TMEM
+                atoms_ok = ng == 0 || mbar_wait(&bb->batfree, (uint32_t)((ng - 1) & 1));
+                if (!atoms_ok) bs_fail(pol.err, 28);
+            }
             named_bar_sync(2, 128);  // every thread's words have landed
+            if (!atoms_ok) {
+                failed = true;
+                break;
+            }
             const int nrows = BS_LIMBS * nt;
             if (lane < nrows)
                 for (int kk = warp - 2; kk < P.nk; kk += 4)
@@ -619,7 +644,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1) k_bsmoe(const __grid_constant__
                             bw[((lane >> 4) * P.g4 + 2 * kk + h) * BS_LIMBS + (lane & 15)];
             fence_proxy_async_smem();  // the rows and atoms, for the tensor core's reads
             named_bar_sync(2, 128);
-            if (t == 0) mbar_arrive(&bb->bready);
+            if (t == 0) mbar_arrive(&bb->bready[gb]);
             ng++;
         }
         if (failed && t == 0) bs_fail(pol.err, BS_ERR_ATOMS);
@@ -733,7 +758,7 @@ static int bs_launch(const BsMapsK &maps, BsPol &pol, size_t ssb, cudaStream_t s
     for (int m = 0; m < 2; m++)
         MG_REQUIRE(pol.ps[m].nk >= 1 && pol.ps[m].nk <= BS_MAX_NK, MG_ERR_ARG,
                    "block-scaled MoE: K of %d chunks unsupported", pol.ps[m].nk);
-    const size_t fixed = 1024 + (size_t)nk_max * (BS_B_STAGE + BS_BATOMS) + ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
+    const size_t fixed = 1024 + (size_t)nk_max * (2 * BS_B_STAGE + BS_BATOMS) + ssb + 64 * BS_TOKG * 4 + sizeof(BsBars);
     const size_t budget = 227 * 1024 - fa.sharedSizeBytes;
     MG_REQUIRE(budget > fixed + 2 * (BS_STAGE + BS_CH * BS_ATOMS), MG_ERR_ARG, "block-scaled MoE: no room for a ring");
     int nst = (int)((budget - fixed) / (BS_STAGE + BS_CH * BS_ATOMS));
