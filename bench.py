@@ -406,7 +406,8 @@ def run_ours(args):
         "config": {"workload": f"{args.config}{'' if args.layers is None else f' ({args.layers} layers)'}: 8 sequences x {prompt_len}-token prompt, "
                                f"{DECODE_PER_STEP} decode steps per bench step",
                    "parallelism": (f"expert-parallel ep{world}: experts and sequences sharded, trunk weights "
-                                   f"replicated, NCCL dispatch/combine per MoE layer") if world > 1 else "single GPU",
+                                   f"replicated, token dispatch/combine over NVLink peer memory per MoE layer (NCCL for "
+                                   f"control only)") if world > 1 else "single GPU",
                    "l2": "working set (~15 GB/step) >> L2, no flush"},
         "prefill_tok_s": round(prefill_tok_s, 1), "prefill_wall_s": round(pf_wall, 3),
         "prefill": {"tok_s": round(prefill_tok_s, 1), "ms": round(pf_ms, 2),
