@@ -182,8 +182,6 @@ def moe_kernel_roofline(torch, m, spec, hbm_peak, reps=40, rank=0, world=1):
     kind = os.environ.get("MIDGE_MOE_KERNELS", "")
     if kind == "mma":
         kname = "k_stream<PolMoeGateUp> + k_stream<PolMoeDown> (mma.sync)"
-    elif kind == "tc":
-        kname = "k_tmoe<GATEUP> + k_tmoe<DOWN> (tcgen05 kind::f16)"
     else:
         kname = "k_bs_limbs + k_bsmoe gate/up + k_bsmoe down (tcgen05 kind::mxf4 block-scaled)"
     return {"kernel": kname + ", 8 tokens, top-4 of 128 experts", "ms": ms,

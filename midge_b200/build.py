@@ -22,7 +22,7 @@ MIDGED = os.path.join(PKG, "bin", "midged")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 GCC = "/usr/bin/gcc"
 
-CU_SOURCES = ["mg_abi.cu", "mg_gemv.cu", "mg_moe.cu", "mg_attn.cu", "mg_model.cu", "mg_stream.cu", "mg_gemm.cu", "mg_prefill.cu", "mg_noalloc.cu", "mg_ep.cu", "mg_ep_xchg.cu", "mg_sample.cu", "mg_selftest.cu", "mg_tmoe.cu", "mg_bsmoe.cu", "mg_q8mma.cu"]
+CU_SOURCES = ["mg_abi.cu", "mg_gemv.cu", "mg_moe.cu", "mg_attn.cu", "mg_model.cu", "mg_stream.cu", "mg_gemm.cu", "mg_prefill.cu", "mg_noalloc.cu", "mg_ep.cu", "mg_ep_xchg.cu", "mg_sample.cu", "mg_selftest.cu", "mg_bsmoe.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -65,13 +65,9 @@ struct MoeStreamArgs {
     float *y;             // [down_ksplit x n_tok*top_k x hidden]
     int down_ksplit;      // requested
     int down_ksplit_out;  // what moe_down_ksplit() returned for it
-    const int *rebase;    // MXFP4: this layer's [n_experts x 3] f16 rebase exponents (null: none)
-    int use_tc;           // run the tensor-core kernels when the format allows
     const BsBuffers *bs;  // block-scaled tensor-core kernels (MXFP4, ue8m0), or null
 };
 int moe_stream(const MoeStreamArgs &a, cudaStream_t st);
-bool tmoe_supported(const mg_expert_layout &L, const int *rebase);
-int moe_tmoe(const MoeStreamArgs &a, const int *rebase, cudaStream_t st);
 int moe_down_ksplit(const mg_expert_layout &L, int want);
 
 struct CombineNormArgs {

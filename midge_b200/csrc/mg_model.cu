@@ -261,10 +261,7 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     const char *ak = getenv("MIDGE_ATTN_KERNELS");
     m->tc_attn = !(ak && !strcmp(ak, "scalar"));
     const char *mk = getenv("MIDGE_MOE_KERNELS");
-    m->tc_moe = mk && !strcmp(mk, "tc");
-    m->bs_moe = !(mk && (!strcmp(mk, "tc") || !strcmp(mk, "mma")));  // where the format allows (set in ready)
-    const char *tk = getenv("MIDGE_TRUNK_KERNELS");
-    m->q8mma = tk && !strcmp(tk, "i8");  // where the trunk is q8r (checked in ready)
+    m->bs_moe = !(mk && !strcmp(mk, "mma"));  // where the format allows (set in ready)
     const char *as = getenv("MIDGE_ATTN_SPLIT");
     if (as && *as) {  // positions per decode-attention split: a multiple of 64, 64..1024
         int v = atoi(as);
@@ -659,8 +656,6 @@ extern "C" int mg_model_ready(mg_model *m) {
     } else {
         m->bs_moe = false;
     }
-    // int8 tensor-core trunk GEMVs: the q8r trunk's TMA maps
-    if (!(m->maps_ok && H % 16 == 0 && q_dim % 16 == 0)) m->q8mma = false;
     m->attn_max_splits = (m->ctx + m->attn_split - 1) / m->attn_split;
     TRY(dalloc(m, &m->attn_part, (size_t)DEC_MAX * s.n_heads * m->attn_max_splits * (s.head_dim + 2) * 4));
     MG_CUDA(cudaHostAlloc(&m->h_toks, R * 4, cudaHostAllocDefault));
@@ -1043,8 +1038,6 @@ static MoeStreamArgs stream_moe_args(mg_model *m, int layer) {
     ma.n_experts = m->n_local; ma.e0 = m->e0; ma.top_k = s.top_k;
     ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit; ma.h = m->h;
     ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
-    ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
-    ma.use_tc = m->tc_moe;
     ma.bs = m->bs_moe ? &m->bs : nullptr;
     return ma;
 }
@@ -1099,7 +1092,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
         g.mat[i].w = mats[i]->data; g.mat[i].scales = mats[i]->scales; g.mat[i].bias = bias[i];
         g.mat[i].rows = mats[i]->rows; g.mat[i].y = m->qkv_part + off[i]; g.mat[i].ldy = qkv_dim;
     }
-    TRY(m->q8mma ? q8mma_gemv(g, st) : stream_gemv(g, st));
+    TRY(stream_gemv(g, st));
     const int cap = m->cap[layer];
     QkvPostArgs qa{};
     qa.q = m->qkv; qa.k = m->qkv + q_dim; qa.v = m->qkv + q_dim + kv_dim; qa.ldq = qkv_dim; qa.ldk = qkv_dim;
@@ -1126,7 +1119,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     go.mat[0].map = &m->map_o[layer];
     go.mat[0].w = m->wo[layer].data; go.mat[0].scales = m->wo[layer].scales; go.mat[0].bias = m->bo[layer];
     go.mat[0].rows = H; go.mat[0].y = m->o_part; go.mat[0].ldy = H;
-    TRY(m->q8mma ? q8mma_gemv(go, st) : stream_gemv(go, st));
+    TRY(stream_gemv(go, st));
     RouterArgs ra{};
     ra.x = m->x; ra.norm_w = m->mlp_norm[layer]; ra.eps = s.norm_eps; ra.xb_out = m->xb;
     ra.rw = (const float *)m->router_w[layer].data; ra.rb = m->router_b[layer];
@@ -1142,8 +1135,6 @@ static int layer_stream(mg_model *m, int layer, int n) {
     ma.n_experts = m->n_local; ma.e0 = m->e0; ma.n_tok = n; ma.top_k = s.top_k; ma.sel = m->sel; ma.xb = m->xb;
     ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit; ma.h = m->h; ma.y = m->moe_y;
     ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
-    ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
-    ma.use_tc = m->tc_moe;
     ma.bs = m->bs_moe ? &m->bs : nullptr;
     if (m->ep.world > 1) return ep_decode_moe(m, layer, n);
     return moe_stream(ma, st);
@@ -1383,8 +1374,6 @@ extern "C" int mg_model_moe_stream(mg_model *m, int layer, int n_tok, const int3
     ma.n_experts = m->n_local; ma.e0 = m->e0; ma.n_tok = n_tok; ma.top_k = s.top_k; ma.sel = sel; ma.xb = m->xb;
     ma.act_plain = s.act_plain; ma.alpha = s.alpha; ma.limit = s.limit; ma.h = m->h; ma.y = m->moe_y;
     ma.down_ksplit = 2; ma.down_ksplit_out = m->ks_down;
-    ma.rebase = m->rebase_ok ? m->pf_rebase + (int64_t)layer * m->n_local * 3 : nullptr;
-    ma.use_tc = m->tc_moe;
     ma.bs = m->bs_moe ? &m->bs : nullptr;
     return moe_stream(ma, m->st);
 }

@@ -9,7 +9,6 @@
 #include <vector>
 
 #include "mg_bsmoe.h"
-#include "mg_q8mma.h"
 #include "mg_ep.h"
 #include "mg_ep_xchg.h"
 #include "midgecuda.h"
@@ -89,12 +88,9 @@ struct mg_model {
     bool tc_prefill = false;
     bool tc_dense = false;  // trunk q/k/v/o of prefill on the tensor cores
     bool tc_attn = true;    // prefill attention on the tensor cores (MIDGE_ATTN_KERNELS=scalar: fp32 kernel)
-    bool tc_moe = false;    // decode MoE on tcgen05 kind::f16 with converted weights (MIDGE_MOE_KERNELS=tc)
     bool bs_moe = false;    // decode MoE on block-scaled tcgen05 MMAs (default for MXFP4 with ue8m0 scales;
-                            // MIDGE_MOE_KERNELS=mma or tc select the mma.sync or kind::f16 kernels)
+                            // MIDGE_MOE_KERNELS=mma selects the mma.sync streamed kernels)
     mg::BsBuffers bs{};
-    bool q8mma = false;     // decode q, k, v, o on tcgen05 kind::i8 (MIDGE_TRUNK_KERNELS=i8; the
-                            // default is the mma.sync streamed kernels, faster at 8 tokens)
     bool rebase_ok = false; // pf_rebase holds exact f16 rebase exponents of every expert matrix
     int *pf_counts = nullptr, *pf_offs = nullptr, *pf_cursor = nullptr, *pf_ntiles = nullptr;
     int *pf_pos = nullptr, *pf_slot = nullptr, *pf_rebase = nullptr;

@@ -225,7 +225,6 @@ int moe_stream(const MoeStreamArgs &a, cudaStream_t st) {
                MG_ERR_ARG, "moe stream: n_tok %d top_k %d unsupported", a.n_tok, a.top_k);
     const mg_expert_layout &L = a.L;
     if (a.bs && bsmoe_supported(L)) return moe_bs(a, st);
-    if (a.use_tc && tmoe_supported(L, a.rebase)) return moe_tmoe(a, a.rebase, st);
     switch (L.dt) {
     case MG_MXFP4:
         if (L.scale_fmt == MG_SCALE_UE8M0)

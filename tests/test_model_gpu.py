@@ -174,11 +174,11 @@ def test_decode_greedy_matches_step_loop(torch_cuda, c1_dir, monkeypatch, kernel
     a.close()
 
 
-@pytest.mark.parametrize("moe", ["bs", "tc", "mma"])
+@pytest.mark.parametrize("moe", ["bs", "mma"])
 def test_decode_moe_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, moe):
-    """Every decode expert kernel (block-scaled tcgen05, the default for
-    MXFP4; tcgen05 with the weights in tensor memory; the mma.sync streamed
-    kernels) against the oracle, 8 concurrent sequences."""
+    """Both decode expert kernels (block-scaled tcgen05, the default for
+    MXFP4; the mma.sync streamed kernels) against the oracle, 8 concurrent
+    sequences."""
     if moe == "bs":
         monkeypatch.delenv("MIDGE_MOE_KERNELS", raising=False)
     else:
@@ -198,16 +198,9 @@ def test_decode_moe_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, moe):
     m.close()
 
 
-@pytest.mark.parametrize("trunk", ["i8", "mma"])
-def test_decode_trunk_kernels_vs_oracle(torch_cuda, c1_dir, monkeypatch, trunk):
-    """Both decode kernels of the int8 trunk (q, k, v, o): tcgen05 kind::i8
-    on exact int8 activation limbs (MIDGE_TRUNK_KERNELS=i8) and the mma.sync
-    streamed kernels (the default), 8 concurrent sequences against the
-    oracle, two steps."""
-    if trunk == "i8":
-        monkeypatch.setenv("MIDGE_TRUNK_KERNELS", trunk)
-    else:
-        monkeypatch.delenv("MIDGE_TRUNK_KERNELS", raising=False)
+def test_decode_trunk_kernels_vs_oracle(torch_cuda, c1_dir):
+    """The decode kernels of the int8 trunk (q, k, v, o: the mma.sync
+    streamed GEMV), 8 concurrent sequences against the oracle, two steps."""
     rng = np.random.default_rng(47)
     prompts = [rng.integers(0, 1024, 4 + i).astype(np.int32) for i in range(8)]
     m = abi.Model.from_dir(c1_dir, ctx=64, max_seqs=8)
