@@ -69,6 +69,7 @@ __global__ void k_qkv_post(QkvPostArgs a) {
 // order from 0 (as k_sum_parts), written back to q / k / v_out after the
 // per-head RMSNorm and RoPE of k_qkv_post, then k and v into the cache.
 constexpr int QP_WARPS = 8;
+constexpr int QP_PLANES = 4;  // K-split planes summed with their loads issued together
 __global__ void __launch_bounds__(QP_WARPS * 32) k_qkv_post_parts(QkvPostArgs a) {
     __shared__ float hv[QP_WARPS][128];
     const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -82,16 +83,31 @@ __global__ void __launch_bounds__(QP_WARPS * 32) k_qkv_post_parts(QkvPostArgs a)
     const int64_t off = (int64_t)t * ld + (int64_t)hh * hd;
     const float *ps = a.parts + (src - a.q) + off;  // parts rows are laid out as q / k / v
     float *vec = hv[w];
+    // the position first: the RoPE table loads that depend on it then overlap
+    // the plane loads, which are all issued together (up to QP_PLANES planes)
+    const int pos = a.tok_pos[t];
+    const int seq = a.tok_seq ? a.tok_seq[t] : 0;
     float ss = 0.f;
-    for (int i = lane; i < hd; i += 32) {
+    const int ks = a.ks;
+#pragma unroll
+    for (int r = 0; r < 4; r++) {  // dimensions lane + 32 r (head_dim <= 128)
+        const int i = lane + 32 * r;
+        if (i >= hd) break;
         float v = 0.f;
-        for (int k = 0; k < a.ks; k++) v += ps[(int64_t)k * a.plane + i];
+        if (ks <= QP_PLANES) {
+            float yv[QP_PLANES];
+#pragma unroll
+            for (int k = 0; k < QP_PLANES; k++) yv[k] = k < ks ? ps[(int64_t)k * a.plane + i] : 0.f;
+#pragma unroll
+            for (int k = 0; k < QP_PLANES; k++)
+                if (k < ks) v += yv[k];
+        } else {
+            for (int k = 0; k < ks; k++) v += ps[(int64_t)k * a.plane + i];
+        }
         vec[i] = v;
         ss = fmaf(v, v, ss);
     }
     __syncwarp();
-    const int pos = a.tok_pos[t];
-    const int seq = a.tok_seq ? a.tok_seq[t] : 0;
     const int kv_dim = nkv * hd;
     const int slot = pos % a.cap;
     if (kind < 2) {
@@ -454,19 +470,41 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
 // ascending order for every output dimension (lane + 32 r), and the eight
 // warp sums are added in warp order.
 constexpr int AC_WARPS = 8;
-__global__ void __launch_bounds__(AC_WARPS * 32) k_attn_combine(AttnDecodeArgs a) {
-    extern __shared__ float cw[];
+__global__ void __launch_bounds__(AC_WARPS * 32) k_attn_combine(AttnDecodeArgs a, int staged) {
+    extern __shared__ float cw[];  // [max_splits] split weights, then (staged) the partials
     __shared__ float red[2][AC_WARPS];
     __shared__ float ws[AC_WARPS][128];
     const int h = blockIdx.x, si = blockIdx.y, t = threadIdx.x, w = t >> 5, lane = t & 31;
-    const int hd = a.head_dim;
+    const int hd = a.head_dim, rs = hd + 2;
+    const float *gpart = a.partial + ((int64_t)si * a.n_heads + h) * (int64_t)a.max_splits * rs;
+    // the position, the sink and (staged) every split slot's partial are
+    // loaded together: no load waits for the position (the slots past the
+    // context are staged too, and skipped below)
     const int pos = a.pos[si];
+    const float sink = a.sinks ? a.sinks[h] : -1e30f;
+    const float *part = gpart;
+    if (staged) {
+        float *sp = cw + ((a.max_splits + 1) & ~1);  // 8-byte aligned
+        const int n2 = a.max_splits * rs / 2;         // float pairs (head_dim even)
+        const float2 *g2 = reinterpret_cast<const float2 *>(gpart);
+        float2 *s2 = reinterpret_cast<float2 *>(sp);
+        constexpr int U = 10;
+        for (int b = t; b < n2; b += U * blockDim.x) {
+            float2 r[U];
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (b + u * (int)blockDim.x < n2) r[u] = g2[b + u * blockDim.x];
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                if (b + u * (int)blockDim.x < n2) s2[b + u * blockDim.x] = r[u];
+        }
+        __syncthreads();
+        part = sp;
+    }
     const int nctx = pos + 1 < a.cap ? pos + 1 : a.cap;
     const int nsplit = (nctx + a.split_len - 1) / a.split_len;
-    const float *part = a.partial + ((int64_t)si * a.n_heads + h) * (int64_t)a.max_splits * (hd + 2);
-    const float sink = a.sinks ? a.sinks[h] : -1e30f;
     float mx = sink;
-    for (int s = t; s < nsplit; s += blockDim.x) mx = fmaxf(mx, part[s * (hd + 2)]);
+    for (int s = t; s < nsplit; s += blockDim.x) mx = fmaxf(mx, part[s * rs]);
     mx = warp_max(mx);
     if (lane == 0) red[0][w] = mx;
     __syncthreads();
@@ -475,9 +513,9 @@ __global__ void __launch_bounds__(AC_WARPS * 32) k_attn_combine(AttnDecodeArgs a
     for (int i = 1; i < AC_WARPS; i++) M = fmaxf(M, red[0][i]);
     float ls = 0.f;
     for (int s = t; s < nsplit; s += blockDim.x) {
-        const float e = expf(part[s * (hd + 2)] - M);
+        const float e = expf(part[s * rs] - M);
         cw[s] = e;
-        ls += part[s * (hd + 2) + 1] * e;
+        ls += part[s * rs + 1] * e;
     }
     ls = warp_sum(ls);
     if (lane == 0) red[1][w] = ls;
@@ -489,7 +527,7 @@ __global__ void __launch_bounds__(AC_WARPS * 32) k_attn_combine(AttnDecodeArgs a
     float o[4] = {0.f, 0.f, 0.f, 0.f};  // dimensions lane + 32 r (head_dim <= 128)
     for (int s = w; s < nsplit; s += AC_WARPS) {
         const float c = cw[s];
-        const float *ps = part + s * (hd + 2) + 2;
+        const float *ps = part + s * rs + 2;
 #pragma unroll
         for (int r = 0; r < 4; r++)
             if (lane + 32 * r < hd) o[r] = fmaf(ps[lane + 32 * r], c, o[r]);
@@ -507,6 +545,20 @@ __global__ void __launch_bounds__(AC_WARPS * 32) k_attn_combine(AttnDecodeArgs a
     }
 }
 
+// the partials staged in shared memory when they fit in AC_STAGE_BYTES
+constexpr size_t AC_STAGE_BYTES = 64 * 1024;
+static int attn_combine(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
+    dim3 g2(a.n_heads, n_seqs);
+    const size_t cw = (size_t)((a.max_splits + 1) & ~1) * 4;
+    const size_t staged = cw + (size_t)a.max_splits * (a.head_dim + 2) * 4;
+    const bool stage = a.head_dim % 2 == 0 && staged <= AC_STAGE_BYTES;
+    const size_t cs = stage ? staged : cw;
+    if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
+    k_attn_combine<<<g2, AC_WARPS * 32, cs, st>>>(a, stage ? 1 : 0);
+    MG_CHECK_LAUNCH();
+    return MG_OK;
+}
+
 template <typename K>
 static int attn_smem_cfg(K kfn, size_t smem) {
     return ensure_smem(kfn, smem);
@@ -522,12 +574,7 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
         if (multi) k_attn_decode_tc<true><<<g1, 32, ts, st>>>(a);
         else k_attn_decode_tc<false><<<g1, 32, ts, st>>>(a);
         MG_CHECK_LAUNCH();
-        dim3 g2(a.n_heads, n_seqs);
-        const size_t cs = (size_t)a.max_splits * 4;
-        if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
-        k_attn_combine<<<g2, AC_WARPS * 32, cs, st>>>(a);
-        MG_CHECK_LAUNCH();
-        return MG_OK;
+        return attn_combine(a, n_seqs, st);
     }
     size_t smem = (size_t)(gq * HD + gq * a.split_len) * 4;
     int rc = attn_smem_cfg(k_attn_decode<HD>, smem);
@@ -535,12 +582,7 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     dim3 g1(a.n_kv_heads, n_seqs, a.max_splits);
     k_attn_decode<HD><<<g1, ATTN_THREADS, smem, st>>>(a);
     MG_CHECK_LAUNCH();
-    dim3 g2(a.n_heads, n_seqs);
-    const size_t cs = (size_t)a.max_splits * 4;
-    if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
-    k_attn_combine<<<g2, AC_WARPS * 32, cs, st>>>(a);
-    MG_CHECK_LAUNCH();
-    return MG_OK;
+    return attn_combine(a, n_seqs, st);
 }
 
 int attn_decode(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {

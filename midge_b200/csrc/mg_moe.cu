@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(ROUTER_THREADS) k_router(RouterArgs a) {
 //   all tokens.
 constexpr int RG = 4;  // experts per logits block (32 blocks stream the 128 rows of the 120b router)
 
+constexpr int RP_PLANES = 8;  // K-split planes whose loads k_router_prep issues together
 __global__ void __launch_bounds__(1024) k_router_prep(RouterArgs a) {
     __shared__ float scratch[32];
     const int64_t H = a.hidden;
@@ -154,19 +155,42 @@ __global__ void __launch_bounds__(1024) k_router_prep(RouterArgs a) {
     float v[PER];
     float ss = 0.f;
     if (H <= (int64_t)blockDim.x * PER) {  // one pass: the row stays in registers through the norm
+        // every load issued together (residual, norm weight, partial planes):
+        // one round trip to memory before the block reduction
+        float nw[PER];
 #pragma unroll
         for (int j = 0; j < PER; j++) {
             const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
             v[j] = c < H ? xr[c] : 0.f;
+            nw[j] = c < H ? a.norm_w[c] : 0.f;
         }
         if (a.x_parts) {
             float p[PER] = {0.f, 0.f, 0.f, 0.f};
-            for (int k = 0; k < a.x_parts_ks; k++) {
-                const float *pp = a.x_parts + (int64_t)k * a.x_parts_stride + (int64_t)tok * H;
+            const int ks = a.x_parts_ks;
+            if (ks <= RP_PLANES) {  // planes added in plane order, as below
+                float yv[RP_PLANES][PER];
 #pragma unroll
-                for (int j = 0; j < PER; j++) {
-                    const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
-                    if (c < H) p[j] += pp[c];
+                for (int k = 0; k < RP_PLANES; k++) {
+                    const float *pp = a.x_parts + (int64_t)k * a.x_parts_stride + (int64_t)tok * H;
+#pragma unroll
+                    for (int j = 0; j < PER; j++) {
+                        const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+                        yv[k][j] = (k < ks && c < H) ? pp[c] : 0.f;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < RP_PLANES; k++)
+#pragma unroll
+                    for (int j = 0; j < PER; j++)
+                        if (k < ks) p[j] += yv[k][j];
+            } else {
+                for (int k = 0; k < ks; k++) {
+                    const float *pp = a.x_parts + (int64_t)k * a.x_parts_stride + (int64_t)tok * H;
+#pragma unroll
+                    for (int j = 0; j < PER; j++) {
+                        const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+                        if (c < H) p[j] += pp[c];
+                    }
                 }
             }
 #pragma unroll
@@ -186,7 +210,7 @@ __global__ void __launch_bounds__(1024) k_router_prep(RouterArgs a) {
 #pragma unroll
         for (int j = 0; j < PER; j++) {
             const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
-            if (c < H) a.xb_out[(int64_t)tok * H + c] = __fmul_rn(__fmul_rn(v[j], inv), a.norm_w[c]);
+            if (c < H) a.xb_out[(int64_t)tok * H + c] = __fmul_rn(__fmul_rn(v[j], inv), nw[j]);
         }
         return;
     }

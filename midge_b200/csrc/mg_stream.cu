@@ -353,8 +353,87 @@ __global__ void __launch_bounds__(1024) k_combine_norm(CombineNormArgs a) {
             a.xb[(int64_t)t * H + c] = __fmul_rn(__fmul_rn(x[c], inv), a.nw[c]);
 }
 
+// The same for one plane of expert outputs (or none), top_k <= MK and hidden
+// <= 1024 PER, with one round trip to memory before the norm's reduction:
+// every thread loads the token's routing slots and weights, its columns'
+// outputs of every slot (valid or not: the buffer holds all n_tok x top_k
+// rows), the residual and the norm weight together, then adds the valid
+// slots in rank order exactly as k_combine_norm.
+template <int MK, int PER>
+__global__ void __launch_bounds__(1024) k_combine_norm1(CombineNormArgs a) {
+    __shared__ float scratch[32];
+    const int t = blockIdx.x;
+    const int64_t H = a.hidden;
+    float *x = a.x + (int64_t)t * H;
+    const float *xi = (a.x_in ? a.x_in : a.x) + (int64_t)t * H;
+    const int k = a.top_k;
+    int ev[MK];
+    float wv[MK];
+#pragma unroll
+    for (int i = 0; i < MK; i++) {
+        const bool s = a.y && i < k;
+        ev[i] = s ? a.sel[t * k + i] : -1;
+        wv[i] = s ? a.w[t * k + i] : 0.f;
+    }
+    float v[PER], nw[PER], yv[MK][PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+        v[j] = c < H ? xi[c] : 0.f;
+        nw[j] = (a.xb && c < H) ? a.nw[c] : 0.f;
+#pragma unroll
+        for (int i = 0; i < MK; i++) yv[i][j] = (a.y && i < k && c < H) ? a.y[(int64_t)(t * k + i) * H + c] : 0.f;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+        if (a.y) {
+            float moe = 0.f;
+#pragma unroll
+            for (int i = 0; i < MK; i++) {
+                float yy = 0.f;
+                yy += yv[i][j];
+                if (i < k && ev[i] >= 0 && ev[i] < a.n_experts) moe = __fadd_rn(moe, __fmul_rn(wv[i], yy));
+            }
+            v[j] = __fadd_rn(v[j], moe);
+            if (c < H) x[c] = v[j];
+        }
+        if (c < H) ss = fmaf(v[j], v[j], ss);
+    }
+    ss = block_sum(ss, scratch);
+    const float inv = 1.0f / sqrtf(ss / (float)H + a.eps);
+    if (a.xb)
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
+            if (c < H) a.xb[(int64_t)t * H + c] = __fmul_rn(__fmul_rn(v[j], inv), nw[j]);
+        }
+}
+
+template <int MK>
+static bool launch_combine_norm1(const CombineNormArgs &a, int per, cudaStream_t st) {
+    switch (per) {
+    case 1: k_combine_norm1<MK, 1><<<a.n_tok, 1024, 0, st>>>(a); return true;
+    case 2: k_combine_norm1<MK, 2><<<a.n_tok, 1024, 0, st>>>(a); return true;
+    case 3: k_combine_norm1<MK, 3><<<a.n_tok, 1024, 0, st>>>(a); return true;
+    }
+    if constexpr (MK <= 4)
+        if (per == 4) { k_combine_norm1<MK, 4><<<a.n_tok, 1024, 0, st>>>(a); return true; }
+    return false;
+}
+
 int combine_norm(const CombineNormArgs &a, cudaStream_t st) {
     if (a.n_tok <= 0) return MG_OK;
+    // one plane of expert outputs (or none): the single-round-trip kernel
+    const int per = (int)((a.hidden + 1023) / 1024);
+    if ((!a.y || a.ksplit == 1) && a.top_k <= 8 && per <= 4) {
+        const bool done = a.top_k <= 4 || !a.y ? launch_combine_norm1<4>(a, per, st) : launch_combine_norm1<8>(a, per, st);
+        if (done) {
+            MG_CHECK_LAUNCH();
+            return MG_OK;
+        }
+    }
     switch (a.y ? a.ksplit : 1) {
     case 1: k_combine_norm<1><<<a.n_tok, 1024, 0, st>>>(a); break;
     case 2: k_combine_norm<2><<<a.n_tok, 1024, 0, st>>>(a); break;

@@ -244,6 +244,41 @@ def test_decode_block_scaled_token_groups_vs_oracle(torch_cuda, tmp_path, monkey
     m.close()
 
 
+@pytest.mark.parametrize("experts,n_seqs", [(322, 8), (128, 5)])
+def test_decode_router_widths_vs_oracle(torch_cuda, tmp_path, experts, n_seqs):
+    """The decode router away from the default shape: 322 experts (the last
+    logits block holds 2 of its 4 expert rows; the top-k scans 11 logits per
+    lane) and 5 sequences (a partly filled token group).  Two decode steps
+    against the oracle; greedy tokens and usage counters equal."""
+    spec, edt = ct.config_spec("c1_tiny")
+    spec["moe"]["experts"] = experts
+    md = ct.write_synthetic_model(str(tmp_path / "m"), spec, edt, seed=11)
+    rng = np.random.default_rng(53)
+    prompts = [rng.integers(0, 1024, 4 + i).astype(np.int32) for i in range(n_seqs)]
+    m = abi.Model.from_dir(md, ctx=64, max_seqs=n_seqs)
+    first = np.array([int(np.argmax(m.forward_batch(i, p, logits_mode=1))) for i, p in enumerate(prompts)], np.int32)
+    seqs = np.arange(n_seqs, dtype=np.int32)
+    u0 = np.asarray(m.usage()).copy()
+    lg1, nxt = m.decode_step(seqs, first, want_logits=True)
+    lg2, nxt2 = m.decode_step(seqs, nxt, want_logits=True)
+    du = np.asarray(m.usage()) - u0
+    want_usage = np.zeros_like(du)
+    for i, p in enumerate(prompts):
+        om = orc.OracleModel(md, 64)
+        om.prefill(list(p))
+        ou0 = np.asarray(om.usage()).copy()
+        w1 = om.forward(int(first[i]))
+        assert max_rel(w1, lg1[i]) < LOGIT_TOL
+        assert int(nxt[i]) == int(np.argmax(w1))
+        w2 = om.forward(int(nxt[i]))
+        assert max_rel(w2, lg2[i]) < LOGIT_TOL
+        assert int(nxt2[i]) == int(np.argmax(w2))
+        want_usage += np.asarray(om.usage()) - ou0
+        om.close()
+    assert np.array_equal(du, want_usage)
+    m.close()
+
+
 def test_ue8m0_container_bit_identical(torch_cuda, c1_dir, tmp_path):
     """An experts.midge rewritten as dtype mxfp4e8 (ue8m0 scales on disk,
     midge_b200.convert_ue8m0) loads without re-expression and gives the same
