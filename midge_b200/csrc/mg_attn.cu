@@ -75,7 +75,10 @@ __global__ void __launch_bounds__(QP_WARPS * 32) k_qkv_post_parts(QkvPostArgs a)
     const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = blockIdx.y * QP_WARPS + w;
     const int hd = a.head_dim, half = hd >> 1, nh = a.n_heads, nkv = a.n_kv_heads;
-    if (h >= nh + 2 * nkv) return;  // warp-uniform; no block barrier follows
+    if (h >= nh + 2 * nkv) {  // warp-uniform; no block barrier follows
+        pdl_wait();
+        return;
+    }
     const int kind = h < nh ? 0 : (h < nh + nkv ? 1 : 2);  // q, k, v
     const int hh = kind == 0 ? h : (kind == 1 ? h - nh : h - nh - nkv);
     const float *src = kind == 0 ? a.q : (kind == 1 ? a.k : a.v);
@@ -83,10 +86,23 @@ __global__ void __launch_bounds__(QP_WARPS * 32) k_qkv_post_parts(QkvPostArgs a)
     const int64_t off = (int64_t)t * ld + (int64_t)hh * hd;
     const float *ps = a.parts + (src - a.q) + off;  // parts rows are laid out as q / k / v
     float *vec = hv[w];
-    // the position first: the RoPE table loads that depend on it then overlap
-    // the plane loads, which are all issued together (up to QP_PLANES planes)
+    // The position first and the RoPE values it selects (this lane's
+    // dimensions lane and lane + 32 of the half); none of these comes from the
+    // GEMV before this kernel, so a programmatic launch reads them before its
+    // wait.  Then the plane loads, all issued together (up to QP_PLANES).
     const int pos = a.tok_pos[t];
     const int seq = a.tok_seq ? a.tok_seq[t] : 0;
+    float rc[2] = {0.f, 0.f}, rsn[2] = {0.f, 0.f};
+    if (kind < 2)
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int i = lane + 32 * r;
+            if (i < half) {
+                rc[r] = a.rope_cos[(int64_t)pos * half + i];
+                rsn[r] = a.rope_sin[(int64_t)pos * half + i];
+            }
+        }
+    pdl_wait();
     float ss = 0.f;
     const int ks = a.ks;
 #pragma unroll
@@ -118,12 +134,14 @@ __global__ void __launch_bounds__(QP_WARPS * 32) k_qkv_post_parts(QkvPostArgs a)
             for (int i = lane; i < hd; i += 32) vec[i] = __fmul_rn(__fmul_rn(vec[i], inv), nw[i]);
             __syncwarp();
         }
-        const float *co = a.rope_cos + (int64_t)pos * half, *si = a.rope_sin + (int64_t)pos * half;
         float *dst = (kind == 0 ? a.q : a.k) + off;
-        for (int i = lane; i < half; i += 32) {
+#pragma unroll
+        for (int r = 0; r < 2; r++) {  // half <= 64
+            const int i = lane + 32 * r;
+            if (i >= half) break;
             const float x0 = vec[i], x1 = vec[i + half];
-            const float y0 = __fsub_rn(__fmul_rn(x0, co[i]), __fmul_rn(x1, si[i]));
-            const float y1 = __fadd_rn(__fmul_rn(x1, co[i]), __fmul_rn(x0, si[i]));
+            const float y0 = __fsub_rn(__fmul_rn(x0, rc[r]), __fmul_rn(x1, rsn[r]));
+            const float y1 = __fadd_rn(__fmul_rn(x1, rc[r]), __fmul_rn(x0, rsn[r]));
             dst[i] = y0;
             dst[i + half] = y1;
             if (kind == 1) {
@@ -156,8 +174,7 @@ int qkv_post_parts(const QkvPostArgs &a, int n_tok, cudaStream_t st) {
                    (a.v - a.q) + (int64_t)a.n_kv_heads * a.head_dim <= a.ldq,
                MG_ERR_ARG, "qkv_post_parts: q, k, v must share one row of stride ldq");
     dim3 g(n_tok, (a.n_heads + 2 * a.n_kv_heads + QP_WARPS - 1) / QP_WARPS);
-    k_qkv_post_parts<<<g, QP_WARPS * 32, 0, st>>>(a);
-    MG_CHECK_LAUNCH();
+    MG_CUDA(launch_k(a.pdl != 0, k_qkv_post_parts, g, dim3(QP_WARPS * 32), 0, st, a));
     return MG_OK;
 }
 
@@ -208,6 +225,7 @@ constexpr int ATTN_THREADS = 128;
 template <int HD>
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn_decode(AttnDecodeArgs a) {
     extern __shared__ __align__(16) float asm_[];
+    pdl_trigger();  // the combine may start and wait for this grid
     const int kh = blockIdx.x, si = blockIdx.y, sp = blockIdx.z;
     const int seq = a.seq_ids[si];
     const int gq = a.n_heads / a.n_kv_heads, kv_dim = a.n_kv_heads * HD;
@@ -303,6 +321,7 @@ constexpr int TCD_POS = 64;
 template <bool MULTI>
 __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
     constexpr int HD = 64;
+    pdl_trigger();  // the combine may start and wait for this grid
     // [buffer][K, V] tiles: two buffers when a split has more than one tile
     extern __shared__ __align__(128) uint16_t kv[];
     const int kh = blockIdx.x, si = blockIdx.y, sp = blockIdx.z;
@@ -477,11 +496,13 @@ __global__ void __launch_bounds__(AC_WARPS * 32) k_attn_combine(AttnDecodeArgs a
     const int h = blockIdx.x, si = blockIdx.y, t = threadIdx.x, w = t >> 5, lane = t & 31;
     const int hd = a.head_dim, rs = hd + 2;
     const float *gpart = a.partial + ((int64_t)si * a.n_heads + h) * (int64_t)a.max_splits * rs;
-    // the position, the sink and (staged) every split slot's partial are
-    // loaded together: no load waits for the position (the slots past the
-    // context are staged too, and skipped below)
+    // the position and the sink (neither written by the attention grid, so a
+    // programmatic launch reads them before its wait); then (staged) every
+    // split slot's partial at once, without waiting for the position (the
+    // slots past the context are staged too, and skipped below)
     const int pos = a.pos[si];
     const float sink = a.sinks ? a.sinks[h] : -1e30f;
+    pdl_wait();
     const float *part = gpart;
     if (staged) {
         float *sp = cw + ((a.max_splits + 1) & ~1);  // 8-byte aligned
@@ -554,8 +575,7 @@ static int attn_combine(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     const bool stage = a.head_dim % 2 == 0 && staged <= AC_STAGE_BYTES;
     const size_t cs = stage ? staged : cw;
     if (cs > 48 * 1024 && ensure_smem(k_attn_combine, cs)) return MG_ERR_CUDA;
-    k_attn_combine<<<g2, AC_WARPS * 32, cs, st>>>(a, stage ? 1 : 0);
-    MG_CHECK_LAUNCH();
+    MG_CUDA(launch_k(a.pdl != 0, k_attn_combine, g2, dim3(AC_WARPS * 32), cs, st, a, stage ? 1 : 0));
     return MG_OK;
 }
 

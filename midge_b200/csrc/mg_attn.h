@@ -21,6 +21,7 @@ struct QkvPostArgs {
     uint16_t *tmp_k, *tmp_v;           // optional [n_tok x kv_dim] f16 copies
     // optional: q, k, v are the sums of ks K-split planes (plane stride
     // `plane`, rows as q/k/v) and written to q, k and v_out (qkv_post_parts)
+    int pdl;  // launched dependent on the q/k/v GEMV: positions, sequences and RoPE values read before the wait
     const float *parts;
     int ks;
     int64_t plane;
@@ -42,6 +43,7 @@ struct AttnDecodeArgs {
     float *out;          // [n_seqs x ldo]
     int64_t ldo;
     int use_tc;          // head_dim 64, split_len 64: the tensor-core kernel
+    int pdl;             // the combine launched dependent on the attention grid
 };
 int attn_decode(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st);
 

@@ -198,6 +198,34 @@ __device__ __forceinline__ float block_sum(float v, float *scratch) {
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
+// Programmatic dependent launch.  pdl_trigger: the next grid on the stream,
+// when launched with the programmatic attribute, may start once every CTA of
+// this grid has triggered or exited.  pdl_wait: blocks until the previous grid
+// has completed and its memory operations are visible (returns at once when
+// this grid was launched without the attribute).  A dependent reads nothing
+// the previous grid (or a grid still running before it) writes, and writes
+// nothing, before its wait; and it waits in every CTA, so that its completion
+// implies the previous grid's for the normally launched kernels after it.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launch with the programmatic-serialization attribute when pdl is set.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(bool pdl, void (*kfn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kfn, args...);
+}
+
 // Number of SMs of the current device (cached per device).
 int num_sms();
 

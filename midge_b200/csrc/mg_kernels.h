@@ -83,6 +83,8 @@ struct CombineNormArgs {
     float eps;
     float *xb;             // normed output (may be null)
     int64_t plane;         // floats between the K-split planes of y (0: n_tok*top_k*hidden)
+    int pdl;               // launched dependent on the MoE grid: slots, weights, residual and norm weight
+                           // are read before its wait (they must not come from the grid just before)
 };
 int combine_norm(const CombineNormArgs &a, cudaStream_t st);
 int sum_parts(const float *part, int ks, int64_t plane, int n_tok, int64_t rows, int64_t ldp, float *out, int64_t ldo,
@@ -114,6 +116,8 @@ struct RouterArgs {
     int x_parts_ks;
     int64_t x_parts_stride;
     int *err;              // decode router: error word set when a bounded wait gives up (may be null)
+    int pdl;               // decode router: logits launched dependent on the norm kernel (weights
+                           // staged before the wait)
 };
 int router(const RouterArgs &a, cudaStream_t st);
 int router_split(const RouterArgs &a, float *logits_scratch, unsigned *ticket, cudaStream_t st);  // decode

@@ -262,6 +262,8 @@ extern "C" int mg_model_create(const mg_spec *spec, int ctx, int max_seqs, int d
     m->tc_attn = !(ak && !strcmp(ak, "scalar"));
     const char *mk = getenv("MIDGE_MOE_KERNELS");
     m->bs_moe = !(mk && !strcmp(mk, "mma"));  // where the format allows (set in ready)
+    const char *pd = getenv("MIDGE_PDL");
+    m->pdl = !(pd && !strcmp(pd, "0"));
     const char *as = getenv("MIDGE_ATTN_SPLIT");
     if (as && *as) {  // positions per decode-attention split: a multiple of 64, 64..1024
         int v = atoi(as);
@@ -1079,6 +1081,9 @@ static int layer_stream(mg_model *m, int layer, int n) {
     cn.sel = m->sel; cn.w = m->wts; cn.n_tok = n; cn.top_k = s.top_k; cn.n_experts = s.n_experts;
     cn.hidden = H; cn.nw = m->attn_norm[layer]; cn.eps = s.norm_eps; cn.xb = m->xb;
     if (m->ep.world > 1) cn.plane = (int64_t)m->dec_nmax * s.top_k * H;
+    // programmatic after the MoE grid; not at layer 0, whose residual comes
+    // from the embedding kernel just before
+    cn.pdl = m->pdl && layer > 0 && m->ep.world == 1;
     TRY(combine_norm(cn, st));
     StreamGemvArgs g{};
     g.dt = MG_Q8R; g.scale_fmt = MG_SCALE_F16; g.nmat = 3; g.cols = H; g.x = m->xb; g.ldx = H; g.n_tok = n;
@@ -1103,6 +1108,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     qa.kc = m->kc[layer]; qa.vc = m->vc[layer]; qa.cap = cap;
     // the K-split partial planes are summed inside (k_sum_parts order)
     qa.parts = m->qkv_part; qa.ks = m->ks_qkv; qa.plane = (int64_t)n * qkv_dim; qa.v_out = m->qkv + q_dim + kv_dim;
+    qa.pdl = m->pdl;
     TRY(qkv_post_parts(qa, n, st));
     AttnDecodeArgs da{};
     da.q = m->qkv; da.ldq = qkv_dim; da.seq_ids = m->tok_seq; da.pos = m->tok_pos;
@@ -1112,6 +1118,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     da.split_len = m->attn_split; da.max_splits = (cap + m->attn_split - 1) / m->attn_split;
     da.use_tc = m->tc_attn;
     da.partial = m->attn_part; da.out = m->ao; da.ldo = q_dim;
+    da.pdl = m->pdl;
     TRY(attn_decode(da, n, st));
     StreamGemvArgs go{};
     go.dt = MG_Q8R; go.scale_fmt = MG_SCALE_F16; go.nmat = 1; go.cols = q_dim; go.x = m->ao; go.ldx = q_dim;
@@ -1128,6 +1135,7 @@ static int layer_stream(mg_model *m, int layer, int n) {
     ra.usage = m->usage + (int64_t)layer * s.n_experts;
     ra.x_parts = m->o_part; ra.x_parts_ks = m->ks_o; ra.x_parts_stride = (int64_t)n * H; ra.x_out = m->xa;
     ra.err = stream_error_word();
+    ra.pdl = m->pdl;
     TRY(router_split(ra, m->rlogits, m->rticket, st));
     MoeStreamArgs ma{};
     ma.L = m->el; ma.experts_layer = m->experts + (int64_t)layer * m->el.layer_stride;
@@ -1157,6 +1165,7 @@ static int decode_core_stream(mg_model *m, int n) {
     cn.top_k = s.top_k; cn.n_experts = s.n_experts; cn.hidden = s.hidden; cn.nw = m->final_norm;
     cn.eps = s.norm_eps; cn.xb = m->xb;
     if (m->ep.world > 1) cn.plane = (int64_t)m->dec_nmax * s.top_k * s.hidden;
+    cn.pdl = m->pdl && m->ep.world == 1;
     TRY(combine_norm(cn, st));
     StreamGemvArgs g{};
     g.dt = MG_Q8R; g.scale_fmt = MG_SCALE_F16; g.nmat = 1; g.cols = s.hidden; g.x = m->xb; g.ldx = s.hidden;

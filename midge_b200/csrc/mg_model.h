@@ -91,6 +91,7 @@ struct mg_model {
     bool bs_moe = false;    // decode MoE on block-scaled tcgen05 MMAs (default for MXFP4 with ue8m0 scales;
                             // MIDGE_MOE_KERNELS=mma selects the mma.sync streamed kernels)
     mg::BsBuffers bs{};
+    bool pdl = true;  // decode: programmatic launches of the small steps after the grids before them (MIDGE_PDL=0: off)
     bool rebase_ok = false; // pf_rebase holds exact f16 rebase exponents of every expert matrix
     int *pf_counts = nullptr, *pf_offs = nullptr, *pf_cursor = nullptr, *pf_ntiles = nullptr;
     int *pf_pos = nullptr, *pf_slot = nullptr, *pf_rebase = nullptr;

@@ -148,6 +148,7 @@ constexpr int RG = 4;  // experts per logits block (32 blocks stream the 128 row
 constexpr int RP_PLANES = 8;  // K-split planes whose loads k_router_prep issues together
 __global__ void __launch_bounds__(1024) k_router_prep(RouterArgs a) {
     __shared__ float scratch[32];
+    pdl_trigger();  // the logits blocks may start staging their weight rows
     const int64_t H = a.hidden;
     const int tok = blockIdx.x;
     const float *xr = a.x + (int64_t)tok * H;
@@ -351,8 +352,12 @@ __global__ void __launch_bounds__(RL_THREADS) k_router_logits(RouterArgs a, floa
     if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(&bar, rowb * (uint32_t)(ne + ntk));
         for (int j = 0; j < ne; j++) bulk_g2s(ws + j * ld, a.rw + (int64_t)(e0 + j) * H, rowb, &bar);
-        for (int t = 0; t < ntk; t++) bulk_g2s(xs + t * ld, a.xb_out + (int64_t)(tok0 + t) * H, rowb, &bar);
     }
+    // the normed rows come from the norm kernel: after its grid (a no-op
+    // unless this launch is programmatic; the weights above are constant)
+    pdl_wait();
+    if (threadIdx.x == 0)
+        for (int t = 0; t < ntk; t++) bulk_g2s(xs + t * ld, a.xb_out + (int64_t)(tok0 + t) * H, rowb, &bar);
     bool ok = true;
     if (threadIdx.x == 0) ok = mbar_wait(&bar, 0);
     if (!__syncthreads_and(ok)) {  // rows never arrived: report; the experts of this step are stale
@@ -419,8 +424,8 @@ int router_split(const RouterArgs &a, float *logits_scratch, unsigned *ticket, c
         if (smem <= 200 * 1024) {
             int rc = ensure_smem(k_router_logits, smem);
             if (rc) return rc;
-            k_router_logits<<<(a.n_experts + RG - 1) / RG, RL_THREADS, smem, st>>>(a, logits_scratch, ticket);
-            MG_CHECK_LAUNCH();
+            MG_CUDA(launch_k(a.pdl != 0, k_router_logits, dim3((a.n_experts + RG - 1) / RG), dim3(RL_THREADS), smem,
+                             st, a, logits_scratch, ticket));
             return MG_OK;
         }
     }

@@ -381,6 +381,14 @@ __global__ void __launch_bounds__(1024) k_combine_norm1(CombineNormArgs a) {
         const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
         v[j] = c < H ? xi[c] : 0.f;
         nw[j] = (a.xb && c < H) ? a.nw[c] : 0.f;
+    }
+    // the expert outputs come from the MoE grid: after it (a no-op unless
+    // this launch is programmatic; the slots, weights and residual above
+    // were written by kernels that completed before the MoE grid started)
+    pdl_wait();
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int64_t c = threadIdx.x + (int64_t)j * blockDim.x;
 #pragma unroll
         for (int i = 0; i < MK; i++) yv[i][j] = (a.y && i < k && c < H) ? a.y[(int64_t)(t * k + i) * H + c] : 0.f;
     }
@@ -411,15 +419,21 @@ __global__ void __launch_bounds__(1024) k_combine_norm1(CombineNormArgs a) {
         }
 }
 
+template <int MK, int PER>
+static cudaError_t launch_cn1(const CombineNormArgs &a, cudaStream_t st) {
+    return launch_k(a.pdl != 0, k_combine_norm1<MK, PER>, dim3(a.n_tok), dim3(1024), 0, st, a);
+}
+
+// false: no instance for this shape (the caller falls back)
 template <int MK>
-static bool launch_combine_norm1(const CombineNormArgs &a, int per, cudaStream_t st) {
+static bool launch_combine_norm1(const CombineNormArgs &a, int per, cudaStream_t st, cudaError_t *e) {
     switch (per) {
-    case 1: k_combine_norm1<MK, 1><<<a.n_tok, 1024, 0, st>>>(a); return true;
-    case 2: k_combine_norm1<MK, 2><<<a.n_tok, 1024, 0, st>>>(a); return true;
-    case 3: k_combine_norm1<MK, 3><<<a.n_tok, 1024, 0, st>>>(a); return true;
+    case 1: *e = launch_cn1<MK, 1>(a, st); return true;
+    case 2: *e = launch_cn1<MK, 2>(a, st); return true;
+    case 3: *e = launch_cn1<MK, 3>(a, st); return true;
     }
     if constexpr (MK <= 4)
-        if (per == 4) { k_combine_norm1<MK, 4><<<a.n_tok, 1024, 0, st>>>(a); return true; }
+        if (per == 4) { *e = launch_cn1<MK, 4>(a, st); return true; }
     return false;
 }
 
@@ -428,9 +442,11 @@ int combine_norm(const CombineNormArgs &a, cudaStream_t st) {
     // one plane of expert outputs (or none): the single-round-trip kernel
     const int per = (int)((a.hidden + 1023) / 1024);
     if ((!a.y || a.ksplit == 1) && a.top_k <= 8 && per <= 4) {
-        const bool done = a.top_k <= 4 || !a.y ? launch_combine_norm1<4>(a, per, st) : launch_combine_norm1<8>(a, per, st);
+        cudaError_t e = cudaSuccess;
+        const bool done =
+            a.top_k <= 4 || !a.y ? launch_combine_norm1<4>(a, per, st, &e) : launch_combine_norm1<8>(a, per, st, &e);
         if (done) {
-            MG_CHECK_LAUNCH();
+            MG_CUDA(e);
             return MG_OK;
         }
     }

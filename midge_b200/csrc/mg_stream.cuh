@@ -396,6 +396,7 @@ __global__ void __launch_bounds__(SW_THREADS, 1) k_stream(const __grid_constant_
     extern __shared__ __align__(1024) uint8_t sw_smem_raw[];
     uint8_t *sw_smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sw_smem_raw) + 1023) & ~(uintptr_t)1023);
     SwShared *sh = reinterpret_cast<SwShared *>(sw_smem);
+    pdl_trigger();  // a programmatically launched next kernel may start its setup
     uint8_t *ring = sw_smem + 1024;  // stages 1024-aligned for the 128-byte swizzle
     uint8_t *ss = ring + (size_t)nstages * SW_STAGE_BYTES;  // sw_nslot scale slots of ssb bytes (ssb % 128 == 0)
     float *red = reinterpret_cast<float *>(ss + sw_nslot(DT) * (size_t)ssb);  // SW_RG x 32 lanes x NT*4 partial sums
