@@ -365,7 +365,10 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
         }
         cp_async_commit();
     };
+    // MULTI: three buffers, two tiles in flight ahead of the one multiplied
+    constexpr int NBUF = MULTI ? 3 : 1;
     load_tile(0, 0);
+    if (MULTI && ntile > 1) load_tile(1, 1);
     // A fragments of [q_hi; q_lo] for the 4 k-steps (row g = head g)
     uint32_t qa[4][4];
     {
@@ -388,15 +391,18 @@ __global__ void __launch_bounds__(32) k_attn_decode_tc(AttnDecodeArgs a) {
         for (int j = 0; j < 4; j++) o[i][j] = 0.f;
 #pragma unroll 1
     for (int it = 0; it < ntile; it++) {
-        if (MULTI && it + 1 < ntile) {
-            load_tile(it + 1, (it + 1) & 1);
+        // tile it must be complete; the groups committed after it may pend
+        if (MULTI && it + 2 < ntile) {
+            load_tile(it + 2, (it + 2) % NBUF);  // into the buffer tile it - 1 left
+            cp_async_wait<2>();
+        } else if (MULTI && it + 1 < ntile) {
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncwarp();
         const int np = min(TCD_POS, npa - it * TCD_POS);
-        const uint32_t kb = sb + (uint32_t)(it & 1) * 2 * MAT, vb = kb + MAT;
+        const uint32_t kb = sb + (uint32_t)(it % NBUF) * 2 * MAT, vb = kb + MAT;
         float sc[8][4];
 #pragma unroll
         for (int i = 0; i < 8; i++)
@@ -590,7 +596,7 @@ static int attn_decode_t(const AttnDecodeArgs &a, int n_seqs, cudaStream_t st) {
     if (HD == 64 && a.use_tc && gq <= 8 && a.split_len % TCD_POS == 0) {
         dim3 g1(a.n_kv_heads, n_seqs, a.max_splits);
         const bool multi = a.split_len > TCD_POS;
-        const size_t ts = (size_t)(multi ? 2 : 1) * 2 * TCD_POS * 64 * 2;
+        const size_t ts = (size_t)(multi ? 3 : 1) * 2 * TCD_POS * 64 * 2;  // K and V tiles per buffer
         if (multi) k_attn_decode_tc<true><<<g1, 32, ts, st>>>(a);
         else k_attn_decode_tc<false><<<g1, 32, ts, st>>>(a);
         MG_CHECK_LAUNCH();

@@ -279,6 +279,35 @@ def test_decode_router_widths_vs_oracle(torch_cuda, tmp_path, experts, n_seqs):
     m.close()
 
 
+@pytest.mark.parametrize("split", ["128", "192"])
+def test_decode_attention_multi_tile_splits_vs_oracle(torch_cuda, c1_dir, monkeypatch, split):
+    """Decode attention with splits of several 64-position tiles
+    (MIDGE_ATTN_SPLIT): the tensor-core kernel's double-buffered tile loop
+    with the running-maximum rescale, a ragged last tile and a partial last
+    split on the full-attention layer (~330-420 positions), and the wrapped
+    128-slot ring of the sliding layer in one split.  Two decode steps of 3
+    sequences against the oracle."""
+    monkeypatch.setenv("MIDGE_ATTN_SPLIT", split)
+    rng = np.random.default_rng(59)
+    prompts = [rng.integers(0, 1024, n).astype(np.int32) for n in (330, 377, 419)]
+    m = abi.Model.from_dir(c1_dir, ctx=512, max_seqs=3)
+    first = np.array([int(np.argmax(m.forward_batch(i, p, logits_mode=1))) for i, p in enumerate(prompts)], np.int32)
+    seqs = np.arange(3, dtype=np.int32)
+    lg1, nxt = m.decode_step(seqs, first, want_logits=True)
+    lg2, nxt2 = m.decode_step(seqs, nxt, want_logits=True)
+    for i, p in enumerate(prompts):
+        om = orc.OracleModel(c1_dir, 512)
+        om.prefill(list(p))
+        w1 = om.forward(int(first[i]))
+        assert max_rel(w1, lg1[i]) < LOGIT_TOL
+        assert int(nxt[i]) == int(np.argmax(w1))
+        w2 = om.forward(int(nxt[i]))
+        assert max_rel(w2, lg2[i]) < LOGIT_TOL
+        assert int(nxt2[i]) == int(np.argmax(w2))
+        om.close()
+    m.close()
+
+
 def test_ue8m0_container_bit_identical(torch_cuda, c1_dir, tmp_path):
     """An experts.midge rewritten as dtype mxfp4e8 (ue8m0 scales on disk,
     midge_b200.convert_ue8m0) loads without re-expression and gives the same
